@@ -1,0 +1,397 @@
+#!/usr/bin/env python
+"""Benchmark of the MiniCPM-4 LM decode workload on B200.
+
+Workload (one "step" = one utterance): 28-layer MiniCPM-4 (hidden 2048, 16 q / 2 kv heads,
+head_dim 128, SwiGLU 6144), tied bf16 embedding of 73448 ids, bf16 weights ~N(0, 0.02)
+(random init, synthetic), a 64-id prompt ~U[0, 73448), then 256 greedy decode steps over a
+static KV cache of capacity 4096, batch 1.
+
+  value   decode tok/s over the 256 greedy steps, device-timed with CUDA events on the
+          library stream (weights and prompt resident; the prefill is excluded and reported
+          separately), summed over ranks (one independent utterance per GPU).
+  e2e     the same tok/s through the public C ABI call vx_lm_greedy with host buffers:
+          prompt H2D, prefill, 256 steps, token ids D2H, wall clock around every call.
+
+Multi-GPU: one process per GPU (torchrun), each decodes its own utterance; no collective on
+the data path (timing only: barrier + max over ranks).  ``--impl reference`` times the CPU
+restatement of the same path on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LAYERS, HIDDEN, INTER, NH, NKV, HD, VOCAB = 28, 2048, 6144, 16, 2, 128, 73448
+PROMPT, STEPS_PER_UTT, MAX_LEN = 64, 256, 4096
+BASELINE_METRIC = "LM decode tok/s/GPU, audio-s/s at 1/2/4/8 B200; fused-op HBM GB/s vs peak"
+
+# Algorithmic bytes (the roofline basis): bf16 weights of one decoder layer, the tied
+# embedding read by the greedy head, and the KV rows read by attention at position p.
+LAYER_WEIGHT_BYTES = ((NH + 2 * NKV) * HD * HIDDEN + HIDDEN * NH * HD + 2 * INTER * HIDDEN + HIDDEN * INTER) * 2
+EMBED_BYTES = VOCAB * HIDDEN * 2
+GATE_UP_BYTES = 2 * INTER * HIDDEN * 2 + HIDDEN * 4 + INTER * 4  # one gate_up GEMV launch
+
+
+def kv_bytes(pos):
+    return LAYERS * 2 * NKV * (pos + 1) * HD * 4
+
+
+def decode_bytes_per_utt():
+    return sum(LAYERS * LAYER_WEIGHT_BYTES + EMBED_BYTES + kv_bytes(p) for p in range(PROMPT, PROMPT + STEPS_PER_UTT))
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks sampling
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ model setup
+def lm_config():
+    from voxcpm_rs_b200 import config
+    return config.lm_decode_config(layers=LAYERS, vocab=VOCAB)
+
+
+def device_weights(seed, device):
+    """Random-init bf16 weights ~N(0, 0.02) generated on the device (torch RNG), in the
+    checkpoint layout.  Norm weights ~N(1, 0.02)."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def w(*shape):
+        return (torch.randn(*shape, generator=g, device=device) * 0.02).to(torch.bfloat16).view(torch.int16)
+
+    def n(k):
+        return (1 + 0.02 * torch.randn(k, generator=g, device=device)).to(torch.bfloat16).float()
+
+    layers = [{"q": w(NH * HD, HIDDEN), "k": w(NKV * HD, HIDDEN), "v": w(NKV * HD, HIDDEN), "o": w(HIDDEN, NH * HD),
+               "gate": w(INTER, HIDDEN), "up": w(INTER, HIDDEN), "down": w(HIDDEN, INTER),
+               "ln_in": n(HIDDEN), "ln_post": n(HIDDEN)} for _ in range(LAYERS)]
+    return {"layers": layers, "norm": n(HIDDEN), "embed": w(VOCAB, HIDDEN)}
+
+
+def load_device_weights(model, w):
+    from voxcpm_rs_b200._lib import check, lib, ptr
+    L = lib()
+    for i, lw in enumerate(w["layers"]):
+        check(L.vx_lm_load_layer(model.h, i, *[ptr(lw[k]) for k in ("q", "k", "v", "o", "gate", "up", "down")],
+                                 ptr(lw["ln_in"]), ptr(lw["ln_post"])), model.ctx.h)
+    check(L.vx_lm_load_norm(model.h, ptr(w["norm"])), model.ctx.h)
+    check(L.vx_lm_load_embed(model.h, ptr(w["embed"])), model.ctx.h)
+
+
+def oracle_weights_from_device(w):
+    """f32 model-layout copy of the device weights for the CPU restatement."""
+    import numpy as np
+    import torch
+
+    def f(t):
+        return t.view(torch.bfloat16).float().cpu().numpy()
+    return {"embed": f(w["embed"]), "norm": w["norm"].cpu().numpy(),
+            "layers": [{"wqkv": np.concatenate([f(l["q"]), f(l["k"]), f(l["v"])]), "wo": f(l["o"]),
+                        "wgu": np.concatenate([f(l["gate"]), f(l["up"])]), "wd": f(l["down"]),
+                        "ln_in": l["ln_in"].cpu().numpy(), "ln_post": l["ln_post"].cpu().numpy()}
+                       for l in w["layers"]]}
+
+
+# ------------------------------------------------------------------ CPU restatement timing
+def cpu_decode_rate(fw, prompt, n_steps, warm=1):
+    """Time the oracle's greedy decode steps (after its causal prefill) on the host cores.
+    Returns (tok/s, steps timed, seconds)."""
+    import numpy as np
+    from oracle import minicpm4 as om
+    cfg = lm_config()
+    rope = om.RopeRows(cfg, PROMPT + n_steps + warm + 2)
+    cache = om.StaticKvCache(LAYERS, NKV, HD, 1, MAX_LEN)
+    y, kvs = om.model_forward(cfg, fw, om.embed(cfg, fw, np.asarray(prompt)[None]), True, rope)
+    cache.fill(kvs)
+    tok = om.argmax_first(om.linear(y[:, -1], fw["embed"])[0])
+    t0 = None
+    for s in range(warm + n_steps):
+        if s == warm:
+            t0 = time.perf_counter()
+        pos = cache.step()
+        h = om.model_forward_step(cfg, fw, om.embed(cfg, fw, [tok]), pos, cache, rope)
+        tok = om.argmax_first(om.linear(h, fw["embed"])[0])
+    dt = time.perf_counter() - t0
+    return n_steps / dt, n_steps, dt
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args):
+    """--impl reference: the CPU restatement of the path (the reference crate itself cannot
+    be built: no Rust toolchain) on the host cores, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+    import torch
+    from __graft_entry__ import load_package
+    load_package()
+    from voxcpm_rs_b200 import synth
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = lm_config()
+    fw = synth.minicpm_f32_view(synth.minicpm_weights(cfg, seed=0))
+    prompt = synth.prompt_ids(PROMPT, VOCAB, seed=0)
+    per_step = 2  # decode tokens per timed step (bounded sample)
+    rates = []
+    for i in range(args.warmup + args.steps):
+        r, _, _ = cpu_decode_rate(fw, prompt, per_step, warm=0)
+        if i >= args.warmup:
+            rates.append(r)
+    value = statistics.mean(rates)
+    line = {"impl": "reference", "metric": "LM decode tok/s", "value": value, "unit": "tok/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * per_step / value, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (random-init weights, seeded prompt)",
+            "config": {"workload": "MiniCPM-4 28-layer greedy LM decode, 64-id prompt, batch 1",
+                       "sample": f"{per_step} greedy decode steps per step after a 64-id prefill"},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": f"{per_step} decode steps per step, numpy f32 restatement "
+                                       f"(oracle/) with {threads} BLAS threads"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ our arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-steps", type=int, default=6)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    args.warmup = max(3, args.warmup)
+
+    import numpy as np
+    import torch
+    from __graft_entry__ import load_package
+    load_package()
+    from voxcpm_rs_b200 import synth
+    from voxcpm_rs_b200._lib import check, lib
+    from voxcpm_rs_b200.minicpm4 import Context, MiniCpmModel, linear_bf16
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def allmax(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    device = f"cuda:{local}"
+    ctx = Context(local)
+    cfg = lm_config()
+    w = device_weights(1234 + rank, device)
+    model = MiniCpmModel(ctx, cfg, None, max_batch=1, max_length=MAX_LEN)
+    load_device_weights(model, w)
+    prompt = synth.prompt_ids(PROMPT, VOCAB, seed=rank)
+    prompt_pinned = torch.from_numpy(prompt).pin_memory()
+    tokens_pinned = torch.empty(STEPS_PER_UTT + 1, dtype=torch.int32).pin_memory()
+    L = lib()
+    pf, dc = ctypes.c_float(), ctypes.c_float()
+
+    def one_utterance():
+        check(L.vx_lm_greedy(model.h, prompt_pinned.data_ptr(), PROMPT, STEPS_PER_UTT, tokens_pinned.data_ptr()),
+              ctx.h)
+        check(L.vx_lm_last_timing(model.h, ctypes.byref(pf), ctypes.byref(dc)), ctx.h)
+        return pf.value, dc.value
+
+    for _ in range(args.warmup):
+        one_utterance()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    launches0 = L.vx_launch_count()
+    stream = torch.cuda.ExternalStream(ctx.stream, device=device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    t0 = time.perf_counter()
+    prefill_ms = decode_ms = 0.0
+    for _ in range(args.steps):
+        a, b = one_utterance()
+        prefill_ms += a
+        decode_ms += b
+    wall = time.perf_counter() - t0
+    ev1.record(stream)
+    ev1.synchronize()
+    total_ms = ev0.elapsed_time(ev1)
+    launches = L.vx_launch_count() - launches0
+    clk = clocks.stop()
+    torch.cuda.synchronize()
+    barrier()
+    decode_ms_max = allmax(decode_ms)
+    total_ms_max = allmax(total_ms)
+    wall_max = allmax(wall)
+    prefill_ms_max = allmax(prefill_ms)
+    tokens_total = STEPS_PER_UTT * args.steps * world
+    value = tokens_total / (decode_ms_max / 1000.0)
+    e2e = tokens_total / wall_max
+
+    # ---- dominant kernel, live: the streamed GEMV on the 28 gate|up weights (50 MB each,
+    # 1.4 GB rotation > L2), CUDA events on the stream it is launched on.
+    gu = [torch.cat([l["gate"], l["up"]], 0) for l in w["layers"]]
+    xs = torch.randn(1, HIDDEN, device=device)
+    cur = torch.cuda.current_stream()
+    for i in range(LAYERS):
+        linear_bf16(ctx, gu[i], xs)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    e0.record(cur)
+    for _ in range(reps):
+        for i in range(LAYERS):
+            linear_bf16(ctx, gu[i], xs)
+    e1.record(cur)
+    e1.synchronize()
+    gemv_us = e0.elapsed_time(e1) * 1000.0 / (reps * LAYERS)
+    peak, peak_kind = measured_peaks()
+    achieved = GATE_UP_BYTES / (gemv_us * 1e-6) / 1e9
+    step_bytes = decode_bytes_per_utt()
+    step_gbs = step_bytes * args.steps / (decode_ms / 1000.0) / 1e9
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", "gemv_gate_up_traffic.json")
+    if os.path.exists(prof):
+        try:
+            traffic = json.load(open(prof)).get("bytes_per_launch")
+        except Exception:
+            traffic = None
+    del gu
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        fw = oracle_weights_from_device(w)
+        rate, n, secs = cpu_decode_rate(fw, prompt, args.cpu_steps)
+        cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"{n} greedy decode steps of the same 28-layer model after a 64-id prefill "
+                         f"({secs:.1f} s), numpy f32 restatement (oracle/), {threads} BLAS threads"}
+        del fw
+
+    if rank == 0:
+        line = {
+            "metric": "LM decode tok/s", "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (bf16 weights)", "data": "synthetic (random-init weights, seeded prompt)",
+            "baseline_metric": BASELINE_METRIC,
+            "config": {"workload": "MiniCPM-4 LM greedy decode: 28 layers, hidden 2048, 16/2 heads, head_dim 128, "
+                                   "SwiGLU 6144, tied vocab 73448, 64-id prompt + 256 greedy steps, KV capacity 4096, "
+                                   "batch 1 per GPU",
+                       "global_batch": world, "seq_len": PROMPT + STEPS_PER_UTT, "parallelism": f"replicas x{world}",
+                       "l2": "inputs larger than L2 (2.94 GB of weights read per decode step)",
+                       "value_scope": "256 decode steps per step, device time; prefill excluded (see prefill_ms)"},
+            "prefill_ms_per_step": prefill_ms_max / args.steps,
+            "decode_ms_per_token": decode_ms_max / (args.steps * STEPS_PER_UTT),
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4,
+                    "d2h_bytes_per_step": (STEPS_PER_UTT + 1) * 4,
+                    "scope": "vx_lm_greedy with host buffers: prompt H2D + prefill + 256 steps + ids D2H, wall clock"},
+            "roofline": {"bound": "hbm", "kernel": "gemv_bf16_kernel (gate|up, N=12288, K=2048)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
+                         "traffic": traffic, "algorithmic_bytes_per_launch": GATE_UP_BYTES,
+                         "launch_us": gemv_us},
+            "step_roofline": {"achieved": step_gbs, "peak": peak, "unit": "GB/s", "frac": step_gbs / peak,
+                              "algorithmic_bytes_per_utterance": step_bytes},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    ctx.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,192 @@
+/*
+ * voxcpm_b200.h -- C ABI of libvoxcpm_b200.so, the B200 (sm_100a) implementation of the
+ * voxcpm-rs hot path: the MiniCPM-4 decode step, the LocDiT flow-matching step and the
+ * AudioVAE decoder.
+ *
+ * Conventions
+ *   - Every function returns a vx_status (0 = VX_OK).  On failure vx_last_error(ctx) holds
+ *     a message.  No function aborts; kernels never trap (bounded device waits report
+ *     VX_ERR_TIMEOUT instead).
+ *   - Op-level calls take caller-owned DEVICE pointers and run on `stream` (a cudaStream_t;
+ *     NULL = the context's stream).  They are asynchronous; vx_ctx_synchronize waits.
+ *   - Model objects (vx_lm, vx_dit, vx_vae) own their weights, KV caches and work buffers.
+ *     Weight loads accept host or device pointers (copied with cudaMemcpyDefault), bf16
+ *     weights as raw bit patterns (uint16_t) in the checkpoint's [out, in] layout.
+ *   - Threading mirrors the reference's !Sync model (README.md:96-103): one host thread per
+ *     context.  vx_cancel is the only call that is safe from another thread.
+ *
+ * Reference citations are paths inside the voxcpm-rs crate.
+ */
+#ifndef VOXCPM_B200_H
+#define VOXCPM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes mirror src/error.rs:7-55 where a counterpart exists. */
+typedef enum {
+  VX_OK = 0,
+  VX_ERR_SHAPE = 1,     /* Error::ShapeMismatch (error.rs:36-41) */
+  VX_ERR_CONFIG = 2,    /* Error::InvalidConfig (error.rs:30-31) */
+  VX_ERR_CANCELLED = 3, /* Error::Cancelled (error.rs:49-51) */
+  VX_ERR_KV_FULL = 4,   /* the `KV cache is full` assert (minicpm4/cache.rs:61) */
+  VX_ERR_CUDA = 5,      /* a CUDA runtime error */
+  VX_ERR_TIMEOUT = 6,   /* a bounded device-side wait gave up */
+  VX_ERR_ARG = 7,       /* null pointer / invalid argument */
+  VX_ERR_OOM = 8,       /* device allocation failed */
+  VX_ERR_NO_DEVICE = 9  /* no usable CUDA device */
+} vx_status;
+
+typedef struct vx_ctx vx_ctx;
+typedef struct vx_lm vx_lm;
+typedef struct vx_dit vx_dit;
+typedef struct vx_vae vx_vae;
+typedef void* vx_stream;
+
+/* MiniCpm4Config + RopeScalingConfig (src/config.rs:42-84).  Factor arrays are host
+ * pointers of rope_factor_len floats (= head_dim/2, asserted as in minicpm4/rope.rs:32). */
+typedef struct {
+  int hidden_size;
+  int intermediate_size;
+  int num_attention_heads;
+  int num_key_value_heads;
+  int num_hidden_layers;
+  int vocab_size;
+  int kv_channels; /* 0 = hidden_size / num_attention_heads */
+  int max_position_embeddings;
+  int original_max_position_embeddings;
+  float rms_norm_eps;
+  float rope_theta;
+  int use_mup;
+  float scale_emb;
+  float scale_depth;
+  int no_rope;
+  const float* rope_short_factor;
+  const float* rope_long_factor;
+  int rope_factor_len;
+} vx_minicpm4_config;
+
+/* ----------------------------------------------------------------- context */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int vx_version(void);
+/* Number of CUDA kernels the calling thread has launched through this library (a graph
+ * replay counts the kernels it holds).  No reference counterpart: instrumentation. */
+unsigned long long vx_launch_count(void);
+/* Create a context bound to CUDA device `device` (its own stream, scratch pool). */
+int vx_ctx_create(int device, vx_ctx** out);
+void vx_ctx_destroy(vx_ctx* ctx);
+/* Message for the last failed call on this context (never NULL). */
+const char* vx_last_error(const vx_ctx* ctx);
+/* The context's cudaStream_t. */
+void* vx_ctx_stream(vx_ctx* ctx);
+/* Wait for the context's stream; reports VX_ERR_TIMEOUT if a device wait gave up. */
+int vx_ctx_synchronize(vx_ctx* ctx);
+/* CancelToken::cancel (voxcpm2/wrapper.rs:57-59): thread-safe; polled between AR steps
+ * (voxcpm2/model.rs:330-334). */
+void vx_cancel(vx_ctx* ctx);
+/* Clear the cancel flag (a fresh CancelToken). */
+void vx_cancel_reset(vx_ctx* ctx);
+/* Copy `bytes` between any two host/device pointers on the context's stream, then wait. */
+int vx_memcpy(vx_ctx* ctx, void* dst, const void* src, size_t bytes);
+
+/* ----------------------------------------------------------------- ops */
+
+/* MiniCpmDecoderLayer::add_residual (minicpm4/layer.rs:33-38) fused with
+ * MiniCpmRmsNorm::forward (minicpm4/mod.rs:54-68):
+ *   h = r + x * resid_scale   (r may be NULL: h = x)
+ *   y = h * (mean(h^2) + eps)^-1/2 * w
+ * x, r, h_out, y_out: [rows, hidden] f32; w: [hidden] f32.  h_out may be NULL. */
+int vx_rmsnorm_residual(vx_ctx* ctx, const float* x, const float* r, const float* w, float resid_scale,
+                        float eps, int rows, int hidden, float* h_out, float* y_out, vx_stream stream);
+
+/* MiniCpmLongRope::new (minicpm4/rope.rs:16-54), host-side: rows 0..n_pos of the f64-built
+ * cos/sin tables rounded to f32, each [n_pos, head_dim] (host pointers). */
+int vx_longrope_table(const vx_minicpm4_config* cfg, int n_pos, float* cos_out, float* sin_out);
+
+/* apply_rotary_pos_emb (minicpm4/rope.rs:76-95), in place on q [B,nh,S,d] and k [B,nkv,S,d]
+ * with gathered cos/sin rows [S, d] (MiniCpmLongRope::gather, rope.rs:58-62). */
+int vx_rope_apply(vx_ctx* ctx, float* q, float* k, const float* cos, const float* sin, int B, int nh, int nkv,
+                  int S, int head_dim, vx_stream stream);
+
+/* burn::nn::Linear::forward with bf16 weights [N, K] ([out, in]) and optional bias [N]:
+ * y[M, N] = x[M, K] . W^T + b.  M = 1 uses the streamed GEMV. */
+int vx_linear_bf16(vx_ctx* ctx, const uint16_t* w, const float* bias, const float* x, int M, int N, int K,
+                   float* y, vx_stream stream);
+
+/* MiniCpmAttention::sdpa + repeat_kv over a static cache (minicpm4/attention.rs:129-150,
+ * 156-204) for one query token per batch row: q [B, nh*d], caches [B, nkv, s_max, d] filled
+ * over 0..cur_len, out [B, nh*d].  Split-K flash-decode; uses context scratch memory. */
+int vx_attention_decode(vx_ctx* ctx, const float* q, const float* kcache, const float* vcache, int B, int nh,
+                        int nkv, int head_dim, int s_max, int cur_len, float* out, vx_stream stream);
+
+/* MiniCpmMlp::forward (minicpm4/mlp.rs:28-34): out = down(silu(gate) * up) with the fused
+ * gate|up weight [2*inter, hidden] (gate first) and down [hidden, inter]; x [rows, hidden]. */
+int vx_mlp_swiglu(vx_ctx* ctx, const uint16_t* w_gate_up, const uint16_t* w_down, const float* x, int rows,
+                  int hidden, int inter, float* out, vx_stream stream);
+
+/* UnifiedCfm::solve_euler's per-step update (locdit/unified_cfm.rs:132-158), fused:
+ * out2b [2B, C, T] holds the conditional rows then the unconditional rows of the DiT
+ * output; x [B, C, T] is updated in place: x -= dt * v, with v the CFG or CFG-zero-star
+ * velocity at guidance `cfg`. */
+int vx_cfg_euler(vx_ctx* ctx, const float* out2b, float* x, int B, int C, int T, float cfg, double dt,
+                 int zero_star, vx_stream stream);
+
+/* ----------------------------------------------------------------- MiniCPM-4 model */
+
+/* MiniCpmModel::new (minicpm4/model.rs:26-41) + StaticKvCache::new (minicpm4/cache.rs:21-44)
+ * for up to max_batch rows and max_length positions. */
+int vx_lm_create(vx_ctx* ctx, const vx_minicpm4_config* cfg, int max_batch, int max_length, vx_lm** out);
+void vx_lm_destroy(vx_lm* lm);
+/* One decoder layer's weights in checkpoint layout; q/k/v and gate/up are fused on upload
+ * as weights.rs:648-772 does. */
+int vx_lm_load_layer(vx_lm* lm, int layer, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                     const uint16_t* o, const uint16_t* gate, const uint16_t* up, const uint16_t* down,
+                     const float* ln_in, const float* ln_post);
+int vx_lm_load_norm(vx_lm* lm, const float* w);
+/* Tied token embedding [vocab, hidden] bf16 (Embedding in minicpm4/model.rs:27-28). */
+int vx_lm_load_embed(vx_lm* lm, const uint16_t* embed);
+/* StaticKvCache::reset (minicpm4/cache.rs:67-69). */
+int vx_lm_reset(vx_lm* lm);
+/* StaticKvCache::current_length. */
+int vx_lm_position(const vx_lm* lm);
+int vx_lm_set_position(vx_lm* lm, int pos);
+/* Write / read positions 0..n_pos of one layer's K and V cache for batch row `b`
+ * ([nkv, n_pos, d] f32 each, host or device pointers). */
+int vx_lm_kv_write(vx_lm* lm, int layer, int b, const float* k, const float* v, int n_pos);
+int vx_lm_kv_read(vx_lm* lm, int layer, int b, float* k, float* v, int n_pos);
+/* MiniCpmModel::embed * scale_emb (minicpm4/model.rs:87-100): ids [n] device int32,
+ * out [n, hidden] device. */
+int vx_lm_embed(vx_lm* lm, const int32_t* ids, int n, float* out);
+/* MiniCpmModel::forward (minicpm4/model.rs:43-62): embeds/hidden_out [B, S, hidden] device.
+ * With fill_cache the post-RoPE K/V of positions 0..S seed the cache and the position
+ * becomes S (StaticKvCache::fill, cache.rs:47-58). */
+int vx_lm_forward(vx_lm* lm, const float* embeds, int B, int S, int causal, int fill_cache, float* hidden_out);
+/* MiniCpmModel::forward_step (minicpm4/model.rs:64-84) for batch 1: takes the position from
+ * StaticKvCache::step (cache.rs:60-65; VX_ERR_KV_FULL when full).  embeds/hidden_out [hidden]. */
+int vx_lm_forward_step(vx_lm* lm, const float* embeds, float* hidden_out);
+/* MiniCpmDecoderLayer::forward_step (minicpm4/layer.rs:57-73) for batch 1 at position `pos`,
+ * in place on hidden [hidden] (device). */
+int vx_lm_layer_forward_step(vx_lm* lm, int layer, float* hidden, int pos);
+/* Greedy decode over the tied embedding (the LM-decode workload; the reference has no LM
+ * head): causal prefill of the prompt (host int32 ids) filling the cache, then n_steps
+ * forward_step calls.  Each pick is argmax(norm(h) . E^T) (ties -> lowest id) and feeds
+ * embed(id) * scale_emb back.  tokens_out (host) receives n_steps + 1 ids (the first from the
+ * prefill's last row).  The decode step runs as one captured CUDA graph replayed per step
+ * with no host round trip; cancellation (vx_cancel) is polled between steps. */
+int vx_lm_greedy(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps, int32_t* tokens_out);
+/* Device time of the last vx_lm_greedy call split into prefill and decode (CUDA events on
+ * the context stream).  Mirrors the VOXCPM_PROFILE split of voxcpm2/model.rs:316-372. */
+int vx_lm_last_timing(const vx_lm* lm, float* prefill_ms, float* decode_ms);
+/* Logits of the last greedy pick (host [vocab]); valid after vx_lm_greedy. */
+int vx_lm_last_logits(vx_lm* lm, float* logits_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VOXCPM_B200_H */

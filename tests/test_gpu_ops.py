@@ -1,0 +1,170 @@
+"""Op-level parity on the GPU: each C-ABI op against the oracle on the same seeded inputs.
+
+Tolerances (max-abs/rel): 1e-3 for f32 ops, 2e-2 for bf16-weight paths.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from tests.conftest import assert_close
+from oracle import audiovae as oav  # noqa: F401
+from oracle import locdit as old
+from oracle import minicpm4 as om
+
+pytestmark = pytest.mark.gpu
+
+F32_TOL = dict(atol=1e-3, rtol=1e-3)
+BF16_TOL = dict(atol=2e-2, rtol=2e-2)
+
+
+def _t(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _bits(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda()
+
+
+@pytest.mark.parametrize("rows,hidden,residual", [(512, 2048, True), (7, 1024, False), (1, 2048, True),
+                                                  (3, 4096, True), (2, 8192, False)])
+def test_rmsnorm_residual(ctx, rows, hidden, residual):
+    """RMSNorm + residual (the RMSNorm microbenchmark workload at [512, 2048], eps 1e-6)."""
+    from voxcpm_rs_b200.minicpm4 import MiniCpmRmsNorm
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((rows, hidden), dtype=np.float32)
+    r = rng.standard_normal((rows, hidden), dtype=np.float32) if residual else None
+    w = (1.0 + 0.02 * rng.standard_normal(hidden)).astype(np.float32)
+    h_ref, y_ref = om.rmsnorm_residual(x, r, w, 1e-6)
+    norm = MiniCpmRmsNorm(ctx, _t(w), 1e-6)
+    h, y = norm.forward(_t(x), None if r is None else _t(r), 1.0, return_residual=True)
+    import torch
+    torch.cuda.synchronize()
+    assert_close(h.cpu().numpy(), h_ref, **F32_TOL, what="h")
+    assert_close(y.cpu().numpy(), y_ref, **F32_TOL, what="y")
+
+
+def test_rmsnorm_residual_scale(ctx):
+    """muP residual scale s = scale_depth / sqrt(L): h = r + x * s."""
+    from voxcpm_rs_b200.minicpm4 import MiniCpmRmsNorm
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((4, 2048), dtype=np.float32)
+    r = rng.standard_normal((4, 2048), dtype=np.float32)
+    w = np.ones(2048, np.float32)
+    s = np.float32(1.4 / math.sqrt(28))
+    h_ref, y_ref = om.rmsnorm_residual(x, r, w, 1e-6, s)
+    h, y = MiniCpmRmsNorm(ctx, _t(w), 1e-6).forward(_t(x), _t(r), float(s), return_residual=True)
+    assert_close(h.cpu().numpy(), h_ref, **F32_TOL, what="h")
+    assert_close(y.cpu().numpy(), y_ref, **F32_TOL, what="y")
+
+
+@pytest.mark.parametrize("max_pos", [32768, 65536])
+def test_rope_apply(ctx, max_pos):
+    """apply_rotary_pos_emb with the LongRoPE tables (short factors at 32768, long above)."""
+    from voxcpm_rs_b200 import config
+    from voxcpm_rs_b200.minicpm4 import MiniCpmLongRope, apply_rotary_pos_emb
+    cfg = config.lm_decode_config(layers=1, vocab=0, max_position_embeddings=max_pos)
+    rope = MiniCpmLongRope(cfg, n_pos=4096)
+    pos = np.array([0, 1, 999, 4095], np.int64)
+    import torch
+    cos, sin = rope.gather(torch.from_numpy(pos).cuda())
+    rng = np.random.default_rng(2)
+    q = rng.standard_normal((1, 16, 4, 128), dtype=np.float32)
+    k = rng.standard_normal((1, 2, 4, 128), dtype=np.float32)
+    cr, sr = om.longrope_table(cfg, 4096)
+    qe, ke = om.apply_rotary_pos_emb(q, k, cr[pos], sr[pos])
+    qg, kg = apply_rotary_pos_emb(ctx, _t(q), _t(k), cos, sin)
+    assert_close(qg.cpu().numpy(), qe, **F32_TOL, what="q")
+    assert_close(kg.cpu().numpy(), ke, **F32_TOL, what="k")
+
+
+@pytest.mark.parametrize("m,n,k,bias", [(1, 2560, 2048, False), (1, 2048, 6144, False), (1, 1024, 1024, True),
+                                        (1, 73448, 2048, False), (22, 1280, 1024, False), (22, 64, 1024, True),
+                                        (64, 2560, 2048, False), (2, 1024, 64, True)])
+def test_linear_bf16(ctx, m, n, k, bias):
+    """burn::nn::Linear with bf16 weights: streamed GEMV (M=1) and the few-row GEMM."""
+    from voxcpm_rs_b200 import synth
+    from voxcpm_rs_b200.minicpm4 import linear_bf16
+    rng = np.random.default_rng(3)
+    wb = synth.bf16_bits(0.02 * rng.standard_normal((n, k), dtype=np.float32))
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    b = (0.02 * rng.standard_normal(n)).astype(np.float32) if bias else None
+    want = om.linear(x, synth.bf16_to_f32(wb), b)
+    got = linear_bf16(ctx, _bits(wb), _t(x), None if b is None else _t(b))
+    assert_close(got.cpu().numpy(), want, **BF16_TOL, what="linear")
+    # the f32 accumulation is far tighter than the stated tolerance
+    assert np.abs(got.cpu().numpy() - want).max() < 1e-4
+
+
+def test_linear_accumulator_alternating(ctx):
+    """f32-accumulator probe (after examples/bf16_matacc.rs:27-35): an alternating +-1 row of
+    K=512 against ones must sum to exactly 0, and a ones row to exactly K."""
+    from voxcpm_rs_b200 import synth
+    from voxcpm_rs_b200.minicpm4 import linear_bf16
+    k = 512
+    w = np.zeros((8, k), np.float32)
+    w[0] = np.where(np.arange(k) % 2 == 0, 1.0, -1.0)
+    w[1] = 1.0
+    got = linear_bf16(ctx, _bits(synth.bf16_bits(w)), _t(np.ones((1, k), np.float32))).cpu().numpy()
+    assert got[0, 0] == 0.0 and got[0, 1] == float(k)
+
+
+@pytest.mark.parametrize("cur_len,d", [(1001, 128), (1, 128), (64, 128), (4096, 128), (11, 64), (777, 64)])
+def test_attention_decode(ctx, cur_len, d):
+    """sdpa over a static KV cache (decode step; the one-layer workload fills it to p=1000)."""
+    from voxcpm_rs_b200.minicpm4 import attention_decode
+    rng = np.random.default_rng(4)
+    nh, nkv, s_max = 16, 2, 4096
+    q = rng.standard_normal((1, nh * d), dtype=np.float32)
+    kc = np.zeros((1, nkv, s_max, d), np.float32)
+    vc = np.zeros((1, nkv, s_max, d), np.float32)
+    kc[:, :, :cur_len] = rng.standard_normal((1, nkv, cur_len, d), dtype=np.float32)
+    vc[:, :, :cur_len] = rng.standard_normal((1, nkv, cur_len, d), dtype=np.float32)
+    qh = q.reshape(1, nh, 1, d)
+    want = om.sdpa(qh, om.repeat_kv(kc[:, :, :cur_len], nh // nkv), om.repeat_kv(vc[:, :, :cur_len], nh // nkv),
+                   1.0 / math.sqrt(d), False).reshape(1, nh * d)
+    got = attention_decode(ctx, _t(q), _t(kc), _t(vc), cur_len)
+    assert_close(got.cpu().numpy(), want, **F32_TOL, what="attn")
+    # replay: the kernel resets its arrival counters itself
+    got2 = attention_decode(ctx, _t(q), _t(kc), _t(vc), cur_len)
+    assert np.array_equal(got.cpu().numpy(), got2.cpu().numpy())
+
+
+@pytest.mark.parametrize("rows", [1, 22])
+def test_mlp_swiglu(ctx, rows):
+    """MiniCpmMlp::forward: down(silu(gate) * up) with fused gate|up."""
+    from voxcpm_rs_b200 import synth
+    from voxcpm_rs_b200.minicpm4 import MiniCpmMlp
+    rng = np.random.default_rng(5)
+    H, I = 2048, 6144
+    wgu = synth.bf16_bits(0.02 * rng.standard_normal((2 * I, H), dtype=np.float32))
+    wd = synth.bf16_bits(0.02 * rng.standard_normal((H, I), dtype=np.float32))
+    x = rng.standard_normal((rows, H), dtype=np.float32)
+
+    class _C:
+        intermediate_size = I
+    want = om.mlp(_C, {"wgu": synth.bf16_to_f32(wgu), "wd": synth.bf16_to_f32(wd)}, x)
+    got = MiniCpmMlp(ctx, _bits(wgu), _bits(wd)).forward(_t(x))
+    assert_close(got.cpu().numpy(), want, **BF16_TOL, what="mlp")
+    assert np.abs(got.cpu().numpy() - want).max() < 1e-4
+
+
+@pytest.mark.parametrize("zero_star", [False, True])
+@pytest.mark.parametrize("cfg_value", [2.0, 1.5])
+def test_cfg_euler(ctx, zero_star, cfg_value):
+    """Fused CFG(-zero-star) + Euler update vs the oracle's cfg_combine + euler_update."""
+    from voxcpm_rs_b200._lib import check, lib, ptr
+    rng = np.random.default_rng(6)
+    B, Cc, T = 3, 64, 4
+    out = rng.standard_normal((2 * B, Cc, T), dtype=np.float32)
+    x = rng.standard_normal((B, Cc, T), dtype=np.float32)
+    dt = 0.1 + 1e-9
+    want = old.euler_update(x, old.cfg_combine(out[:B], out[B:], cfg_value, zero_star), dt)
+    xg, og = _t(x), _t(out)
+    import torch
+    torch.cuda.synchronize()
+    check(lib().vx_cfg_euler(ctx.h, ptr(og), ptr(xg), B, Cc, T, cfg_value, dt, int(zero_star), None), ctx.h)
+    ctx.synchronize()
+    assert_close(xg.cpu().numpy(), want, **F32_TOL, what="cfg_euler")

@@ -1,0 +1,262 @@
+// Row-wise and elementwise kernels of the hot path (sm_100a):
+//   * fused residual-add + RMSNorm          (layer.rs:33-38 + mod.rs:54-68)
+//   * RoPE + KV-cache scatter for S>1 rows  (rope.rs:76-95, attention.rs:55-88, cache.rs:47-58)
+//   * SiLU-gate multiply for S>1 rows       (mlp.rs:31-33)
+//   * token embedding * scale_emb           (minicpm4/model.rs:87-92, voxcpm2/model.rs:145)
+//   * fused CFG(-zero-star) + Euler update   (unified_cfm.rs:132-158)
+#include <cfloat>
+
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace vx {
+
+// ------------------------------------------------------------ residual add + RMSNorm
+// h = r + x * resid_scale (r optional); y = h * (mean(h^2)+eps)^-1/2 * w.
+// One CTA per row; each thread keeps its slice of the row in registers (hidden <= 8192).
+template <int VPT>  // float4 per thread
+__global__ void __launch_bounds__(256) rmsnorm_residual_kernel(const float* __restrict__ x,
+                                                               const float* __restrict__ r,
+                                                               const float* __restrict__ w, float resid_scale,
+                                                               float eps, int hidden, float* h_out, float* y_out) {
+  __shared__ float red[8];
+  pdl_wait();
+  pdl_launch_dependents();
+  const size_t row = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * hidden);
+  const float4* rr = r ? reinterpret_cast<const float4*>(r + row * hidden) : nullptr;
+  float4 v[VPT];
+  float ss = 0.f;
+  const int n4 = hidden / 4;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = threadIdx.x + i * 256;
+    if (c < n4) {
+      float4 a = __ldcs(xr + c);
+      if (rr) {
+        const float4 b = __ldcs(rr + c);
+        a.x = b.x + a.x * resid_scale;
+        a.y = b.y + a.y * resid_scale;
+        a.z = b.z + a.z * resid_scale;
+        a.w = b.w + a.w * resid_scale;
+      }
+      v[i] = a;
+      ss = fmaf(a.x, a.x, ss);
+      ss = fmaf(a.y, a.y, ss);
+      ss = fmaf(a.z, a.z, ss);
+      ss = fmaf(a.w, a.w, ss);
+    }
+  }
+  ss = warp_sum(ss);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float inv = 1.0f / sqrtf(tot / (float)hidden + eps);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = threadIdx.x + i * 256;
+    if (c < n4) {
+      if (h_out) __stcs(reinterpret_cast<float4*>(h_out + row * hidden) + c, v[i]);
+      const float4 ww = __ldg(w4 + c);
+      float4 y;
+      y.x = (v[i].x * inv) * ww.x;
+      y.y = (v[i].y * inv) * ww.y;
+      y.z = (v[i].z * inv) * ww.z;
+      y.w = (v[i].w * inv) * ww.w;
+      __stcs(reinterpret_cast<float4*>(y_out + row * hidden) + c, y);
+    }
+  }
+}
+
+cudaError_t launch_rmsnorm_residual(const float* x, const float* r, const float* w, float resid_scale,
+                                    float eps, int rows, int hidden, float* h_out, float* y_out,
+                                    cudaStream_t st) {
+  if (hidden % 4 != 0 || hidden > 8192 || rows <= 0) return cudaErrorInvalidValue;
+  const int n4 = hidden / 4;
+  const int vpt = (n4 + 255) / 256;
+  count_launch();
+  if (vpt <= 2)
+    rmsnorm_residual_kernel<2><<<rows, 256, 0, st>>>(x, r, w, resid_scale, eps, hidden, h_out, y_out);
+  else if (vpt <= 4)
+    rmsnorm_residual_kernel<4><<<rows, 256, 0, st>>>(x, r, w, resid_scale, eps, hidden, h_out, y_out);
+  else
+    rmsnorm_residual_kernel<8><<<rows, 256, 0, st>>>(x, r, w, resid_scale, eps, hidden, h_out, y_out);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ RoPE + KV scatter (S rows)
+// qkv [B*S, (nh+2nkv)*d] raw projections.  q_out [B*S, nh*d] (rotated);
+// k (rotated) and v written to cache [B, nkv, s_max, d] at position pos0 + s.
+// Rope angles use position pos0 + s, formed in f64 (rope.rs:38-46).
+__global__ void rope_scatter_kernel(const float* __restrict__ qkv, int B, int S, int nh, int nkv, int d,
+                                    const RopeParams* rope, int pos0, float* q_out, float* kcache,
+                                    float* vcache, int s_max) {
+  const int half = d / 2;
+  const int heads = nh + 2 * nkv;
+  const size_t total = (size_t)B * S * heads * half;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const int i = idx % half;
+    const int h = (idx / half) % heads;
+    const size_t tok = idx / ((size_t)half * heads);
+    const int b = tok / S, s = tok % S;
+    const int pos = pos0 + s;
+    const float* src = qkv + tok * (size_t)heads * d + (size_t)h * d;
+    const float xa = src[i], xb = src[i + half];
+    float oa = xa, ob = xb;
+    if (h < nh + nkv && rope != nullptr) {
+      const double f = ((double)pos * rope->inv_freq[i]) / rope->ext[i];
+      double sd, cd;
+      sincos(f, &sd, &cd);
+      const float c = (float)(cd * rope->scaling_factor), sn = (float)(sd * rope->scaling_factor);
+      oa = __fadd_rn(__fmul_rn(xa, c), __fmul_rn(-xb, sn));
+      ob = __fadd_rn(__fmul_rn(xb, c), __fmul_rn(xa, sn));
+    }
+    if (h < nh) {
+      float* dst = q_out + tok * (size_t)nh * d + (size_t)h * d;
+      dst[i] = oa;
+      dst[i + half] = ob;
+    } else {
+      const bool is_k = h < nh + nkv;
+      const int g = is_k ? h - nh : h - nh - nkv;
+      float* dst = (is_k ? kcache : vcache) + (((size_t)b * nkv + g) * s_max + pos) * d;
+      dst[i] = oa;
+      dst[i + half] = ob;
+    }
+  }
+}
+
+cudaError_t launch_rope_scatter(const float* qkv, int B, int S, int nh, int nkv, int d, const RopeParams* rope,
+                                int pos0, float* q_out, float* kcache, float* vcache, int s_max,
+                                cudaStream_t st) {
+  const size_t total = (size_t)B * S * (nh + 2 * nkv) * (d / 2);
+  const int grid = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  count_launch();
+  rope_scatter_kernel<<<grid, 256, 0, st>>>(qkv, B, S, nh, nkv, d, rope, pos0, q_out, kcache, vcache, s_max);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ RoPE apply on [B,H,S,D]
+// apply_rotary_pos_emb with explicit cos/sin rows [S, D] (rope.rs:76-95), in place.
+__global__ void rope_apply_kernel(float* x, int B, int H, int S, int d, const float* cos, const float* sin) {
+  const int half = d / 2;
+  const size_t total = (size_t)B * H * S * half;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const int i = idx % half;
+    const size_t rowi = idx / half;  // (b, h, s)
+    const int s = rowi % S;
+    float* p = x + rowi * d;
+    const float xa = p[i], xb = p[i + half];
+    const float ca = cos[(size_t)s * d + i], cb = cos[(size_t)s * d + i + half];
+    const float sa = sin[(size_t)s * d + i], sb = sin[(size_t)s * d + i + half];
+    p[i] = __fadd_rn(__fmul_rn(xa, ca), __fmul_rn(-xb, sa));
+    p[i + half] = __fadd_rn(__fmul_rn(xb, cb), __fmul_rn(xa, sb));
+  }
+}
+
+cudaError_t launch_rope_apply(float* x, int B, int H, int S, int d, const float* cos, const float* sin,
+                              cudaStream_t st) {
+  const size_t total = (size_t)B * H * S * (d / 2);
+  if (total == 0) return cudaSuccess;
+  const int grid = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  count_launch();
+  rope_apply_kernel<<<grid, 256, 0, st>>>(x, B, H, S, d, cos, sin);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ SiLU gate * up (S rows)
+__global__ void silu_mul_kernel(const float* __restrict__ gu, int M, int inter, float* __restrict__ act) {
+  const size_t total = (size_t)M * inter;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const size_t m = idx / inter, i = idx % inter;
+    const float g = gu[m * 2 * inter + i], u = gu[m * 2 * inter + inter + i];
+    act[idx] = silu(g) * u;
+  }
+}
+
+cudaError_t launch_silu_mul(const float* gu, int M, int inter, float* act, cudaStream_t st) {
+  const size_t total = (size_t)M * inter;
+  const int grid = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  count_launch();
+  silu_mul_kernel<<<grid, 256, 0, st>>>(gu, M, inter, act);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ embedding gather
+__global__ void embed_kernel(const uint16_t* __restrict__ E, const int* __restrict__ ids, int n, int H,
+                             float scale, float* __restrict__ out) {
+  for (int m = blockIdx.x; m < n; m += gridDim.x) {
+    const uint16_t* e = E + (size_t)ids[m] * H;
+    for (int k = threadIdx.x; k < H; k += blockDim.x)
+      out[(size_t)m * H + k] = __uint_as_float(((uint32_t)e[k]) << 16) * scale;
+  }
+}
+
+cudaError_t launch_embed(const uint16_t* E, const int* ids, int n, int H, float scale, float* out,
+                         cudaStream_t st) {
+  count_launch();
+  embed_kernel<<<n < 1024 ? n : 1024, 256, 0, st>>>(E, ids, n, H, scale, out);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ CFG + Euler (fused)
+// out2b [2B, C, T]: rows 0..B are the conditional (pos) branch, B..2B the unconditional
+// (neg) one.  One CTA per batch element: the zero-star projection st = <pos,neg>/(|neg|^2+1e-8)
+// is a block reduction, then v and x <- x - dt * v are applied in the same pass.
+__global__ void __launch_bounds__(256) cfg_euler_kernel(const float* __restrict__ out2b, float* __restrict__ x,
+                                                        int B, int n, float cfg, float one_minus_cfg, float dt,
+                                                        int zero_star) {
+  __shared__ float red[2][8];
+  const int b = blockIdx.x;
+  const float* pos = out2b + (size_t)b * n;
+  const float* neg = out2b + (size_t)(B + b) * n;
+  float* xb = x + (size_t)b * n;
+  float st_scaled = 0.f;
+  if (zero_star) {
+    float dot = 0.f, sq = 0.f;
+    for (int i = threadIdx.x; i < n; i += 256) {
+      const float p = pos[i], q = neg[i];
+      dot = fmaf(p, q, dot);
+      sq = fmaf(q, q, sq);
+    }
+    dot = warp_sum(dot);
+    sq = warp_sum(sq);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+      red[0][warp] = dot;
+      red[1][warp] = sq;
+    }
+    __syncthreads();
+    float D = 0.f, Q = 0.f;
+    for (int w = 0; w < 8; ++w) {
+      D += red[0][w];
+      Q += red[1][w];
+    }
+    const float st = D / (Q + 1e-8f);
+    st_scaled = st * one_minus_cfg;  // st.mul_scalar(1 - cfg), 1-cfg formed in f64 (unified_cfm.rs:148)
+  }
+  for (int i = threadIdx.x; i < n; i += 256) {
+    const float p = pos[i], q = neg[i];
+    float v;
+    if (zero_star)
+      v = q * st_scaled + p * cfg;  // neg*st*(1-cfg) + pos*cfg (unified_cfm.rs:149)
+    else
+      v = q + (p - q) * cfg;  // neg + (pos-neg)*cfg (unified_cfm.rs:151)
+    xb[i] = xb[i] - v * dt;   // x - dphi*dt (unified_cfm.rs:155)
+  }
+}
+
+cudaError_t launch_cfg_euler(const float* out2b, float* x, int B, int n, double cfg, double dt, int zero_star,
+                             cudaStream_t st) {
+  count_launch();
+  cfg_euler_kernel<<<B, 256, 0, st>>>(out2b, x, B, n, (float)cfg, (float)(1.0 - cfg), (float)dt, zero_star);
+  return cudaGetLastError();
+}
+
+}  // namespace vx

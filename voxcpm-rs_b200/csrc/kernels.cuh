@@ -1,0 +1,44 @@
+// Argument blocks of the attention and few-row GEMM kernels (shared by the kernels and
+// the host runtime).
+#pragma once
+#include <cstdint>
+
+namespace vx {
+
+struct AttnDecodeArgs {
+  const float* q;       // [B, nh*d]
+  const float* kcache;  // [B, nkv, s_max, d]
+  const float* vcache;
+  int B, nh, nkv, d, s_max;
+  const int* pos_ptr;  // if non-null: len = *pos_ptr + 1 (device position of the new token)
+  int len;             // otherwise the filled length
+  float scale;
+  int nsplit;
+  float* partials;         // [B, nkv, nsplit, n_rep, d + 2]
+  unsigned int* counters;  // [B * nkv], zero-initialised; reset by the kernel
+  float* out;              // [B, nh*d]
+};
+
+struct AttnPrefillArgs {
+  const float* q;  // [B, S, nh*d]
+  const float* k;  // [B, nkv, s_max, d]
+  const float* v;
+  int B, S, nh, nkv, d, s_max;
+  float scale;
+  int causal;
+  float* out;  // [B, S, nh*d]
+};
+
+struct GemmArgs {
+  const float* X;  // [M, K] (row stride ldx)
+  int ldx;
+  const uint16_t* W;  // [N, K]
+  const float* bias;  // [N] or null
+  const float* R;     // [M, N] residual or null (row stride ldy); may alias Y
+  float res_scale;
+  float* Y;  // [M, N] (row stride ldy)
+  int ldy;
+  int M, N, K;
+};
+
+}  // namespace vx

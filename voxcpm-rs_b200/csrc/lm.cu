@@ -1,0 +1,607 @@
+// MiniCPM-4 model object: weights, static KV cache, prefill, the batch-1 decode step and
+// the graph-captured greedy decode loop (reference src/minicpm4/model.rs, layer.rs,
+// attention.rs, mlp.rs, cache.rs).
+//
+// HBM layout (per model):
+//   weights  bf16, per layer: wqkv [(nh+2nkv)*d, H] | wo [H, nh*d] | wgu [2I, H] | wd [H, I]
+//            (checkpoint [out, in] layout, q|k|v and gate|up fused along out)
+//   norms    f32 [H] (ln_in, ln_post per layer; final norm)
+//   embed    bf16 [V, H] (tied: input embedding and greedy LM head)
+//   KV cache f32 [L][B][nkv][max_length][d] for K and for V (post-RoPE K)
+//   state    device ints: position of the token being decoded, greedy step index, token ids
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+#include "runtime.cuh"
+
+using namespace vx;
+
+namespace {
+
+struct LmLayer {
+  uint16_t* wqkv = nullptr;
+  uint16_t* wo = nullptr;
+  uint16_t* wgu = nullptr;
+  uint16_t* wd = nullptr;
+  float* ln_in = nullptr;
+  float* ln_post = nullptr;
+};
+
+}  // namespace
+
+struct vx_lm {
+  vx_ctx* ctx = nullptr;
+  vx_minicpm4_config cfg{};
+  int H = 0, I = 0, nh = 0, nkv = 0, d = 0, L = 0, V = 0, qs = 0, ks = 0;
+  float res_scale = 1.f, emb_scale = 1.f, attn_scale = 1.f;
+  int max_batch = 1, max_length = 0;
+  int cur_len = 0;  // StaticKvCache::current_length (host mirror)
+
+  std::vector<LmLayer> layers;
+  void* weight_slab = nullptr;
+  float* norm_w = nullptr;
+  uint16_t* embed = nullptr;
+  RopeParams* rope = nullptr;  // device, nullptr when no_rope
+  float* kcache = nullptr;
+  float* vcache = nullptr;
+
+  // device state for the graph-replayed decode step
+  int* d_pos = nullptr;
+  int* d_step = nullptr;
+  int* d_tokens = nullptr;
+  // batch-1 decode buffers
+  float* x = nullptr;       // residual stream [H]
+  float* q = nullptr;       // [nh*d]
+  float* attn = nullptr;    // [nh*d]
+  float* act = nullptr;     // [I]
+  float* logits = nullptr;  // [V]
+  float* attn_partials = nullptr;
+  unsigned* attn_counters = nullptr;
+  float2* argmax_partials = nullptr;
+  unsigned* argmax_counter = nullptr;
+  int attn_nsplit = 16;
+  // prefill buffers (grown on demand)
+  size_t pf_rows = 0;
+  float *pf_x = nullptr, *pf_xn = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_attn = nullptr,
+        *pf_gu = nullptr, *pf_act = nullptr, *pf_k = nullptr, *pf_v = nullptr;
+  int* pf_ids = nullptr;
+  int pf_ids_cap = 0;
+
+  cudaGraphExec_t step_exec = nullptr;
+  unsigned long long step_kernels = 0;
+  cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+  float t_prefill_ms = 0.f, t_decode_ms = 0.f;
+  int pos_host = 0;
+
+  size_t kv_layer_stride() const { return (size_t)max_batch * nkv * max_length * d; }
+  float* kc(int l, int b) { return kcache + l * kv_layer_stride() + (size_t)b * nkv * max_length * d; }
+  float* vc(int l, int b) { return vcache + l * kv_layer_stride() + (size_t)b * nkv * max_length * d; }
+};
+
+namespace {
+
+void free_prefill(vx_lm* lm) {
+  for (float** p : {&lm->pf_x, &lm->pf_xn, &lm->pf_qkv, &lm->pf_q, &lm->pf_attn, &lm->pf_gu, &lm->pf_act,
+                    &lm->pf_k, &lm->pf_v}) {
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+  }
+  lm->pf_rows = 0;
+}
+
+int ensure_prefill(vx_lm* lm, size_t rows, int B, int S, bool need_kv) {
+  if (rows <= lm->pf_rows && (!need_kv || lm->pf_k)) return VX_OK;
+  free_prefill(lm);
+  const size_t H = lm->H, q = lm->qs, qkv = lm->qs + 2 * lm->ks, I = lm->I;
+  bool ok = cudaMalloc(&lm->pf_x, rows * H * 4) == cudaSuccess && cudaMalloc(&lm->pf_xn, rows * H * 4) == cudaSuccess &&
+            cudaMalloc(&lm->pf_qkv, rows * qkv * 4) == cudaSuccess && cudaMalloc(&lm->pf_q, rows * q * 4) == cudaSuccess &&
+            cudaMalloc(&lm->pf_attn, rows * q * 4) == cudaSuccess && cudaMalloc(&lm->pf_gu, rows * 2 * I * 4) == cudaSuccess &&
+            cudaMalloc(&lm->pf_act, rows * I * 4) == cudaSuccess &&
+            cudaMalloc(&lm->pf_k, rows * lm->ks * 4) == cudaSuccess && cudaMalloc(&lm->pf_v, rows * lm->ks * 4) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    free_prefill(lm);
+    return fail(lm->ctx, VX_ERR_OOM, "prefill buffers (%zu rows) allocation failed", rows);
+  }
+  lm->pf_rows = rows;
+  return VX_OK;
+}
+
+// ----------------------------------------------------------------- kernel sequences
+
+// One decoder layer for batch row 0 at the device position *d_pos (or `pos` when
+// pos_from_device is false): 5 launches.
+int enqueue_layer_step(vx_lm* lm, int l, cudaStream_t st, bool pos_from_device, int pos) {
+  vx_ctx* ctx = lm->ctx;
+  const LmLayer& w = lm->layers[l];
+  const bool pdl = ctx->pdl;
+  // (1) input_layernorm -> qkv_proj -> LongRoPE -> KV cache write  (layer.rs:64-66, attention.rs:102-127)
+  GemvArgs a = {};
+  a.W = w.wqkv;
+  a.N = lm->qs + 2 * lm->ks;
+  a.K = lm->H;
+  a.x = lm->x;
+  a.norm_w = w.ln_in;
+  a.eps = lm->cfg.rms_norm_eps;
+  a.map_mode = MAP_ROPE_PAIRS;
+  a.map_param = lm->d / 16;
+  a.groups_per_cta = 2 * pick_groups(a.N / 16);
+  a.nh = lm->nh;
+  a.nkv = lm->nkv;
+  a.hd = lm->d;
+  a.rope = lm->rope;
+  a.pos_ptr = pos_from_device ? lm->d_pos : nullptr;
+  a.pos_val = pos;
+  a.q_out = lm->q;
+  a.kcache = lm->kc(l, 0);
+  a.vcache = lm->vc(l, 0);
+  a.s_max = lm->max_length;
+  VX_CUDA(ctx, launch_gemv(a, EPI_QKV_ROPE, st, pdl, ctx->dev_err));
+  // (2) sdpa over the cached prefix 0..pos+1 (attention.rs:129-150)
+  AttnDecodeArgs ad = {lm->q, lm->kc(l, 0), lm->vc(l, 0), 1, lm->nh, lm->nkv, lm->d, lm->max_length,
+                       pos_from_device ? lm->d_pos : nullptr, pos + 1, lm->attn_scale, lm->attn_nsplit,
+                       lm->attn_partials, lm->attn_counters, lm->attn};
+  VX_CUDA(ctx, launch_attn_decode(ad, st, pdl));
+  // (3) o_proj + residual (attention.rs:153, layer.rs:67)
+  GemvArgs o = {};
+  o.W = w.wo;
+  o.N = lm->H;
+  o.K = lm->qs;
+  o.x = lm->attn;
+  o.y = lm->x;
+  o.residual = lm->x;
+  o.res_scale = lm->res_scale;
+  o.groups_per_cta = pick_groups(o.N / 8);
+  VX_CUDA(ctx, launch_gemv(o, EPI_STORE, st, pdl, ctx->dev_err));
+  // (4) post_attention_layernorm -> gate_up -> silu(gate)*up (layer.rs:69-71, mlp.rs:29-33)
+  GemvArgs g = {};
+  g.W = w.wgu;
+  g.N = 2 * lm->I;
+  g.K = lm->H;
+  g.x = lm->x;
+  g.norm_w = w.ln_post;
+  g.eps = lm->cfg.rms_norm_eps;
+  g.map_mode = MAP_GATE_UP;
+  g.map_param = lm->I / 8;
+  g.groups_per_cta = 2 * pick_groups(lm->I / 8);
+  g.inter = lm->I;
+  g.act = lm->act;
+  VX_CUDA(ctx, launch_gemv(g, EPI_SILU_MUL, st, pdl, ctx->dev_err));
+  // (5) down_proj + residual (mlp.rs:33, layer.rs:72)
+  GemvArgs dn = {};
+  dn.W = w.wd;
+  dn.N = lm->H;
+  dn.K = lm->I;
+  dn.x = lm->act;
+  dn.y = lm->x;
+  dn.residual = lm->x;
+  dn.res_scale = lm->res_scale;
+  dn.groups_per_cta = pick_groups(dn.N / 8);
+  VX_CUDA(ctx, launch_gemv(dn, EPI_STORE, st, pdl, ctx->dev_err));
+  return VX_OK;
+}
+
+// Greedy LM head over the tied embedding: final norm -> logits -> argmax -> next input.
+int enqueue_lm_head(vx_lm* lm, cudaStream_t st, bool advance_pos, bool write_logits) {
+  GemvArgs h = {};
+  h.W = lm->embed;
+  h.N = lm->V;
+  h.K = lm->H;
+  h.x = lm->x;
+  h.norm_w = lm->norm_w;
+  h.eps = lm->cfg.rms_norm_eps;
+  h.groups_per_cta = pick_groups(lm->V / 8);
+  h.logits = write_logits ? lm->logits : nullptr;
+  h.partials = lm->argmax_partials;
+  h.counter = lm->argmax_counter;
+  h.token_out = lm->d_tokens;
+  h.step_ptr = lm->d_step;
+  h.embed = lm->embed;
+  h.embed_dim = lm->H;
+  h.embed_scale = lm->emb_scale;
+  h.next_x = lm->x;
+  h.pos_inc = advance_pos ? lm->d_pos : nullptr;
+  VX_CUDA(lm->ctx, launch_gemv(h, EPI_ARGMAX, st, lm->ctx->pdl, lm->ctx->dev_err));
+  return VX_OK;
+}
+
+int enqueue_decode_step(vx_lm* lm, cudaStream_t st) {
+  for (int l = 0; l < lm->L; ++l) {
+    int rc = enqueue_layer_step(lm, l, st, true, 0);
+    if (rc) return rc;
+  }
+  return enqueue_lm_head(lm, st, true, true);
+}
+
+int build_step_graph(vx_lm* lm) {
+  if (lm->step_exec) return VX_OK;
+  vx_ctx* ctx = lm->ctx;
+  cudaGraph_t graph = nullptr;
+  const unsigned long long before = g_launches;
+  VX_CUDA(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_decode_step(lm, ctx->stream);
+  cudaError_t e = cudaStreamEndCapture(ctx->stream, &graph);
+  lm->step_kernels = g_launches - before;  // captured, not launched
+  g_launches = before;
+  if (rc) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamEndCapture");
+  e = cudaGraphInstantiate(&lm->step_exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaGraphInstantiate");
+  return VX_OK;
+}
+
+int check_device_error(vx_ctx* ctx) { return vx_ctx_synchronize(ctx); }
+
+}  // namespace
+
+extern "C" {
+
+int vx_lm_create(vx_ctx* ctx, const vx_minicpm4_config* cfg, int max_batch, int max_length, vx_lm** out) {
+  if (!ctx || !cfg || !out) return VX_ERR_ARG;
+  *out = nullptr;
+  const int d = cfg->kv_channels > 0 ? cfg->kv_channels : cfg->hidden_size / cfg->num_attention_heads;
+  if (cfg->hidden_size <= 0 || cfg->num_attention_heads <= 0 || cfg->num_key_value_heads <= 0 ||
+      cfg->num_attention_heads % cfg->num_key_value_heads != 0 || cfg->num_hidden_layers < 0 ||
+      cfg->intermediate_size <= 0 || max_batch <= 0 || max_length <= 0)
+    return fail(ctx, VX_ERR_CONFIG, "lm_create: invalid config");
+  if (cfg->hidden_size % 256 != 0 || cfg->intermediate_size % 256 != 0 || d % 16 != 0 ||
+      (cfg->num_attention_heads * d) % 256 != 0)
+    return fail(ctx, VX_ERR_CONFIG, "lm_create: hidden/intermediate/q widths must be multiples of 256, head_dim of 16");
+  cudaSetDevice(ctx->device);
+  vx_lm* lm = new vx_lm();
+  lm->ctx = ctx;
+  lm->cfg = *cfg;
+  lm->cfg.rope_short_factor = nullptr;
+  lm->cfg.rope_long_factor = nullptr;
+  lm->H = cfg->hidden_size;
+  lm->I = cfg->intermediate_size;
+  lm->nh = cfg->num_attention_heads;
+  lm->nkv = cfg->num_key_value_heads;
+  lm->d = d;
+  lm->L = cfg->num_hidden_layers;
+  lm->V = cfg->vocab_size;
+  lm->qs = lm->nh * d;
+  lm->ks = lm->nkv * d;
+  lm->res_scale = (float)residual_scale_of(*cfg);
+  lm->emb_scale = cfg->use_mup ? cfg->scale_emb : 1.0f;
+  lm->attn_scale = (float)(1.0 / std::sqrt((double)d));  // MiniCpmAttention::new scale (attention.rs:48)
+  lm->max_batch = max_batch;
+  lm->max_length = max_length;
+  lm->attn_nsplit = std::max(4, std::min(32, max_length / 128));
+
+  auto fail_free = [&](int code, const char* msg) {
+    vx_lm_destroy(lm);
+    return fail(ctx, code, "%s", msg);
+  };
+  if (!cfg->no_rope) {
+    RopeParams rp;
+    std::string err;
+    int rc = fill_rope_params(*cfg, &rp, &err);
+    if (rc) {
+      delete lm;
+      return fail(ctx, rc, "%s", err.c_str());
+    }
+    if (cudaMalloc(&lm->rope, sizeof(RopeParams)) != cudaSuccess ||
+        cudaMemcpy(lm->rope, &rp, sizeof(RopeParams), cudaMemcpyHostToDevice) != cudaSuccess)
+      return fail_free(VX_ERR_OOM, "rope params allocation failed");
+  }
+  const size_t H = lm->H, I = lm->I;
+  const size_t per_layer = ((size_t)(lm->qs + 2 * lm->ks) * H + H * lm->qs + 2 * I * H + H * I) * 2 + 2 * H * 4;
+  if (cudaMalloc(&lm->weight_slab, per_layer * std::max(1, lm->L) + 256) != cudaSuccess)
+    return fail_free(VX_ERR_OOM, "weight allocation failed");
+  char* p = static_cast<char*>(lm->weight_slab);
+  lm->layers.resize(lm->L);
+  for (int l = 0; l < lm->L; ++l) {
+    LmLayer& w = lm->layers[l];
+    w.wqkv = reinterpret_cast<uint16_t*>(p); p += (size_t)(lm->qs + 2 * lm->ks) * H * 2;
+    w.wo = reinterpret_cast<uint16_t*>(p); p += H * lm->qs * 2;
+    w.wgu = reinterpret_cast<uint16_t*>(p); p += 2 * I * H * 2;
+    w.wd = reinterpret_cast<uint16_t*>(p); p += H * I * 2;
+    w.ln_in = reinterpret_cast<float*>(p); p += H * 4;
+    w.ln_post = reinterpret_cast<float*>(p); p += H * 4;
+  }
+  const size_t kv_bytes = (size_t)std::max(1, lm->L) * lm->kv_layer_stride() * 4;
+  bool ok = cudaMalloc(&lm->norm_w, H * 4) == cudaSuccess &&
+            cudaMalloc(&lm->kcache, kv_bytes) == cudaSuccess && cudaMalloc(&lm->vcache, kv_bytes) == cudaSuccess &&
+            cudaMemset(lm->kcache, 0, kv_bytes) == cudaSuccess && cudaMemset(lm->vcache, 0, kv_bytes) == cudaSuccess &&
+            cudaMalloc(&lm->d_pos, 64) == cudaSuccess && cudaMalloc(&lm->d_step, 64) == cudaSuccess &&
+            cudaMalloc(&lm->d_tokens, (size_t)(max_length + 8) * 4) == cudaSuccess &&
+            cudaMalloc(&lm->x, H * 4 * max_batch) == cudaSuccess && cudaMalloc(&lm->q, lm->qs * 4 * max_batch) == cudaSuccess &&
+            cudaMalloc(&lm->attn, lm->qs * 4 * max_batch) == cudaSuccess && cudaMalloc(&lm->act, I * 4 * max_batch) == cudaSuccess &&
+            cudaMalloc(&lm->attn_partials, (size_t)max_batch * lm->nkv * 32 * lm->nh / lm->nkv * (d + 2) * 4) == cudaSuccess &&
+            cudaMalloc(&lm->attn_counters, (size_t)max_batch * lm->nkv * 4) == cudaSuccess &&
+            cudaMemset(lm->attn_counters, 0, (size_t)max_batch * lm->nkv * 4) == cudaSuccess &&
+            cudaMalloc(&lm->argmax_partials, 4096 * sizeof(float2)) == cudaSuccess &&
+            cudaMalloc(&lm->argmax_counter, 64) == cudaSuccess && cudaMemset(lm->argmax_counter, 0, 64) == cudaSuccess &&
+            cudaMemset(lm->d_pos, 0, 64) == cudaSuccess && cudaMemset(lm->d_step, 0, 64) == cudaSuccess;
+  if (ok && lm->V > 0) {
+    ok = cudaMalloc(&lm->embed, (size_t)lm->V * H * 2) == cudaSuccess &&
+         cudaMalloc(&lm->logits, (size_t)lm->V * 4) == cudaSuccess;
+  }
+  if (!ok) {
+    cudaGetLastError();
+    return fail_free(VX_ERR_OOM, "model buffer allocation failed");
+  }
+  *out = lm;
+  return VX_OK;
+}
+
+void vx_lm_destroy(vx_lm* lm) {
+  if (!lm) return;
+  cudaSetDevice(lm->ctx->device);
+  cudaStreamSynchronize(lm->ctx->stream);
+  if (lm->step_exec) cudaGraphExecDestroy(lm->step_exec);
+  for (auto& e : lm->ev)
+    if (e) cudaEventDestroy(e);
+  free_prefill(lm);
+  void* ptrs[] = {lm->weight_slab, lm->norm_w, lm->embed, lm->rope, lm->kcache, lm->vcache, lm->d_pos,
+                  lm->d_step, lm->d_tokens, lm->x, lm->q, lm->attn, lm->act, lm->logits, lm->attn_partials,
+                  lm->attn_counters, lm->argmax_partials, lm->argmax_counter, lm->pf_ids};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+  delete lm;
+}
+
+int vx_lm_load_layer(vx_lm* lm, int layer, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                     const uint16_t* o, const uint16_t* gate, const uint16_t* up, const uint16_t* down,
+                     const float* ln_in, const float* ln_post) {
+  if (!lm || !q || !k || !v || !o || !gate || !up || !down || !ln_in || !ln_post) return VX_ERR_ARG;
+  if (layer < 0 || layer >= lm->L) return fail(lm->ctx, VX_ERR_ARG, "layer %d out of range", layer);
+  vx_ctx* ctx = lm->ctx;
+  cudaSetDevice(ctx->device);
+  const LmLayer& w = lm->layers[layer];
+  const size_t H = lm->H, I = lm->I;
+  cudaStream_t st = ctx->stream;
+  // fuse_qkv / fuse_gate_up (weights.rs:648-772): row-major [out, in] concat along out
+  VX_CUDA(ctx, cudaMemcpyAsync(w.wqkv, q, (size_t)lm->qs * H * 2, cudaMemcpyDefault, st));
+  VX_CUDA(ctx, cudaMemcpyAsync(w.wqkv + (size_t)lm->qs * H, k, (size_t)lm->ks * H * 2, cudaMemcpyDefault, st));
+  VX_CUDA(ctx, cudaMemcpyAsync(w.wqkv + (size_t)(lm->qs + lm->ks) * H, v, (size_t)lm->ks * H * 2, cudaMemcpyDefault, st));
+  VX_CUDA(ctx, cudaMemcpyAsync(w.wo, o, H * lm->qs * 2, cudaMemcpyDefault, st));
+  VX_CUDA(ctx, cudaMemcpyAsync(w.wgu, gate, I * H * 2, cudaMemcpyDefault, st));
+  VX_CUDA(ctx, cudaMemcpyAsync(w.wgu + I * H, up, I * H * 2, cudaMemcpyDefault, st));
+  VX_CUDA(ctx, cudaMemcpyAsync(w.wd, down, H * I * 2, cudaMemcpyDefault, st));
+  VX_CUDA(ctx, cudaMemcpyAsync(w.ln_in, ln_in, H * 4, cudaMemcpyDefault, st));
+  VX_CUDA(ctx, cudaMemcpyAsync(w.ln_post, ln_post, H * 4, cudaMemcpyDefault, st));
+  VX_CUDA(ctx, cudaStreamSynchronize(st));
+  return VX_OK;
+}
+
+int vx_lm_load_norm(vx_lm* lm, const float* w) {
+  if (!lm || !w) return VX_ERR_ARG;
+  cudaSetDevice(lm->ctx->device);
+  VX_CUDA(lm->ctx, cudaMemcpy(lm->norm_w, w, (size_t)lm->H * 4, cudaMemcpyDefault));
+  return VX_OK;
+}
+
+int vx_lm_load_embed(vx_lm* lm, const uint16_t* embed) {
+  if (!lm || !embed) return VX_ERR_ARG;
+  if (!lm->embed) return fail(lm->ctx, VX_ERR_CONFIG, "model has no vocabulary");
+  cudaSetDevice(lm->ctx->device);
+  VX_CUDA(lm->ctx, cudaMemcpy(lm->embed, embed, (size_t)lm->V * lm->H * 2, cudaMemcpyDefault));
+  return VX_OK;
+}
+
+int vx_lm_reset(vx_lm* lm) {
+  if (!lm) return VX_ERR_ARG;
+  lm->cur_len = 0;
+  return VX_OK;
+}
+
+int vx_lm_position(const vx_lm* lm) { return lm ? lm->cur_len : -1; }
+
+int vx_lm_set_position(vx_lm* lm, int pos) {
+  if (!lm) return VX_ERR_ARG;
+  if (pos < 0 || pos > lm->max_length) return fail(lm->ctx, VX_ERR_ARG, "position out of range");
+  lm->cur_len = pos;
+  return VX_OK;
+}
+
+int vx_lm_kv_write(vx_lm* lm, int layer, int b, const float* k, const float* v, int n_pos) {
+  if (!lm || !k || !v) return VX_ERR_ARG;
+  if (layer < 0 || layer >= lm->L || b < 0 || b >= lm->max_batch || n_pos < 0 || n_pos > lm->max_length)
+    return fail(lm->ctx, VX_ERR_ARG, "kv_write: index out of range");
+  cudaSetDevice(lm->ctx->device);
+  const size_t row = (size_t)n_pos * lm->d * 4;
+  for (int g = 0; g < lm->nkv; ++g) {
+    VX_CUDA(lm->ctx, cudaMemcpy(lm->kc(layer, b) + (size_t)g * lm->max_length * lm->d, k + (size_t)g * n_pos * lm->d,
+                                row, cudaMemcpyDefault));
+    VX_CUDA(lm->ctx, cudaMemcpy(lm->vc(layer, b) + (size_t)g * lm->max_length * lm->d, v + (size_t)g * n_pos * lm->d,
+                                row, cudaMemcpyDefault));
+  }
+  return VX_OK;
+}
+
+int vx_lm_kv_read(vx_lm* lm, int layer, int b, float* k, float* v, int n_pos) {
+  if (!lm || !k || !v) return VX_ERR_ARG;
+  if (layer < 0 || layer >= lm->L || b < 0 || b >= lm->max_batch || n_pos < 0 || n_pos > lm->max_length)
+    return fail(lm->ctx, VX_ERR_ARG, "kv_read: index out of range");
+  cudaSetDevice(lm->ctx->device);
+  VX_CUDA(lm->ctx, cudaStreamSynchronize(lm->ctx->stream));
+  const size_t row = (size_t)n_pos * lm->d * 4;
+  for (int g = 0; g < lm->nkv; ++g) {
+    VX_CUDA(lm->ctx, cudaMemcpy(k + (size_t)g * n_pos * lm->d, lm->kc(layer, b) + (size_t)g * lm->max_length * lm->d,
+                                row, cudaMemcpyDefault));
+    VX_CUDA(lm->ctx, cudaMemcpy(v + (size_t)g * n_pos * lm->d, lm->vc(layer, b) + (size_t)g * lm->max_length * lm->d,
+                                row, cudaMemcpyDefault));
+  }
+  return VX_OK;
+}
+
+int vx_lm_embed(vx_lm* lm, const int32_t* ids, int n, float* out) {
+  if (!lm || !ids || !out || n <= 0) return VX_ERR_ARG;
+  if (!lm->embed) return fail(lm->ctx, VX_ERR_CONFIG, "model has no vocabulary");
+  cudaSetDevice(lm->ctx->device);
+  VX_CUDA(lm->ctx, launch_embed(lm->embed, ids, n, lm->H, lm->emb_scale, out, lm->ctx->stream));
+  return VX_OK;
+}
+
+int vx_lm_forward(vx_lm* lm, const float* embeds, int B, int S, int causal, int fill_cache, float* hidden_out) {
+  if (!lm || !embeds || !hidden_out) return VX_ERR_ARG;
+  vx_ctx* ctx = lm->ctx;
+  if (B <= 0 || S <= 0) return fail(ctx, VX_ERR_SHAPE, "forward: empty input");
+  if (fill_cache && (B > lm->max_batch || S > lm->max_length))
+    return fail(ctx, VX_ERR_KV_FULL, "forward: %d positions exceed the cache (%d)", S, lm->max_length);
+  cudaSetDevice(ctx->device);
+  const size_t M = (size_t)B * S;
+  int rc = ensure_prefill(lm, M, B, S, !fill_cache);
+  if (rc) return rc;
+  cudaStream_t st = ctx->stream;
+  const int H = lm->H, I = lm->I, qkvw = lm->qs + 2 * lm->ks;
+  VX_CUDA(ctx, cudaMemcpyAsync(lm->pf_x, embeds, M * H * 4, cudaMemcpyDefault, st));
+  for (int l = 0; l < lm->L; ++l) {
+    const LmLayer& w = lm->layers[l];
+    // K/V for this layer: the cache itself (prefill) or a [B, nkv, S, d] temporary
+    float* kd = fill_cache ? lm->kc(l, 0) : lm->pf_k;
+    float* vd = fill_cache ? lm->vc(l, 0) : lm->pf_v;
+    const int s_max = fill_cache ? lm->max_length : S;
+    VX_CUDA(ctx, launch_rmsnorm_residual(lm->pf_x, nullptr, w.ln_in, 1.f, lm->cfg.rms_norm_eps, (int)M, H, nullptr,
+                                         lm->pf_xn, st));
+    GemmArgs g1 = {lm->pf_xn, H, w.wqkv, nullptr, nullptr, 1.f, lm->pf_qkv, qkvw, (int)M, qkvw, H};
+    VX_CUDA(ctx, launch_gemm_smallm(g1, st));
+    if (fill_cache) {
+      for (int b = 0; b < B; ++b)
+        VX_CUDA(ctx, launch_rope_scatter(lm->pf_qkv + (size_t)b * S * qkvw, 1, S, lm->nh, lm->nkv, lm->d, lm->rope, 0,
+                                         lm->pf_q + (size_t)b * S * lm->qs, lm->kc(l, b), lm->vc(l, b), lm->max_length,
+                                         st));
+    } else {
+      VX_CUDA(ctx, launch_rope_scatter(lm->pf_qkv, B, S, lm->nh, lm->nkv, lm->d, lm->rope, 0, lm->pf_q, kd, vd, S, st));
+    }
+    if (fill_cache) {
+      for (int b = 0; b < B; ++b) {
+        AttnPrefillArgs ap = {lm->pf_q + (size_t)b * S * lm->qs, lm->kc(l, b), lm->vc(l, b), 1, S, lm->nh, lm->nkv,
+                              lm->d, s_max, lm->attn_scale, causal, lm->pf_attn + (size_t)b * S * lm->qs};
+        VX_CUDA(ctx, launch_attn_prefill(ap, st, false));
+      }
+    } else {
+      AttnPrefillArgs ap = {lm->pf_q, kd, vd, B, S, lm->nh, lm->nkv, lm->d, s_max, lm->attn_scale, causal, lm->pf_attn};
+      VX_CUDA(ctx, launch_attn_prefill(ap, st, false));
+    }
+    GemmArgs g2 = {lm->pf_attn, lm->qs, w.wo, nullptr, lm->pf_x, lm->res_scale, lm->pf_x, H, (int)M, H, lm->qs};
+    VX_CUDA(ctx, launch_gemm_smallm(g2, st));
+    VX_CUDA(ctx, launch_rmsnorm_residual(lm->pf_x, nullptr, w.ln_post, 1.f, lm->cfg.rms_norm_eps, (int)M, H, nullptr,
+                                         lm->pf_xn, st));
+    GemmArgs g3 = {lm->pf_xn, H, w.wgu, nullptr, nullptr, 1.f, lm->pf_gu, 2 * I, (int)M, 2 * I, H};
+    VX_CUDA(ctx, launch_gemm_smallm(g3, st));
+    VX_CUDA(ctx, launch_silu_mul(lm->pf_gu, (int)M, I, lm->pf_act, st));
+    GemmArgs g4 = {lm->pf_act, I, w.wd, nullptr, lm->pf_x, lm->res_scale, lm->pf_x, H, (int)M, H, I};
+    VX_CUDA(ctx, launch_gemm_smallm(g4, st));
+  }
+  VX_CUDA(ctx, launch_rmsnorm_residual(lm->pf_x, nullptr, lm->norm_w, 1.f, lm->cfg.rms_norm_eps, (int)M, H, nullptr,
+                                       hidden_out, st));
+  if (fill_cache) lm->cur_len = S;
+  return VX_OK;
+}
+
+int vx_lm_layer_forward_step(vx_lm* lm, int layer, float* hidden, int pos) {
+  if (!lm || !hidden) return VX_ERR_ARG;
+  vx_ctx* ctx = lm->ctx;
+  if (layer < 0 || layer >= lm->L) return fail(ctx, VX_ERR_ARG, "layer %d out of range", layer);
+  if (pos < 0 || pos >= lm->max_length) return fail(ctx, VX_ERR_KV_FULL, "KV cache is full");
+  cudaSetDevice(ctx->device);
+  cudaStream_t st = ctx->stream;
+  if (hidden != lm->x) VX_CUDA(ctx, cudaMemcpyAsync(lm->x, hidden, (size_t)lm->H * 4, cudaMemcpyDefault, st));
+  int rc = enqueue_layer_step(lm, layer, st, false, pos);
+  if (rc) return rc;
+  if (hidden != lm->x) VX_CUDA(ctx, cudaMemcpyAsync(hidden, lm->x, (size_t)lm->H * 4, cudaMemcpyDefault, st));
+  return VX_OK;
+}
+
+int vx_lm_forward_step(vx_lm* lm, const float* embeds, float* hidden_out) {
+  if (!lm || !embeds || !hidden_out) return VX_ERR_ARG;
+  vx_ctx* ctx = lm->ctx;
+  // StaticKvCache::step (cache.rs:60-65)
+  if (!(lm->cur_len < lm->max_length)) return fail(ctx, VX_ERR_KV_FULL, "KV cache is full");
+  const int pos = lm->cur_len;
+  cudaSetDevice(ctx->device);
+  cudaStream_t st = ctx->stream;
+  VX_CUDA(ctx, cudaMemcpyAsync(lm->x, embeds, (size_t)lm->H * 4, cudaMemcpyDefault, st));
+  for (int l = 0; l < lm->L; ++l) {
+    int rc = enqueue_layer_step(lm, l, st, false, pos);
+    if (rc) return rc;
+  }
+  VX_CUDA(ctx, launch_rmsnorm_residual(lm->x, nullptr, lm->norm_w, 1.f, lm->cfg.rms_norm_eps, 1, lm->H, nullptr,
+                                       hidden_out, st));
+  lm->cur_len = pos + 1;
+  return VX_OK;
+}
+
+int vx_lm_greedy(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps, int32_t* tokens_out) {
+  if (!lm || !prompt_ids || !tokens_out || n_prompt <= 0 || n_steps < 0) return VX_ERR_ARG;
+  vx_ctx* ctx = lm->ctx;
+  if (!lm->embed) return fail(ctx, VX_ERR_CONFIG, "greedy decode needs a vocabulary");
+  if (n_prompt + n_steps > lm->max_length)
+    return fail(ctx, VX_ERR_KV_FULL, "KV cache is full: %d prompt + %d steps > %d", n_prompt, n_steps, lm->max_length);
+  cudaSetDevice(ctx->device);
+  cudaStream_t st = ctx->stream;
+  if (lm->pf_ids_cap < n_prompt) {
+    if (lm->pf_ids) cudaFree(lm->pf_ids);
+    lm->pf_ids = nullptr;
+    lm->pf_ids_cap = 0;
+    VX_CUDA(ctx, cudaMalloc(&lm->pf_ids, (size_t)n_prompt * 4));
+    lm->pf_ids_cap = n_prompt;
+  }
+  int rc = ensure_prefill(lm, n_prompt, 1, n_prompt, false);
+  if (rc) return rc;
+  if (!lm->ev[0])
+    for (auto& e : lm->ev) VX_CUDA(ctx, cudaEventCreate(&e));
+  rc = build_step_graph(lm);
+  if (rc) return rc;
+  VX_CUDA(ctx, cudaEventRecord(lm->ev[0], st));
+  // prefill: embed * scale_emb -> causal forward -> StaticKvCache::fill (voxcpm2/model.rs:144-191)
+  VX_CUDA(ctx, cudaMemcpyAsync(lm->pf_ids, prompt_ids, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, st));
+  VX_CUDA(ctx, launch_embed(lm->embed, lm->pf_ids, n_prompt, lm->H, lm->emb_scale, lm->pf_xn, st));
+  // vx_lm_forward consumes the embeddings through its own copy; pf_xn is only the source
+  rc = vx_lm_forward(lm, lm->pf_xn, 1, n_prompt, 1, 1, lm->pf_gu);
+  if (rc) return rc;
+  // The last un-normed hidden row feeds the LM head, which applies the final norm itself.
+  VX_CUDA(ctx, cudaMemcpyAsync(lm->x, lm->pf_x + (size_t)(n_prompt - 1) * lm->H, (size_t)lm->H * 4,
+                               cudaMemcpyDeviceToDevice, st));
+  VX_CUDA(ctx, cudaMemsetAsync(lm->d_step, 0, 4, st));
+  rc = enqueue_lm_head(lm, st, false, n_steps == 0);
+  if (rc) return rc;
+  const int pos0 = n_prompt;
+  lm->pos_host = pos0;
+  VX_CUDA(ctx, cudaMemcpyAsync(lm->d_pos, &lm->pos_host, 4, cudaMemcpyHostToDevice, st));
+  VX_CUDA(ctx, cudaEventRecord(lm->ev[1], st));
+  for (int s = 0; s < n_steps; ++s) {
+    if (ctx->cancel.load(std::memory_order_relaxed)) {
+      cudaStreamSynchronize(st);
+      lm->cur_len = pos0 + s;
+      return fail(ctx, VX_ERR_CANCELLED, "generation cancelled");
+    }
+    VX_CUDA(ctx, cudaGraphLaunch(lm->step_exec, st));
+    count_launch(lm->step_kernels);
+  }
+  VX_CUDA(ctx, cudaEventRecord(lm->ev[2], st));
+  VX_CUDA(ctx, cudaMemcpyAsync(tokens_out, lm->d_tokens, (size_t)(n_steps + 1) * 4, cudaMemcpyDeviceToHost, st));
+  rc = check_device_error(ctx);
+  if (rc) return rc;
+  cudaEventElapsedTime(&lm->t_prefill_ms, lm->ev[0], lm->ev[1]);
+  cudaEventElapsedTime(&lm->t_decode_ms, lm->ev[1], lm->ev[2]);
+  lm->cur_len = pos0 + n_steps;
+  return VX_OK;
+}
+
+int vx_lm_last_timing(const vx_lm* lm, float* prefill_ms, float* decode_ms) {
+  if (!lm || !prefill_ms || !decode_ms) return VX_ERR_ARG;
+  *prefill_ms = lm->t_prefill_ms;
+  *decode_ms = lm->t_decode_ms;
+  return VX_OK;
+}
+
+int vx_lm_last_logits(vx_lm* lm, float* logits_out) {
+  if (!lm || !logits_out) return VX_ERR_ARG;
+  if (!lm->logits) return fail(lm->ctx, VX_ERR_CONFIG, "model has no vocabulary");
+  cudaSetDevice(lm->ctx->device);
+  VX_CUDA(lm->ctx, cudaStreamSynchronize(lm->ctx->stream));
+  VX_CUDA(lm->ctx, cudaMemcpy(logits_out, lm->logits, (size_t)lm->V * 4, cudaMemcpyDeviceToHost));
+  return VX_OK;
+}
+
+}  // extern "C"

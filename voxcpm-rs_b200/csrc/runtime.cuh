@@ -1,0 +1,102 @@
+// Host-side runtime shared by the C ABI translation units: the context, status handling
+// and the kernel launcher declarations.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+#include <vector>
+
+#include "../../include/voxcpm_b200.h"
+#include "gemv.cuh"
+#include "kernels.cuh"
+
+namespace vx {
+
+// Groups (or group pairs) per CTA so that a GEMV grid is about two CTAs per SM.
+inline int pick_groups(int units, int target_ctas = 296) {
+  int g = (units + target_ctas - 1) / target_ctas;
+  return g < 1 ? 1 : g;
+}
+
+cudaError_t launch_gemv(GemvArgs a, int epi, cudaStream_t st, bool pdl, int* err);
+cudaError_t gemv_configure();
+int gemv_grid(const GemvArgs& a);
+int gemv_pick_kc(int K);
+cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_gemm_smallm(const GemmArgs& a, cudaStream_t st);
+cudaError_t launch_rmsnorm_residual(const float* x, const float* r, const float* w, float resid_scale, float eps,
+                                    int rows, int hidden, float* h_out, float* y_out, cudaStream_t st);
+cudaError_t launch_rope_scatter(const float* qkv, int B, int S, int nh, int nkv, int d, const RopeParams* rope,
+                                int pos0, float* q_out, float* kcache, float* vcache, int s_max, cudaStream_t st);
+cudaError_t launch_rope_apply(float* x, int B, int H, int S, int d, const float* cos, const float* sin,
+                              cudaStream_t st);
+cudaError_t launch_silu_mul(const float* gu, int M, int inter, float* act, cudaStream_t st);
+cudaError_t launch_embed(const uint16_t* E, const int* ids, int n, int H, float scale, float* out,
+                         cudaStream_t st);
+cudaError_t launch_cfg_euler(const float* out2b, float* x, int B, int n, double cfg, double dt, int zero_star,
+                             cudaStream_t st);
+
+// A growable device scratch region owned by a context (op-level calls that need
+// workspace).  Counters that kernels use for last-CTA detection live in a separate
+// zero-initialised region that kernels reset after use.
+struct Scratch {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+
+}  // namespace vx
+
+struct vx_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::string last_error;
+  std::atomic<int> cancel{0};
+  vx::Scratch scratch;
+  unsigned int* counters = nullptr;  // 4096 zeroed counters
+  int* dev_err = nullptr;            // device error word written by bounded waits
+  bool pdl = true;
+};
+
+namespace vx {
+
+inline int fail(vx_ctx* ctx, int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (ctx) ctx->last_error = buf;
+  return code;
+}
+
+inline int cuda_fail(vx_ctx* ctx, cudaError_t e, const char* where) {
+  return fail(ctx, VX_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+}
+
+#define VX_CUDA(ctx, call)                                   \
+  do {                                                       \
+    cudaError_t e_ = (call);                                 \
+    if (e_ != cudaSuccess) return vx::cuda_fail(ctx, e_, #call); \
+  } while (0)
+
+inline cudaStream_t pick_stream(vx_ctx* ctx, vx_stream s) {
+  return s ? reinterpret_cast<cudaStream_t>(s) : ctx->stream;
+}
+
+// Ensure the context scratch has at least `bytes`; returns nullptr on failure.
+void* ctx_scratch(vx_ctx* ctx, size_t bytes);
+
+inline double residual_scale_of(const vx_minicpm4_config& c) {
+  // MiniCpmDecoderLayer::new (minicpm4/layer.rs:20-22): scale_depth (f32) / sqrt(L) in f64
+  return c.use_mup ? (double)c.scale_depth / std::sqrt((double)c.num_hidden_layers) : 1.0;
+}
+
+int fill_rope_params(const vx_minicpm4_config& c, RopeParams* rp, std::string* err);
+
+}  // namespace vx
