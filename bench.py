@@ -222,6 +222,34 @@ def run_reference(args):
     return 0
 
 
+def run_kernel_only():
+    """Small profiling case for the dominant kernel: the streamed GEMV on gate|up-shaped
+    weights (N=12288, K=2048, 50 MB each, 4 distinct matrices = 201 MB > L2), 3 passes."""
+    import torch
+    from __graft_entry__ import load_package
+    load_package()
+    from voxcpm_rs_b200.minicpm4 import Context, linear_bf16
+    ctx = Context(0)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    ws = [(torch.randn(2 * INTER, HIDDEN, generator=g, device="cuda") * 0.02).to(torch.bfloat16).view(torch.int16)
+          for _ in range(4)]
+    x = torch.randn(1, HIDDEN, device="cuda")
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(3):
+        for w in ws:
+            linear_bf16(ctx, w, x)
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000 / 12
+    print(json.dumps({"kernel": "gemv_bf16_kernel gate|up", "launch_us": us,
+                      "achieved_gbs": GATE_UP_BYTES / (us * 1e-6) / 1e9}))
+    ctx.close()
+    return 0
+
+
 # ------------------------------------------------------------------ our arm
 def main():
     ap = argparse.ArgumentParser()
@@ -231,9 +259,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=6)
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="profiling case: only the gate|up GEMV over 4 distinct 50 MB weights")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.kernel_only:
+        return run_kernel_only()
     args.warmup = max(3, args.warmup)
 
     import numpy as np

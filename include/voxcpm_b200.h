@@ -8,7 +8,8 @@
  *     a message.  No function aborts; kernels never trap (bounded device waits report
  *     VX_ERR_TIMEOUT instead).
  *   - Op-level calls take caller-owned DEVICE pointers and run on `stream` (a cudaStream_t;
- *     NULL = the context's stream).  They are asynchronous; vx_ctx_synchronize waits.
+ *     NULL = the legacy default stream, as in cuBLAS; pass vx_ctx_stream(ctx) for the
+ *     context's own stream).  They are asynchronous with respect to the host.
  *   - Model objects (vx_lm, vx_dit, vx_vae) own their weights, KV caches and work buffers.
  *     Weight loads accept host or device pointers (copied with cudaMemcpyDefault), bf16
  *     weights as raw bit patterns (uint16_t) in the checkpoint's [out, in] layout.

@@ -11,8 +11,8 @@ thread_local unsigned long long g_launches = 0;
 
 void* ctx_scratch(vx_ctx* ctx, size_t bytes) {
   if (ctx->scratch.bytes >= bytes) return ctx->scratch.ptr;
-  // scratch is used stream-ordered by earlier launches; wait before replacing it
-  cudaStreamSynchronize(ctx->stream);
+  // scratch may be in use by earlier launches on any stream; wait before replacing it
+  cudaDeviceSynchronize();
   if (ctx->scratch.ptr) cudaFree(ctx->scratch.ptr);
   ctx->scratch.ptr = nullptr;
   ctx->scratch.bytes = 0;

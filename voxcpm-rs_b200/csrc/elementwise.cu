@@ -189,19 +189,21 @@ cudaError_t launch_silu_mul(const float* gu, int M, int inter, float* act, cudaS
 }
 
 // ------------------------------------------------------------ embedding gather
-__global__ void embed_kernel(const uint16_t* __restrict__ E, const int* __restrict__ ids, int n, int H,
+__global__ void embed_kernel(const uint16_t* __restrict__ E, const int* __restrict__ ids, int n, int H, int V,
                              float scale, float* __restrict__ out) {
   for (int m = blockIdx.x; m < n; m += gridDim.x) {
-    const uint16_t* e = E + (size_t)ids[m] * H;
+    int id = ids[m];
+    if (id < 0 || id >= V) id = 0;  // out-of-range ids never index past the table
+    const uint16_t* e = E + (size_t)id * H;
     for (int k = threadIdx.x; k < H; k += blockDim.x)
       out[(size_t)m * H + k] = __uint_as_float(((uint32_t)e[k]) << 16) * scale;
   }
 }
 
-cudaError_t launch_embed(const uint16_t* E, const int* ids, int n, int H, float scale, float* out,
+cudaError_t launch_embed(const uint16_t* E, const int* ids, int n, int H, int V, float scale, float* out,
                          cudaStream_t st) {
   count_launch();
-  embed_kernel<<<n < 1024 ? n : 1024, 256, 0, st>>>(E, ids, n, H, scale, out);
+  embed_kernel<<<n < 1024 ? n : 1024, 256, 0, st>>>(E, ids, n, H, V, scale, out);
   return cudaGetLastError();
 }
 

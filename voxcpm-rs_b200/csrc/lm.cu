@@ -437,7 +437,7 @@ int vx_lm_embed(vx_lm* lm, const int32_t* ids, int n, float* out) {
   if (!lm || !ids || !out || n <= 0) return VX_ERR_ARG;
   if (!lm->embed) return fail(lm->ctx, VX_ERR_CONFIG, "model has no vocabulary");
   cudaSetDevice(lm->ctx->device);
-  VX_CUDA(lm->ctx, launch_embed(lm->embed, ids, n, lm->H, lm->emb_scale, out, lm->ctx->stream));
+  VX_CUDA(lm->ctx, launch_embed(lm->embed, ids, n, lm->H, lm->V, lm->emb_scale, out, lm->ctx->stream));
   return VX_OK;
 }
 
@@ -537,6 +537,9 @@ int vx_lm_greedy(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps
   if (!lm->embed) return fail(ctx, VX_ERR_CONFIG, "greedy decode needs a vocabulary");
   if (n_prompt + n_steps > lm->max_length)
     return fail(ctx, VX_ERR_KV_FULL, "KV cache is full: %d prompt + %d steps > %d", n_prompt, n_steps, lm->max_length);
+  for (int i = 0; i < n_prompt; ++i)
+    if (prompt_ids[i] < 0 || prompt_ids[i] >= lm->V)
+      return fail(ctx, VX_ERR_ARG, "prompt id %d at %d outside the vocabulary", prompt_ids[i], i);
   cudaSetDevice(ctx->device);
   cudaStream_t st = ctx->stream;
   if (lm->pf_ids_cap < n_prompt) {
@@ -555,7 +558,7 @@ int vx_lm_greedy(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps
   VX_CUDA(ctx, cudaEventRecord(lm->ev[0], st));
   // prefill: embed * scale_emb -> causal forward -> StaticKvCache::fill (voxcpm2/model.rs:144-191)
   VX_CUDA(ctx, cudaMemcpyAsync(lm->pf_ids, prompt_ids, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, st));
-  VX_CUDA(ctx, launch_embed(lm->embed, lm->pf_ids, n_prompt, lm->H, lm->emb_scale, lm->pf_xn, st));
+  VX_CUDA(ctx, launch_embed(lm->embed, lm->pf_ids, n_prompt, lm->H, lm->V, lm->emb_scale, lm->pf_xn, st));
   // vx_lm_forward consumes the embeddings through its own copy; pf_xn is only the source
   rc = vx_lm_forward(lm, lm->pf_xn, 1, n_prompt, 1, 1, lm->pf_gu);
   if (rc) return rc;

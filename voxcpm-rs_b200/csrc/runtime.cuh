@@ -37,7 +37,7 @@ cudaError_t launch_rope_scatter(const float* qkv, int B, int S, int nh, int nkv,
 cudaError_t launch_rope_apply(float* x, int B, int H, int S, int d, const float* cos, const float* sin,
                               cudaStream_t st);
 cudaError_t launch_silu_mul(const float* gu, int M, int inter, float* act, cudaStream_t st);
-cudaError_t launch_embed(const uint16_t* E, const int* ids, int n, int H, float scale, float* out,
+cudaError_t launch_embed(const uint16_t* E, const int* ids, int n, int H, int V, float scale, float* out,
                          cudaStream_t st);
 cudaError_t launch_cfg_euler(const float* out2b, float* x, int B, int n, double cfg, double dt, int zero_star,
                              cudaStream_t st);
@@ -85,9 +85,9 @@ inline int cuda_fail(vx_ctx* ctx, cudaError_t e, const char* where) {
     if (e_ != cudaSuccess) return vx::cuda_fail(ctx, e_, #call); \
   } while (0)
 
-inline cudaStream_t pick_stream(vx_ctx* ctx, vx_stream s) {
-  return s ? reinterpret_cast<cudaStream_t>(s) : ctx->stream;
-}
+// Op-level calls run on the caller's stream; NULL is the legacy default stream (as in
+// cuBLAS), so work queued by a framework on its default stream is ordered before them.
+inline cudaStream_t pick_stream(vx_ctx*, vx_stream s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // Ensure the context scratch has at least `bytes`; returns nullptr on failure.
 void* ctx_scratch(vx_ctx* ctx, size_t bytes);
