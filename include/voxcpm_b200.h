@@ -180,6 +180,12 @@ int vx_lm_layer_forward_step(vx_lm* lm, int layer, float* hidden, int pos);
  * prefill's last row).  The decode step runs as one captured CUDA graph replayed per step
  * with no host round trip; cancellation (vx_cancel) is polled between steps. */
 int vx_lm_greedy(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps, int32_t* tokens_out);
+/* One batch-1 decode step at `pos` run eagerly (no graph, no programmatic dependent launch)
+ * with a CUDA event after every kernel: kernel_us receives num_hidden_layers*5 + 1 durations
+ * (per layer: qkv+rope, attention, o_proj, gate_up, down; then the greedy head).  Writes the
+ * KV cache at `pos` and does not advance the position.  Instrumentation, no reference
+ * counterpart beyond the VOXCPM_PROFILE timing split (voxcpm2/model.rs:316-372). */
+int vx_lm_profile_decode_step(vx_lm* lm, int pos, float* kernel_us, int n);
 /* Device time of the last vx_lm_greedy call split into prefill and decode (CUDA events on
  * the context stream).  Mirrors the VOXCPM_PROFILE split of voxcpm2/model.rs:316-372. */
 int vx_lm_last_timing(const vx_lm* lm, float* prefill_ms, float* decode_ms);

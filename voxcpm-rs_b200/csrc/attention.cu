@@ -2,12 +2,17 @@
 // (reference src/minicpm4/attention.rs:156-204).
 //
 // * attn_decode_kernel: one query token per batch row against the static KV cache
-//   (forward_step, attention.rs:129-150).  Split-K flash-decode: the filled prefix 0..len is
-//   cut into `nsplit` chunks; grid = (nsplit, n_kv_heads, B).  Each CTA serves all n_rep
-//   query heads of its KV head (GQA without materialising repeat_kv), keeps an online
-//   softmax per head, and writes (m, l, o[d]) partials to scratch.  The last CTA to finish
-//   for a (batch, kv head) merges the partials and writes the output; it also resets the
-//   arrival counter, so the kernel replays inside a CUDA graph with no host work.
+//   (forward_step, attention.rs:129-150).  Split-K flash-decode over GQA groups:
+//   grid = (max_splits, n_kv_heads, B); only ceil(len/32) splits (at most max_splits) are
+//   active, each covering a contiguous span of the filled prefix 0..len.  A CTA stages
+//   32-position K/V tiles of its KV head in shared memory ONCE and all n_rep (= 8) query
+//   heads of the group read them there: warp r is query head r, lane j scores position j of
+//   the tile (K tile XOR-swizzled in 16-byte chunks so the row-per-lane reads are
+//   conflict-free), an online softmax runs per warp, and P.V accumulates d/32 output dims
+//   per lane.  With one active split the CTA writes the result directly; otherwise each
+//   writes an (m, l, o[d]) partial to scratch and the last CTA to arrive (atomic counter,
+//   no waiting) merges them lane-parallel and resets the counter, so the kernel replays
+//   inside a CUDA graph with no host work.
 // * attn_prefill_kernel: S query rows against S keys of a KV layout [B, nkv, s_max, d]
 //   (forward / prefill and the non-causal DiT / LocEnc paths, attention.rs:55-88), causal
 //   or not, one warp per query row with an online softmax.
@@ -18,14 +23,20 @@
 
 namespace vx {
 
+constexpr int ATT_TILE = 32;
 
+template <int D>
+__device__ __forceinline__ int kswz(int row, int chunk) {  // float4-chunk index inside a K row
+  return row * (D / 4) + (chunk ^ (row & 7));
+}
 
 template <int D, int NREP>
-__global__ void __launch_bounds__(256) attn_decode_kernel(const AttnDecodeArgs a) {
-  constexpr int DPL = D / 32;  // dims per lane
-  __shared__ float qs[NREP][D];
-  __shared__ float wm[8][NREP], wl[8][NREP];
-  __shared__ float wo[8][NREP][D];
+__global__ void __launch_bounds__(32 * NREP) attn_decode_kernel(const AttnDecodeArgs a) {
+  constexpr int DPL = D / 32;  // output dims per lane
+  constexpr int NC = D / 4;    // float4 chunks per row
+  __shared__ __align__(16) float qs[NREP][D];
+  __shared__ __align__(16) float4 ks[ATT_TILE * NC];
+  __shared__ __align__(16) float vs[ATT_TILE][D];
   __shared__ int last_flag;
 
   pdl_wait();
@@ -33,122 +44,118 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const AttnDecodeArgs a
   const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int len = a.pos_ptr ? (*a.pos_ptr + 1) : a.len;
-  const int chunk = (len + a.nsplit - 1) / a.nsplit;
-  const int j0 = split * chunk, j1 = min(len, j0 + chunk);
+  const int active = min(a.nsplit, (len + ATT_TILE - 1) / ATT_TILE);
+  if (split >= active) return;
+  const int span = (len + active - 1) / active;
+  const int j0 = split * span, j1 = min(len, j0 + span);
 
-  for (int i = tid; i < NREP * D; i += 256) {
-    const int r = i / D, e = i % D;
-    qs[r][e] = a.q[(size_t)b * a.nh * D + (g * NREP + r) * D + e];
-  }
-  __syncthreads();
+  for (int i = tid; i < NREP * D; i += 32 * NREP) qs[i / D][i % D] = a.q[(size_t)b * a.nh * D + g * NREP * D + i];
 
-  float qr[NREP][DPL], o[NREP][DPL], m[NREP], l[NREP];
-#pragma unroll
-  for (int r = 0; r < NREP; ++r) {
-    m[r] = -INFINITY;
-    l[r] = 0.f;
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) {
-      qr[r][e] = qs[r][lane * DPL + e];
-      o[r][e] = 0.f;
-    }
-  }
   const float* kb = a.kcache + ((size_t)(b * a.nkv + g) * a.s_max) * D;
   const float* vb = a.vcache + ((size_t)(b * a.nkv + g) * a.s_max) * D;
-  for (int j = j0 + warp; j < j1; j += 8) {
-    float kr[DPL], vr[DPL];
-    if constexpr (DPL == 4) {
-      const float4 k4 = __ldg(reinterpret_cast<const float4*>(kb + (size_t)j * D) + lane);
-      const float4 v4 = __ldg(reinterpret_cast<const float4*>(vb + (size_t)j * D) + lane);
-      kr[0] = k4.x; kr[1] = k4.y; kr[2] = k4.z; kr[3] = k4.w;
-      vr[0] = v4.x; vr[1] = v4.y; vr[2] = v4.z; vr[3] = v4.w;
-    } else {
-      const float2 k2 = __ldg(reinterpret_cast<const float2*>(kb + (size_t)j * D) + lane);
-      const float2 v2 = __ldg(reinterpret_cast<const float2*>(vb + (size_t)j * D) + lane);
-      kr[0] = k2.x; kr[1] = k2.y;
-      vr[0] = v2.x; vr[1] = v2.y;
+  const int r = warp;  // query head within the group
+  float m = -INFINITY, l = 0.f, o[DPL];
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) o[e] = 0.f;
+
+  for (int t0 = j0; t0 < j1; t0 += ATT_TILE) {
+    const int nt = min(ATT_TILE, j1 - t0);
+    __syncthreads();  // previous tile fully consumed (and qs written on the first pass)
+    for (int c = tid; c < ATT_TILE * NC; c += 32 * NREP) {
+      const int row = c / NC, ch = c % NC;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (row < nt) {
+        kv = __ldg(reinterpret_cast<const float4*>(kb + (size_t)(t0 + row) * D) + ch);
+        vv = __ldg(reinterpret_cast<const float4*>(vb + (size_t)(t0 + row) * D) + ch);
+      }
+      ks[kswz<D>(row, ch)] = kv;
+      *reinterpret_cast<float4*>(&vs[row][ch * 4]) = vv;
     }
-#pragma unroll
-    for (int r = 0; r < NREP; ++r) {
-      float s = 0.f;
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) s = fmaf(qr[r][e], kr[e], s);
-      s = warp_sum(s) * a.scale;  // scores = q.k^T * scale (attention.rs:166)
-      const float mn = fmaxf(m[r], s);
-      const float alpha = expf(m[r] - mn);
-      const float p = expf(s - mn);
-      l[r] = l[r] * alpha + p;
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) o[r][e] = fmaf(p, vr[e], o[r][e] * alpha);
-      m[r] = mn;
+    __syncthreads();
+    // scores: lane j <-> position t0 + j;  scores = q.k^T * scale (attention.rs:166)
+    float s = 0.f;
+#pragma unroll 8
+    for (int ch = 0; ch < NC; ++ch) {
+      const float4 kk = ks[kswz<D>(lane, ch)];
+      const float4 qq = *reinterpret_cast<const float4*>(&qs[r][ch * 4]);
+      s = fmaf(qq.x, kk.x, s);
+      s = fmaf(qq.y, kk.y, s);
+      s = fmaf(qq.z, kk.z, s);
+      s = fmaf(qq.w, kk.w, s);
     }
-  }
+    s = lane < nt ? s * a.scale : -INFINITY;
+    const float mn = fmaxf(m, warp_max(s));
+    const float alpha = expf(m - mn);  // m == -inf on the first tile -> 0
+    const float p = lane < nt ? expf(s - mn) : 0.f;
+    l = l * alpha + warp_sum(p);
 #pragma unroll
-  for (int r = 0; r < NREP; ++r) {
-    if (lane == 0) {
-      wm[warp][r] = m[r];
-      wl[warp][r] = l[r];
-    }
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) wo[warp][r][lane * DPL + e] = o[r][e];
-  }
-  __syncthreads();
-  // merge the 8 warps of this CTA into one (m, l, o) partial per head
-  const size_t pbase = ((size_t)((b * a.nkv + g) * a.nsplit + split)) * NREP * (D + 2);
-  for (int i = tid; i < NREP * D; i += 256) {
-    const int r = i / D, e = i % D;
-    float M = -INFINITY;
-    for (int w = 0; w < 8; ++w) M = fmaxf(M, wm[w][r]);
-    float L = 0.f, O = 0.f;
-    if (M > -INFINITY) {
-      for (int w = 0; w < 8; ++w) {
-        const float f = (wm[w][r] > -INFINITY) ? expf(wm[w][r] - M) : 0.f;
-        L = fmaf(wl[w][r], f, L);
-        O = fmaf(wo[w][r][e], f, O);
+    for (int e = 0; e < DPL; ++e) o[e] *= alpha;
+    for (int jj = 0; jj < nt; ++jj) {
+      const float pj = __shfl_sync(0xffffffffu, p, jj);
+      if constexpr (DPL == 4) {
+        const float4 vv = *reinterpret_cast<const float4*>(&vs[jj][lane * 4]);
+        o[0] = fmaf(pj, vv.x, o[0]);
+        o[1] = fmaf(pj, vv.y, o[1]);
+        o[2] = fmaf(pj, vv.z, o[2]);
+        o[3] = fmaf(pj, vv.w, o[3]);
+      } else {
+        const float2 vv = *reinterpret_cast<const float2*>(&vs[jj][lane * 2]);
+        o[0] = fmaf(pj, vv.x, o[0]);
+        o[1] = fmaf(pj, vv.y, o[1]);
       }
     }
-    float* p = a.partials + pbase + (size_t)r * (D + 2);
-    p[e] = O;
-    if (e == 0) {
-      p[D] = M;
-      p[D + 1] = L;
-    }
+    m = mn;
+  }
+
+  float* outp = a.out + (size_t)b * a.nh * D + (g * NREP + r) * D + lane * DPL;
+  if (active == 1) {
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) outp[e] = o[e] / l;
+    return;
+  }
+  // partial (o[d], m, l) of this split for head r
+  float* p = a.partials + (((size_t)(b * a.nkv + g) * a.nsplit + split) * NREP + r) * (D + 2);
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) p[lane * DPL + e] = o[e];
+  if (lane == 0) {
+    p[D] = m;
+    p[D + 1] = l;
   }
   __threadfence();
   __syncthreads();
   if (tid == 0) {
     const unsigned prev = atomicAdd(&a.counters[b * a.nkv + g], 1u);
-    last_flag = (prev == (unsigned)a.nsplit - 1);
+    last_flag = (prev == (unsigned)active - 1);
   }
   __syncthreads();
   if (!last_flag) return;
   __threadfence();
-  const size_t cbase = ((size_t)((b * a.nkv + g) * a.nsplit)) * NREP * (D + 2);
-  for (int i = tid; i < NREP * D; i += 256) {
-    const int r = i / D, e = i % D;
-    float M = -INFINITY;
-    for (int s = 0; s < a.nsplit; ++s)
-      M = fmaxf(M, __ldcg(a.partials + cbase + ((size_t)s * NREP + r) * (D + 2) + D));
-    float L = 0.f, O = 0.f;
-    for (int s = 0; s < a.nsplit; ++s) {
-      const float* p = a.partials + cbase + ((size_t)s * NREP + r) * (D + 2);
-      const float ms = __ldcg(p + D);
-      if (ms == -INFINITY) continue;
-      const float f = expf(ms - M);
-      L = fmaf(__ldcg(p + D + 1), f, L);
-      O = fmaf(__ldcg(p + e), f, O);
-    }
-    a.out[(size_t)b * a.nh * D + (g * NREP + r) * D + e] = O / L;
+  // last CTA: merge the `active` partials of head r, lane-parallel over splits
+  const float* pb = a.partials + ((size_t)(b * a.nkv + g) * a.nsplit * NREP + r) * (D + 2);
+  const size_t sstride = (size_t)NREP * (D + 2);
+  const float ms = lane < active ? __ldcg(pb + lane * sstride + D) : -INFINITY;
+  const float M = warp_max(ms);
+  const float f = lane < active ? expf(ms - M) : 0.f;
+  const float L = warp_sum(lane < active ? f * __ldcg(pb + lane * sstride + D + 1) : 0.f);
+  float acc[DPL];
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) acc[e] = 0.f;
+  for (int sp = 0; sp < active; ++sp) {
+    const float fs = __shfl_sync(0xffffffffu, f, sp);
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) acc[e] = fmaf(fs, __ldcg(pb + sp * sstride + lane * DPL + e), acc[e]);
   }
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) outp[e] = acc[e] / L;
   if (tid == 0) a.counters[b * a.nkv + g] = 0u;
 }
 
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl) {
   const int nrep = a.nh / a.nkv;
-  if (nrep != 8 || (a.d != 128 && a.d != 64)) return cudaErrorInvalidValue;
+  if (nrep != 8 || (a.d != 128 && a.d != 64) || a.nsplit < 1 || a.nsplit > 32) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.nsplit, a.nkv, a.B);
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(32 * 8);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

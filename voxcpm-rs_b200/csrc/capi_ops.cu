@@ -68,6 +68,10 @@ int vx_ctx_create(int device, vx_ctx** out) {
   if (device < 0 || device >= n) return VX_ERR_ARG;
   vx_ctx* ctx = new vx_ctx();
   ctx->device = device;
+  // tuning knobs (documented in DESIGN.md): GEMV grid target and programmatic dependent launch
+  if (const char* s = getenv("VX_GEMV_CTAS")) ctx->gemv_ctas = std::max(1, atoi(s));
+  if (const char* s = getenv("VX_PDL")) ctx->pdl = atoi(s) != 0;
+  if (const char* s = getenv("VX_L2_PREFETCH")) ctx->l2_prefetch = atoi(s) != 0;
   if (cudaSetDevice(device) != cudaSuccess ||
       cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&ctx->counters, 4096 * sizeof(unsigned)) != cudaSuccess ||
@@ -207,7 +211,7 @@ int vx_attention_decode(vx_ctx* ctx, const float* q, const float* kcache, const 
   if (cur_len <= 0 || cur_len > s_max) return fail(ctx, VX_ERR_SHAPE, "attention_decode: cur_len out of range");
   if (B * nkv > 4096) return fail(ctx, VX_ERR_SHAPE, "attention_decode: B*nkv > 4096");
   cudaSetDevice(ctx->device);
-  const int nsplit = std::min(32, std::max(1, (cur_len + 63) / 64));
+  const int nsplit = 32;  // upper bound; the kernel activates ceil(cur_len/32) of them
   const size_t pbytes = (size_t)B * nkv * nsplit * 8 * (head_dim + 2) * sizeof(float);
   float* partials = static_cast<float*>(ctx_scratch(ctx, pbytes));
   if (!partials) return fail(ctx, VX_ERR_OOM, "attention_decode: scratch allocation failed");

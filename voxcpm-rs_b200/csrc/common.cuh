@@ -132,6 +132,25 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Bulk prefetch of a global range into L2 (TMA engine, no shared-memory destination).
+// addr 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// Issue L2 prefetches for this CTA's 1/gridDim share of [ptr, ptr + bytes), 32 KB per request.
+__device__ __forceinline__ void prefetch_share_l2(const void* ptr, size_t bytes) {
+  if (!ptr || bytes == 0) return;
+  const size_t share = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~size_t(15);
+  size_t b0 = share * blockIdx.x;
+  const size_t b1 = b0 + share < bytes ? b0 + share : bytes;
+  const char* p = static_cast<const char*>(ptr);
+  for (; b0 < b1; b0 += 32768) {
+    const size_t n = (b1 - b0) < 32768 ? (b1 - b0) : 32768;
+    bulk_prefetch_l2(p + b0, (uint32_t)(n & ~size_t(15)));
+  }
+}
+
 // Programmatic dependent launch: wait for the preceding grid's memory to be visible /
 // allow the next grid to start launching.  Both are no-ops without the launch attribute.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -91,6 +91,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_bf16_kernel(const GemvAr
           for (int r = 0; r < GEMV_ROWS; ++r)
             bulk_g2s(dst + r * KC, a.W + (size_t)(row0 + r) * a.K + (size_t)c * KC, KC * 2, &full[slot]);
         }
+        if (s == NST - 1 || (s == nstage_total - 1 && nstage_total < NST)) prefetch_share_l2(a.pf_ptr, a.pf_bytes);
       }
       if (!ok) {  // give copies already in flight time to land before the CTA can exit
         const long long t0 = clock64();

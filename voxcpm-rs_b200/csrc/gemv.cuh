@@ -75,6 +75,11 @@ struct GemvArgs {
   int* pos_inc;             // optional device position to increment
 
   int* err;  // device error word (bounded waits record VX_DEVICE_ERR_TIMEOUT here)
+
+  // Optional L2 prefetch of the next kernel's weights (split evenly over the CTAs), issued
+  // once this CTA's first stages are in flight, so HBM stays busy across kernel boundaries.
+  const void* pf_ptr;
+  size_t pf_bytes;
 };
 
 }  // namespace vx

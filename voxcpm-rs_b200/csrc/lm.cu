@@ -113,8 +113,11 @@ int ensure_prefill(vx_lm* lm, size_t rows, int B, int S, bool need_kv) {
 
 // One decoder layer for batch row 0 at the device position *d_pos (or `pos` when
 // pos_from_device is false): 5 launches.
-int enqueue_layer_step(vx_lm* lm, int l, cudaStream_t st, bool pos_from_device, int pos) {
+int enqueue_layer_step(vx_lm* lm, int l, cudaStream_t st, bool pos_from_device, int pos,
+                       cudaEvent_t* ev_after = nullptr) {
   vx_ctx* ctx = lm->ctx;
+  int evi = 0;
+  auto mark = [&]() -> cudaError_t { return ev_after ? cudaEventRecord(ev_after[evi++], st) : cudaSuccess; };
   const LmLayer& w = lm->layers[l];
   const bool pdl = ctx->pdl;
   // (1) input_layernorm -> qkv_proj -> LongRoPE -> KV cache write  (layer.rs:64-66, attention.rs:102-127)
@@ -127,7 +130,7 @@ int enqueue_layer_step(vx_lm* lm, int l, cudaStream_t st, bool pos_from_device, 
   a.eps = lm->cfg.rms_norm_eps;
   a.map_mode = MAP_ROPE_PAIRS;
   a.map_param = lm->d / 16;
-  a.groups_per_cta = 2 * pick_groups(a.N / 16);
+  a.groups_per_cta = 2 * pick_groups(a.N / 16, ctx->gemv_ctas);
   a.nh = lm->nh;
   a.nkv = lm->nkv;
   a.hd = lm->d;
@@ -138,12 +141,21 @@ int enqueue_layer_step(vx_lm* lm, int l, cudaStream_t st, bool pos_from_device, 
   a.kcache = lm->kc(l, 0);
   a.vcache = lm->vc(l, 0);
   a.s_max = lm->max_length;
+  // L2 prefetch chain: every weight-streaming kernel prefetches the next one's weights
+  const bool pf = ctx->l2_prefetch;
+  const size_t H = lm->H, I = lm->I;
+  if (pf) {
+    a.pf_ptr = w.wo;
+    a.pf_bytes = H * lm->qs * 2;
+  }
   VX_CUDA(ctx, launch_gemv(a, EPI_QKV_ROPE, st, pdl, ctx->dev_err));
+  VX_CUDA(ctx, mark());
   // (2) sdpa over the cached prefix 0..pos+1 (attention.rs:129-150)
   AttnDecodeArgs ad = {lm->q, lm->kc(l, 0), lm->vc(l, 0), 1, lm->nh, lm->nkv, lm->d, lm->max_length,
                        pos_from_device ? lm->d_pos : nullptr, pos + 1, lm->attn_scale, lm->attn_nsplit,
                        lm->attn_partials, lm->attn_counters, lm->attn};
   VX_CUDA(ctx, launch_attn_decode(ad, st, pdl));
+  VX_CUDA(ctx, mark());
   // (3) o_proj + residual (attention.rs:153, layer.rs:67)
   GemvArgs o = {};
   o.W = w.wo;
@@ -153,8 +165,13 @@ int enqueue_layer_step(vx_lm* lm, int l, cudaStream_t st, bool pos_from_device, 
   o.y = lm->x;
   o.residual = lm->x;
   o.res_scale = lm->res_scale;
-  o.groups_per_cta = pick_groups(o.N / 8);
+  o.groups_per_cta = pick_groups(o.N / 8, ctx->gemv_ctas);
+  if (pf) {
+    o.pf_ptr = w.wgu;
+    o.pf_bytes = 2 * I * H * 2;
+  }
   VX_CUDA(ctx, launch_gemv(o, EPI_STORE, st, pdl, ctx->dev_err));
+  VX_CUDA(ctx, mark());
   // (4) post_attention_layernorm -> gate_up -> silu(gate)*up (layer.rs:69-71, mlp.rs:29-33)
   GemvArgs g = {};
   g.W = w.wgu;
@@ -165,10 +182,15 @@ int enqueue_layer_step(vx_lm* lm, int l, cudaStream_t st, bool pos_from_device, 
   g.eps = lm->cfg.rms_norm_eps;
   g.map_mode = MAP_GATE_UP;
   g.map_param = lm->I / 8;
-  g.groups_per_cta = 2 * pick_groups(lm->I / 8);
+  g.groups_per_cta = 2 * pick_groups(lm->I / 8, ctx->gemv_ctas);
   g.inter = lm->I;
   g.act = lm->act;
+  if (pf) {
+    g.pf_ptr = w.wd;
+    g.pf_bytes = H * I * 2;
+  }
   VX_CUDA(ctx, launch_gemv(g, EPI_SILU_MUL, st, pdl, ctx->dev_err));
+  VX_CUDA(ctx, mark());
   // (5) down_proj + residual (mlp.rs:33, layer.rs:72)
   GemvArgs dn = {};
   dn.W = w.wd;
@@ -178,8 +200,16 @@ int enqueue_layer_step(vx_lm* lm, int l, cudaStream_t st, bool pos_from_device, 
   dn.y = lm->x;
   dn.residual = lm->x;
   dn.res_scale = lm->res_scale;
-  dn.groups_per_cta = pick_groups(dn.N / 8);
+  dn.groups_per_cta = pick_groups(dn.N / 8, ctx->gemv_ctas);
+  if (pf && l + 1 < lm->L) {
+    dn.pf_ptr = lm->layers[l + 1].wqkv;
+    dn.pf_bytes = (size_t)(lm->qs + 2 * lm->ks) * H * 2;
+  } else if (pf && lm->embed) {
+    dn.pf_ptr = lm->embed;  // the head of the greedy LM head's table
+    dn.pf_bytes = std::min<size_t>((size_t)lm->V * H * 2, 48u << 20);
+  }
   VX_CUDA(ctx, launch_gemv(dn, EPI_STORE, st, pdl, ctx->dev_err));
+  VX_CUDA(ctx, mark());
   return VX_OK;
 }
 
@@ -192,7 +222,7 @@ int enqueue_lm_head(vx_lm* lm, cudaStream_t st, bool advance_pos, bool write_log
   h.x = lm->x;
   h.norm_w = lm->norm_w;
   h.eps = lm->cfg.rms_norm_eps;
-  h.groups_per_cta = pick_groups(lm->V / 8);
+  h.groups_per_cta = pick_groups(lm->V / 8, lm->ctx->gemv_ctas);
   h.logits = write_logits ? lm->logits : nullptr;
   h.partials = lm->argmax_partials;
   h.counter = lm->argmax_counter;
@@ -273,7 +303,7 @@ int vx_lm_create(vx_ctx* ctx, const vx_minicpm4_config* cfg, int max_batch, int 
   lm->attn_scale = (float)(1.0 / std::sqrt((double)d));  // MiniCpmAttention::new scale (attention.rs:48)
   lm->max_batch = max_batch;
   lm->max_length = max_length;
-  lm->attn_nsplit = std::max(4, std::min(32, max_length / 128));
+  lm->attn_nsplit = 32;  // upper bound; the kernel activates ceil(len/32) of them
 
   auto fail_free = [&](int code, const char* msg) {
     vx_lm_destroy(lm);
@@ -589,6 +619,41 @@ int vx_lm_greedy(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps
   cudaEventElapsedTime(&lm->t_decode_ms, lm->ev[1], lm->ev[2]);
   lm->cur_len = pos0 + n_steps;
   return VX_OK;
+}
+
+int vx_lm_profile_decode_step(vx_lm* lm, int pos, float* kernel_us, int n) {
+  if (!lm || !kernel_us) return VX_ERR_ARG;
+  vx_ctx* ctx = lm->ctx;
+  const int nk = lm->L * 5 + 1;
+  if (n < nk) return fail(ctx, VX_ERR_ARG, "kernel_us needs %d entries", nk);
+  if (pos < 0 || pos >= lm->max_length || !lm->embed) return fail(ctx, VX_ERR_ARG, "bad position or no vocabulary");
+  cudaSetDevice(ctx->device);
+  cudaStream_t st = ctx->stream;
+  std::vector<cudaEvent_t> ev(nk + 1);
+  for (auto& e : ev) VX_CUDA(ctx, cudaEventCreate(&e));
+  const bool pdl = ctx->pdl;
+  ctx->pdl = false;  // serialised: each kernel timed alone
+  lm->pos_host = pos;
+  VX_CUDA(ctx, cudaMemcpyAsync(lm->d_pos, &lm->pos_host, 4, cudaMemcpyHostToDevice, st));
+  int rc = VX_OK;
+  int k = 0;
+  VX_CUDA(ctx, cudaEventRecord(ev[0], st));
+  for (int l = 0; l < lm->L && !rc; ++l) {
+    rc = enqueue_layer_step(lm, l, st, true, 0, &ev[k + 1]);  // one event after each launch
+    k += 5;
+  }
+  if (!rc) rc = enqueue_lm_head(lm, st, false, false);
+  VX_CUDA(ctx, cudaEventRecord(ev[++k], st));
+  ctx->pdl = pdl;
+  VX_CUDA(ctx, cudaStreamSynchronize(st));
+  for (int i = 0; i < nk; ++i) kernel_us[i] = 0.f;
+  for (int i = 0; i < k; ++i) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+    kernel_us[i] = ms * 1000.f;
+  }
+  for (auto& e : ev) cudaEventDestroy(e);
+  return rc;
 }
 
 int vx_lm_last_timing(const vx_lm* lm, float* prefill_ms, float* decode_ms) {

@@ -60,7 +60,10 @@ struct vx_ctx {
   vx::Scratch scratch;
   unsigned int* counters = nullptr;  // 4096 zeroed counters
   int* dev_err = nullptr;            // device error word written by bounded waits
-  bool pdl = true;
+  bool pdl = true;                   // programmatic dependent launch between decode kernels
+  int gemv_ctas = 296;               // target GEMV grid (CTAs); env VX_GEMV_CTAS overrides
+  bool l2_prefetch = false;          // decode kernels prefetch the next kernel's weights into L2
+                                     // (env VX_L2_PREFETCH=1; measured: no gain with separate kernels)
 };
 
 namespace vx {
