@@ -125,6 +125,19 @@ int vx_linear_bf16(vx_ctx* ctx, const uint16_t* w, const float* bias, const floa
 int vx_attention_decode(vx_ctx* ctx, const float* q, const float* kcache, const float* vcache, int B, int nh,
                         int nkv, int head_dim, int s_max, int cur_len, float* out, vx_stream stream);
 
+/* vx_attention_decode for callers that cannot allocate device memory (a host that gives
+ * the library a fixed memory budget, or a real-time thread where a cudaMalloc could stall
+ * the device): no context, no allocation of any kind.  Its scratch is a file-scope device
+ * array of 1 MiB plus 64 counters, held by every GPU that loads the library until exit, so
+ * it accepts B * nkv <= 64 and B * nkv * 16 * 8 * (head_dim + 2) * 4 <= 1 MiB (else
+ * VX_ERR_SHAPE).  The first call on a device looks up the array's device address; make that
+ * call before any stream capture.  All calls share the array: calls that overlap on the GPU
+ * race and must be serialised by the caller.  Returns a status code only (no context, so no
+ * message).  Same arguments and results as vx_attention_decode; `stream` NULL = the legacy
+ * default stream.  No counterpart in the reference. */
+int vx_attention_decode_static(const float* q, const float* kcache, const float* vcache, int B, int nh, int nkv,
+                               int head_dim, int s_max, int cur_len, float* out, vx_stream stream);
+
 /* MiniCpmMlp::forward (minicpm4/mlp.rs:28-34): out = down(silu(gate) * up) with the fused
  * gate|up weight [2*inter, hidden] (gate first) and down [hidden, inter]; x [rows, hidden]. */
 int vx_mlp_swiglu(vx_ctx* ctx, const uint16_t* w_gate_up, const uint16_t* w_down, const float* x, int rows,

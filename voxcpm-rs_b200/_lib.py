@@ -64,6 +64,7 @@ SIGNATURES = {
     "vx_rope_apply": (I32, [P, P, P, P, P, I32, I32, I32, I32, I32, P]),
     "vx_linear_bf16": (I32, [P, P, P, P, I32, I32, I32, P, P]),
     "vx_attention_decode": (I32, [P, P, P, P, I32, I32, I32, I32, I32, I32, P, P]),
+    "vx_attention_decode_static": (I32, [P, P, P, I32, I32, I32, I32, I32, I32, P, P]),
     "vx_mlp_swiglu": (I32, [P, P, P, P, I32, I32, I32, P, P]),
     "vx_cfg_euler": (I32, [P, P, P, I32, I32, I32, F32, F64, I32, P]),
     "vx_lm_create": (I32, [P, C.POINTER(MiniCpm4ConfigC), I32, I32, C.POINTER(P)]),

@@ -17,7 +17,10 @@
 //   (forward / prefill and the non-causal DiT / LocEnc paths, attention.rs:55-88), causal
 //   or not, one warp per query row with an online softmax.
 #include <cfloat>
+#include <cmath>
+#include <mutex>
 
+#include "../../include/voxcpm_b200.h"
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -226,3 +229,79 @@ cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t st, bool 
 }
 
 }  // namespace vx
+
+// --------------------------------------------------------------------------- no allocation
+//
+// Decode attention for callers that must not allocate device memory.  Some hosts of this
+// library hand it a fixed memory budget (an audio server that reserves everything at
+// start-up, a plugin whose host owns the allocator) or call it from threads where a
+// cudaMalloc would stall the device (cudaMalloc can synchronise, which breaks real-time
+// audio deadlines).  vx_attention_decode needs a context, whose creation and scratch pool
+// allocate; this variant takes no context and keeps its split partials and arrival
+// counters in file-scope __device__ arrays instead:
+//   * partials: 1 MiB (kStaticPartialBytes), enough for B * n_kv_heads * 16 splits *
+//     8 heads * (head_dim + 2) floats; larger shapes are rejected with VX_ERR_SHAPE;
+//   * counters: 64 words, so B * n_kv_heads <= 64.
+// Every GPU that loads the library holds these arrays until the process exits.  All calls
+// share them: two calls whose kernels overlap on the GPU (different streams, or different
+// host threads) race on the same scratch and must be serialised by the caller.
+namespace vx {
+namespace {
+
+constexpr size_t kStaticPartialBytes = 1u << 20;
+constexpr int kStaticCounters = 64;
+constexpr int kStaticMaxSplits = 16;
+
+static __device__ __align__(256) float g_static_partials[kStaticPartialBytes / sizeof(float)];
+static __device__ __align__(256) unsigned int g_static_counters[kStaticCounters];
+
+// Device addresses of the two arrays, looked up once per device.  In host code the array
+// names are host-side stand-ins, not device addresses, so they are never passed to a kernel.
+struct StaticScratchAddr {
+  float* partials = nullptr;
+  unsigned int* counters = nullptr;
+};
+StaticScratchAddr g_static_addr[128];
+std::mutex g_static_mu;
+
+int static_scratch_for_current_device(StaticScratchAddr* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return VX_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  StaticScratchAddr& a = g_static_addr[dev];
+  if (!a.partials) {
+    void* p = nullptr;
+    void* c = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_partials) != cudaSuccess) return VX_ERR_CUDA;
+    if (cudaGetSymbolAddress(&c, g_static_counters) != cudaSuccess) return VX_ERR_CUDA;
+    a.partials = static_cast<float*>(p);
+    a.counters = static_cast<unsigned int*>(c);
+  }
+  *out = a;
+  return VX_OK;
+}
+
+}  // namespace
+}  // namespace vx
+
+extern "C" int vx_attention_decode_static(const float* q, const float* kcache, const float* vcache, int B,
+                                          int nh, int nkv, int head_dim, int s_max, int cur_len, float* out,
+                                          void* stream) {
+  using namespace vx;
+  if (!q || !kcache || !vcache || !out) return VX_ERR_ARG;
+  if (B <= 0 || nkv <= 0 || nh % nkv != 0 || nh / nkv != 8 || (head_dim != 128 && head_dim != 64))
+    return VX_ERR_SHAPE;
+  if (cur_len <= 0 || cur_len > s_max) return VX_ERR_SHAPE;
+  const size_t need = (size_t)B * nkv * kStaticMaxSplits * 8 * (head_dim + 2) * sizeof(float);
+  if (B * nkv > kStaticCounters || need > kStaticPartialBytes) return VX_ERR_SHAPE;
+  StaticScratchAddr sa;
+  const int rc = static_scratch_for_current_device(&sa);
+  if (rc != VX_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // the arrays keep the previous call's contents: start this call's counters from zero
+  if (cudaMemsetAsync(sa.counters, 0, (size_t)B * nkv * sizeof(unsigned int), st) != cudaSuccess)
+    return VX_ERR_CUDA;
+  AttnDecodeArgs a = {q, kcache, vcache, B, nh, nkv, head_dim, s_max, nullptr, cur_len,
+                      (float)(1.0 / std::sqrt((double)head_dim)), kStaticMaxSplits, sa.partials, sa.counters, out};
+  return launch_attn_decode(a, st, false) == cudaSuccess ? VX_OK : VX_ERR_CUDA;
+}
