@@ -205,6 +205,39 @@ int vx_lm_last_timing(const vx_lm* lm, float* prefill_ms, float* decode_ms);
 /* Logits of the last greedy pick (host [vocab]); valid after vx_lm_greedy. */
 int vx_lm_last_logits(vx_lm* lm, float* logits_out);
 
+/* ----------------------------------------------------------------- LocDiT + CFM */
+
+/* VoxCpmLocDiTV2::new (locdit/local_dit.rs:83-96): the DiT decoder is a MiniCPM-4 built from
+ * `cfg` (vocab_size must be 0, as asserted at local_dit.rs:84); max_rows bounds the batch of
+ * DiT rows (2B for a CFG solve of B latents). */
+int vx_dit_create(vx_ctx* ctx, const vx_minicpm4_config* cfg, int in_channels, int max_rows, vx_dit** out);
+void vx_dit_destroy(vx_dit* dit);
+/* in_proj [H, C], cond_proj [H, C], out_proj [C, H] (bf16, with f32 biases), and the two
+ * TimestepEmbedding MLPs time_mlp / delta_time_mlp: linear_1 [H, H] + b, linear_2 [H, H] + b
+ * (local_dit.rs:35-55). */
+int vx_dit_load(vx_dit* dit, const uint16_t* in_w, const float* in_b, const uint16_t* cond_w, const float* cond_b,
+                const uint16_t* out_w, const float* out_b, const uint16_t* t1_w, const float* t1_b,
+                const uint16_t* t2_w, const float* t2_b, const uint16_t* dt1_w, const float* dt1_b,
+                const uint16_t* dt2_w, const float* dt2_b);
+/* Decoder layer / final norm weights (as vx_lm_load_layer / vx_lm_load_norm). */
+int vx_dit_load_layer(vx_dit* dit, int layer, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                      const uint16_t* o, const uint16_t* gate, const uint16_t* up, const uint16_t* down,
+                      const float* ln_in, const float* ln_post);
+int vx_dit_load_norm(vx_dit* dit, const float* w);
+/* VoxCpmLocDiTV2::forward (local_dit.rs:102-112): x [N, C, T], mu [N, C_mu], cond [N, C, Tc]
+ * device; t and dt [N] host or device; out [N, C, T] device.  Synchronises. */
+int vx_dit_forward(vx_dit* dit, const float* x, const float* mu, const float* t, const float* cond, const float* dt,
+                   int N, int C_mu, int T, int Tc, float* out);
+/* UnifiedCfm::forward + solve_euler (locdit/unified_cfm.rs:34-163), non-mean mode, with the
+ * initial noise z [B, C, T] supplied by the caller (already scaled by temperature; the
+ * reference draws it from the backend RNG, or zeros under VOXCPM_Z_ZERO).  mu [B, C_mu],
+ * cond [B, C, Tc], x_out [B, C, T], all device.  Runs 2B DiT rows per step (cond | uncond
+ * with mu zeroed), the fused CFG(-zero-star) + Euler update, and skips the DiT on the first
+ * max(1, floor(0.04*(n+1))) steps when zero-star is on.  Polls vx_cancel between steps.
+ * Synchronises. */
+int vx_cfm_solve(vx_dit* dit, const float* mu, const float* cond, const float* z, int B, int C_mu, int T, int Tc,
+                 int n_timesteps, float cfg_value, float sway_sampling_coef, int use_cfg_zero_star, float* x_out);
+
 #ifdef __cplusplus
 }
 #endif

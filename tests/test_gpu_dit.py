@@ -1,0 +1,88 @@
+"""LocDiT forward and the CFM solve on the GPU through the C ABI, against the golden
+fixture (small DiT) and the oracle (the full LocDiT workload: 8 layers, hidden 1024,
+16/2 heads, head_dim 64, MLP 4096, 4-frame x 64-dim patches, CFG 2.0, 10 Euler steps).
+Tolerance 2e-2 max-abs/rel (bf16-weight path)."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import locdit as old
+from tests.conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+TOL = dict(atol=2e-2, rtol=2e-2)
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _t(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
+
+
+def test_golden_cfm_small(ctx):
+    from tests.golden.make_golden import small_dit_config
+    from voxcpm_rs_b200 import synth
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    g = dict(np.load(os.path.join(GOLDEN, "cfm_small.npz")))
+    dcfg = small_dit_config()
+    dit = VoxCpmLocDiTV2(ctx, dcfg, synth.locdit_weights(dcfg, in_channels=64, seed=6))
+    rng = np.random.default_rng(60)
+    mu = rng.standard_normal((1, 1024), dtype=np.float32)
+    cond = rng.standard_normal((1, 64, 4), dtype=np.float32)
+    z = rng.standard_normal((1, 64, 4), dtype=np.float32)
+    got = dit.cfm_forward(_t(mu), 4, _t(cond), _t(z), 2.0, 0.0, False).cpu().numpy()
+    assert_close(got, g["x_uniform"], **TOL, what="cfm uniform")
+    got = dit.cfm_forward(_t(mu), 4, _t(cond), _t(z), 2.0, 1.0, True).cpu().numpy()
+    assert_close(got, g["x_sway_zero_star"], **TOL, what="cfm sway + zero-star")
+    x2 = rng.standard_normal((2, 64, 4), dtype=np.float32)
+    mu2 = np.concatenate([mu, np.zeros_like(mu)])
+    got = dit.forward(_t(x2), _t(mu2), [0.7, 0.7], _t(np.concatenate([cond, cond])), [0.0, 0.0]).cpu().numpy()
+    assert_close(got, g["dit_forward"], **TOL, what="dit forward")
+    dit.close()
+
+
+@pytest.fixture(scope="module")
+def full_dit():
+    from voxcpm_rs_b200 import config, synth
+    lm = config.lm_decode_config(layers=1, vocab=0)
+    dcfg = config.locdit_config(lm)
+    w = synth.locdit_weights(dcfg, in_channels=64, seed=0)
+    return dcfg, w, synth.locdit_f32_view(w)
+
+
+def test_dit_forward_full(ctx, full_dit):
+    """One LocDiT forward at the full width with per-row t and dt (mean-mode inputs)."""
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    dcfg, w, fw = full_dit
+    rng = np.random.default_rng(20)
+    x = rng.standard_normal((2, 64, 4), dtype=np.float32)
+    mu = rng.standard_normal((2, 2048), dtype=np.float32)
+    cond = rng.standard_normal((2, 64, 4), dtype=np.float32)
+    t = np.array([0.3, 0.9], np.float32)
+    dt = np.array([0.1, 0.0], np.float32)
+    want = old.dit_forward(dcfg, fw, x, mu, t, cond, dt)
+    dit = VoxCpmLocDiTV2(ctx, dcfg, w)
+    got = dit.forward(_t(x), _t(mu), t, _t(cond), dt).cpu().numpy()
+    assert_close(got, want, **TOL, what="dit forward")
+    dit.close()
+
+
+@pytest.mark.parametrize("sway,zero_star", [(0.0, False), (1.0, True)])
+def test_cfm_solve_full(ctx, full_dit, sway, zero_star):
+    """UnifiedCfm::forward at the LocDiT workload: CFG 2.0, 10 Euler steps, t uniform
+    (sway 0, zero-star off) and the reference default (sway 1, zero-star on); B = 2."""
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    dcfg, w, fw = full_dit
+    rng = np.random.default_rng(21)
+    B = 2
+    mu = rng.standard_normal((B, 2048), dtype=np.float32)
+    cond = np.zeros((B, 64, 4), np.float32)
+    cond[1] = rng.standard_normal((64, 4), dtype=np.float32)
+    z = rng.standard_normal((B, 64, 4), dtype=np.float32)
+    want = old.cfm_forward(dcfg, fw, mu, 10, cond, z, 2.0, sway, zero_star)
+    dit = VoxCpmLocDiTV2(ctx, dcfg, w)
+    got = dit.cfm_forward(_t(mu), 10, _t(cond), _t(z), 2.0, sway, zero_star).cpu().numpy()
+    assert_close(got, want, **TOL, what="cfm solve")
+    assert np.abs(got - want).max() < 2e-3
+    dit.close()

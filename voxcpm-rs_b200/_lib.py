@@ -82,6 +82,13 @@ SIGNATURES = {
     "vx_lm_forward_step": (I32, [P, P, P]),
     "vx_lm_layer_forward_step": (I32, [P, I32, P, I32]),
     "vx_lm_greedy": (I32, [P, P, I32, I32, P]),
+    "vx_dit_create": (I32, [P, C.POINTER(MiniCpm4ConfigC), I32, I32, C.POINTER(P)]),
+    "vx_dit_destroy": (None, [P]),
+    "vx_dit_load": (I32, [P] + [P] * 14),
+    "vx_dit_load_layer": (I32, [P, I32, P, P, P, P, P, P, P, P, P]),
+    "vx_dit_load_norm": (I32, [P, P]),
+    "vx_dit_forward": (I32, [P, P, P, P, P, P, I32, I32, I32, I32, P]),
+    "vx_cfm_solve": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F32, F32, I32, P]),
     "vx_lm_last_logits": (I32, [P, P]),
 }
 

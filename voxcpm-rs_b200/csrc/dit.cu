@@ -1,0 +1,368 @@
+// LocDiT V2 + unified CFM sampler (reference src/locdit/local_dit.rs, unified_cfm.rs).
+//
+// The DiT decoder is a MiniCPM-4 model object (vx_lm without vocabulary) run non-causally
+// over the token sequence [mu tokens | time token | cond tokens | x tokens]
+// (local_dit.rs:152).  Around it, small kernels do the channel-major projections
+// (in_proj / cond_proj read [N, C, T] directly, out_proj writes [N, C, T] directly, so no
+// swap_dims copies exist), the sinusoidal time embedding and the sequence assembly.
+// vx_cfm_solve runs UnifiedCfm::forward + solve_euler with the noise z supplied by the
+// caller; each Euler step is: time MLP (one row: t is the same for every row) -> assemble ->
+// decoder -> out_proj -> fused CFG(-zero-star) + Euler update.
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+#include "runtime.cuh"
+
+using namespace vx;
+
+namespace {
+
+// dst[(n + k*Ns), row_off + t, h] = b[h] + sum_c W[h, c] * src[n, c, t]   for k < copies
+// src [Ns, C, T] (channel-major, as the reference's [N, C, T] tensors), W bf16 [H, C].
+__global__ void chan_proj_kernel(const float* __restrict__ src, int Ns, int C, int T, const uint16_t* __restrict__ W,
+                                 const float* __restrict__ b, int H, float* __restrict__ dst, int S, int row_off,
+                                 int copies) {
+  extern __shared__ float xs[];  // [C] column of one (n, t)
+  const int n = blockIdx.x / T, t = blockIdx.x % T;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) xs[c] = src[((size_t)n * C + c) * T + t];
+  __syncthreads();
+  for (int h = threadIdx.x; h < H; h += blockDim.x) {
+    const uint16_t* w = W + (size_t)h * C;
+    float acc = 0.f;
+    for (int c = 0; c < C; ++c) acc = fmaf(__uint_as_float(((uint32_t)w[c]) << 16), xs[c], acc);
+    const float v = acc + b[h];
+    for (int k = 0; k < copies; ++k) dst[((size_t)(n + k * Ns) * S + row_off + t) * H + h] = v;
+  }
+}
+
+// out[n, c, t] = b[c] + sum_h W[c, h] * hid[n, skip + t, h]   (out_proj + swap_dims, local_dit.rs:155-158)
+__global__ void out_proj_kernel(const float* __restrict__ hid, int N, int S, int skip, int T, int H,
+                                const uint16_t* __restrict__ W, const float* __restrict__ b, int C,
+                                float* __restrict__ out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= N * C * T) return;
+  const int t = warp % T, c = (warp / T) % C, n = warp / (T * C);
+  const float* x = hid + ((size_t)n * S + skip + t) * H;
+  const uint16_t* w = W + (size_t)c * H;
+  float acc = 0.f;
+  for (int h = lane; h < H; h += 32) acc = fmaf(__uint_as_float(((uint32_t)w[h]) << 16), x[h], acc);
+  acc = warp_sum(acc);
+  if (lane == 0) out[((size_t)n * C + c) * T + t] = acc + b[c];
+}
+
+// SinusoidalPosEmb::forward (local_dit.rs:24-32): out[n] = [sin(t_n*scale*f), cos(t_n*scale*f)]
+// with f32 frequencies formed in f64 on the host.
+__global__ void sinusoidal_kernel(const float* __restrict__ t, int n, float scale, const float* __restrict__ freqs,
+                                  int half, float* __restrict__ out) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n * half; i += gridDim.x * blockDim.x) {
+    const int r = i / half, k = i % half;
+    const float a = (t[r] * scale) * freqs[k];
+    out[(size_t)r * 2 * half + k] = sinf(a);
+    out[(size_t)r * 2 * half + half + k] = cosf(a);
+  }
+}
+
+__global__ void silu_inplace_kernel(float* x, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    x[i] = silu(x[i]);
+}
+
+// seq rows 0..mu_tokens: mu (reshape [N, C_mu] -> [N, mu_tokens, H]); row mu_tokens: the time
+// token temb[n % nt] + dtemb[n % nd] (local_dit.rs:147-152).
+__global__ void seq_head_kernel(const float* __restrict__ mu, int mu_tokens, const float* __restrict__ temb, int nt,
+                                const float* __restrict__ dtemb, int nd, int N, int S, int H, float* __restrict__ seq) {
+  const int n = blockIdx.x;
+  for (int i = threadIdx.x; i < (mu_tokens + 1) * H; i += blockDim.x) {
+    const int r = i / H, h = i % H;
+    float v;
+    if (r < mu_tokens)
+      v = mu[(size_t)n * mu_tokens * H + i];
+    else
+      v = temb[(size_t)(n % nt) * H + h] + dtemb[(size_t)(n % nd) * H + h];
+    seq[((size_t)n * S + r) * H + h] = v;
+  }
+}
+
+}  // namespace
+
+struct vx_dit {
+  vx_ctx* ctx = nullptr;
+  vx_lm* dec = nullptr;
+  int H = 0, C = 0, max_rows = 0;
+  float emb_scale_unused = 0.f;
+  // weights
+  uint16_t *in_w = nullptr, *cond_w = nullptr, *out_w = nullptr, *t1_w = nullptr, *t2_w = nullptr,
+           *dt1_w = nullptr, *dt2_w = nullptr;
+  float *in_b = nullptr, *cond_b = nullptr, *out_b = nullptr, *t1_b = nullptr, *t2_b = nullptr, *dt1_b = nullptr,
+        *dt2_b = nullptr;
+  float* freqs = nullptr;  // [H/2]
+  // work buffers (grown on demand)
+  int cap_rows = 0, cap_S = 0;
+  float *seq = nullptr, *hid = nullptr, *temb = nullptr, *dtemb = nullptr, *tmp = nullptr, *tvals = nullptr,
+        *out2b = nullptr, *mu_in = nullptr, *cond_in = nullptr;
+};
+
+namespace {
+
+int dit_buffers(vx_dit* d, int rows, int S, int C, int T, int Tc, int Cmu) {
+  if (rows <= d->cap_rows && S <= d->cap_S) return VX_OK;
+  float** bufs[] = {&d->seq, &d->hid, &d->temb, &d->dtemb, &d->tmp, &d->tvals, &d->out2b, &d->mu_in, &d->cond_in};
+  for (float** p : bufs) {
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+  }
+  const size_t H = d->H;
+  const int r = std::max(rows, 2), s = std::max(S, 16);
+  // T, Tc <= S and C_mu <= S*H, so sizing by s covers every later call with S <= cap_S
+  (void)T;
+  (void)Tc;
+  (void)Cmu;
+  const int tt = s, tc = s, cmu = s * (int)H;
+  bool ok = cudaMalloc(&d->seq, (size_t)r * s * H * 4) == cudaSuccess &&
+            cudaMalloc(&d->hid, (size_t)r * s * H * 4) == cudaSuccess &&
+            cudaMalloc(&d->temb, (size_t)r * H * 4) == cudaSuccess && cudaMalloc(&d->dtemb, (size_t)r * H * 4) == cudaSuccess &&
+            cudaMalloc(&d->tmp, (size_t)r * H * 4) == cudaSuccess && cudaMalloc(&d->tvals, (size_t)r * 4 + 64) == cudaSuccess &&
+            cudaMalloc(&d->out2b, (size_t)r * C * tt * 4) == cudaSuccess &&
+            cudaMalloc(&d->mu_in, (size_t)r * cmu * 4) == cudaSuccess &&
+            cudaMalloc(&d->cond_in, (size_t)r * C * tc * 4) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    d->cap_rows = 0;
+    return fail(d->ctx, VX_ERR_OOM, "DiT work buffers allocation failed");
+  }
+  d->cap_rows = r;
+  d->cap_S = s;
+  return VX_OK;
+}
+
+int launch_time_mlp(vx_dit* d, const uint16_t* w1, const float* b1, const uint16_t* w2, const float* b2,
+                    const float* tvals, int rows, float* out, cudaStream_t st) {
+  // TimestepEmbedding::forward(SinusoidalPosEmb(t, 1000)) (local_dit.rs:50-54, 147-148)
+  vx_ctx* ctx = d->ctx;
+  const int H = d->H, half = H / 2;
+  count_launch();
+  sinusoidal_kernel<<<std::max(1, (rows * half + 255) / 256), 256, 0, st>>>(tvals, rows, 1000.0f, d->freqs, half,
+                                                                              d->tmp);
+  VX_CUDA(ctx, cudaGetLastError());
+  GemmArgs g1 = {d->tmp, H, w1, b1, nullptr, 1.f, out, H, rows, H, H};
+  VX_CUDA(ctx, launch_gemm_smallm(g1, st));
+  count_launch();
+  silu_inplace_kernel<<<std::max(1, (rows * H + 255) / 256), 256, 0, st>>>(out, (size_t)rows * H);
+  VX_CUDA(ctx, cudaGetLastError());
+  GemmArgs g2 = {out, H, w2, b2, nullptr, 1.f, d->tmp, H, rows, H, H};
+  VX_CUDA(ctx, launch_gemm_smallm(g2, st));
+  VX_CUDA(ctx, cudaMemcpyAsync(out, d->tmp, (size_t)rows * H * 4, cudaMemcpyDeviceToDevice, st));
+  return VX_OK;
+}
+
+// One DiT forward on prepared inputs: seq rows [0, mu_tokens] already hold mu and the time
+// token, rows [mu_tokens+1, mu_tokens+1+Tc) the projected cond.  Writes x tokens, runs the
+// decoder and out_proj into `out` [N, C, T].
+int dit_forward_prepared(vx_dit* d, const float* x, int Nx, int copies, int N, int S, int skip, int T, float* out,
+                         cudaStream_t st) {
+  vx_ctx* ctx = d->ctx;
+  const int H = d->H, C = d->C;
+  count_launch();
+  chan_proj_kernel<<<Nx * T, 256, C * sizeof(float), st>>>(x, Nx, C, T, d->in_w, d->in_b, H, d->seq, S, skip, copies);
+  VX_CUDA(ctx, cudaGetLastError());
+  int rc = vx_lm_forward(d->dec, d->seq, N, S, 0, 0, d->hid);
+  if (rc) return rc;
+  const int warps = N * C * T;
+  count_launch();
+  out_proj_kernel<<<(warps * 32 + 255) / 256, 256, 0, st>>>(d->hid, N, S, skip, T, H, d->out_w, d->out_b, C, out);
+  VX_CUDA(ctx, cudaGetLastError());
+  return VX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int vx_dit_create(vx_ctx* ctx, const vx_minicpm4_config* cfg, int in_channels, int max_rows, vx_dit** out) {
+  if (!ctx || !cfg || !out || in_channels <= 0 || max_rows <= 0) return VX_ERR_ARG;
+  *out = nullptr;
+  if (cfg->vocab_size != 0) return fail(ctx, VX_ERR_CONFIG, "vocab_size must be 0 for local DiT");
+  if (cfg->hidden_size % 2) return fail(ctx, VX_ERR_CONFIG, "SinusoidalPosEmb requires even dim");
+  vx_dit* d = new vx_dit();
+  d->ctx = ctx;
+  d->H = cfg->hidden_size;
+  d->C = in_channels;
+  d->max_rows = max_rows;
+  int rc = vx_lm_create(ctx, cfg, max_rows, 64, &d->dec);
+  if (rc) {
+    delete d;
+    return rc;
+  }
+  cudaSetDevice(ctx->device);
+  const size_t H = d->H, C = in_channels;
+  bool ok = cudaMalloc(&d->in_w, H * C * 2) == cudaSuccess && cudaMalloc(&d->cond_w, H * C * 2) == cudaSuccess &&
+            cudaMalloc(&d->out_w, C * H * 2) == cudaSuccess && cudaMalloc(&d->t1_w, H * H * 2) == cudaSuccess &&
+            cudaMalloc(&d->t2_w, H * H * 2) == cudaSuccess && cudaMalloc(&d->dt1_w, H * H * 2) == cudaSuccess &&
+            cudaMalloc(&d->dt2_w, H * H * 2) == cudaSuccess && cudaMalloc(&d->in_b, H * 4) == cudaSuccess &&
+            cudaMalloc(&d->cond_b, H * 4) == cudaSuccess && cudaMalloc(&d->out_b, C * 4) == cudaSuccess &&
+            cudaMalloc(&d->t1_b, H * 4) == cudaSuccess && cudaMalloc(&d->t2_b, H * 4) == cudaSuccess &&
+            cudaMalloc(&d->dt1_b, H * 4) == cudaSuccess && cudaMalloc(&d->dt2_b, H * 4) == cudaSuccess &&
+            cudaMalloc(&d->freqs, H / 2 * 4) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    vx_dit_destroy(d);
+    return fail(ctx, VX_ERR_OOM, "DiT allocation failed");
+  }
+  // SinusoidalPosEmb frequencies: exp(-ln(1e4) * i / (half - 1)) in f64, stored as f32
+  const int half = d->H / 2;
+  std::vector<float> f(half);
+  const double emb_scale = std::log(10000.0) / ((double)half - 1.0);
+  for (int i = 0; i < half; ++i) f[i] = (float)std::exp(-emb_scale * (double)i);
+  if (cudaMemcpy(d->freqs, f.data(), half * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+    vx_dit_destroy(d);
+    return fail(ctx, VX_ERR_CUDA, "DiT frequency upload failed");
+  }
+  *out = d;
+  return VX_OK;
+}
+
+void vx_dit_destroy(vx_dit* d) {
+  if (!d) return;
+  cudaSetDevice(d->ctx->device);
+  cudaStreamSynchronize(d->ctx->stream);
+  if (d->dec) vx_lm_destroy(d->dec);
+  void* ptrs[] = {d->in_w, d->cond_w, d->out_w, d->t1_w, d->t2_w, d->dt1_w, d->dt2_w, d->in_b, d->cond_b,
+                  d->out_b, d->t1_b, d->t2_b, d->dt1_b, d->dt2_b, d->freqs, d->seq, d->hid, d->temb,
+                  d->dtemb, d->tmp, d->tvals, d->out2b, d->mu_in, d->cond_in};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+  delete d;
+}
+
+int vx_dit_load(vx_dit* d, const uint16_t* in_w, const float* in_b, const uint16_t* cond_w, const float* cond_b,
+                const uint16_t* out_w, const float* out_b, const uint16_t* t1_w, const float* t1_b,
+                const uint16_t* t2_w, const float* t2_b, const uint16_t* dt1_w, const float* dt1_b,
+                const uint16_t* dt2_w, const float* dt2_b) {
+  if (!d || !in_w || !in_b || !cond_w || !cond_b || !out_w || !out_b || !t1_w || !t1_b || !t2_w || !t2_b ||
+      !dt1_w || !dt1_b || !dt2_w || !dt2_b)
+    return VX_ERR_ARG;
+  vx_ctx* ctx = d->ctx;
+  cudaSetDevice(ctx->device);
+  const size_t H = d->H, C = d->C;
+  struct Cp {
+    void* dst;
+    const void* src;
+    size_t n;
+  } cps[] = {{d->in_w, in_w, H * C * 2},   {d->in_b, in_b, H * 4},     {d->cond_w, cond_w, H * C * 2},
+             {d->cond_b, cond_b, H * 4},   {d->out_w, out_w, C * H * 2}, {d->out_b, out_b, C * 4},
+             {d->t1_w, t1_w, H * H * 2},   {d->t1_b, t1_b, H * 4},     {d->t2_w, t2_w, H * H * 2},
+             {d->t2_b, t2_b, H * 4},       {d->dt1_w, dt1_w, H * H * 2}, {d->dt1_b, dt1_b, H * 4},
+             {d->dt2_w, dt2_w, H * H * 2}, {d->dt2_b, dt2_b, H * 4}};
+  for (const Cp& c : cps) VX_CUDA(ctx, cudaMemcpy(c.dst, c.src, c.n, cudaMemcpyDefault));
+  return VX_OK;
+}
+
+int vx_dit_load_layer(vx_dit* d, int layer, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                      const uint16_t* o, const uint16_t* gate, const uint16_t* up, const uint16_t* down,
+                      const float* ln_in, const float* ln_post) {
+  if (!d) return VX_ERR_ARG;
+  return vx_lm_load_layer(d->dec, layer, q, k, v, o, gate, up, down, ln_in, ln_post);
+}
+
+int vx_dit_load_norm(vx_dit* d, const float* w) {
+  if (!d) return VX_ERR_ARG;
+  return vx_lm_load_norm(d->dec, w);
+}
+
+int vx_dit_forward(vx_dit* d, const float* x, const float* mu, const float* t, const float* cond, const float* dt,
+                   int N, int C_mu, int T, int Tc, float* out) {
+  if (!d || !x || !mu || !t || !cond || !dt || !out) return VX_ERR_ARG;
+  vx_ctx* ctx = d->ctx;
+  const int H = d->H, C = d->C;
+  if (N <= 0 || N > d->max_rows || T <= 0 || Tc <= 0 || C_mu % H != 0)
+    return fail(ctx, VX_ERR_SHAPE, "dit_forward: N=%d (max %d), T=%d, Tc=%d, C_mu=%d (multiple of %d)", N, d->max_rows,
+                T, Tc, C_mu, H);
+  const int mu_tokens = C_mu / H, skip = Tc + mu_tokens + 1, S = skip + T;
+  if (S > 64) return fail(ctx, VX_ERR_SHAPE, "dit_forward: sequence %d > 64", S);
+  cudaSetDevice(ctx->device);
+  cudaStream_t st = ctx->stream;
+  int rc = dit_buffers(d, N, S, C, T, Tc, C_mu);
+  if (rc) return rc;
+  // prepare (local_dit.rs:116-134): cond_proj, delta-time MLP(dt)
+  count_launch();
+  chan_proj_kernel<<<N * Tc, 256, C * sizeof(float), st>>>(cond, N, C, Tc, d->cond_w, d->cond_b, H, d->seq, S,
+                                                           mu_tokens + 1, 1);
+  VX_CUDA(ctx, cudaGetLastError());
+  VX_CUDA(ctx, cudaMemcpyAsync(d->tvals, dt, (size_t)N * 4, cudaMemcpyDefault, st));
+  rc = launch_time_mlp(d, d->dt1_w, d->dt1_b, d->dt2_w, d->dt2_b, d->tvals, N, d->dtemb, st);
+  if (rc) return rc;
+  VX_CUDA(ctx, cudaMemcpyAsync(d->tvals, t, (size_t)N * 4, cudaMemcpyDefault, st));
+  rc = launch_time_mlp(d, d->t1_w, d->t1_b, d->t2_w, d->t2_b, d->tvals, N, d->temb, st);
+  if (rc) return rc;
+  count_launch();
+  seq_head_kernel<<<N, 256, 0, st>>>(mu, mu_tokens, d->temb, N, d->dtemb, N, N, S, H, d->seq);
+  VX_CUDA(ctx, cudaGetLastError());
+  rc = dit_forward_prepared(d, x, N, 1, N, S, skip, T, out, st);
+  if (rc) return rc;
+  return vx_ctx_synchronize(ctx);
+}
+
+int vx_cfm_solve(vx_dit* d, const float* mu, const float* cond, const float* z, int B, int C_mu, int T, int Tc,
+                 int n_timesteps, float cfg_value, float sway_sampling_coef, int use_cfg_zero_star, float* x_out) {
+  if (!d || !mu || !cond || !z || !x_out) return VX_ERR_ARG;
+  vx_ctx* ctx = d->ctx;
+  const int H = d->H, C = d->C, N = 2 * B;
+  if (B <= 0 || N > d->max_rows || T <= 0 || Tc <= 0 || C_mu % H != 0 || n_timesteps < 1)
+    return fail(ctx, VX_ERR_SHAPE, "cfm_solve: B=%d (2B <= %d), T=%d, Tc=%d, C_mu=%d, steps=%d", B, d->max_rows, T, Tc,
+                C_mu, n_timesteps);
+  const int mu_tokens = C_mu / H, skip = Tc + mu_tokens + 1, S = skip + T;
+  if (S > 64) return fail(ctx, VX_ERR_SHAPE, "cfm_solve: sequence %d > 64", S);
+  cudaSetDevice(ctx->device);
+  cudaStream_t st = ctx->stream;
+  int rc = dit_buffers(d, N, S, C, T, Tc, C_mu);
+  if (rc) return rc;
+
+  // t-span with sway (unified_cfm.rs:59-67): t_i = f32(1 - i/n), sway in f64, stored as f32
+  const int n = n_timesteps + 1;
+  std::vector<float> ts(n);
+  const double stepw = 1.0 / (double)n_timesteps;
+  for (int i = 0; i < n; ++i) {
+    const double tt = (double)(float)(1.0 - (double)i * stepw);
+    ts[i] = (float)(tt + (double)sway_sampling_coef * (std::cos(M_PI / 2.0 * tt) - 1.0 + tt));
+  }
+  // solve_euler (unified_cfm.rs:72-163)
+  double t = ts[0];
+  double dt = (double)(ts[0] - ts[1]);
+  const int zero_init_steps = (int)std::max((double)n * 0.04, 1.0);
+  // mu_in = [mu; 0], cond_in = [cond; cond] (unified_cfm.rs:96-98); prepare once with dt = 0
+  VX_CUDA(ctx, cudaMemcpyAsync(d->mu_in, mu, (size_t)B * C_mu * 4, cudaMemcpyDefault, st));
+  VX_CUDA(ctx, cudaMemsetAsync(d->mu_in + (size_t)B * C_mu, 0, (size_t)B * C_mu * 4, st));
+  VX_CUDA(ctx, cudaMemcpyAsync(d->cond_in, cond, (size_t)B * C * Tc * 4, cudaMemcpyDefault, st));
+  count_launch();
+  chan_proj_kernel<<<B * Tc, 256, C * sizeof(float), st>>>(d->cond_in, B, C, Tc, d->cond_w, d->cond_b, H, d->seq, S,
+                                                           mu_tokens + 1, 2);
+  VX_CUDA(ctx, cudaGetLastError());
+  VX_CUDA(ctx, cudaMemsetAsync(d->tvals, 0, 4, st));
+  rc = launch_time_mlp(d, d->dt1_w, d->dt1_b, d->dt2_w, d->dt2_b, d->tvals, 1, d->dtemb, st);
+  if (rc) return rc;
+  VX_CUDA(ctx, cudaMemcpyAsync(x_out, z, (size_t)B * C * T * 4, cudaMemcpyDefault, st));
+  std::vector<float> tf(n);
+  for (int step = 1; step < n; ++step) {
+    if (ctx->cancel.load(std::memory_order_relaxed)) return fail(ctx, VX_ERR_CANCELLED, "generation cancelled");
+    if (!(use_cfg_zero_star && step <= zero_init_steps)) {
+      tf[step] = (float)t;
+      VX_CUDA(ctx, cudaMemcpyAsync(d->tvals + 1, &tf[step], 4, cudaMemcpyHostToDevice, st));
+      rc = launch_time_mlp(d, d->t1_w, d->t1_b, d->t2_w, d->t2_b, d->tvals + 1, 1, d->temb, st);
+      if (rc) return rc;
+      count_launch();
+      seq_head_kernel<<<N, 256, 0, st>>>(d->mu_in, mu_tokens, d->temb, 1, d->dtemb, 1, N, S, H, d->seq);
+      VX_CUDA(ctx, cudaGetLastError());
+      rc = dit_forward_prepared(d, x_out, B, 2, N, S, skip, T, d->out2b, st);
+      if (rc) return rc;
+      VX_CUDA(ctx, launch_cfg_euler(d->out2b, x_out, B, C * T, (double)cfg_value, dt, use_cfg_zero_star, st));
+    }
+    // else: dphi_dt = 0, x - 0*dt == x
+    t -= dt;
+    if (step < n - 1) dt = t - (double)ts[step + 1];
+  }
+  return vx_ctx_synchronize(ctx);
+}
+
+}  // extern "C"
