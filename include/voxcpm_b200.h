@@ -238,6 +238,55 @@ int vx_dit_forward(vx_dit* dit, const float* x, const float* mu, const float* t,
 int vx_cfm_solve(vx_dit* dit, const float* mu, const float* cond, const float* z, int B, int C_mu, int T, int Tc,
                  int n_timesteps, float cfg_value, float sway_sampling_coef, int use_cfg_zero_star, float* x_out);
 
+/* ----------------------------------------------------------------- AudioVAE decoder */
+
+/* AudioVaeConfig (config.rs:219-309), decoder side.  Block i maps decoder_dim>>i to
+ * decoder_dim>>(i+1) channels with stride rates[i]; every output channel count must be a
+ * multiple of 64.  The sample-rate bucket is chosen once from out_sample_rate (sr_bucket,
+ * audiovae/layers.rs:225-228); n_sr_boundaries = 0 disables SR conditioning. */
+typedef struct {
+  int latent_dim;
+  int decoder_dim;
+  const int* rates;
+  int n_rates;
+  int depthwise;       /* only 1 is supported (the shipped VoxCPM2 decoder) */
+  int use_noise_block; /* only 0 is supported (NoiseBlock is off in VoxCPM2) */
+  int out_sample_rate;
+  const int* sr_boundaries;
+  int n_sr_boundaries;
+} vx_vae_config;
+
+/* One CausalDecoderBlock (audiovae/decoder.rs:11-56) in checkpoint layouts: snake alpha [C_in];
+ * ConvTranspose1d weight [C_in, C_out, 2*stride] bf16 + bias [C_out]; three
+ * CausalResidualUnits (dilations 1, 3, 9): snake alphas [C_out], depthwise conv [C_out, 1, 7]
+ * bf16 + bias, pointwise conv [C_out, C_out, 1] bf16 + bias; SampleRateConditionLayer
+ * embedding tables [n_buckets, C_in] (scale, bias). */
+typedef struct {
+  const float* alpha;
+  const uint16_t* up_w;
+  const float* up_b;
+  const float* res_alpha1[3];
+  const uint16_t* res_w1[3];
+  const float* res_b1[3];
+  const float* res_alpha2[3];
+  const uint16_t* res_w2[3];
+  const float* res_b2[3];
+  const float* sr_scale;
+  const float* sr_bias;
+} vx_vae_block_weights;
+
+/* CausalDecoder::new (audiovae/decoder.rs:103-147). */
+int vx_vae_create(vx_ctx* ctx, const vx_vae_config* cfg, vx_vae** out);
+void vx_vae_destroy(vx_vae* vae);
+/* DecoderFirstConv (decoder.rs:60-90), depthwise mode: dw [latent, 1, 7] + b, pw [dim, latent, 1] + b. */
+int vx_vae_load_first(vx_vae* vae, const uint16_t* dw_w, const float* dw_b, const uint16_t* pw_w, const float* pw_b);
+int vx_vae_load_block(vx_vae* vae, int block, const vx_vae_block_weights* w);
+/* snake_out alpha [C_last] and the last CausalConv1d [1, C_last, 7] + bias [1] (decoder.rs:124-125). */
+int vx_vae_load_out(vx_vae* vae, const float* alpha_out, const uint16_t* last_w, const float* last_b);
+/* AudioVae::decode (audiovae/vae.rs:55-59): z [B, latent, T] -> wav [B, 1, T * prod(rates)],
+ * device pointers.  Synchronises. */
+int vx_vae_decode(vx_vae* vae, const float* z, int B, int T, float* wav);
+
 #ifdef __cplusplus
 }
 #endif

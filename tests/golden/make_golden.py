@@ -83,7 +83,8 @@ def cfm_case():
 
 
 def small_vae_config():
-    return config.vae_config(decoder_dim=256, decoder_rates=[2, 5, 8])
+    """decoder_dim 512, rates [2, 5, 8]: channels 512 -> 256 -> 128 -> 64, hop 80."""
+    return config.vae_config(decoder_dim=512, decoder_rates=[2, 5, 8])
 
 
 def vae_case():

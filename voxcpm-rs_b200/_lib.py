@@ -45,6 +45,18 @@ I32 = C.c_int
 F32 = C.c_float
 F64 = C.c_double
 
+
+class VaeConfigC(C.Structure):
+    _fields_ = [("latent_dim", C.c_int), ("decoder_dim", C.c_int), ("rates", C.POINTER(C.c_int)),
+                ("n_rates", C.c_int), ("depthwise", C.c_int), ("use_noise_block", C.c_int),
+                ("out_sample_rate", C.c_int), ("sr_boundaries", C.POINTER(C.c_int)), ("n_sr_boundaries", C.c_int)]
+
+
+class VaeBlockWeightsC(C.Structure):
+    _fields_ = [("alpha", P), ("up_w", P), ("up_b", P), ("res_alpha1", P * 3), ("res_w1", P * 3),
+                ("res_b1", P * 3), ("res_alpha2", P * 3), ("res_w2", P * 3), ("res_b2", P * 3),
+                ("sr_scale", P), ("sr_bias", P)]
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "vx_version": (I32, []),
@@ -89,6 +101,12 @@ SIGNATURES = {
     "vx_dit_load_norm": (I32, [P, P]),
     "vx_dit_forward": (I32, [P, P, P, P, P, P, I32, I32, I32, I32, P]),
     "vx_cfm_solve": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F32, F32, I32, P]),
+    "vx_vae_create": (I32, [P, C.POINTER(VaeConfigC), C.POINTER(P)]),
+    "vx_vae_destroy": (None, [P]),
+    "vx_vae_load_first": (I32, [P, P, P, P, P]),
+    "vx_vae_load_block": (I32, [P, I32, C.POINTER(VaeBlockWeightsC)]),
+    "vx_vae_load_out": (I32, [P, P, P, P]),
+    "vx_vae_decode": (I32, [P, P, I32, I32, P]),
     "vx_lm_last_logits": (I32, [P, P]),
 }
 
