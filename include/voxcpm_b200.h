@@ -287,6 +287,29 @@ int vx_vae_load_out(vx_vae* vae, const float* alpha_out, const uint16_t* last_w,
  * device pointers.  Synchronises. */
 int vx_vae_decode(vx_vae* vae, const float* z, int B, int T, float* wav);
 
+/* ----------------------------------------------------------------- synthesis */
+
+/* GenerateOptions (voxcpm2/wrapper.rs:146-187) as this library's synthesis loop uses them. */
+typedef struct {
+  float cfg_value;          /* classifier-free guidance scale (default 2.0) */
+  int inference_timesteps;  /* Euler steps of the CFM solve (default 10) */
+  int max_len;              /* latent patches to generate (the loop has no stop head) */
+  int patch_size;           /* frames per patch (VoxCPM2: 4) */
+  float sway_sampling_coef; /* dit_step passes 1.0 (voxcpm2/model.rs:236) */
+  int use_cfg_zero_star;    /* dit_step passes true (voxcpm2/model.rs:237) */
+} vx_generate_options;
+
+/* One utterance end to end, shaped like VoxCpm2Model::inference + VoxCPM::generate
+ * (voxcpm2/model.rs:301-375, wrapper.rs:401-423): greedy decode of the prompt ids with the
+ * LM (graph-replayed steps); after decode step i, a CFM solve with mu = the LM's final-norm
+ * hidden, cond = the previous patch (zeros first) and z = noise[i] ([C, P]; noise holds
+ * max_len patches, host or device); patches stacked [C, max_len*P] (stack_pred_feats,
+ * model.rs:283-287) and decoded by the VAE.  wav_out (host or device) receives
+ * max_len*P*prod(rates) samples; latent_out (optional) the stacked latent.  The three
+ * objects must share one context.  vx_cancel is polled every step (model.rs:330-334). */
+int vx_generate(vx_lm* lm, vx_dit* dit, vx_vae* vae, const int32_t* prompt_ids, int n_prompt,
+                const vx_generate_options* opts, const float* noise, float* wav_out, float* latent_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,45 @@
+"""End-to-end synthesis on the GPU (vx_generate) against the oracle's loop: greedy LM decode,
+a CFM solve per step on the step's final-norm hidden, stacked latent, AudioVAE decode.
+Small models (2-layer LM at full width with vocab 4096, 2-layer DiT of hidden 512, a
+512-wide 3-block VAE) and 6 patches.  Tolerance 2e-2 max-abs/rel."""
+import numpy as np
+import pytest
+
+from oracle import voxcpm as ovx
+from tests.conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+TOL = dict(atol=2e-2, rtol=2e-2)
+
+
+def test_generate_small(ctx):
+    from tests.golden.make_golden import small_dit_config, small_vae_config
+    from voxcpm_rs_b200 import config, synth
+    from voxcpm_rs_b200.audiovae import AudioVae
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    from voxcpm_rs_b200.minicpm4 import MiniCpmModel
+    from voxcpm_rs_b200.voxcpm import GenerateOptions, VoxCPM
+    lm_cfg = config.lm_decode_config(layers=2, vocab=4096)
+    lm_w = synth.minicpm_weights(lm_cfg, seed=3)
+    dcfg, vcfg = small_dit_config(), small_vae_config()
+    dit_w = synth.locdit_weights(dcfg, in_channels=64, seed=4)
+    vae_w = synth.vae_weights(vcfg, seed=5)
+    prompt = synth.prompt_ids(16, lm_cfg.vocab_size, seed=1)
+    opts = GenerateOptions(max_len=6, inference_timesteps=4)
+    noise = np.random.default_rng(8).standard_normal((6, 64, 4), dtype=np.float32)
+    want_wav, want_lat, _ = ovx.generate(lm_cfg, synth.minicpm_f32_view(lm_w), dcfg, synth.locdit_f32_view(dit_w),
+                                         vcfg, synth.vae_f32_view(vae_w), prompt, 6, noise, inference_timesteps=4)
+    vox = VoxCPM(ctx, MiniCpmModel(ctx, lm_cfg, lm_w, max_length=64), VoxCpmLocDiTV2(ctx, dcfg, dit_w),
+                 AudioVae(ctx, vcfg, vae_w))
+    wav, lat = vox.generate(prompt, opts, noise, return_latent=True)
+    assert wav.shape == (6 * 4 * 80,)
+    assert_close(lat, want_lat, **TOL, what="latent")
+    assert_close(wav, want_wav, **TOL, what="wav")
+    # cancellation between steps surfaces as Error::Cancelled
+    from voxcpm_rs_b200._lib import Cancelled
+    ctx.cancel()
+    try:
+        with pytest.raises(Cancelled):
+            vox.generate(prompt, opts, noise)
+    finally:
+        ctx.cancel_reset()

@@ -52,6 +52,11 @@ class VaeConfigC(C.Structure):
                 ("out_sample_rate", C.c_int), ("sr_boundaries", C.POINTER(C.c_int)), ("n_sr_boundaries", C.c_int)]
 
 
+class GenerateOptionsC(C.Structure):
+    _fields_ = [("cfg_value", C.c_float), ("inference_timesteps", C.c_int), ("max_len", C.c_int),
+                ("patch_size", C.c_int), ("sway_sampling_coef", C.c_float), ("use_cfg_zero_star", C.c_int)]
+
+
 class VaeBlockWeightsC(C.Structure):
     _fields_ = [("alpha", P), ("up_w", P), ("up_b", P), ("res_alpha1", P * 3), ("res_w1", P * 3),
                 ("res_b1", P * 3), ("res_alpha2", P * 3), ("res_w2", P * 3), ("res_b2", P * 3),
@@ -107,6 +112,7 @@ SIGNATURES = {
     "vx_vae_load_block": (I32, [P, I32, C.POINTER(VaeBlockWeightsC)]),
     "vx_vae_load_out": (I32, [P, P, P, P]),
     "vx_vae_decode": (I32, [P, P, I32, I32, P]),
+    "vx_generate": (I32, [P, P, P, P, I32, C.POINTER(GenerateOptionsC), P, P, P]),
     "vx_lm_last_logits": (I32, [P, P]),
 }
 

@@ -366,3 +366,8 @@ int vx_cfm_solve(vx_dit* d, const float* mu, const float* cond, const float* z, 
 }
 
 }  // extern "C"
+
+namespace vx {
+vx_ctx* dit_ctx(vx_dit* d) { return d->ctx; }
+int dit_in_channels(const vx_dit* d) { return d->C; }
+}  // namespace vx

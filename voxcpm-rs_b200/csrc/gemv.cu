@@ -129,6 +129,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_bf16_kernel(const GemvAr
     }
   }
   named_sync(1, GEMV_CWARPS * 32);
+  if (a.norm_out != nullptr && blockIdx.x == 0)
+    for (int k = tid * 4; k < a.K; k += 256 * 4)
+      *reinterpret_cast<float4*>(a.norm_out + k) = *reinterpret_cast<const float4*>(xs + k);
 
   constexpr int NJ = KC / 256;
   float xr[NJ * 8];

@@ -76,6 +76,10 @@ struct GemvArgs {
 
   int* err;  // device error word (bounded waits record VX_DEVICE_ERR_TIMEOUT here)
 
+  // Optional copy of the normalised input vector (CTA 0 writes it), e.g. the final-norm
+  // hidden state the greedy head sees, which the synthesis loop feeds to the DiT.
+  float* norm_out;
+
   // Optional L2 prefetch of the next kernel's weights (split evenly over the CTAs), issued
   // once this CTA's first stages are in flight, so HBM stays busy across kernel boundaries.
   const void* pf_ptr;

@@ -57,6 +57,7 @@ struct vx_lm {
   float* attn = nullptr;    // [nh*d]
   float* act = nullptr;     // [I]
   float* logits = nullptr;  // [V]
+  float* hid_norm = nullptr;  // final-norm hidden of the last greedy pick [H]
   float* attn_partials = nullptr;
   unsigned* attn_counters = nullptr;
   float2* argmax_partials = nullptr;
@@ -233,6 +234,7 @@ int enqueue_lm_head(vx_lm* lm, cudaStream_t st, bool advance_pos, bool write_log
   h.embed_scale = lm->emb_scale;
   h.next_x = lm->x;
   h.pos_inc = advance_pos ? lm->d_pos : nullptr;
+  h.norm_out = lm->hid_norm;
   VX_CUDA(lm->ctx, launch_gemv(h, EPI_ARGMAX, st, lm->ctx->pdl, lm->ctx->dev_err));
   return VX_OK;
 }
@@ -342,7 +344,8 @@ int vx_lm_create(vx_ctx* ctx, const vx_minicpm4_config* cfg, int max_batch, int 
             cudaMemset(lm->kcache, 0, kv_bytes) == cudaSuccess && cudaMemset(lm->vcache, 0, kv_bytes) == cudaSuccess &&
             cudaMalloc(&lm->d_pos, 64) == cudaSuccess && cudaMalloc(&lm->d_step, 64) == cudaSuccess &&
             cudaMalloc(&lm->d_tokens, (size_t)(max_length + 8) * 4) == cudaSuccess &&
-            cudaMalloc(&lm->x, H * 4 * max_batch) == cudaSuccess && cudaMalloc(&lm->q, lm->qs * 4 * max_batch) == cudaSuccess &&
+            cudaMalloc(&lm->x, H * 4 * max_batch) == cudaSuccess && cudaMalloc(&lm->hid_norm, H * 4) == cudaSuccess &&
+            cudaMalloc(&lm->q, lm->qs * 4 * max_batch) == cudaSuccess &&
             cudaMalloc(&lm->attn, lm->qs * 4 * max_batch) == cudaSuccess && cudaMalloc(&lm->act, I * 4 * max_batch) == cudaSuccess &&
             cudaMalloc(&lm->attn_partials, (size_t)max_batch * lm->nkv * 32 * lm->nh / lm->nkv * (d + 2) * 4) == cudaSuccess &&
             cudaMalloc(&lm->attn_counters, (size_t)max_batch * lm->nkv * 4) == cudaSuccess &&
@@ -371,7 +374,8 @@ void vx_lm_destroy(vx_lm* lm) {
     if (e) cudaEventDestroy(e);
   free_prefill(lm);
   void* ptrs[] = {lm->weight_slab, lm->norm_w, lm->embed, lm->rope, lm->kcache, lm->vcache, lm->d_pos,
-                  lm->d_step, lm->d_tokens, lm->x, lm->q, lm->attn, lm->act, lm->logits, lm->attn_partials,
+                  lm->d_step, lm->d_tokens, lm->x, lm->hid_norm, lm->q, lm->attn, lm->act, lm->logits,
+                  lm->attn_partials,
                   lm->attn_counters, lm->argmax_partials, lm->argmax_counter, lm->pf_ids};
   for (void* p : ptrs)
     if (p) cudaFree(p);
@@ -561,8 +565,17 @@ int vx_lm_forward_step(vx_lm* lm, const float* embeds, float* hidden_out) {
   return VX_OK;
 }
 
-int vx_lm_greedy(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps, int32_t* tokens_out) {
-  if (!lm || !prompt_ids || !tokens_out || n_prompt <= 0 || n_steps < 0) return VX_ERR_ARG;
+}  // extern "C"
+
+namespace vx {
+
+vx_ctx* lm_ctx(vx_lm* lm) { return lm->ctx; }
+int lm_hidden_size(const vx_lm* lm) { return lm->H; }
+const float* lm_hid_norm(const vx_lm* lm) { return lm->hid_norm; }
+
+// Validate, prefill the prompt (causal forward + cache fill), pick the first id with the
+// greedy head and set the device position for the decode steps.  Records ev[0], ev[1].
+int lm_greedy_begin(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps) {
   vx_ctx* ctx = lm->ctx;
   if (!lm->embed) return fail(ctx, VX_ERR_CONFIG, "greedy decode needs a vocabulary");
   if (n_prompt + n_steps > lm->max_length)
@@ -598,10 +611,35 @@ int vx_lm_greedy(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps
   VX_CUDA(ctx, cudaMemsetAsync(lm->d_step, 0, 4, st));
   rc = enqueue_lm_head(lm, st, false, n_steps == 0);
   if (rc) return rc;
-  const int pos0 = n_prompt;
-  lm->pos_host = pos0;
+  lm->pos_host = n_prompt;
   VX_CUDA(ctx, cudaMemcpyAsync(lm->d_pos, &lm->pos_host, 4, cudaMemcpyHostToDevice, st));
   VX_CUDA(ctx, cudaEventRecord(lm->ev[1], st));
+  lm->cur_len = n_prompt;
+  return VX_OK;
+}
+
+// One graph-replayed decode step: consumes the last picked id at the device position,
+// writes the next id, the final-norm hidden (hid_norm) and advances the position.
+int lm_greedy_step(vx_lm* lm) {
+  vx_ctx* ctx = lm->ctx;
+  if (!(lm->cur_len < lm->max_length)) return fail(ctx, VX_ERR_KV_FULL, "KV cache is full");
+  VX_CUDA(ctx, cudaGraphLaunch(lm->step_exec, ctx->stream));
+  count_launch(lm->step_kernels);
+  lm->cur_len += 1;
+  return VX_OK;
+}
+
+}  // namespace vx
+
+extern "C" {
+
+int vx_lm_greedy(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps, int32_t* tokens_out) {
+  if (!lm || !prompt_ids || !tokens_out || n_prompt <= 0 || n_steps < 0) return VX_ERR_ARG;
+  vx_ctx* ctx = lm->ctx;
+  int rc = lm_greedy_begin(lm, prompt_ids, n_prompt, n_steps);
+  if (rc) return rc;
+  cudaStream_t st = ctx->stream;
+  const int pos0 = n_prompt;
   for (int s = 0; s < n_steps; ++s) {
     if (ctx->cancel.load(std::memory_order_relaxed)) {
       cudaStreamSynchronize(st);

@@ -102,4 +102,17 @@ inline double residual_scale_of(const vx_minicpm4_config& c) {
 
 int fill_rope_params(const vx_minicpm4_config& c, RopeParams* rp, std::string* err);
 
+// Greedy LM decoding, split for the synthesis loop (lm.cu).
+vx_ctx* lm_ctx(vx_lm* lm);
+int lm_hidden_size(const vx_lm* lm);
+const float* lm_hid_norm(const vx_lm* lm);
+int lm_greedy_begin(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps);
+int lm_greedy_step(vx_lm* lm);
+// DiT / VAE accessors (dit.cu, vae.cu).
+vx_ctx* dit_ctx(vx_dit* d);
+int dit_in_channels(const vx_dit* d);
+vx_ctx* vae_ctx(vx_vae* v);
+int vae_latent(const vx_vae* v);
+int vae_hop(const vx_vae* v);
+
 }  // namespace vx

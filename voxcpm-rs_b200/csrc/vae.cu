@@ -461,3 +461,13 @@ int vx_vae_decode(vx_vae* v, const float* z, int B, int T, float* wav) {
 }
 
 }  // extern "C"
+
+namespace vx {
+vx_ctx* vae_ctx(vx_vae* v) { return v->ctx; }
+int vae_latent(const vx_vae* v) { return v->latent; }
+int vae_hop(const vx_vae* v) {
+  int h = 1;
+  for (int r : v->rates) h *= r;
+  return h;
+}
+}  // namespace vx
