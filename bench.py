@@ -250,6 +250,32 @@ def run_kernel_only():
     return 0
 
 
+def run_cfm_only():
+    """Small profiling case: the LocDiT CFM solve (8 layers, hidden 1024, CFG 2.0, 10 uniform
+    Euler steps, B=1) run twice (the first call captures the solve graph)."""
+    import numpy as np
+    import torch
+    from __graft_entry__ import load_package
+    load_package()
+    from voxcpm_rs_b200 import config, synth
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    from voxcpm_rs_b200.minicpm4 import Context
+    ctx = Context(0)
+    dcfg = config.locdit_config(lm_config())
+    dit = VoxCpmLocDiTV2(ctx, dcfg, synth.locdit_weights(dcfg, in_channels=64, seed=0))
+    rng = np.random.default_rng(0)
+    mu = torch.from_numpy(rng.standard_normal((1, 2048), dtype=np.float32)).cuda()
+    cond = torch.zeros(1, 64, 4, device="cuda")
+    z = torch.from_numpy(rng.standard_normal((1, 64, 4), dtype=np.float32)).cuda()
+    for _ in range(2):
+        t0 = time.perf_counter()
+        dit.cfm_forward(mu, 10, cond, z, 2.0, 0.0, False)
+        print(json.dumps({"cfm_solve_ms": (time.perf_counter() - t0) * 1e3}))
+    dit.close()
+    ctx.close()
+    return 0
+
+
 # ------------------------------------------------------------------ our arm
 def main():
     ap = argparse.ArgumentParser()
@@ -261,11 +287,15 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=6)
     ap.add_argument("--kernel-only", action="store_true",
                     help="profiling case: only the gate|up GEMV over 4 distinct 50 MB weights")
+    ap.add_argument("--cfm-only", action="store_true",
+                    help="profiling case: two CFM solves of the LocDiT workload (B=1, 10 Euler steps)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
     if args.kernel_only:
         return run_kernel_only()
+    if args.cfm_only:
+        return run_cfm_only()
     args.warmup = max(3, args.warmup)
 
     import numpy as np

@@ -176,37 +176,56 @@ cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pd
 
 template <int D>
 __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnPrefillArgs a) {
+  // The 8 query rows of a CTA share one (batch, head) and so one KV head: 32-position K/V
+  // tiles are staged in shared memory once per CTA (coalesced) and every warp reads them there.
   constexpr int DPL = D / 32;
+  __shared__ __align__(16) float ks[ATT_TILE][D];
+  __shared__ __align__(16) float vs[ATT_TILE][D];
   pdl_wait();
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int i = blockIdx.x * 8 + warp;  // query row
   const int h = blockIdx.y, b = blockIdx.z;
-  if (i >= a.S) return;
+  const bool active = i < a.S;
   const int g = h / (a.nh / a.nkv);  // repeat_kv head map (attention.rs:196-204)
-  const float* qrow = a.q + ((size_t)b * a.S + i) * a.nh * D + h * D;
   float qr[DPL], o[DPL];
 #pragma unroll
   for (int e = 0; e < DPL; ++e) {
-    qr[e] = qrow[lane * DPL + e];
+    qr[e] = active ? a.q[((size_t)b * a.S + i) * a.nh * D + h * D + lane * DPL + e] : 0.f;
     o[e] = 0.f;
   }
   float m = -INFINITY, l = 0.f;
   const float* kb = a.k + ((size_t)(b * a.nkv + g) * a.s_max) * D;
   const float* vb = a.v + ((size_t)(b * a.nkv + g) * a.s_max) * D;
-  const int jn = a.causal ? (i + 1) : a.S;  // causal mask: j > i -> -inf (attention.rs:168-182)
-  for (int j = 0; j < jn; ++j) {
-    float s = 0.f;
+  // keys this CTA needs: all S (non-causal) or up to its last query row (causal mask j > i)
+  const int last_row = min(a.S, (int)blockIdx.x * 8 + 8);
+  const int jmax = a.causal ? last_row : a.S;
+  const int jn = a.causal ? (i + 1) : a.S;  // this warp's keys (attention.rs:168-182)
+  for (int t0 = 0; t0 < jmax; t0 += ATT_TILE) {
+    const int nt = min(ATT_TILE, jmax - t0);
+    __syncthreads();
+    for (int c = threadIdx.x; c < nt * (D / 4); c += 256) {
+      const int row = c / (D / 4), ch = c % (D / 4);
+      *reinterpret_cast<float4*>(&ks[row][ch * 4]) = __ldg(reinterpret_cast<const float4*>(kb + (size_t)(t0 + row) * D) + ch);
+      *reinterpret_cast<float4*>(&vs[row][ch * 4]) = __ldg(reinterpret_cast<const float4*>(vb + (size_t)(t0 + row) * D) + ch);
+    }
+    __syncthreads();
+    if (!active) continue;
+    const int jend = min(nt, jn - t0);
+    for (int jj = 0; jj < jend; ++jj) {
+      float s = 0.f;
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) s = fmaf(qr[e], kb[(size_t)j * D + lane * DPL + e], s);
-    s = warp_sum(s) * a.scale;
-    const float mn = fmaxf(m, s);
-    const float alpha = expf(m - mn), p = expf(s - mn);
-    l = l * alpha + p;
+      for (int e = 0; e < DPL; ++e) s = fmaf(qr[e], ks[jj][lane * DPL + e], s);
+      s = warp_sum(s) * a.scale;
+      const float mn = fmaxf(m, s);
+      const float alpha = expf(m - mn), p = expf(s - mn);
+      l = l * alpha + p;
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) o[e] = fmaf(p, vb[(size_t)j * D + lane * DPL + e], o[e] * alpha);
-    m = mn;
+      for (int e = 0; e < DPL; ++e) o[e] = fmaf(p, vs[jj][lane * DPL + e], o[e] * alpha);
+      m = mn;
+    }
   }
+  if (!active) return;
   float* orow = a.out + ((size_t)b * a.S + i) * a.nh * D + h * D;
 #pragma unroll
   for (int e = 0; e < DPL; ++e) orow[lane * DPL + e] = o[e] / l;

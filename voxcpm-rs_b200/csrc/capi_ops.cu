@@ -22,6 +22,57 @@ void* ctx_scratch(vx_ctx* ctx, size_t bytes) {
   return ctx->scratch.ptr;
 }
 
+int workspace_init(vx_ctx* ctx, LinearWorkspace* ws, int max_n, int max_k) {
+  ws->bytes = tc_gemm_scratch_bytes(128, max_n, max_k, ctx->gemv_ctas);
+  if (cudaMalloc(&ws->scratch, ws->bytes) != cudaSuccess || cudaMalloc(&ws->counters, 1024 * 4) != cudaSuccess ||
+      cudaMemset(ws->counters, 0, 1024 * 4) != cudaSuccess) {
+    cudaGetLastError();
+    workspace_free(ws);
+    return fail(ctx, VX_ERR_OOM, "linear workspace allocation failed");
+  }
+  return VX_OK;
+}
+
+void workspace_free(LinearWorkspace* ws) {
+  if (ws->scratch) cudaFree(ws->scratch);
+  if (ws->counters) cudaFree(ws->counters);
+  ws->scratch = nullptr;
+  ws->counters = nullptr;
+  ws->bytes = 0;
+}
+
+int linear(vx_ctx* ctx, const LinearWorkspace* ws, const float* X, int ldx, int M, int N, int K, const uint16_t* W,
+           const float* bias, const float* R, float res_scale, float* Y, int ldy, cudaStream_t st) {
+  if (M == 1 && N % 8 == 0 && gemv_pick_kc(K) != 0 && ((uintptr_t)X & 15) == 0) {
+    GemvArgs a = {};
+    a.W = W;
+    a.N = N;
+    a.K = K;
+    a.x = X;
+    a.y = Y;
+    a.bias = bias;
+    a.residual = R;
+    a.res_scale = R ? res_scale : 1.f;
+    a.groups_per_cta = pick_groups(N / 8, ctx->gemv_ctas);
+    VX_CUDA(ctx, launch_gemv(a, EPI_STORE, st, false, ctx->dev_err));
+    return VX_OK;
+  }
+  if (ctx->tc_gemm && ws && ws->scratch && tc_gemm_supported(std::min(M, 128), N, K) &&
+      tc_gemm_scratch_bytes(std::min(M, 128), N, K, ctx->gemv_ctas) <= ws->bytes) {
+    for (int m0 = 0; m0 < M; m0 += 128) {
+      const int mm = std::min(128, M - m0);
+      VX_CUDA(ctx, launch_tc_gemm(X + (size_t)m0 * ldx, ldx, mm, N, K, W, bias, R ? R + (size_t)m0 * ldy : nullptr,
+                                  res_scale, Y + (size_t)m0 * ldy, ldy, ws->scratch, ws->counters, ctx->dev_err, st,
+                                  ctx->gemv_ctas));
+    }
+    return VX_OK;
+  }
+  if (K % 64 != 0) return fail(ctx, VX_ERR_SHAPE, "linear: K must be a multiple of 64 (got %d)", K);
+  GemmArgs g = {X, ldx, W, bias, R, res_scale, Y, ldy, M, N, K};
+  VX_CUDA(ctx, launch_gemm_smallm(g, st));
+  return VX_OK;
+}
+
 int fill_rope_params(const vx_minicpm4_config& c, RopeParams* rp, std::string* err) {
   // MiniCpmLongRope::new (src/minicpm4/rope.rs:16-32), all in f64
   const int d = c.kv_channels > 0 ? c.kv_channels : c.hidden_size / c.num_attention_heads;
@@ -72,12 +123,13 @@ int vx_ctx_create(int device, vx_ctx** out) {
   if (const char* s = getenv("VX_GEMV_CTAS")) ctx->gemv_ctas = std::max(1, atoi(s));
   if (const char* s = getenv("VX_PDL")) ctx->pdl = atoi(s) != 0;
   if (const char* s = getenv("VX_L2_PREFETCH")) ctx->l2_prefetch = atoi(s) != 0;
+  if (const char* s = getenv("VX_TC_GEMM")) ctx->tc_gemm = atoi(s) != 0;
   if (cudaSetDevice(device) != cudaSuccess ||
       cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&ctx->counters, 4096 * sizeof(unsigned)) != cudaSuccess ||
       cudaMemset(ctx->counters, 0, 4096 * sizeof(unsigned)) != cudaSuccess ||
       cudaMalloc(&ctx->dev_err, 64) != cudaSuccess || cudaMemset(ctx->dev_err, 0, 64) != cudaSuccess ||
-      gemv_configure() != cudaSuccess) {
+      gemv_configure() != cudaSuccess || tc_gemm_configure() != cudaSuccess) {
     cudaGetLastError();
     delete ctx;
     return VX_ERR_CUDA;
@@ -184,23 +236,14 @@ int vx_linear_bf16(vx_ctx* ctx, const uint16_t* w, const float* bias, const floa
   if (M <= 0 || N <= 0 || K <= 0) return fail(ctx, VX_ERR_SHAPE, "linear: empty shape");
   cudaSetDevice(ctx->device);
   cudaStream_t st = pick_stream(ctx, stream);
-  if (M == 1 && N % 8 == 0 && gemv_pick_kc(K) != 0) {
-    GemvArgs a = {};
-    a.W = w;
-    a.N = N;
-    a.K = K;
-    a.x = x;
-    a.y = y;
-    a.bias = bias;
-    a.res_scale = 1.f;
-    a.groups_per_cta = pick_groups(N / 8);
-    VX_CUDA(ctx, launch_gemv(a, EPI_STORE, st, false, ctx->dev_err));
-    return VX_OK;
+  LinearWorkspace ws;
+  if (M > 1 && ctx->tc_gemm && tc_gemm_supported(std::min(M, 128), N, K)) {
+    ws.bytes = tc_gemm_scratch_bytes(std::min(M, 128), N, K, ctx->gemv_ctas);
+    ws.scratch = ctx_scratch(ctx, ws.bytes);
+    if (!ws.scratch) return fail(ctx, VX_ERR_OOM, "linear: scratch allocation failed");
+    ws.counters = ctx->counters;
   }
-  if (K % 64 != 0) return fail(ctx, VX_ERR_SHAPE, "linear: K must be a multiple of 64 (got %d)", K);
-  GemmArgs g = {x, K, w, bias, nullptr, 1.f, y, N, M, N, K};
-  VX_CUDA(ctx, launch_gemm_smallm(g, st));
-  return VX_OK;
+  return linear(ctx, &ws, x, K, M, N, K, w, bias, nullptr, 1.f, y, N, st);
 }
 
 int vx_attention_decode(vx_ctx* ctx, const float* q, const float* kcache, const float* vcache, int B, int nh,

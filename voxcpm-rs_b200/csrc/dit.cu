@@ -24,17 +24,26 @@ namespace {
 __global__ void chan_proj_kernel(const float* __restrict__ src, int Ns, int C, int T, const uint16_t* __restrict__ W,
                                  const float* __restrict__ b, int H, float* __restrict__ dst, int S, int row_off,
                                  int copies) {
+  // grid (Ns*T, ceil(H/256)): one output channel h per thread; the W row is read in 16-byte
+  // chunks (C % 8 == 0), the input column (n, :, t) is staged in shared memory
   extern __shared__ float xs[];  // [C] column of one (n, t)
   const int n = blockIdx.x / T, t = blockIdx.x % T;
   for (int c = threadIdx.x; c < C; c += blockDim.x) xs[c] = src[((size_t)n * C + c) * T + t];
   __syncthreads();
-  for (int h = threadIdx.x; h < H; h += blockDim.x) {
-    const uint16_t* w = W + (size_t)h * C;
-    float acc = 0.f;
-    for (int c = 0; c < C; ++c) acc = fmaf(__uint_as_float(((uint32_t)w[c]) << 16), xs[c], acc);
-    const float v = acc + b[h];
-    for (int k = 0; k < copies; ++k) dst[((size_t)(n + k * Ns) * S + row_off + t) * H + h] = v;
-  }
+  const int h = blockIdx.y * blockDim.x + threadIdx.x;
+  if (h >= H) return;
+  const uint4* w = reinterpret_cast<const uint4*>(W + (size_t)h * C);
+  float acc = 0.f;
+  for (int c8 = 0; c8 < C / 8; ++c8) acc = dot8(__ldg(w + c8), xs + c8 * 8, acc);
+  const float v = acc + b[h];
+  for (int k = 0; k < copies; ++k) dst[((size_t)(n + k * Ns) * S + row_off + t) * H + h] = v;
+}
+
+void launch_chan_proj(const float* src, int Ns, int C, int T, const uint16_t* W, const float* b, int H, float* dst,
+                      int S, int row_off, int copies, cudaStream_t st) {
+  count_launch();
+  chan_proj_kernel<<<dim3(Ns * T, (H + 255) / 256), 256, C * sizeof(float), st>>>(src, Ns, C, T, W, b, H, dst, S,
+                                                                                  row_off, copies);
 }
 
 // out[n, c, t] = b[c] + sum_h W[c, h] * hid[n, skip + t, h]   (out_proj + swap_dims, local_dit.rs:155-158)
@@ -85,6 +94,17 @@ __global__ void seq_head_kernel(const float* __restrict__ mu, int mu_tokens, con
   }
 }
 
+// Everything a captured CFM solve graph depends on besides the (fixed) buffers.
+struct CfmKey {
+  int B, C_mu, T, Tc, steps;
+  float cfg, sway;
+  int zero_star;
+  bool operator==(const CfmKey& o) const {
+    return B == o.B && C_mu == o.C_mu && T == o.T && Tc == o.Tc && steps == o.steps && cfg == o.cfg &&
+           sway == o.sway && zero_star == o.zero_star;
+  }
+};
+
 }  // namespace
 
 struct vx_dit {
@@ -102,6 +122,14 @@ struct vx_dit {
   int cap_rows = 0, cap_S = 0;
   float *seq = nullptr, *hid = nullptr, *temb = nullptr, *dtemb = nullptr, *tmp = nullptr, *tvals = nullptr,
         *out2b = nullptr, *mu_in = nullptr, *cond_in = nullptr;
+  // CFM solve: staged x, the per-step time schedule, and the captured solve graph
+  float* xw = nullptr;
+  size_t xw_cap = 0;
+  float* tsched = nullptr;
+  int tsched_cap = 0;
+  cudaGraphExec_t solve_exec = nullptr;
+  CfmKey solve_key{};
+  unsigned long long solve_kernels = 0;
 };
 
 namespace {
@@ -146,13 +174,14 @@ int launch_time_mlp(vx_dit* d, const uint16_t* w1, const float* b1, const uint16
   sinusoidal_kernel<<<std::max(1, (rows * half + 255) / 256), 256, 0, st>>>(tvals, rows, 1000.0f, d->freqs, half,
                                                                               d->tmp);
   VX_CUDA(ctx, cudaGetLastError());
-  GemmArgs g1 = {d->tmp, H, w1, b1, nullptr, 1.f, out, H, rows, H, H};
-  VX_CUDA(ctx, launch_gemm_smallm(g1, st));
+  const LinearWorkspace* ws = lm_workspace(d->dec);
+  int rc = linear(ctx, ws, d->tmp, H, rows, H, H, w1, b1, nullptr, 1.f, out, H, st);
+  if (rc) return rc;
   count_launch();
   silu_inplace_kernel<<<std::max(1, (rows * H + 255) / 256), 256, 0, st>>>(out, (size_t)rows * H);
   VX_CUDA(ctx, cudaGetLastError());
-  GemmArgs g2 = {out, H, w2, b2, nullptr, 1.f, d->tmp, H, rows, H, H};
-  VX_CUDA(ctx, launch_gemm_smallm(g2, st));
+  rc = linear(ctx, ws, out, H, rows, H, H, w2, b2, nullptr, 1.f, d->tmp, H, st);
+  if (rc) return rc;
   VX_CUDA(ctx, cudaMemcpyAsync(out, d->tmp, (size_t)rows * H * 4, cudaMemcpyDeviceToDevice, st));
   return VX_OK;
 }
@@ -164,8 +193,7 @@ int dit_forward_prepared(vx_dit* d, const float* x, int Nx, int copies, int N, i
                          cudaStream_t st) {
   vx_ctx* ctx = d->ctx;
   const int H = d->H, C = d->C;
-  count_launch();
-  chan_proj_kernel<<<Nx * T, 256, C * sizeof(float), st>>>(x, Nx, C, T, d->in_w, d->in_b, H, d->seq, S, skip, copies);
+  launch_chan_proj(x, Nx, C, T, d->in_w, d->in_b, H, d->seq, S, skip, copies, st);
   VX_CUDA(ctx, cudaGetLastError());
   int rc = vx_lm_forward(d->dec, d->seq, N, S, 0, 0, d->hid);
   if (rc) return rc;
@@ -173,6 +201,78 @@ int dit_forward_prepared(vx_dit* d, const float* x, int Nx, int copies, int N, i
   count_launch();
   out_proj_kernel<<<(warps * 32 + 255) / 256, 256, 0, st>>>(d->hid, N, S, skip, T, H, d->out_w, d->out_b, C, out);
   VX_CUDA(ctx, cudaGetLastError());
+  return VX_OK;
+}
+
+// Capture UnifiedCfm::solve_euler (unified_cfm.rs:72-163) for one shape / schedule as a CUDA
+// graph over the staged buffers (mu_in, cond_in, xw).  The time grid (unified_cfm.rs:59-67,
+// f64 arithmetic, f32 storage) is computed here and uploaded before the capture; skipped
+// zero-star steps (dphi = 0, so x - 0*dt == x) are simply not recorded.
+int build_solve_graph(vx_dit* d, const CfmKey& k) {
+  vx_ctx* ctx = d->ctx;
+  cudaStream_t st = ctx->stream;
+  const int H = d->H, C = d->C, B = k.B, N = 2 * B;
+  const int mu_tokens = k.C_mu / H, skip = k.Tc + mu_tokens + 1, S = skip + k.T;
+  const int n = k.steps + 1;
+  std::vector<float> ts(n);
+  const double stepw = 1.0 / (double)k.steps;
+  for (int i = 0; i < n; ++i) {
+    const double tt = (double)(float)(1.0 - (double)i * stepw);
+    ts[i] = (float)(tt + (double)k.sway * (std::cos(M_PI / 2.0 * tt) - 1.0 + tt));
+  }
+  double t = ts[0];
+  double dt = (double)(ts[0] - ts[1]);
+  const int zero_init_steps = (int)std::max((double)n * 0.04, 1.0);
+  std::vector<float> tt(n, 0.f);  // tt[0] = 0: the delta-time embedding (non-mean mode, dt = 0)
+  std::vector<double> dts(n, 0.0);
+  std::vector<char> run(n, 0);
+  for (int step = 1; step < n; ++step) {
+    run[step] = !(k.zero_star && step <= zero_init_steps);
+    tt[step] = (float)t;
+    dts[step] = dt;
+    t -= dt;
+    if (step < n - 1) dt = t - (double)ts[step + 1];
+  }
+  VX_CUDA(ctx, cudaMemcpy(d->tsched, tt.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+
+  const unsigned long long before = g_launches;
+  cudaGraph_t g = nullptr;
+  VX_CUDA(ctx, cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  int rc = VX_OK;
+  do {
+    launch_chan_proj(d->cond_in, B, C, k.Tc, d->cond_w, d->cond_b, H, d->seq, S, mu_tokens + 1, 2, st);
+    if (cudaGetLastError() != cudaSuccess) {
+      rc = fail(ctx, VX_ERR_CUDA, "cfm graph: cond projection launch failed");
+      break;
+    }
+    rc = launch_time_mlp(d, d->dt1_w, d->dt1_b, d->dt2_w, d->dt2_b, d->tsched, 1, d->dtemb, st);
+    for (int step = 1; step < n && !rc; ++step) {
+      if (!run[step]) continue;
+      rc = launch_time_mlp(d, d->t1_w, d->t1_b, d->t2_w, d->t2_b, d->tsched + step, 1, d->temb, st);
+      if (rc) break;
+      count_launch();
+      seq_head_kernel<<<N, 256, 0, st>>>(d->mu_in, mu_tokens, d->temb, 1, d->dtemb, 1, N, S, H, d->seq);
+      if (cudaGetLastError() != cudaSuccess) {
+        rc = fail(ctx, VX_ERR_CUDA, "cfm graph: sequence assembly launch failed");
+        break;
+      }
+      rc = dit_forward_prepared(d, d->xw, B, 2, N, S, skip, k.T, d->out2b, st);
+      if (rc) break;
+      if (launch_cfg_euler(d->out2b, d->xw, B, C * k.T, (double)k.cfg, dts[step], k.zero_star, st) != cudaSuccess)
+        rc = fail(ctx, VX_ERR_CUDA, "cfm graph: CFG/Euler launch failed");
+    }
+  } while (0);
+  const cudaError_t e = cudaStreamEndCapture(st, &g);
+  d->solve_kernels = g_launches - before;  // captured, not launched
+  g_launches = before;
+  if (rc || e != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return rc ? rc : cuda_fail(ctx, e, "cudaStreamEndCapture (cfm solve)");
+  }
+  const cudaError_t ei = cudaGraphInstantiate(&d->solve_exec, g, 0);
+  cudaGraphDestroy(g);
+  if (ei != cudaSuccess) return cuda_fail(ctx, ei, "cudaGraphInstantiate (cfm solve)");
+  d->solve_key = k;
   return VX_OK;
 }
 
@@ -185,6 +285,7 @@ int vx_dit_create(vx_ctx* ctx, const vx_minicpm4_config* cfg, int in_channels, i
   *out = nullptr;
   if (cfg->vocab_size != 0) return fail(ctx, VX_ERR_CONFIG, "vocab_size must be 0 for local DiT");
   if (cfg->hidden_size % 2) return fail(ctx, VX_ERR_CONFIG, "SinusoidalPosEmb requires even dim");
+  if (in_channels % 8) return fail(ctx, VX_ERR_CONFIG, "in_channels must be a multiple of 8");
   vx_dit* d = new vx_dit();
   d->ctx = ctx;
   d->H = cfg->hidden_size;
@@ -227,10 +328,11 @@ void vx_dit_destroy(vx_dit* d) {
   if (!d) return;
   cudaSetDevice(d->ctx->device);
   cudaStreamSynchronize(d->ctx->stream);
+  if (d->solve_exec) cudaGraphExecDestroy(d->solve_exec);
   if (d->dec) vx_lm_destroy(d->dec);
   void* ptrs[] = {d->in_w, d->cond_w, d->out_w, d->t1_w, d->t2_w, d->dt1_w, d->dt2_w, d->in_b, d->cond_b,
                   d->out_b, d->t1_b, d->t2_b, d->dt1_b, d->dt2_b, d->freqs, d->seq, d->hid, d->temb,
-                  d->dtemb, d->tmp, d->tvals, d->out2b, d->mu_in, d->cond_in};
+                  d->dtemb, d->tmp, d->tvals, d->out2b, d->mu_in, d->cond_in, d->xw, d->tsched};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   delete d;
@@ -286,9 +388,7 @@ int vx_dit_forward(vx_dit* d, const float* x, const float* mu, const float* t, c
   int rc = dit_buffers(d, N, S, C, T, Tc, C_mu);
   if (rc) return rc;
   // prepare (local_dit.rs:116-134): cond_proj, delta-time MLP(dt)
-  count_launch();
-  chan_proj_kernel<<<N * Tc, 256, C * sizeof(float), st>>>(cond, N, C, Tc, d->cond_w, d->cond_b, H, d->seq, S,
-                                                           mu_tokens + 1, 1);
+  launch_chan_proj(cond, N, C, Tc, d->cond_w, d->cond_b, H, d->seq, S, mu_tokens + 1, 1, st);
   VX_CUDA(ctx, cudaGetLastError());
   VX_CUDA(ctx, cudaMemcpyAsync(d->tvals, dt, (size_t)N * 4, cudaMemcpyDefault, st));
   rc = launch_time_mlp(d, d->dt1_w, d->dt1_b, d->dt2_w, d->dt2_b, d->tvals, N, d->dtemb, st);
@@ -314,54 +414,43 @@ int vx_cfm_solve(vx_dit* d, const float* mu, const float* cond, const float* z, 
                 C_mu, n_timesteps);
   const int mu_tokens = C_mu / H, skip = Tc + mu_tokens + 1, S = skip + T;
   if (S > 64) return fail(ctx, VX_ERR_SHAPE, "cfm_solve: sequence %d > 64", S);
+  if (ctx->cancel.load(std::memory_order_relaxed)) return fail(ctx, VX_ERR_CANCELLED, "generation cancelled");
   cudaSetDevice(ctx->device);
   cudaStream_t st = ctx->stream;
+  // every allocation happens here, outside any capture
   int rc = dit_buffers(d, N, S, C, T, Tc, C_mu);
   if (rc) return rc;
-
-  // t-span with sway (unified_cfm.rs:59-67): t_i = f32(1 - i/n), sway in f64, stored as f32
-  const int n = n_timesteps + 1;
-  std::vector<float> ts(n);
-  const double stepw = 1.0 / (double)n_timesteps;
-  for (int i = 0; i < n; ++i) {
-    const double tt = (double)(float)(1.0 - (double)i * stepw);
-    ts[i] = (float)(tt + (double)sway_sampling_coef * (std::cos(M_PI / 2.0 * tt) - 1.0 + tt));
+  rc = lm_prepare_rows(d->dec, (size_t)N * S);
+  if (rc) return rc;
+  if (!d->xw || d->xw_cap < (size_t)B * C * T) {
+    if (d->xw) cudaFree(d->xw);
+    d->xw = nullptr;
+    d->xw_cap = 0;
+    VX_CUDA(ctx, cudaMalloc(&d->xw, (size_t)B * C * T * 4));
+    d->xw_cap = (size_t)B * C * T;
   }
-  // solve_euler (unified_cfm.rs:72-163)
-  double t = ts[0];
-  double dt = (double)(ts[0] - ts[1]);
-  const int zero_init_steps = (int)std::max((double)n * 0.04, 1.0);
-  // mu_in = [mu; 0], cond_in = [cond; cond] (unified_cfm.rs:96-98); prepare once with dt = 0
+  if (!d->tsched || d->tsched_cap < n_timesteps + 2) {
+    if (d->tsched) cudaFree(d->tsched);
+    d->tsched = nullptr;
+    VX_CUDA(ctx, cudaMalloc(&d->tsched, (size_t)(n_timesteps + 2) * 4));
+    d->tsched_cap = n_timesteps + 2;
+  }
+  // inputs staged into fixed buffers so one captured graph serves every call with this shape:
+  // mu_in = [mu; 0], cond_in = [cond; cond] (unified_cfm.rs:96-98), x = z
   VX_CUDA(ctx, cudaMemcpyAsync(d->mu_in, mu, (size_t)B * C_mu * 4, cudaMemcpyDefault, st));
   VX_CUDA(ctx, cudaMemsetAsync(d->mu_in + (size_t)B * C_mu, 0, (size_t)B * C_mu * 4, st));
   VX_CUDA(ctx, cudaMemcpyAsync(d->cond_in, cond, (size_t)B * C * Tc * 4, cudaMemcpyDefault, st));
-  count_launch();
-  chan_proj_kernel<<<B * Tc, 256, C * sizeof(float), st>>>(d->cond_in, B, C, Tc, d->cond_w, d->cond_b, H, d->seq, S,
-                                                           mu_tokens + 1, 2);
-  VX_CUDA(ctx, cudaGetLastError());
-  VX_CUDA(ctx, cudaMemsetAsync(d->tvals, 0, 4, st));
-  rc = launch_time_mlp(d, d->dt1_w, d->dt1_b, d->dt2_w, d->dt2_b, d->tvals, 1, d->dtemb, st);
-  if (rc) return rc;
-  VX_CUDA(ctx, cudaMemcpyAsync(x_out, z, (size_t)B * C * T * 4, cudaMemcpyDefault, st));
-  std::vector<float> tf(n);
-  for (int step = 1; step < n; ++step) {
-    if (ctx->cancel.load(std::memory_order_relaxed)) return fail(ctx, VX_ERR_CANCELLED, "generation cancelled");
-    if (!(use_cfg_zero_star && step <= zero_init_steps)) {
-      tf[step] = (float)t;
-      VX_CUDA(ctx, cudaMemcpyAsync(d->tvals + 1, &tf[step], 4, cudaMemcpyHostToDevice, st));
-      rc = launch_time_mlp(d, d->t1_w, d->t1_b, d->t2_w, d->t2_b, d->tvals + 1, 1, d->temb, st);
-      if (rc) return rc;
-      count_launch();
-      seq_head_kernel<<<N, 256, 0, st>>>(d->mu_in, mu_tokens, d->temb, 1, d->dtemb, 1, N, S, H, d->seq);
-      VX_CUDA(ctx, cudaGetLastError());
-      rc = dit_forward_prepared(d, x_out, B, 2, N, S, skip, T, d->out2b, st);
-      if (rc) return rc;
-      VX_CUDA(ctx, launch_cfg_euler(d->out2b, x_out, B, C * T, (double)cfg_value, dt, use_cfg_zero_star, st));
-    }
-    // else: dphi_dt = 0, x - 0*dt == x
-    t -= dt;
-    if (step < n - 1) dt = t - (double)ts[step + 1];
+  VX_CUDA(ctx, cudaMemcpyAsync(d->xw, z, (size_t)B * C * T * 4, cudaMemcpyDefault, st));
+  const CfmKey key = {B, C_mu, T, Tc, n_timesteps, cfg_value, sway_sampling_coef, use_cfg_zero_star};
+  if (!d->solve_exec || !(key == d->solve_key)) {
+    if (d->solve_exec) cudaGraphExecDestroy(d->solve_exec);
+    d->solve_exec = nullptr;
+    rc = build_solve_graph(d, key);
+    if (rc) return rc;
   }
+  VX_CUDA(ctx, cudaGraphLaunch(d->solve_exec, st));
+  count_launch(d->solve_kernels);
+  VX_CUDA(ctx, cudaMemcpyAsync(x_out, d->xw, (size_t)B * C * T * 4, cudaMemcpyDefault, st));
   return vx_ctx_synchronize(ctx);
 }
 

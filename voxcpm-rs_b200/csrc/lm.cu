@@ -72,6 +72,7 @@ struct vx_lm {
 
   cudaGraphExec_t step_exec = nullptr;
   unsigned long long step_kernels = 0;
+  LinearWorkspace ws;  // tcgen05 few-row GEMM workspace (prefill, non-causal forward)
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
   float t_prefill_ms = 0.f, t_decode_ms = 0.f;
   int pos_host = 0;
@@ -361,6 +362,9 @@ int vx_lm_create(vx_ctx* ctx, const vx_minicpm4_config* cfg, int max_batch, int 
     cudaGetLastError();
     return fail_free(VX_ERR_OOM, "model buffer allocation failed");
   }
+  if (workspace_init(ctx, &lm->ws, std::max({lm->qs + 2 * lm->ks, 2 * lm->I, lm->H}),
+                     std::max({lm->H, lm->I, lm->qs})) != VX_OK)
+    return fail_free(VX_ERR_OOM, "linear workspace allocation failed");
   *out = lm;
   return VX_OK;
 }
@@ -373,6 +377,7 @@ void vx_lm_destroy(vx_lm* lm) {
   for (auto& e : lm->ev)
     if (e) cudaEventDestroy(e);
   free_prefill(lm);
+  workspace_free(&lm->ws);
   void* ptrs[] = {lm->weight_slab, lm->norm_w, lm->embed, lm->rope, lm->kcache, lm->vcache, lm->d_pos,
                   lm->d_step, lm->d_tokens, lm->x, lm->hid_norm, lm->q, lm->attn, lm->act, lm->logits,
                   lm->attn_partials,
@@ -496,8 +501,8 @@ int vx_lm_forward(vx_lm* lm, const float* embeds, int B, int S, int causal, int 
     const int s_max = fill_cache ? lm->max_length : S;
     VX_CUDA(ctx, launch_rmsnorm_residual(lm->pf_x, nullptr, w.ln_in, 1.f, lm->cfg.rms_norm_eps, (int)M, H, nullptr,
                                          lm->pf_xn, st));
-    GemmArgs g1 = {lm->pf_xn, H, w.wqkv, nullptr, nullptr, 1.f, lm->pf_qkv, qkvw, (int)M, qkvw, H};
-    VX_CUDA(ctx, launch_gemm_smallm(g1, st));
+    rc = linear(ctx, &lm->ws, lm->pf_xn, H, (int)M, qkvw, H, w.wqkv, nullptr, nullptr, 1.f, lm->pf_qkv, qkvw, st);
+    if (rc) return rc;
     if (fill_cache) {
       for (int b = 0; b < B; ++b)
         VX_CUDA(ctx, launch_rope_scatter(lm->pf_qkv + (size_t)b * S * qkvw, 1, S, lm->nh, lm->nkv, lm->d, lm->rope, 0,
@@ -516,15 +521,16 @@ int vx_lm_forward(vx_lm* lm, const float* embeds, int B, int S, int causal, int 
       AttnPrefillArgs ap = {lm->pf_q, kd, vd, B, S, lm->nh, lm->nkv, lm->d, s_max, lm->attn_scale, causal, lm->pf_attn};
       VX_CUDA(ctx, launch_attn_prefill(ap, st, false));
     }
-    GemmArgs g2 = {lm->pf_attn, lm->qs, w.wo, nullptr, lm->pf_x, lm->res_scale, lm->pf_x, H, (int)M, H, lm->qs};
-    VX_CUDA(ctx, launch_gemm_smallm(g2, st));
+    rc = linear(ctx, &lm->ws, lm->pf_attn, lm->qs, (int)M, H, lm->qs, w.wo, nullptr, lm->pf_x, lm->res_scale, lm->pf_x,
+                H, st);
+    if (rc) return rc;
     VX_CUDA(ctx, launch_rmsnorm_residual(lm->pf_x, nullptr, w.ln_post, 1.f, lm->cfg.rms_norm_eps, (int)M, H, nullptr,
                                          lm->pf_xn, st));
-    GemmArgs g3 = {lm->pf_xn, H, w.wgu, nullptr, nullptr, 1.f, lm->pf_gu, 2 * I, (int)M, 2 * I, H};
-    VX_CUDA(ctx, launch_gemm_smallm(g3, st));
+    rc = linear(ctx, &lm->ws, lm->pf_xn, H, (int)M, 2 * I, H, w.wgu, nullptr, nullptr, 1.f, lm->pf_gu, 2 * I, st);
+    if (rc) return rc;
     VX_CUDA(ctx, launch_silu_mul(lm->pf_gu, (int)M, I, lm->pf_act, st));
-    GemmArgs g4 = {lm->pf_act, I, w.wd, nullptr, lm->pf_x, lm->res_scale, lm->pf_x, H, (int)M, H, I};
-    VX_CUDA(ctx, launch_gemm_smallm(g4, st));
+    rc = linear(ctx, &lm->ws, lm->pf_act, I, (int)M, H, I, w.wd, nullptr, lm->pf_x, lm->res_scale, lm->pf_x, H, st);
+    if (rc) return rc;
   }
   VX_CUDA(ctx, launch_rmsnorm_residual(lm->pf_x, nullptr, lm->norm_w, 1.f, lm->cfg.rms_norm_eps, (int)M, H, nullptr,
                                        hidden_out, st));
@@ -570,6 +576,8 @@ int vx_lm_forward_step(vx_lm* lm, const float* embeds, float* hidden_out) {
 namespace vx {
 
 vx_ctx* lm_ctx(vx_lm* lm) { return lm->ctx; }
+const LinearWorkspace* lm_workspace(const vx_lm* lm) { return &lm->ws; }
+int lm_prepare_rows(vx_lm* lm, size_t rows) { return ensure_prefill(lm, rows, 1, (int)rows, false); }
 int lm_hidden_size(const vx_lm* lm) { return lm->H; }
 const float* lm_hid_norm(const vx_lm* lm) { return lm->hid_norm; }
 

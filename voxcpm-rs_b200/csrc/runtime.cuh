@@ -30,6 +30,11 @@ int gemv_pick_kc(int K);
 cudaError_t launch_attn_decode(const AttnDecodeArgs& a, cudaStream_t st, bool pdl);
 cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t st, bool pdl);
 cudaError_t launch_gemm_smallm(const GemmArgs& a, cudaStream_t st);
+bool tc_gemm_supported(int M, int N, int K);
+size_t tc_gemm_scratch_bytes(int M, int N, int K, int target_ctas);
+cudaError_t launch_tc_gemm(const float* X, int ldx, int M, int N, int K, const uint16_t* W, const float* bias,
+                           const float* R, float res_scale, float* Y, int ldy, void* scratch, unsigned* counters,
+                           int* err, cudaStream_t st, int target_ctas);
 cudaError_t launch_rmsnorm_residual(const float* x, const float* r, const float* w, float resid_scale, float eps,
                                     int rows, int hidden, float* h_out, float* y_out, cudaStream_t st);
 cudaError_t launch_rope_scatter(const float* qkv, int B, int S, int nh, int nkv, int d, const RopeParams* rope,
@@ -62,6 +67,7 @@ struct vx_ctx {
   int* dev_err = nullptr;            // device error word written by bounded waits
   bool pdl = true;                   // programmatic dependent launch between decode kernels
   int gemv_ctas = 296;               // target GEMV grid (CTAs); env VX_GEMV_CTAS overrides
+  bool tc_gemm = true;               // tcgen05 path for few-row GEMMs (env VX_TC_GEMM=0: CUDA cores)
   bool l2_prefetch = false;          // decode kernels prefetch the next kernel's weights into L2
                                      // (env VX_L2_PREFETCH=1; measured: no gain with separate kernels)
 };
@@ -102,8 +108,27 @@ inline double residual_scale_of(const vx_minicpm4_config& c) {
 
 int fill_rope_params(const vx_minicpm4_config& c, RopeParams* rp, std::string* err);
 
+// Workspace for linear(): bf16-split activations and split-K partials of the tcgen05 path,
+// plus its zeroed tile counters.  Sized for up to 128 rows, N <= max_n, K <= max_k.
+struct LinearWorkspace {
+  void* scratch = nullptr;
+  size_t bytes = 0;
+  unsigned* counters = nullptr;  // 1024 zeroed words
+};
+int workspace_init(vx_ctx* ctx, LinearWorkspace* ws, int max_n, int max_k);
+void workspace_free(LinearWorkspace* ws);
+
+// burn::nn::Linear for M rows: Y[m, :] = X[m, :] . W^T (+ bias) (or Y = R + s * (...)).
+// M == 1: streamed GEMV; 2..128-row chunks: tcgen05 GEMM; otherwise the CUDA-core GEMM.
+int linear(vx_ctx* ctx, const LinearWorkspace* ws, const float* X, int ldx, int M, int N, int K, const uint16_t* W,
+           const float* bias, const float* R, float res_scale, float* Y, int ldy, cudaStream_t st);
+
 // Greedy LM decoding, split for the synthesis loop (lm.cu).
 vx_ctx* lm_ctx(vx_lm* lm);
+const LinearWorkspace* lm_workspace(const vx_lm* lm);
+// Grow the forward() work buffers to `rows` token rows (so a later capture allocates nothing).
+int lm_prepare_rows(vx_lm* lm, size_t rows);
+cudaError_t tc_gemm_configure();
 int lm_hidden_size(const vx_lm* lm);
 const float* lm_hid_norm(const vx_lm* lm);
 int lm_greedy_begin(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps);

@@ -1,0 +1,378 @@
+// Few-row GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+//   Y[m, n] = sum_k W[n, k] * X[m, k]  (+ bias[n]) (or Y = R + s * (...))   m < M <= 128
+//
+// W is a bf16 weight matrix [N, K] (checkpoint [out, in] layout), X f32 activations.  The
+// weights are the MMA's A operand (M_mma = 128 weight rows per tile) and the activations
+// the B operand ("swap AB": tokens become the MMA N dimension, so 1..128 tokens map onto
+// N = 16..256 without padding the weight side).  For f32-grade accuracy the activations are
+// split exactly into two bf16 halves, X = X_hi + X_lo (X_hi = bf16(X), X_lo = bf16(X - X_hi)),
+// stacked as 2M B-rows; products of bf16 values are exact in the f32 accumulator, so the
+// result carries ~2^-16 relative error per term instead of bf16's 2^-8.  The epilogue adds
+// the hi and lo columns.
+//
+// Pipeline per CTA (one 128-row weight tile x one K split): warp 0 lane 0 issues TMA tile
+// loads (SWIZZLE_128B, 64-element K blocks, no multicast) into a ring of shared-memory
+// stages; warp 1 lane 0 issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32 in TMEM) and
+// releases each stage with tcgen05.commit; after the last block all four warps read the
+// accumulator with tcgen05.ld (warp w owns TMEM lanes 32w..32w+31 = weight rows).  With
+// K split across CTAs, each writes an f32 partial tile to scratch and the last CTA to
+// arrive (atomic counter, no waiting) sums the splits in order (deterministic) and runs
+// the epilogue.  Every mbarrier wait is bounded; on a timeout the CTA records an error,
+// frees its TMEM and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "runtime.cuh"
+
+namespace vx {
+
+constexpr int TC_BM = 128;   // weight rows per tile (MMA M)
+constexpr int TC_BK = 64;    // K elements per TMA box (128 bytes: one SW128 row)
+constexpr int TC_THREADS = 128;
+constexpr int TC_MAX_SPLITS = 8;  // K splits per tile (partials summed by the last CTA)
+
+struct TcGemmArgs {
+  int M, N, K, NB;       // NB = padded B rows (2M rounded up to 16)
+  int splits, kblocks_per_split;
+  const float* bias;     // [N] or null
+  const float* R;        // residual [M, ldy] or null (may alias Y)
+  float res_scale;
+  float* Y;              // [M, ldy]
+  int ldy;
+  float* partials;       // [tiles][splits][M][128]
+  unsigned int* counters;  // [tiles], zero-initialised, reset by the last CTA
+  int* err;
+  int nstages;
+};
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(tm), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// K-major SWIZZLE_128B shared-memory matrix descriptor (tile rows of 128 bytes, 8-row groups
+// 1024 bytes apart): start>>4 | LBO=1 | SBO=64 | version 1 | layout 2.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)64 << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor: D f32, A/B bf16, both K-major, N = nb, M = 128.
+__host__ __device__ constexpr uint32_t tc_idesc(int nb) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(nb >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const TcGemmArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 1024-byte aligned stage buffers: [A tile 16 KB | B tile NB*128 B] per stage
+  unsigned char* base = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int a_bytes = TC_BM * TC_BK * 2;
+  const int b_bytes = a.NB * TC_BK * 2;
+  const int stage_bytes = a_bytes + ((b_bytes + 1023) & ~1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + a.nstages * stage_bytes);
+  uint64_t* empty = full + a.nstages;
+  uint64_t* done = empty + a.nstages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort, [1] last-CTA
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int kb0 = split * a.kblocks_per_split;
+  const int nkb = a.kblocks_per_split;
+  uint32_t ncols = 32;
+  while ((int)ncols < a.NB) ncols <<= 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.nstages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    flags[0] = 0;
+    flags[1] = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {  // TMEM allocation (warp-wide, converged)
+    __syncwarp();
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+  pdl_launch_dependents();
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % a.nstages;
+      if (i >= a.nstages && !mbar_wait(&empty[s], ((i / a.nstages) - 1) & 1, a.err)) {
+        atomicExch(&flags[0], 1);
+        break;
+      }
+      unsigned char* st = base + s * stage_bytes;
+      mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
+      const int kx = (kb0 + i) * TC_BK;
+      tma_load_2d(st, &tmW, kx, tile * TC_BM, &full[s]);
+      tma_load_2d(st + a_bytes, &tmX, kx, 0, &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer
+    const uint32_t idesc = tc_idesc(a.NB);
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % a.nstages;
+      if (!mbar_wait(&full[s], (i / a.nstages) & 1, a.err)) {
+        atomicExch(&flags[0], 1);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sa = smem_u32(base + s * stage_bytes);
+      const uint32_t sb = sa + a_bytes;
+#pragma unroll
+      for (int kk = 0; kk < TC_BK / 16; ++kk)  // 16-element K steps: +32 bytes inside the swizzle row
+        tc_mma(tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, (i > 0 || kk > 0) ? 1 : 0);
+      tc_commit(&empty[s]);
+    }
+    // always: `done` completes once every MMA issued above has finished, so TMEM is never
+    // freed under an in-flight MMA, also on the abort path
+    tc_commit(done);
+  }
+  __syncwarp();
+  // ---- epilogue: all four warps
+  const bool ok = mbar_wait(done, 0, a.err);
+  tc_fence_after();
+  if (!ok) atomicExch(&flags[0], 1);
+  __syncthreads();
+  const int n = tile * TC_BM + warp * 32 + lane;  // this thread's weight row
+  if (!flags[0]) {
+    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    float* part = a.splits > 1 ? a.partials + (((size_t)tile * a.splits + split) * a.M) * TC_BM : nullptr;
+    for (int c0 = 0; c0 < a.M; c0 += 16) {
+      float hi[16], lo[16];
+      tmem_ld16(trow + c0, hi);
+      tmem_ld16(trow + a.M + c0, lo);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int m = c0 + j;
+        if (m >= a.M) break;
+        const float acc = hi[j] + lo[j];
+        if (part) {
+          part[(size_t)m * TC_BM + warp * 32 + lane] = acc;
+        } else if (n < a.N) {
+          float v = acc;
+          if (a.bias) v += a.bias[n];
+          if (a.R) v = a.R[(size_t)m * a.ldy + n] + v * a.res_scale;
+          a.Y[(size_t)m * a.ldy + n] = v;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+  if (flags[0] || a.splits == 1) return;
+  // ---- split-K: the last CTA of this tile sums the partials in split order
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(&a.counters[tile], 1u);
+    flags[1] = (prev == (unsigned)a.splits - 1);
+  }
+  __syncthreads();
+  if (!flags[1]) return;
+  __threadfence();
+  const float* __restrict__ pt = a.partials + ((size_t)tile * a.splits * a.M) * TC_BM + threadIdx.x;
+  const float bn = (a.bias && n < a.N) ? a.bias[n] : 0.f;
+  constexpr int RB = 4;  // rows per batch: RB * splits independent loads in flight
+  for (int m0 = 0; m0 < a.M; m0 += RB) {
+    float v[RB][TC_MAX_SPLITS];
+    float r[RB];
+#pragma unroll
+    for (int i = 0; i < RB; ++i) {
+      const int m = m0 + i;
+#pragma unroll
+      for (int s = 0; s < TC_MAX_SPLITS; ++s)
+        v[i][s] = (m < a.M && s < a.splits) ? __ldcg(pt + ((size_t)s * a.M + m) * TC_BM) : 0.f;
+      r[i] = (a.R && m < a.M && n < a.N) ? a.R[(size_t)m * a.ldy + n] : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < RB; ++i) {
+      const int m = m0 + i;
+      if (m >= a.M || n >= a.N) continue;
+      float acc = 0.f;  // split order: deterministic
+#pragma unroll
+      for (int s = 0; s < TC_MAX_SPLITS; ++s)
+        if (s < a.splits) acc += v[i][s];
+      float y = acc + bn;
+      if (a.R) y = r[i] + y * a.res_scale;
+      a.Y[(size_t)m * a.ldy + n] = y;
+    }
+  }
+  if (threadIdx.x == 0) a.counters[tile] = 0u;
+}
+
+// X [M, K] f32 (row stride ldx) -> Xs [NB, K] bf16: rows 0..M hi, M..2M lo, the rest zero.
+__global__ void split_bf16_kernel(const float* __restrict__ X, int ldx, int M, int K, int NB, uint16_t* __restrict__ Xs) {
+  const size_t total = (size_t)NB * K;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / K), k = (int)(i % K);
+    float v = 0.f;
+    if (r < M) {
+      v = X[(size_t)r * ldx + k];
+    } else if (r < 2 * M) {
+      const float x = X[(size_t)(r - M) * ldx + k];
+      v = x - __bfloat162float(__float2bfloat16_rn(x));
+    }
+    Xs[i] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::mutex g_encode_mu;
+
+cudaError_t get_encoder() {
+  std::lock_guard<std::mutex> lk(g_encode_mu);
+  if (g_encode) return cudaSuccess;
+  cudaDriverEntryPointQueryResult q;
+  void* fn = nullptr;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return cudaSuccess;
+}
+
+cudaError_t make_map(CUtensorMap* m, const void* ptr, int rows, int K, int box_rows) {
+  if (((uintptr_t)ptr & 15) || (K * 2) % 16) return cudaErrorInvalidValue;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+// Raise the dynamic shared-memory limit on the current device; called once per context,
+// before any launch or capture.
+cudaError_t tc_gemm_configure() {
+  cudaError_t e = get_encoder();
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
+
+bool tc_gemm_supported(int M, int N, int K) { return M >= 1 && M <= 128 && N % TC_BM == 0 && K % TC_BK == 0 && K > 0; }
+
+// Scratch needed by launch_tc_gemm for these shapes (bf16 split X, split-K partials): the
+// grid is at most max(target_ctas, N/128) CTAs, each with one [M, 128] partial.
+size_t tc_gemm_scratch_bytes(int M, int N, int K, int target_ctas) {
+  const int NB = ((2 * M + 15) / 16) * 16;
+  const int tiles = N / TC_BM;
+  const size_t xs = ((size_t)NB * K * 2 + 255) & ~(size_t)255;
+  const size_t part = (size_t)std::max(tiles, target_ctas) * M * TC_BM * 4;
+  return xs + part + 4096;
+}
+
+// scratch: >= tc_gemm_scratch_bytes; counters: >= N/128 zeroed words (reset by the kernel).
+cudaError_t launch_tc_gemm(const float* X, int ldx, int M, int N, int K, const uint16_t* W, const float* bias,
+                           const float* R, float res_scale, float* Y, int ldy, void* scratch, unsigned* counters,
+                           int* err, cudaStream_t st, int target_ctas) {
+  if (!tc_gemm_supported(M, N, K)) return cudaErrorInvalidValue;
+  cudaError_t e = get_encoder();
+  if (e != cudaSuccess) return e;
+  const int NB = ((2 * M + 15) / 16) * 16;
+  const int tiles = N / TC_BM, kblocks = K / TC_BK;
+  // K splits: the largest divisor of the K blocks (at most TC_MAX_SPLITS) keeping the grid
+  // within about one CTA per SM; a tile's CTAs each stream >= 1 K block of 16 KB
+  int splits = 1;
+  const int cap = std::max(tiles, target_ctas / 2);
+  for (int s = 1; s <= std::min(TC_MAX_SPLITS, kblocks); ++s)
+    if (kblocks % s == 0 && tiles * s <= cap) splits = s;
+  uint16_t* Xs = static_cast<uint16_t*>(scratch);
+  float* partials = reinterpret_cast<float*>(static_cast<char*>(scratch) + (((size_t)NB * K * 2 + 255) & ~(size_t)255));
+  count_launch();
+  split_bf16_kernel<<<std::min(4096, (NB * K + 255) / 256), 256, 0, st>>>(X, ldx, M, K, NB, Xs);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  CUtensorMap tmW, tmX;
+  if ((e = make_map(&tmW, W, N, K, TC_BM)) != cudaSuccess) return e;
+  if ((e = make_map(&tmX, Xs, NB, K, NB)) != cudaSuccess) return e;
+  TcGemmArgs a = {};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.NB = NB;
+  a.splits = splits;
+  a.kblocks_per_split = kblocks / splits;
+  a.bias = bias;
+  a.R = R;
+  a.res_scale = res_scale;
+  a.Y = Y;
+  a.ldy = ldy;
+  a.partials = partials;
+  a.counters = counters;
+  a.err = err;
+  const int stage_bytes = TC_BM * TC_BK * 2 + ((NB * TC_BK * 2 + 1023) & ~1023);
+  a.nstages = std::max(1, std::min({6, a.kblocks_per_split, (200 * 1024) / stage_bytes}));
+  const int smem = 1024 + a.nstages * stage_bytes + 256;
+  count_launch();
+  tc_gemm_kernel<<<dim3(tiles, splits), TC_THREADS, smem, st>>>(tmW, tmX, a);
+  return cudaGetLastError();
+}
+
+}  // namespace vx
