@@ -222,30 +222,164 @@ def run_reference(args):
     return 0
 
 
+def measure_rmsnorm(ctx, device):
+    """RMSNorm + residual op at [512, 2048] f32, eps 1e-6 (x, r ~N(0,1), w ~N(1,0.02), seed 0):
+    16 rotating buffer sets (268 MB > L2), 30 warm-up + 1000 timed calls (CUDA events)."""
+    import torch
+    from voxcpm_rs_b200.minicpm4 import MiniCpmRmsNorm
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
+    sets = [(torch.randn(512, 2048, generator=g, device=device), torch.randn(512, 2048, generator=g, device=device),
+             torch.empty(512, 2048, device=device), torch.empty(512, 2048, device=device)) for _ in range(16)]
+    norm = MiniCpmRmsNorm(ctx, 1 + 0.02 * torch.randn(2048, generator=g, device=device), 1e-6)
+    from voxcpm_rs_b200._lib import check, lib, ptr
+    L = lib()
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def call(i):
+        x, r, h, y = sets[i % 16]
+        check(L.vx_rmsnorm_residual(ctx.h, ptr(x), ptr(r), ptr(norm.weight), 1.0, 1e-6, 512, 2048, ptr(h), ptr(y),
+                                    stream), ctx.h)
+    for i in range(30):
+        call(i)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(1000):
+        call(i)
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000 / 1000
+    nbytes = 16_785_408
+    return {"workload": "RMSNorm + residual [512, 2048] f32", "us_per_call": us, "gb_s": nbytes / (us * 1e-6) / 1e9,
+            "algorithmic_bytes": nbytes}
+
+
+def measure_layer_step(model, device, peak):
+    """One MiniCPM-4 decoder layer, single-token decode at position 1000 (cache filled with
+    N(0,1) up to 1000), 100 timed steps after 10 warm-up (CUDA events, library stream)."""
+    import numpy as np
+    import torch
+    rng = np.random.default_rng(0)
+    k = rng.standard_normal((NKV, 1000, HD), dtype=np.float32)
+    v = rng.standard_normal((NKV, 1000, HD), dtype=np.float32)
+    model.kv_write(0, k, v)
+    from voxcpm_rs_b200._lib import check, lib, ptr
+    L = lib()
+    h = torch.randn(HIDDEN, device=device)
+    torch.cuda.synchronize()
+    stream = torch.cuda.ExternalStream(model.ctx.stream, device=device)
+    for _ in range(10):
+        check(L.vx_lm_layer_forward_step(model.h, 0, ptr(h), 1000), model.ctx.h)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(100):
+        check(L.vx_lm_layer_forward_step(model.h, 0, ptr(h), 1000), model.ctx.h)
+    e1.record(stream)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000 / 100
+    nbytes = LAYER_WEIGHT_BYTES + 2 * NKV * 1001 * HD * 4
+    return {"workload": "one decoder layer, decode step at p=1000", "us_per_step": us,
+            "gb_s": nbytes / (us * 1e-6) / 1e9, "frac_of_hbm_peak": nbytes / (us * 1e-6) / 1e9 / peak,
+            "algorithmic_bytes": nbytes}
+
+
+def measure_cfm(ctx, device, dcfg, dit_w):
+    """LocDiT CFM solve (8 layers, hidden 1024, CFG 2.0, 10 Euler steps, B=1) in both modes:
+    uniform t (sway 0, zero-star off) and the reference default (sway 1, zero-star on)."""
+    import numpy as np
+    import torch
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    dit = VoxCpmLocDiTV2(ctx, dcfg, dit_w)
+    rng = np.random.default_rng(0)
+    mu = torch.from_numpy(rng.standard_normal((1, 2048), dtype=np.float32)).to(device)
+    cond = torch.zeros(1, 64, 4, device=device)
+    z = torch.from_numpy(rng.standard_normal((1, 64, 4), dtype=np.float32)).to(device)
+    out = {"workload": "LocDiT CFM solve, 8 layers, CFG 2.0, 10 Euler steps, 1 patch [64, 4]"}
+    for name, sway, zs in (("uniform", 0.0, False), ("sway_zero_star", 1.0, True)):
+        for _ in range(3):
+            dit.cfm_forward(mu, 10, cond, z, 2.0, sway, zs)
+        t0 = time.perf_counter()
+        for _ in range(20):
+            dit.cfm_forward(mu, 10, cond, z, 2.0, sway, zs)
+        dt = (time.perf_counter() - t0) / 20
+        out[f"patches_per_s_{name}"] = 1.0 / dt
+    dit.close()
+    return out
+
+
+def gemv_graph_us(ctx, weights, x, reps):
+    """Average device time of one streamed-GEMV launch over ``weights`` (each [N, K] bf16
+    bits), measured by replaying a CUDA graph of one launch per weight ``reps`` times between
+    CUDA events on the launching stream (no per-call host overhead inside the timed region;
+    the first, module-loading launch happens before capture)."""
+    import torch
+    from voxcpm_rs_b200._lib import check, lib, ptr
+    L = lib()
+    n, k = weights[0].shape
+    ys = [torch.empty(1, n, device=x.device) for _ in weights]
+
+    def launch_all():
+        s = torch.cuda.current_stream().cuda_stream
+        for w, y in zip(weights, ys):
+            check(L.vx_linear_bf16(ctx.h, ptr(w), None, ptr(x), 1, n, k, ptr(y), s), ctx.h)
+    launch_all()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        launch_all()
+    graph.replay()
+    cur = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for _ in range(reps):
+        graph.replay()
+    e1.record(cur)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / (reps * len(weights))
+    del graph
+    return us
+
+
 def run_kernel_only():
     """Small profiling case for the dominant kernel: the streamed GEMV on gate|up-shaped
-    weights (N=12288, K=2048, 50 MB each, 4 distinct matrices = 201 MB > L2), 3 passes."""
+    weights (N=12288, K=2048, 50 MB each, 4 distinct matrices = 201 MB > L2).  Launches: 4
+    (direct, module load) + 4 (graph capture warm replay) + 4 x 3 (timed replays)."""
     import torch
     from __graft_entry__ import load_package
     load_package()
-    from voxcpm_rs_b200.minicpm4 import Context, linear_bf16
+    from voxcpm_rs_b200.minicpm4 import Context
     ctx = Context(0)
     g = torch.Generator(device="cuda")
     g.manual_seed(0)
     ws = [(torch.randn(2 * INTER, HIDDEN, generator=g, device="cuda") * 0.02).to(torch.bfloat16).view(torch.int16)
           for _ in range(4)]
     x = torch.randn(1, HIDDEN, device="cuda")
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(3):
-        for w in ws:
-            linear_bf16(ctx, w, x)
-    e1.record()
-    e1.synchronize()
-    us = e0.elapsed_time(e1) * 1000 / 12
+    us = gemv_graph_us(ctx, ws, x, 3)
     print(json.dumps({"kernel": "gemv_bf16_kernel gate|up", "launch_us": us,
                       "achieved_gbs": GATE_UP_BYTES / (us * 1e-6) / 1e9}))
+    ctx.close()
+    return 0
+
+
+def run_lm_only():
+    """Small profiling case for the decode step: the full LM-decode model (28 layers, vocab
+    73448), two greedy runs of a 64-id prompt + 8 steps.  Launches per run: 255 (prefill +
+    first pick) + 8 x 141 (decode steps)."""
+    import torch
+    from __graft_entry__ import load_package
+    load_package()
+    from voxcpm_rs_b200 import synth
+    from voxcpm_rs_b200.minicpm4 import Context, MiniCpmModel
+    ctx = Context(0)
+    model = MiniCpmModel(ctx, lm_config(), None, max_length=MAX_LEN)
+    load_device_weights(model, device_weights(1234, "cuda:0"))
+    prompt = synth.prompt_ids(PROMPT, VOCAB, seed=0)
+    for _ in range(2):
+        t0 = time.perf_counter()
+        toks = model.greedy(prompt, 8)
+        torch.cuda.synchronize()
+        print(json.dumps({"greedy_8_ms": (time.perf_counter() - t0) * 1e3, "ids": toks.tolist()}))
+    model.close()
     ctx.close()
     return 0
 
@@ -284,16 +418,21 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the side workloads (RMSNorm, layer, CFM, synthesis)")
     ap.add_argument("--cpu-steps", type=int, default=6)
     ap.add_argument("--kernel-only", action="store_true",
                     help="profiling case: only the gate|up GEMV over 4 distinct 50 MB weights")
     ap.add_argument("--cfm-only", action="store_true",
                     help="profiling case: two CFM solves of the LocDiT workload (B=1, 10 Euler steps)")
+    ap.add_argument("--lm-only", action="store_true",
+                    help="profiling case: the LM-decode model, two greedy runs of 8 decode steps each")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
     if args.kernel_only:
         return run_kernel_only()
+    if args.lm_only:
+        return run_lm_only()
     if args.cfm_only:
         return run_cfm_only()
     args.warmup = max(3, args.warmup)
@@ -321,12 +460,10 @@ def main():
         if dist is not None:
             dist.barrier()
 
+    from voxcpm_rs_b200 import dist as vxd
+
     def allmax(x):
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return vxd.allmax(x, device=f"cuda:{local}")
 
     device = f"cuda:{local}"
     ctx = Context(local)
@@ -382,18 +519,7 @@ def main():
     # 1.4 GB rotation > L2), CUDA events on the stream it is launched on.
     gu = [torch.cat([l["gate"], l["up"]], 0) for l in w["layers"]]
     xs = torch.randn(1, HIDDEN, device=device)
-    cur = torch.cuda.current_stream()
-    for i in range(LAYERS):
-        linear_bf16(ctx, gu[i], xs)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 3
-    e0.record(cur)
-    for _ in range(reps):
-        for i in range(LAYERS):
-            linear_bf16(ctx, gu[i], xs)
-    e1.record(cur)
-    e1.synchronize()
-    gemv_us = e0.elapsed_time(e1) * 1000.0 / (reps * LAYERS)
+    gemv_us = gemv_graph_us(ctx, gu, xs, 5)
     peak, peak_kind = measured_peaks()
     achieved = GATE_UP_BYTES / (gemv_us * 1e-6) / 1e9
     step_bytes = decode_bytes_per_utt()
@@ -406,6 +532,38 @@ def main():
         except Exception:
             traffic = None
     del gu
+
+    # ---- the other workloads, measured once per run (side figures, not the headline)
+    extras = {}
+    if not args.no_extras:
+        import numpy as np
+        from voxcpm_rs_b200 import config
+        from voxcpm_rs_b200.audiovae import AudioVae
+        from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+        from voxcpm_rs_b200.voxcpm import GenerateOptions, VoxCPM
+        extras["rmsnorm"] = measure_rmsnorm(ctx, device)
+        extras["decoder_layer_step"] = measure_layer_step(model, device, peak)
+        dcfg = config.locdit_config(cfg)
+        dit_w = synth.locdit_weights(dcfg, in_channels=64, seed=rank)
+        extras["locdit_cfm"] = measure_cfm(ctx, device, dcfg, dit_w)
+        # end-to-end synthesis: one utterance per GPU (LM 64-id prompt + 256 steps, a CFM solve
+        # per step with the reference-default sampler, AudioVAE 16 kHz); weak scaling
+        vcfg = config.vae_config()
+        vox = VoxCPM(ctx, model, VoxCpmLocDiTV2(ctx, dcfg, dit_w), AudioVae(ctx, vcfg, synth.vae_weights(vcfg, seed=rank)))
+        noise = np.random.default_rng(100 + rank).standard_normal((STEPS_PER_UTT, 64, 4), dtype=np.float32)
+        vox.generate(prompt, GenerateOptions(max_len=4), noise[:4])
+        barrier()
+        t0 = time.perf_counter()
+        wav = vox.generate(prompt, GenerateOptions(max_len=STEPS_PER_UTT), noise)
+        e2e_s = allmax(time.perf_counter() - t0)
+        audio_s = len(wav) / 16000.0
+        extras["synthesis"] = {"workload": "end-to-end synthesis, 1 utterance per GPU: LM (64-id prompt, 256 steps) "
+                                           "+ CFM solve per step (sway 1, zero-star, CFG 2, 10 steps) + AudioVAE "
+                                           "(rates 2,5,8,8; 16 kHz)",
+                               "audio_seconds_per_utterance": audio_s, "wall_s": e2e_s,
+                               "audio_s_per_s": world * audio_s / e2e_s, "n_gpus": world}
+        vox.dit.close()
+        vox.vae.close()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -446,6 +604,7 @@ def main():
             "gpu_launches": int(launches),
             "clocks": clk,
             "cpu_baseline": cpu,
+            "extras": extras,
         }
         print(json.dumps(line), flush=True)
     model.close()
