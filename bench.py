@@ -363,8 +363,8 @@ def run_kernel_only():
 
 def run_lm_only():
     """Small profiling case for the decode step: the full LM-decode model (28 layers, vocab
-    73448), two greedy runs of a 64-id prompt + 8 steps.  Launches per run: 255 (prefill +
-    first pick) + 8 x 141 (decode steps)."""
+    73448), two greedy runs of a 64-id prompt + 32 steps.  Launches per run: 255 (prefill +
+    first pick) + 32 decode steps (1 persistent launch each, or 141 with VX_PERSIST=0)."""
     import torch
     from __graft_entry__ import load_package
     load_package()
@@ -374,11 +374,15 @@ def run_lm_only():
     model = MiniCpmModel(ctx, lm_config(), None, max_length=MAX_LEN)
     load_device_weights(model, device_weights(1234, "cuda:0"))
     prompt = synth.prompt_ids(PROMPT, VOCAB, seed=0)
+    from voxcpm_rs_b200._lib import check, lib
+    pf, dc = ctypes.c_float(), ctypes.c_float()
     for _ in range(2):
         t0 = time.perf_counter()
-        toks = model.greedy(prompt, 8)
+        toks = model.greedy(prompt, 32)
         torch.cuda.synchronize()
-        print(json.dumps({"greedy_8_ms": (time.perf_counter() - t0) * 1e3, "ids": toks.tolist()}))
+        check(lib().vx_lm_last_timing(model.h, ctypes.byref(pf), ctypes.byref(dc)), ctx.h)
+        print(json.dumps({"greedy_32_ms": (time.perf_counter() - t0) * 1e3, "prefill_ms": pf.value,
+                          "decode_ms_per_token": dc.value / 32, "ids": toks.tolist()[:12]}))
     model.close()
     ctx.close()
     return 0

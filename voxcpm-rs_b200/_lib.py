@@ -68,6 +68,7 @@ SIGNATURES = {
     "vx_launch_count": (C.c_ulonglong, []),
     "vx_lm_last_timing": (I32, [P, C.POINTER(F32), C.POINTER(F32)]),
     "vx_lm_profile_decode_step": (I32, [P, I32, P, I32]),
+    "vx_lm_trace_decode_step": (I32, [P, I32, P, I32, P]),
     "vx_ctx_create": (I32, [I32, C.POINTER(P)]),
     "vx_ctx_destroy": (None, [P]),
     "vx_last_error": (C.c_char_p, [P]),

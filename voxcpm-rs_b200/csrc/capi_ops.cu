@@ -124,6 +124,8 @@ int vx_ctx_create(int device, vx_ctx** out) {
   if (const char* s = getenv("VX_PDL")) ctx->pdl = atoi(s) != 0;
   if (const char* s = getenv("VX_L2_PREFETCH")) ctx->l2_prefetch = atoi(s) != 0;
   if (const char* s = getenv("VX_TC_GEMM")) ctx->tc_gemm = atoi(s) != 0;
+  if (const char* s = getenv("VX_PERSIST")) ctx->persist = atoi(s) != 0;
+  if (const char* s = getenv("VX_PERSIST_NST")) ctx->persist_nst = std::max(0, atoi(s));
   if (cudaSetDevice(device) != cudaSuccess ||
       cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&ctx->counters, 4096 * sizeof(unsigned)) != cudaSuccess ||

@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "persist.cuh"
 #include "runtime.cuh"
 
 using namespace vx;
@@ -72,6 +73,12 @@ struct vx_lm {
 
   cudaGraphExec_t step_exec = nullptr;
   unsigned long long step_kernels = 0;
+  // persistent decode step (one launch per token), when the shape allows it
+  int pk_grid = 0;
+  float* x_mid = nullptr;              // residual stream after attention [H]
+  PersistLayer* pk_layers = nullptr;   // device [L]
+  unsigned* pk_cnt = nullptr;          // phase counters [5L + 2]
+  float* pk_att_part = nullptr;        // attention split partials of the persistent step
   LinearWorkspace ws;  // tcgen05 few-row GEMM workspace (prefill, non-causal forward)
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
   float t_prefill_ms = 0.f, t_decode_ms = 0.f;
@@ -248,25 +255,87 @@ int enqueue_decode_step(vx_lm* lm, cudaStream_t st) {
   return enqueue_lm_head(lm, st, true, true);
 }
 
-int build_step_graph(vx_lm* lm) {
-  if (lm->step_exec) return VX_OK;
+// The whole decode step as one persistent launch (batch row 0).
+cudaError_t enqueue_persist_step(vx_lm* lm, cudaStream_t st, bool cooperative,
+                                 unsigned long long* trace = nullptr) {
+  PersistArgs a = {};
+  a.L = lm->L;
+  a.H = lm->H;
+  a.I = lm->I;
+  a.nh = lm->nh;
+  a.nkv = lm->nkv;
+  a.d = lm->d;
+  a.V = lm->V;
+  a.s_max = lm->max_length;
+  a.eps = lm->cfg.rms_norm_eps;
+  a.res_scale = lm->res_scale;
+  a.attn_scale = lm->attn_scale;
+  a.emb_scale = lm->emb_scale;
+  a.layers = lm->pk_layers;
+  a.final_norm = lm->norm_w;
+  a.embed = lm->embed;
+  a.rope = lm->rope;
+  a.kcache = lm->kc(0, 0);
+  a.vcache = lm->vc(0, 0);
+  a.kv_layer_stride = lm->kv_layer_stride();
+  a.pos = lm->d_pos;
+  a.step = lm->d_step;
+  a.tokens = lm->d_tokens;
+  a.x0 = lm->x;
+  a.x1 = lm->x_mid;
+  a.q = lm->q;
+  a.attn = lm->attn;
+  a.act = lm->act;
+  a.logits = lm->logits;
+  a.hid_norm = lm->hid_norm;
+  a.att_part = lm->pk_att_part;
+  a.att_cnt = lm->attn_counters;
+  a.am_part = lm->argmax_partials;
+  a.phase_cnt = lm->pk_cnt;
+  a.err = lm->ctx->dev_err;
+  a.trace = trace;
+  return launch_persist(a, lm->pk_grid, lm->ctx->persist_nst, st, cooperative);
+}
+
+int capture_step(vx_lm* lm, int mode, cudaGraphExec_t* exec) {
+  // mode 0: per-kernel step; 1: persistent, cooperative launch; 2: persistent, plain launch
   vx_ctx* ctx = lm->ctx;
   cudaGraph_t graph = nullptr;
   const unsigned long long before = g_launches;
-  VX_CUDA(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
-  int rc = enqueue_decode_step(lm, ctx->stream);
-  cudaError_t e = cudaStreamEndCapture(ctx->stream, &graph);
+  cudaError_t e = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamBeginCapture");
+  int rc = VX_OK;
+  cudaError_t le = cudaSuccess;
+  if (mode == 0)
+    rc = enqueue_decode_step(lm, ctx->stream);
+  else
+    le = enqueue_persist_step(lm, ctx->stream, mode == 1);
+  e = cudaStreamEndCapture(ctx->stream, &graph);
   lm->step_kernels = g_launches - before;  // captured, not launched
   g_launches = before;
-  if (rc) {
+  if (rc || le != cudaSuccess || e != cudaSuccess) {
     if (graph) cudaGraphDestroy(graph);
-    return rc;
+    cudaGetLastError();
+    if (rc) return rc;
+    return cuda_fail(ctx, le != cudaSuccess ? le : e, "decode step capture");
   }
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamEndCapture");
-  e = cudaGraphInstantiate(&lm->step_exec, graph, 0);
+  e = cudaGraphInstantiate(exec, graph, 0);
   cudaGraphDestroy(graph);
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaGraphInstantiate");
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return cuda_fail(ctx, e, "cudaGraphInstantiate");
+  }
   return VX_OK;
+}
+
+int build_step_graph(vx_lm* lm) {
+  if (lm->step_exec) return VX_OK;
+  if (lm->pk_grid > 0) {
+    for (int mode : {1, 2})
+      if (capture_step(lm, mode, &lm->step_exec) == VX_OK) return VX_OK;
+    lm->pk_grid = 0;  // neither launch form captures: use the per-kernel step
+  }
+  return capture_step(lm, 0, &lm->step_exec);
 }
 
 int check_device_error(vx_ctx* ctx) { return vx_ctx_synchronize(ctx); }
@@ -365,6 +434,28 @@ int vx_lm_create(vx_ctx* ctx, const vx_minicpm4_config* cfg, int max_batch, int 
   if (workspace_init(ctx, &lm->ws, std::max({lm->qs + 2 * lm->ks, 2 * lm->I, lm->H}),
                      std::max({lm->H, lm->I, lm->qs})) != VX_OK)
     return fail_free(VX_ERR_OOM, "linear workspace allocation failed");
+  if (ctx->persist && lm->L > 0 && lm->embed &&
+      persist_supported(lm->H, lm->I, lm->nh, lm->nkv, d, lm->V, max_length)) {
+    const int grid = persist_configure(lm->H, lm->I, lm->nh, lm->nkv, d, max_length, ctx->persist_nst);
+    if (grid > 0) {
+      std::vector<PersistLayer> pl(lm->L);
+      for (int l = 0; l < lm->L; ++l)
+        pl[l] = {lm->layers[l].wqkv, lm->layers[l].wo, lm->layers[l].wgu, lm->layers[l].wd, lm->layers[l].ln_in,
+                 lm->layers[l].ln_post};
+      const size_t nc = persist_counter_count(lm->L);
+      ok = cudaMalloc(&lm->x_mid, H * 4) == cudaSuccess &&
+           cudaMalloc(&lm->pk_layers, sizeof(PersistLayer) * lm->L) == cudaSuccess &&
+           cudaMemcpy(lm->pk_layers, pl.data(), sizeof(PersistLayer) * lm->L, cudaMemcpyHostToDevice) == cudaSuccess &&
+           cudaMalloc(&lm->pk_cnt, nc * 4) == cudaSuccess && cudaMemset(lm->pk_cnt, 0, nc * 4) == cudaSuccess &&
+           cudaMalloc(&lm->pk_att_part, persist_att_part_floats(lm->nkv, lm->nh, d, lm->H, lm->I, max_length) * 4) ==
+               cudaSuccess;
+      if (!ok) {
+        cudaGetLastError();
+        return fail_free(VX_ERR_OOM, "persistent decode buffers allocation failed");
+      }
+      lm->pk_grid = grid;
+    }
+  }
   *out = lm;
   return VX_OK;
 }
@@ -381,7 +472,8 @@ void vx_lm_destroy(vx_lm* lm) {
   void* ptrs[] = {lm->weight_slab, lm->norm_w, lm->embed, lm->rope, lm->kcache, lm->vcache, lm->d_pos,
                   lm->d_step, lm->d_tokens, lm->x, lm->hid_norm, lm->q, lm->attn, lm->act, lm->logits,
                   lm->attn_partials,
-                  lm->attn_counters, lm->argmax_partials, lm->argmax_counter, lm->pf_ids};
+                  lm->attn_counters, lm->argmax_partials, lm->argmax_counter, lm->pf_ids,
+                  lm->x_mid,         lm->pk_layers, lm->pk_cnt, lm->pk_att_part};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   delete lm;
@@ -607,6 +699,9 @@ int lm_greedy_begin(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_st
   rc = build_step_graph(lm);
   if (rc) return rc;
   VX_CUDA(ctx, cudaEventRecord(lm->ev[0], st));
+  if (lm->pk_cnt) VX_CUDA(ctx, cudaMemsetAsync(lm->pk_cnt, 0, persist_counter_count(lm->L) * 4, st));
+  VX_CUDA(ctx, cudaMemsetAsync(lm->attn_counters, 0, (size_t)lm->max_batch * lm->nkv * 4, st));
+  VX_CUDA(ctx, cudaMemsetAsync(lm->argmax_counter, 0, 4, st));
   // prefill: embed * scale_emb -> causal forward -> StaticKvCache::fill (voxcpm2/model.rs:144-191)
   VX_CUDA(ctx, cudaMemcpyAsync(lm->pf_ids, prompt_ids, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, st));
   VX_CUDA(ctx, launch_embed(lm->embed, lm->pf_ids, n_prompt, lm->H, lm->V, lm->emb_scale, lm->pf_xn, st));
@@ -700,6 +795,32 @@ int vx_lm_profile_decode_step(vx_lm* lm, int pos, float* kernel_us, int n) {
   }
   for (auto& e : ev) cudaEventDestroy(e);
   return rc;
+}
+
+int vx_lm_trace_decode_step(vx_lm* lm, int pos, unsigned long long* trace_out, int n, int* grid_out) {
+  if (!lm || !trace_out || !grid_out) return VX_ERR_ARG;
+  vx_ctx* ctx = lm->ctx;
+  if (lm->pk_grid <= 0) return fail(ctx, VX_ERR_CONFIG, "this model runs the per-kernel decode step");
+  const size_t ne = persist_trace_entries(lm->L, lm->pk_grid);
+  if ((size_t)n < ne) return fail(ctx, VX_ERR_ARG, "trace_out needs %zu entries", ne);
+  if (pos < 0 || pos >= lm->max_length) return fail(ctx, VX_ERR_KV_FULL, "position out of range");
+  cudaSetDevice(ctx->device);
+  cudaStream_t st = ctx->stream;
+  unsigned long long* dtrace = nullptr;
+  VX_CUDA(ctx, cudaMalloc(&dtrace, ne * 8));
+  int rc = VX_OK;
+  lm->pos_host = pos;
+  cudaError_t e = cudaMemsetAsync(dtrace, 0, ne * 8, st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(lm->d_pos, &lm->pos_host, 4, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(lm->pk_cnt, 0, persist_counter_count(lm->L) * 4, st);
+  if (e == cudaSuccess) e = enqueue_persist_step(lm, st, true, dtrace);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(trace_out, dtrace, ne * 8, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) rc = cuda_fail(ctx, e, "trace decode step");
+  cudaFree(dtrace);
+  if (rc) return rc;
+  *grid_out = lm->pk_grid;
+  return check_device_error(ctx);
 }
 
 int vx_lm_last_timing(const vx_lm* lm, float* prefill_ms, float* decode_ms) {

@@ -1,0 +1,71 @@
+// Persistent batch-1 decode step: one launch per token runs every decoder layer and the
+// greedy head (reference MiniCpmModel::forward_step, src/minicpm4/model.rs:64-84, with the
+// layer / attention / MLP steps of layer.rs:57-73, attention.rs:91-154, mlp.rs:28-34).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "gemv.cuh"
+
+namespace vx {
+
+struct PersistLayer {
+  const uint16_t* wqkv;  // [(nh+2nkv)*d, H]
+  const uint16_t* wo;    // [H, nh*d]
+  const uint16_t* wgu;   // [2I, H]
+  const uint16_t* wd;    // [H, I]
+  const float* ln_in;    // [H]
+  const float* ln_post;  // [H]
+};
+
+struct PersistArgs {
+  int L, H, I, nh, nkv, d, V, s_max;
+  float eps, res_scale, attn_scale, emb_scale;
+  const PersistLayer* layers;  // device array [L]
+  const float* final_norm;     // [H]
+  const uint16_t* embed;       // [V, H] (tied input embedding and LM head)
+  const RopeParams* rope;      // nullptr = no_rope
+  float* kcache;               // layer l at kcache + l * kv_layer_stride, layout [nkv][s_max][d]
+  float* vcache;
+  size_t kv_layer_stride;      // elements
+  int* pos;                    // device position of the token being decoded (incremented)
+  int* step;                   // device greedy step index (incremented)
+  int* tokens;                 // picked ids, tokens[*step]
+  float* x0;                   // residual stream [H]: input of each layer, output of its MLP
+  float* x1;                   // residual stream after attention [H]
+  float* q;                    // post-RoPE queries [nh*d]
+  float* attn;                 // attention output [nh*d]
+  float* act;                  // silu(gate)*up [I]
+  float* logits;               // optional [V]
+  float* hid_norm;             // final-norm hidden [H]
+  float* att_part;             // [nkv][ceil(s_max/span)][nh/nkv][d+2] split partials
+  unsigned* att_cnt;           // [nkv] split arrival counters (self-resetting)
+  float2* am_part;             // [grid] per-CTA argmax partials
+  unsigned* phase_cnt;         // [5L + 2] phase arrival counters, zero between launches
+  int* err;                    // device error word
+  // Optional phase trace (nullptr: off): per phase p (5 per layer, then the head) and CTA c,
+  // trace[(p * grid + c) * PERSIST_TRACE_FIELDS + k] = %globaltimer ns at k = 0 consumer
+  // phase start, 1 inputs ready (dependency met, x loaded), 2 phase published, 3 producer's
+  // first copy of the phase issued, 4 its last copy issued, 5 last unit computed, 6 first
+  // stage available, 7 first unit's dot products done (GEMV phases).  Zero where the CTA had
+  // no units.
+  unsigned long long* trace;
+};
+
+constexpr int PERSIST_TRACE_FIELDS = 8;
+inline size_t persist_trace_entries(int L, int grid) { return ((size_t)5 * L + 1) * grid * PERSIST_TRACE_FIELDS; }
+
+// Sizes of the device buffers the caller provides.
+inline size_t persist_counter_count(int L) { return (size_t)5 * L + 2; }
+size_t persist_att_part_floats(int nkv, int nh, int d, int H, int I, int s_max);
+
+// Whether the persistent step supports this model shape (else the per-kernel step is used).
+bool persist_supported(int H, int I, int nh, int nkv, int d, int V, int s_max);
+// Once per context, before capture: raise the kernel's shared-memory limit and return the
+// grid (one CTA per SM) or 0 when the device cannot hold it.  nst_cap (> 1) caps the ring
+// depth in stages (0: as deep as shared memory allows).
+int persist_configure(int H, int I, int nh, int nkv, int d, int s_max, int nst_cap);
+cudaError_t launch_persist(const PersistArgs& a, int grid, int nst_cap, cudaStream_t st, bool cooperative);
+
+}  // namespace vx

@@ -69,6 +69,8 @@ struct vx_ctx {
   int gemv_ctas = 296;               // target GEMV grid (CTAs); env VX_GEMV_CTAS overrides
   bool tc_gemm = true;               // tcgen05 path for few-row GEMMs (env VX_TC_GEMM=0: CUDA cores)
   bool l2_prefetch = false;          // decode kernels prefetch the next kernel's weights into L2
+  bool persist = true;               // batch-1 decode step as one persistent launch (env VX_PERSIST=0: 141 launches)
+  int persist_nst = 0;               // its ring depth cap in stages, 0 = shared-memory limit (env VX_PERSIST_NST)
                                      // (env VX_L2_PREFETCH=1; measured: no gain with separate kernels)
 };
 
