@@ -361,15 +361,18 @@ def run_kernel_only():
     return 0
 
 
-def run_lm_only():
-    """Small profiling case for the decode step: the full LM-decode model (28 layers, vocab
-    73448), two greedy runs of a 64-id prompt + 32 steps.  Launches per run: 255 (prefill +
-    first pick) + 32 decode steps (1 persistent launch each, or 141 with VX_PERSIST=0)."""
+def run_lm_only(layers=LAYERS):
+    """Small profiling case for the decode step: the LM-decode model (28 layers unless
+    `layers` says fewer; vocab 73448), two greedy runs of a 64-id prompt + 32 steps.  Per run:
+    the prefill launches + first pick, then 32 decode steps (1 persistent launch each, or
+    5 * layers + 1 with VX_PERSIST=0)."""
     import torch
     from __graft_entry__ import load_package
     load_package()
     from voxcpm_rs_b200 import synth
     from voxcpm_rs_b200.minicpm4 import Context, MiniCpmModel
+    global LAYERS
+    LAYERS = layers
     ctx = Context(0)
     model = MiniCpmModel(ctx, lm_config(), None, max_length=MAX_LEN)
     load_device_weights(model, device_weights(1234, "cuda:0"))
@@ -429,14 +432,16 @@ def main():
     ap.add_argument("--cfm-only", action="store_true",
                     help="profiling case: two CFM solves of the LocDiT workload (B=1, 10 Euler steps)")
     ap.add_argument("--lm-only", action="store_true",
-                    help="profiling case: the LM-decode model, two greedy runs of 8 decode steps each")
+                    help="profiling case: the LM-decode model, two greedy runs of 32 decode steps each")
+    ap.add_argument("--lm-layers", type=int, default=LAYERS,
+                    help="decoder layers of the --lm-only case (fewer for an ncu capture)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
     if args.kernel_only:
         return run_kernel_only()
     if args.lm_only:
-        return run_lm_only()
+        return run_lm_only(args.lm_layers)
     if args.cfm_only:
         return run_cfm_only()
     args.warmup = max(3, args.warmup)
@@ -519,22 +524,28 @@ def main():
     value = tokens_total / (decode_ms_max / 1000.0)
     e2e = tokens_total / wall_max
 
-    # ---- dominant kernel, live: the streamed GEMV on the 28 gate|up weights (50 MB each,
-    # 1.4 GB rotation > L2), CUDA events on the stream it is launched on.
-    gu = [torch.cat([l["gate"], l["up"]], 0) for l in w["layers"]]
-    xs = torch.randn(1, HIDDEN, device=device)
-    gemv_us = gemv_graph_us(ctx, gu, xs, 5)
+    # ---- dominant kernel: the persistent decode step, one launch per token (the per-kernel
+    # step when VX_PERSIST=0).  Its launch duration is the device time of the replayed steps
+    # (CUDA events on the context stream the graphs run on) divided by the steps.
+    persistent = os.environ.get("VX_PERSIST", "1") != "0"
     peak, peak_kind = measured_peaks()
-    achieved = GATE_UP_BYTES / (gemv_us * 1e-6) / 1e9
     step_bytes = decode_bytes_per_utt()
-    step_gbs = step_bytes * args.steps / (decode_ms / 1000.0) / 1e9
+    launch_us = decode_ms_max * 1000.0 / (args.steps * STEPS_PER_UTT)
+    bytes_per_launch = step_bytes / STEPS_PER_UTT
+    achieved = bytes_per_launch / (launch_us * 1e-6) / 1e9
     traffic = None
-    prof = os.path.join(ROOT, "profiles", "gemv_gate_up_traffic.json")
-    if os.path.exists(prof):
+    prof = os.path.join(ROOT, "profiles", "persist_decode_traffic.json")
+    if persistent and os.path.exists(prof):
         try:
             traffic = json.load(open(prof)).get("bytes_per_launch")
         except Exception:
             traffic = None
+    # the per-kernel step's dominant kernel, live: the streamed GEMV on the 28 gate|up weights
+    # (50 MB each, 1.4 GB rotation > L2), graph-replayed between CUDA events
+    gu = [torch.cat([l["gate"], l["up"]], 0) for l in w["layers"]]
+    xs = torch.randn(1, HIDDEN, device=device)
+    gemv_us = gemv_graph_us(ctx, gu, xs, 5)
+    gemv_gbs = GATE_UP_BYTES / (gemv_us * 1e-6) / 1e9
     del gu
 
     # ---- the other workloads, measured once per run (side figures, not the headline)
@@ -598,13 +609,18 @@ def main():
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": PROMPT * 4,
                     "d2h_bytes_per_step": (STEPS_PER_UTT + 1) * 4,
                     "scope": "vx_lm_greedy with host buffers: prompt H2D + prefill + 256 steps + ids D2H, wall clock"},
-            "roofline": {"bound": "hbm", "kernel": "gemv_bf16_kernel (gate|up, N=12288, K=2048)",
+            "roofline": {"bound": "hbm",
+                         "kernel": "persist_decode_kernel (whole decode step, one launch per token)" if persistent
+                         else "decode step (141 launches per token)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
-                         "traffic": traffic, "algorithmic_bytes_per_launch": GATE_UP_BYTES,
-                         "launch_us": gemv_us},
-            "step_roofline": {"achieved": step_gbs, "peak": peak, "unit": "GB/s", "frac": step_gbs / peak,
-                              "algorithmic_bytes_per_utterance": step_bytes},
+                         "traffic": traffic, "algorithmic_bytes_per_launch": bytes_per_launch,
+                         "launch_us": launch_us,
+                         "basis": "28 layers x 94,371,840 B bf16 weights + 300,843,008 B tied embedding + KV rows "
+                                  "read at each position, averaged over the 256 steps"},
+            "gemv_roofline": {"kernel": "gemv_bf16_kernel (gate|up, N=12288, K=2048), per-kernel step",
+                              "achieved": gemv_gbs, "peak": peak, "unit": "GB/s", "frac": gemv_gbs / peak,
+                              "launch_us": gemv_us, "algorithmic_bytes_per_launch": GATE_UP_BYTES},
             "gpu_launches": int(launches),
             "clocks": clk,
             "cpu_baseline": cpu,
