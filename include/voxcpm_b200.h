@@ -150,6 +150,14 @@ int vx_mlp_swiglu(vx_ctx* ctx, const uint16_t* w_gate_up, const uint16_t* w_down
 int vx_cfg_euler(vx_ctx* ctx, const float* out2b, float* x, int B, int C, int T, float cfg, double dt,
                  int zero_star, vx_stream stream);
 
+/* ScalarQuantizationLayer::forward (fsq.rs:24-29): out = out_proj(round(tanh(in_proj(h)) *
+ * scale) / scale), in_proj / out_proj Linears with bias (bf16 weights in the checkpoint's
+ * [out, in] layout, f32 biases; biases may be NULL).  h [rows, in_dim] -> out [rows, out_dim];
+ * latent_dim is in_proj's width.  Rounding is half away from zero (Rust f32::round). */
+int vx_fsq(vx_ctx* ctx, const uint16_t* w_in, const float* b_in, const uint16_t* w_out, const float* b_out,
+           int in_dim, int latent_dim, int out_dim, float scale, const float* hidden, int rows, float* out,
+           vx_stream stream);
+
 /* ----------------------------------------------------------------- MiniCPM-4 model */
 
 /* MiniCpmModel::new (minicpm4/model.rs:26-41) + StaticKvCache::new (minicpm4/cache.rs:21-44)

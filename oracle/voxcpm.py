@@ -37,3 +37,26 @@ def generate(lm_cfg, lm_w, dit_cfg, dit_w, vae_cfg, vae_w, prompt_ids, max_len, 
     latent = np.concatenate(patches, axis=1)  # [C, T*P]: latent[:, i*P + p] = patch_i[:, p]
     wav = oav.decoder_forward(vae_cfg, vae_w, latent[None])[0, 0]
     return wav, latent, toks
+
+
+def round_half_away(x):
+    """Rust ``f32::round`` (ties away from zero), elementwise in f32."""
+    x = np.asarray(x, F32)
+    return (np.sign(x) * np.floor(np.abs(x) + F32(0.5))).astype(F32)
+
+
+def scalar_quantization(h, w_in, b_in, w_out, b_out, scale):
+    """``ScalarQuantizationLayer::forward`` (reference ``src/fsq.rs:24-29``):
+    ``out_proj(round(tanh(in_proj(h)) * scale) / scale)``; ``w_*`` in the ``[out, in]``
+    layout (f32 copies of the bf16 weights), biases may be None.  Also returns the
+    pre-rounding values ``tanh(in_proj(h)) * scale`` so callers can check tie margins."""
+    h = np.asarray(h, F32)
+    lat = h @ np.asarray(w_in, F32).T
+    if b_in is not None:
+        lat = lat + np.asarray(b_in, F32)
+    pre = (np.tanh(lat.astype(F32)) * F32(scale)).astype(F32)
+    q = (round_half_away(pre) / F32(scale)).astype(F32)
+    out = q @ np.asarray(w_out, F32).T
+    if b_out is not None:
+        out = out + np.asarray(b_out, F32)
+    return out.astype(F32), pre

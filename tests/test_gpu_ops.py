@@ -168,3 +168,30 @@ def test_cfg_euler(ctx, zero_star, cfg_value):
     check(lib().vx_cfg_euler(ctx.h, ptr(og), ptr(xg), B, Cc, T, cfg_value, dt, int(zero_star), None), ctx.h)
     ctx.synchronize()
     assert_close(xg.cpu().numpy(), want, **F32_TOL, what="cfg_euler")
+
+
+@pytest.mark.parametrize("rows", [1, 4])
+def test_fsq(ctx, rows):
+    """ScalarQuantizationLayer::forward (fsq.rs:24-29) at the VoxCPM2 shape (2048 -> 512 ->
+    2048, scale 9), rows 1 (GEMV path) and 4 (tcgen05 path), bf16 weights ~N(0,0.02) with
+    biases.  Seeds whose pre-rounding values sit within 1e-3 of a rounding tie are skipped, so
+    the comparison measures arithmetic, not tie luck."""
+    from oracle.voxcpm import scalar_quantization
+    from voxcpm_rs_b200 import synth
+    from voxcpm_rs_b200.voxcpm import ScalarQuantizationLayer
+    for seed in range(64):
+        rng = np.random.default_rng(seed)
+        h = rng.standard_normal((rows, 2048), dtype=np.float32)
+        w_in = synth.bf16_bits((0.02 * rng.standard_normal((512, 2048))).astype(np.float32))
+        w_out = synth.bf16_bits((0.02 * rng.standard_normal((2048, 512))).astype(np.float32))
+        b_in = (0.02 * rng.standard_normal(512)).astype(np.float32)
+        b_out = (0.02 * rng.standard_normal(2048)).astype(np.float32)
+        f = lambda b: (b.astype(np.uint32) << 16).view(np.float32)  # noqa: E731
+        want, pre = scalar_quantization(h, f(w_in), b_in, f(w_out), b_out, 9)
+        if np.abs(np.abs(pre - np.trunc(pre)) - 0.5).min() > 1e-3:
+            break
+    else:
+        pytest.skip("no seed without a near-tie")
+    layer = ScalarQuantizationLayer(ctx, _bits(w_in), _t(b_in), _bits(w_out), _t(b_out), 9)
+    got = layer.forward(_t(h)).cpu().numpy()
+    assert_close(got, want, **BF16_TOL, what=f"fsq rows={rows}")

@@ -155,3 +155,28 @@ def test_golden_vae():
     got = vae_case()
     for k, v in g.items():
         assert np.abs(got[k] - v).max() <= 1e-5 * max(1.0, np.abs(v).max()), k
+
+
+def test_round_half_away():
+    """Rust f32::round semantics used by the FSQ restatement: ties away from zero."""
+    from oracle.voxcpm import round_half_away
+    got = round_half_away(np.array([0.5, 1.5, 2.5, -0.5, -1.5, 0.49, -2.51], np.float32))
+    assert got.tolist() == [1.0, 2.0, 3.0, -1.0, -2.0, 0.0, -3.0]
+
+
+def test_scalar_quantization_vs_torch():
+    """ScalarQuantizationLayer::forward (fsq.rs:24-29) restated in numpy vs torch-CPU."""
+    import torch
+    from oracle.voxcpm import scalar_quantization
+    rng = np.random.default_rng(3)
+    h = rng.standard_normal((3, 256), dtype=np.float32)
+    w_in = (0.05 * rng.standard_normal((64, 256))).astype(np.float32)
+    b_in = (0.02 * rng.standard_normal(64)).astype(np.float32)
+    w_out = (0.05 * rng.standard_normal((128, 64))).astype(np.float32)
+    b_out = (0.02 * rng.standard_normal(128)).astype(np.float32)
+    got, _ = scalar_quantization(h, w_in, b_in, w_out, b_out, 9)
+    t = lambda a: torch.from_numpy(a)  # noqa: E731
+    lat = torch.tanh(torch.nn.functional.linear(t(h), t(w_in), t(b_in))) * 9
+    q = torch.sign(lat) * torch.floor(lat.abs() + 0.5) / 9
+    want = torch.nn.functional.linear(q, t(w_out), t(b_out)).numpy()
+    np.testing.assert_allclose(got, want, atol=1e-5, rtol=1e-5)

@@ -85,6 +85,7 @@ SIGNATURES = {
     "vx_attention_decode_static": (I32, [P, P, P, I32, I32, I32, I32, I32, I32, P, P]),
     "vx_mlp_swiglu": (I32, [P, P, P, P, I32, I32, I32, P, P]),
     "vx_cfg_euler": (I32, [P, P, P, I32, I32, I32, F32, F64, I32, P]),
+    "vx_fsq": (I32, [P, P, P, P, P, I32, I32, I32, F32, P, I32, P, P]),
     "vx_lm_create": (I32, [P, C.POINTER(MiniCpm4ConfigC), I32, I32, C.POINTER(P)]),
     "vx_lm_destroy": (None, [P]),
     "vx_lm_load_layer": (I32, [P, I32, P, P, P, P, P, P, P, P, P]),

@@ -266,6 +266,39 @@ int vx_attention_decode(vx_ctx* ctx, const float* q, const float* kcache, const 
   return VX_OK;
 }
 
+int vx_fsq(vx_ctx* ctx, const uint16_t* w_in, const float* b_in, const uint16_t* w_out, const float* b_out,
+           int in_dim, int latent_dim, int out_dim, float scale, const float* hidden, int rows, float* out,
+           vx_stream stream) {
+  if (!ctx || !w_in || !w_out || !hidden || !out) return VX_ERR_ARG;
+  if (rows <= 0 || in_dim <= 0 || latent_dim <= 0 || out_dim <= 0 || !(scale > 0.f))
+    return fail(ctx, VX_ERR_SHAPE, "fsq: empty shape or non-positive scale");
+  if (in_dim % 64 != 0 || latent_dim % 64 != 0 || out_dim % 8 != 0)
+    return fail(ctx, VX_ERR_SHAPE, "fsq: in_dim and latent_dim must be multiples of 64, out_dim of 8");
+  cudaSetDevice(ctx->device);
+  cudaStream_t st = pick_stream(ctx, stream);
+  // scratch: the latent activations, then the few-row GEMM workspace
+  const size_t lat_bytes = (((size_t)rows * latent_dim * 4) + 255) & ~size_t(255);
+  size_t gb = 0;
+  const int mm = std::min(rows, 128);
+  if (rows > 1 && ctx->tc_gemm) {
+    if (tc_gemm_supported(mm, latent_dim, in_dim)) gb = std::max(gb, tc_gemm_scratch_bytes(mm, latent_dim, in_dim, ctx->gemv_ctas));
+    if (tc_gemm_supported(mm, out_dim, latent_dim)) gb = std::max(gb, tc_gemm_scratch_bytes(mm, out_dim, latent_dim, ctx->gemv_ctas));
+  }
+  char* base = static_cast<char*>(ctx_scratch(ctx, lat_bytes + gb));
+  if (!base) return fail(ctx, VX_ERR_OOM, "fsq: scratch allocation failed");
+  LinearWorkspace ws;
+  if (gb) {
+    ws.scratch = base + lat_bytes;
+    ws.bytes = gb;
+    ws.counters = ctx->counters;
+  }
+  float* lat = reinterpret_cast<float*>(base);
+  int rc = linear(ctx, &ws, hidden, in_dim, rows, latent_dim, in_dim, w_in, b_in, nullptr, 1.f, lat, latent_dim, st);
+  if (rc) return rc;
+  VX_CUDA(ctx, launch_fsq_quant(lat, (size_t)rows * latent_dim, scale, st));
+  return linear(ctx, &ws, lat, latent_dim, rows, out_dim, latent_dim, w_out, b_out, nullptr, 1.f, out, out_dim, st);
+}
+
 int vx_mlp_swiglu(vx_ctx* ctx, const uint16_t* w_gate_up, const uint16_t* w_down, const float* x, int rows,
                   int hidden, int inter, float* out, vx_stream stream) {
   if (!ctx || !w_gate_up || !w_down || !x || !out) return VX_ERR_ARG;

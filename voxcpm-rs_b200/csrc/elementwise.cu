@@ -4,6 +4,7 @@
 //   * SiLU-gate multiply for S>1 rows       (mlp.rs:31-33)
 //   * token embedding * scale_emb           (minicpm4/model.rs:87-92, voxcpm2/model.rs:145)
 //   * fused CFG(-zero-star) + Euler update   (unified_cfm.rs:132-158)
+#include <algorithm>
 #include <cfloat>
 
 #include "common.cuh"
@@ -252,6 +253,21 @@ __global__ void __launch_bounds__(256) cfg_euler_kernel(const float* __restrict_
       v = q + (p - q) * cfg;  // neg + (pos-neg)*cfg (unified_cfm.rs:151)
     xb[i] = xb[i] - v * dt;   // x - dphi*dt (unified_cfm.rs:155)
   }
+}
+
+// ScalarQuantizationLayer::forward's quantiser (fsq.rs:26-27): round(tanh(h) * scale) / scale,
+// each step in f32 (the reference's f64 scalar is applied to an f32 tensor), round half away
+// from zero as Rust's f32::round.
+__global__ void __launch_bounds__(256) fsq_quant_kernel(float* __restrict__ h, size_t n, float scale) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    h[i] = roundf(tanhf(h[i]) * scale) / scale;
+}
+
+cudaError_t launch_fsq_quant(float* h, size_t n, float scale, cudaStream_t st) {
+  count_launch();
+  const int grid = (int)std::min<size_t>((n + 255) / 256, 148 * 8);
+  fsq_quant_kernel<<<grid, 256, 0, st>>>(h, n, scale);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_cfg_euler(const float* out2b, float* x, int B, int n, double cfg, double dt, int zero_star,

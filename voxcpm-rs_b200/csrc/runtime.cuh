@@ -44,6 +44,7 @@ cudaError_t launch_rope_apply(float* x, int B, int H, int S, int d, const float*
 cudaError_t launch_silu_mul(const float* gu, int M, int inter, float* act, cudaStream_t st);
 cudaError_t launch_embed(const uint16_t* E, const int* ids, int n, int H, int V, float scale, float* out,
                          cudaStream_t st);
+cudaError_t launch_fsq_quant(float* h, size_t n, float scale, cudaStream_t st);
 cudaError_t launch_cfg_euler(const float* out2b, float* x, int B, int n, double cfg, double dt, int zero_star,
                              cudaStream_t st);
 

@@ -42,6 +42,27 @@ class CancelToken:
         self.ctx.cancel_reset()
 
 
+class ScalarQuantizationLayer:
+    """``ScalarQuantizationLayer`` (reference ``src/fsq.rs``): ``forward(h)`` =
+    ``out_proj(round(tanh(in_proj(h)) * scale) / scale)`` on the device.  Weights are torch
+    CUDA tensors: ``w_in`` [latent, in] and ``w_out`` [out, latent] as bf16 bits (int16),
+    biases f32 or None."""
+
+    def __init__(self, ctx, w_in, b_in, w_out, b_out, scale=9):
+        self.ctx, self.w_in, self.b_in, self.w_out, self.b_out = ctx, w_in, b_in, w_out, b_out
+        self.scale = float(scale)
+        self.latent_dim, self.in_dim = w_in.shape
+        self.out_dim = w_out.shape[0]
+
+    def forward(self, hidden, stream=None):
+        import torch
+        h = hidden.reshape(-1, self.in_dim).contiguous()
+        out = torch.empty(h.shape[0], self.out_dim, device=h.device, dtype=torch.float32)
+        check(lib().vx_fsq(self.ctx.h, ptr(self.w_in), ptr(self.b_in), ptr(self.w_out), ptr(self.b_out), self.in_dim,
+                           self.latent_dim, self.out_dim, self.scale, ptr(h), h.shape[0], ptr(out), stream), self.ctx.h)
+        return out.reshape(*hidden.shape[:-1], self.out_dim)
+
+
 class VoxCPM:
     """Owns the LM (``MiniCpmModel``), the DiT (``VoxCpmLocDiTV2``) and the VAE
     (``AudioVae``) objects on one context."""
