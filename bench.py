@@ -162,6 +162,17 @@ def oracle_weights_from_device(w):
 
 
 # ------------------------------------------------------------------ CPU restatement timing
+def cpu_threads():
+    """All host cores for the CPU arms: torch and the BLAS pool numpy uses (torchrun sets
+    OMP_NUM_THREADS=1 in every process, so the pool is set explicitly)."""
+    import torch
+    from threadpoolctl import threadpool_limits
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    threadpool_limits(limits=n)
+    return n
+
+
 def cpu_decode_rate(fw, prompt, n_steps, warm=1):
     """Time the oracle's greedy decode steps (after its causal prefill) on the host cores.
     Returns (tok/s, steps timed, seconds)."""
@@ -196,15 +207,14 @@ def run_reference(args):
     from __graft_entry__ import load_package
     load_package()
     from voxcpm_rs_b200 import synth
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
+    threads = cpu_threads()
     cfg = lm_config()
     fw = synth.minicpm_f32_view(synth.minicpm_weights(cfg, seed=0))
     prompt = synth.prompt_ids(PROMPT, VOCAB, seed=0)
     per_step = 2  # decode tokens per timed step (bounded sample)
     rates = []
     for i in range(args.warmup + args.steps):
-        r, _, _ = cpu_decode_rate(fw, prompt, per_step, warm=0)
+        r, _, _ = cpu_decode_rate(fw, prompt, per_step, warm=1)
         if i >= args.warmup:
             rates.append(r)
     value = statistics.mean(rates)
@@ -213,7 +223,8 @@ def run_reference(args):
             "ms_per_step": 1000.0 * per_step / value, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (random-init weights, seeded prompt)",
             "config": {"workload": "MiniCPM-4 28-layer greedy LM decode, 64-id prompt, batch 1",
-                       "sample": f"{per_step} greedy decode steps per step after a 64-id prefill"},
+                       "sample": f"{per_step} timed greedy decode steps per step, after a 64-id prefill "
+                                 f"and one untimed decode step"},
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
                              "sample": f"{per_step} decode steps per step, numpy f32 restatement "
                                        f"(oracle/) with {threads} BLAS threads"},
@@ -582,8 +593,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        torch.set_num_threads(threads)
+        threads = cpu_threads()
         fw = oracle_weights_from_device(w)
         rate, n, secs = cpu_decode_rate(fw, prompt, args.cpu_steps)
         cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
