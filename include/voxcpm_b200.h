@@ -328,6 +328,15 @@ typedef struct {
 int vx_generate(vx_lm* lm, vx_dit* dit, vx_vae* vae, const int32_t* prompt_ids, int n_prompt,
                 const vx_generate_options* opts, const float* noise, float* wav_out, float* latent_out);
 
+/* vx_generate for B utterances at once: the LM decodes the B prompts (equal lengths,
+ * prompt_ids [B][n_prompt]) as B rows of one batched step (few-row GEMMs) and each patch's CFM
+ * solve runs the B latents together; no reference counterpart beyond running B generate calls
+ * (the reference is one utterance per VoxCPM).  noise [B][max_len][C][P]; wav_out
+ * [B][max_len*P*prod(rates)]; latent_out (optional) [B][C][max_len*P].  Needs the LM created
+ * with max_batch >= B and the DiT with max_rows >= 2B. */
+int vx_generate_batch(vx_lm* lm, vx_dit* dit, vx_vae* vae, const int32_t* prompt_ids, int B, int n_prompt,
+                      const vx_generate_options* opts, const float* noise, float* wav_out, float* latent_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -43,3 +43,34 @@ def test_generate_small(ctx):
             vox.generate(prompt, opts, noise)
     finally:
         ctx.cancel_reset()
+
+
+def test_generate_batch_small(ctx):
+    """vx_generate_batch: 3 utterances (different prompts of one length, different noise) in
+    one batched run, each against the oracle's single-utterance loop; also the batched LM
+    decode's ids against the oracle's greedy ids."""
+    from tests.golden.make_golden import small_dit_config, small_vae_config
+    from voxcpm_rs_b200 import config, synth
+    from voxcpm_rs_b200.audiovae import AudioVae
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    from voxcpm_rs_b200.minicpm4 import MiniCpmModel
+    from voxcpm_rs_b200.voxcpm import GenerateOptions, VoxCPM
+    B, n, steps = 3, 16, 5
+    lm_cfg = config.lm_decode_config(layers=2, vocab=4096)
+    lm_w = synth.minicpm_weights(lm_cfg, seed=3)
+    dcfg, vcfg = small_dit_config(), small_vae_config()
+    dit_w = synth.locdit_weights(dcfg, in_channels=64, seed=4)
+    vae_w = synth.vae_weights(vcfg, seed=5)
+    prompts = np.stack([synth.prompt_ids(n, lm_cfg.vocab_size, seed=10 + b) for b in range(B)])
+    noise = np.random.default_rng(9).standard_normal((B, steps, 64, 4), dtype=np.float32)
+    opts = GenerateOptions(max_len=steps, inference_timesteps=4)
+    vox = VoxCPM(ctx, MiniCpmModel(ctx, lm_cfg, lm_w, max_batch=B, max_length=64),
+                 VoxCpmLocDiTV2(ctx, dcfg, dit_w, max_rows=2 * B), AudioVae(ctx, vcfg, vae_w))
+    wav, lat = vox.generate_batch(prompts, opts, noise, return_latent=True)
+    assert wav.shape == (B, steps * 4 * 80) and lat.shape == (B, 64, steps * 4)
+    fl, fd, fv = synth.minicpm_f32_view(lm_w), synth.locdit_f32_view(dit_w), synth.vae_f32_view(vae_w)
+    for b in range(B):
+        want_wav, want_lat, _ = ovx.generate(lm_cfg, fl, dcfg, fd, vcfg, fv, prompts[b], steps, noise[b],
+                                             inference_timesteps=4)
+        assert_close(lat[b], want_lat, **TOL, what=f"latent[{b}]")
+        assert_close(wav[b], want_wav, **TOL, what=f"wav[{b}]")

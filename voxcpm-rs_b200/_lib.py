@@ -115,6 +115,7 @@ SIGNATURES = {
     "vx_vae_load_out": (I32, [P, P, P, P]),
     "vx_vae_decode": (I32, [P, P, I32, I32, P]),
     "vx_generate": (I32, [P, P, P, P, I32, C.POINTER(GenerateOptionsC), P, P, P]),
+    "vx_generate_batch": (I32, [P, P, P, P, I32, I32, C.POINTER(GenerateOptionsC), P, P, P]),
     "vx_lm_last_logits": (I32, [P, P]),
 }
 

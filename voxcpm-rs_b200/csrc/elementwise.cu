@@ -6,6 +6,7 @@
 //   * fused CFG(-zero-star) + Euler update   (unified_cfm.rs:132-158)
 #include <algorithm>
 #include <cfloat>
+#include <climits>
 
 #include "common.cuh"
 #include "gemv.cuh"
@@ -26,9 +27,15 @@ __global__ void __launch_bounds__(256) rmsnorm_residual_kernel(const float* __re
   const size_t row = blockIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(x + row * hidden);
   const float4* rr = r ? reinterpret_cast<const float4*>(r + row * hidden) : nullptr;
-  float4 v[VPT];
+  float4 v[VPT], ww[VPT];
   float ss = 0.f;
   const int n4 = hidden / 4;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {  // the norm weight is fetched with x, before the reduction
+    const int c = threadIdx.x + i * 256;
+    if (c < n4) ww[i] = __ldg(w4 + c);
+  }
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int c = threadIdx.x + i * 256;
@@ -56,18 +63,16 @@ __global__ void __launch_bounds__(256) rmsnorm_residual_kernel(const float* __re
 #pragma unroll
   for (int i = 0; i < 8; ++i) tot += red[i];
   const float inv = 1.0f / sqrtf(tot / (float)hidden + eps);
-  const float4* w4 = reinterpret_cast<const float4*>(w);
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int c = threadIdx.x + i * 256;
     if (c < n4) {
       if (h_out) __stcs(reinterpret_cast<float4*>(h_out + row * hidden) + c, v[i]);
-      const float4 ww = __ldg(w4 + c);
       float4 y;
-      y.x = (v[i].x * inv) * ww.x;
-      y.y = (v[i].y * inv) * ww.y;
-      y.z = (v[i].z * inv) * ww.z;
-      y.w = (v[i].w * inv) * ww.w;
+      y.x = (v[i].x * inv) * ww[i].x;
+      y.y = (v[i].y * inv) * ww[i].y;
+      y.z = (v[i].z * inv) * ww[i].z;
+      y.w = (v[i].w * inv) * ww[i].w;
       __stcs(reinterpret_cast<float4*>(y_out + row * hidden) + c, y);
     }
   }
@@ -80,24 +85,35 @@ cudaError_t launch_rmsnorm_residual(const float* x, const float* r, const float*
   const int n4 = hidden / 4;
   const int vpt = (n4 + 255) / 256;
   count_launch();
+  // programmatic dependent launch: the kernel waits for its predecessor at entry, so its CTAs
+  // may be scheduled while the previous kernel drains
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(rows);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (vpt <= 2)
-    rmsnorm_residual_kernel<2><<<rows, 256, 0, st>>>(x, r, w, resid_scale, eps, hidden, h_out, y_out);
-  else if (vpt <= 4)
-    rmsnorm_residual_kernel<4><<<rows, 256, 0, st>>>(x, r, w, resid_scale, eps, hidden, h_out, y_out);
-  else
-    rmsnorm_residual_kernel<8><<<rows, 256, 0, st>>>(x, r, w, resid_scale, eps, hidden, h_out, y_out);
-  return cudaGetLastError();
+    return cudaLaunchKernelEx(&cfg, rmsnorm_residual_kernel<2>, x, r, w, resid_scale, eps, hidden, h_out, y_out);
+  if (vpt <= 4)
+    return cudaLaunchKernelEx(&cfg, rmsnorm_residual_kernel<4>, x, r, w, resid_scale, eps, hidden, h_out, y_out);
+  return cudaLaunchKernelEx(&cfg, rmsnorm_residual_kernel<8>, x, r, w, resid_scale, eps, hidden, h_out, y_out);
 }
 
 // ------------------------------------------------------------ RoPE + KV scatter (S rows)
 // qkv [B*S, (nh+2nkv)*d] raw projections.  q_out [B*S, nh*d] (rotated);
-// k (rotated) and v written to cache [B, nkv, s_max, d] at position pos0 + s.
+// k (rotated) and v written to cache [B, nkv, s_max, d] at position pos0 + s, where pos0 is
+// *pos_ptr when pos_ptr is given (a graph-replayed batched decode step).
 // Rope angles use position pos0 + s, formed in f64 (rope.rs:38-46).
 __global__ void rope_scatter_kernel(const float* __restrict__ qkv, int B, int S, int nh, int nkv, int d,
-                                    const RopeParams* rope, int pos0, float* q_out, float* kcache,
+                                    const RopeParams* rope, int pos0, const int* pos_ptr, float* q_out, float* kcache,
                                     float* vcache, int s_max) {
   const int half = d / 2;
   const int heads = nh + 2 * nkv;
+  if (pos_ptr) pos0 = *pos_ptr;
   const size_t total = (size_t)B * S * heads * half;
   for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
        idx += (size_t)gridDim.x * blockDim.x) {
@@ -133,11 +149,12 @@ __global__ void rope_scatter_kernel(const float* __restrict__ qkv, int B, int S,
 
 cudaError_t launch_rope_scatter(const float* qkv, int B, int S, int nh, int nkv, int d, const RopeParams* rope,
                                 int pos0, float* q_out, float* kcache, float* vcache, int s_max,
-                                cudaStream_t st) {
+                                cudaStream_t st, const int* pos_ptr) {
   const size_t total = (size_t)B * S * (nh + 2 * nkv) * (d / 2);
   const int grid = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
   count_launch();
-  rope_scatter_kernel<<<grid, 256, 0, st>>>(qkv, B, S, nh, nkv, d, rope, pos0, q_out, kcache, vcache, s_max);
+  rope_scatter_kernel<<<grid, 256, 0, st>>>(qkv, B, S, nh, nkv, d, rope, pos0, pos_ptr, q_out, kcache, vcache,
+                                            s_max);
   return cudaGetLastError();
 }
 
@@ -205,6 +222,72 @@ cudaError_t launch_embed(const uint16_t* E, const int* ids, int n, int H, int V,
                          cudaStream_t st) {
   count_launch();
   embed_kernel<<<n < 1024 ? n : 1024, 256, 0, st>>>(E, ids, n, H, V, scale, out);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ batched greedy pick
+// One CTA per row b of logits [B, V]: argmax (ties -> lowest id), the id goes to
+// tokens[*step * ld_tokens + b] and the row's next input embed(id) * scale to next_x [B, H].
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* __restrict__ logits, int V, const int* step,
+                                                           int* tokens, int ld_tokens, const uint16_t* __restrict__ E,
+                                                           int H, float scale, float* next_x) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float* row = logits + (size_t)b * V;
+  float bv = -FLT_MAX;
+  int bi = INT_MAX;
+  for (int i = tid; i < V; i += blockDim.x) {
+    const float v = __ldg(row + i);
+    if (v > bv || (v == bv && i < bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) {
+        bv = sv[w];
+        bi = si[w];
+      }
+    if (bi < 0 || bi >= V) bi = 0;
+    tokens[(size_t)(*step) * ld_tokens + b] = bi;
+    si[0] = bi;
+  }
+  __syncthreads();
+  const uint16_t* e = E + (size_t)si[0] * H;
+  for (int k = tid; k < H; k += blockDim.x) next_x[(size_t)b * H + k] = __uint_as_float(((uint32_t)e[k]) << 16) * scale;
+}
+
+__global__ void advance_kernel(int* pos, int* step, int inc_pos) {
+  if (inc_pos) *pos += 1;
+  *step += 1;
+}
+
+cudaError_t launch_argmax_rows(const float* logits, int B, int V, const int* step, int* tokens, int ld_tokens,
+                               const uint16_t* E, int H, float scale, float* next_x, cudaStream_t st) {
+  count_launch();
+  argmax_rows_kernel<<<B, 1024, 0, st>>>(logits, V, step, tokens, ld_tokens, E, H, scale, next_x);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_advance(int* pos, int* step, bool inc_pos, cudaStream_t st) {
+  count_launch();
+  advance_kernel<<<1, 1, 0, st>>>(pos, step, inc_pos ? 1 : 0);
   return cudaGetLastError();
 }
 

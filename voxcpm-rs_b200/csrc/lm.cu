@@ -71,6 +71,13 @@ struct vx_lm {
   int* pf_ids = nullptr;
   int pf_ids_cap = 0;
 
+  // batched greedy decode: B rows in lockstep (equal prompt lengths), one shared position
+  int bt_B = 0;                         // rows of the captured batch step graph
+  cudaGraphExec_t bstep_exec = nullptr;
+  unsigned long long bstep_kernels = 0;
+  float *bx = nullptr, *bxn = nullptr, *bqkv = nullptr, *bq = nullptr, *battn = nullptr, *bgu = nullptr,
+        *bact = nullptr, *blogits = nullptr, *bhid = nullptr;
+  int* btokens = nullptr;  // [max_length + 8][max_batch]
   cudaGraphExec_t step_exec = nullptr;
   unsigned long long step_kernels = 0;
   // persistent decode step (one launch per token), when the shape allows it
@@ -338,6 +345,93 @@ int build_step_graph(vx_lm* lm) {
   return capture_step(lm, 0, &lm->step_exec);
 }
 
+// ----------------------------------------------------------------- batched decode step
+
+int ensure_batch(vx_lm* lm) {
+  if (lm->bx) return VX_OK;
+  const size_t Bm = lm->max_batch, H = lm->H, I = lm->I, qkvw = lm->qs + 2 * lm->ks;
+  bool ok = cudaMalloc(&lm->bx, Bm * H * 4) == cudaSuccess && cudaMalloc(&lm->bxn, Bm * H * 4) == cudaSuccess &&
+            cudaMalloc(&lm->bqkv, Bm * qkvw * 4) == cudaSuccess && cudaMalloc(&lm->bq, Bm * lm->qs * 4) == cudaSuccess &&
+            cudaMalloc(&lm->battn, Bm * lm->qs * 4) == cudaSuccess && cudaMalloc(&lm->bgu, Bm * 2 * I * 4) == cudaSuccess &&
+            cudaMalloc(&lm->bact, Bm * I * 4) == cudaSuccess &&
+            cudaMalloc(&lm->blogits, Bm * (size_t)lm->V * 4) == cudaSuccess &&
+            cudaMalloc(&lm->bhid, Bm * H * 4) == cudaSuccess &&
+            cudaMalloc(&lm->btokens, (size_t)(lm->max_length + 8) * Bm * 4) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    return fail(lm->ctx, VX_ERR_OOM, "batched decode buffers allocation failed");
+  }
+  return VX_OK;
+}
+
+// Greedy head for B rows: final norm (kept as the hidden the DiT consumes), logits over the
+// tied embedding, per-row argmax -> token and next input embedding, then step (and position).
+int enqueue_batch_head(vx_lm* lm, int B, cudaStream_t st, bool advance_pos) {
+  vx_ctx* ctx = lm->ctx;
+  const int H = lm->H;
+  VX_CUDA(ctx, launch_rmsnorm_residual(lm->bx, nullptr, lm->norm_w, 1.f, lm->cfg.rms_norm_eps, B, H, nullptr, lm->bhid,
+                                       st));
+  int rc = linear(ctx, &lm->ws, lm->bhid, H, B, lm->V, H, lm->embed, nullptr, nullptr, 1.f, lm->blogits, lm->V, st);
+  if (rc) return rc;
+  VX_CUDA(ctx, launch_argmax_rows(lm->blogits, B, lm->V, lm->d_step, lm->btokens, lm->max_batch, lm->embed, H,
+                                  lm->emb_scale, lm->bx, st));
+  VX_CUDA(ctx, launch_advance(lm->d_pos, lm->d_step, advance_pos, st));
+  return VX_OK;
+}
+
+// One decode step for B rows at the device position (forward_step, model.rs:64-84, per row):
+// per layer RMSNorm -> qkv (few-row GEMM) -> LongRoPE + KV write -> split-K attention ->
+// o_proj + residual -> RMSNorm -> gate|up -> SiLU*up -> down + residual; then the head.
+int enqueue_batch_step(vx_lm* lm, int B, cudaStream_t st) {
+  vx_ctx* ctx = lm->ctx;
+  const int H = lm->H, I = lm->I, qkvw = lm->qs + 2 * lm->ks;
+  const float eps = lm->cfg.rms_norm_eps;
+  int rc = VX_OK;
+  for (int l = 0; l < lm->L; ++l) {
+    const LmLayer& w = lm->layers[l];
+    VX_CUDA(ctx, launch_rmsnorm_residual(lm->bx, nullptr, w.ln_in, 1.f, eps, B, H, nullptr, lm->bxn, st));
+    if ((rc = linear(ctx, &lm->ws, lm->bxn, H, B, qkvw, H, w.wqkv, nullptr, nullptr, 1.f, lm->bqkv, qkvw, st))) return rc;
+    VX_CUDA(ctx, launch_rope_scatter(lm->bqkv, B, 1, lm->nh, lm->nkv, lm->d, lm->rope, 0, lm->bq, lm->kc(l, 0),
+                                     lm->vc(l, 0), lm->max_length, st, lm->d_pos));
+    AttnDecodeArgs ad = {lm->bq, lm->kc(l, 0), lm->vc(l, 0), B, lm->nh, lm->nkv, lm->d, lm->max_length, lm->d_pos, 0,
+                         lm->attn_scale, lm->attn_nsplit, lm->attn_partials, lm->attn_counters, lm->battn};
+    VX_CUDA(ctx, launch_attn_decode(ad, st, false));
+    if ((rc = linear(ctx, &lm->ws, lm->battn, lm->qs, B, H, lm->qs, w.wo, nullptr, lm->bx, lm->res_scale, lm->bx, H, st)))
+      return rc;
+    VX_CUDA(ctx, launch_rmsnorm_residual(lm->bx, nullptr, w.ln_post, 1.f, eps, B, H, nullptr, lm->bxn, st));
+    if ((rc = linear(ctx, &lm->ws, lm->bxn, H, B, 2 * I, H, w.wgu, nullptr, nullptr, 1.f, lm->bgu, 2 * I, st))) return rc;
+    VX_CUDA(ctx, launch_silu_mul(lm->bgu, B, I, lm->bact, st));
+    if ((rc = linear(ctx, &lm->ws, lm->bact, I, B, H, I, w.wd, nullptr, lm->bx, lm->res_scale, lm->bx, H, st))) return rc;
+  }
+  return enqueue_batch_head(lm, B, st, true);
+}
+
+int build_batch_graph(vx_lm* lm, int B) {
+  if (lm->bstep_exec && lm->bt_B == B) return VX_OK;
+  vx_ctx* ctx = lm->ctx;
+  if (lm->bstep_exec) {
+    cudaGraphExecDestroy(lm->bstep_exec);
+    lm->bstep_exec = nullptr;
+  }
+  cudaGraph_t graph = nullptr;
+  const unsigned long long before = g_launches;
+  VX_CUDA(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_batch_step(lm, B, ctx->stream);
+  cudaError_t e = cudaStreamEndCapture(ctx->stream, &graph);
+  lm->bstep_kernels = g_launches - before;  // captured, not launched
+  g_launches = before;
+  if (rc || e != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    return rc ? rc : cuda_fail(ctx, e, "batch decode step capture");
+  }
+  e = cudaGraphInstantiate(&lm->bstep_exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaGraphInstantiate");
+  lm->bt_B = B;
+  return VX_OK;
+}
+
 int check_device_error(vx_ctx* ctx) { return vx_ctx_synchronize(ctx); }
 
 }  // namespace
@@ -469,6 +563,10 @@ void vx_lm_destroy(vx_lm* lm) {
     if (e) cudaEventDestroy(e);
   free_prefill(lm);
   workspace_free(&lm->ws);
+  if (lm->bstep_exec) cudaGraphExecDestroy(lm->bstep_exec);
+  for (void* p : {(void*)lm->bx, (void*)lm->bxn, (void*)lm->bqkv, (void*)lm->bq, (void*)lm->battn, (void*)lm->bgu,
+                  (void*)lm->bact, (void*)lm->blogits, (void*)lm->bhid, (void*)lm->btokens})
+    if (p) cudaFree(p);
   void* ptrs[] = {lm->weight_slab, lm->norm_w, lm->embed, lm->rope, lm->kcache, lm->vcache, lm->d_pos,
                   lm->d_step, lm->d_tokens, lm->x, lm->hid_norm, lm->q, lm->attn, lm->act, lm->logits,
                   lm->attn_partials,
@@ -720,6 +818,61 @@ int lm_greedy_begin(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_st
   lm->cur_len = n_prompt;
   return VX_OK;
 }
+
+// Batched greedy start for B prompts of equal length (ids [B][n_prompt]): causal prefill of
+// all rows filling the cache rows 0..B-1, then the head picks each row's first id.
+int lm_batch_begin(vx_lm* lm, const int32_t* prompt_ids, int B, int n_prompt, int n_steps) {
+  vx_ctx* ctx = lm->ctx;
+  if (!lm->embed) return fail(ctx, VX_ERR_CONFIG, "greedy decode needs a vocabulary");
+  if (B <= 0 || B > lm->max_batch) return fail(ctx, VX_ERR_SHAPE, "batch %d outside 1..%d", B, lm->max_batch);
+  if (B > 128) return fail(ctx, VX_ERR_SHAPE, "batch %d > 128", B);
+  if (n_prompt + n_steps > lm->max_length)
+    return fail(ctx, VX_ERR_KV_FULL, "KV cache is full: %d prompt + %d steps > %d", n_prompt, n_steps, lm->max_length);
+  for (int i = 0; i < B * n_prompt; ++i)
+    if (prompt_ids[i] < 0 || prompt_ids[i] >= lm->V)
+      return fail(ctx, VX_ERR_ARG, "prompt id %d at %d outside the vocabulary", prompt_ids[i], i);
+  cudaSetDevice(ctx->device);
+  cudaStream_t st = ctx->stream;
+  int rc = ensure_batch(lm);
+  if (rc) return rc;
+  const int rows = B * n_prompt;
+  if (lm->pf_ids_cap < rows) {
+    if (lm->pf_ids) cudaFree(lm->pf_ids);
+    lm->pf_ids = nullptr;
+    lm->pf_ids_cap = 0;
+    VX_CUDA(ctx, cudaMalloc(&lm->pf_ids, (size_t)rows * 4));
+    lm->pf_ids_cap = rows;
+  }
+  if ((rc = ensure_prefill(lm, rows, B, n_prompt, false))) return rc;
+  if ((rc = build_batch_graph(lm, B))) return rc;
+  VX_CUDA(ctx, cudaMemsetAsync(lm->attn_counters, 0, (size_t)lm->max_batch * lm->nkv * 4, st));
+  VX_CUDA(ctx, cudaMemcpyAsync(lm->pf_ids, prompt_ids, (size_t)rows * 4, cudaMemcpyHostToDevice, st));
+  VX_CUDA(ctx, launch_embed(lm->embed, lm->pf_ids, rows, lm->H, lm->V, lm->emb_scale, lm->pf_xn, st));
+  if ((rc = vx_lm_forward(lm, lm->pf_xn, B, n_prompt, 1, 1, lm->pf_gu))) return rc;
+  // each row's last un-normed hidden feeds the head
+  VX_CUDA(ctx, cudaMemcpy2DAsync(lm->bx, (size_t)lm->H * 4, lm->pf_x + (size_t)(n_prompt - 1) * lm->H,
+                                 (size_t)n_prompt * lm->H * 4, (size_t)lm->H * 4, B, cudaMemcpyDeviceToDevice, st));
+  VX_CUDA(ctx, cudaMemsetAsync(lm->d_step, 0, 4, st));
+  if ((rc = enqueue_batch_head(lm, B, st, false))) return rc;
+  lm->pos_host = n_prompt;
+  VX_CUDA(ctx, cudaMemcpyAsync(lm->d_pos, &lm->pos_host, 4, cudaMemcpyHostToDevice, st));
+  lm->cur_len = n_prompt;
+  return VX_OK;
+}
+
+// One graph-replayed batched decode step (B rows as at lm_batch_begin).
+int lm_batch_step(vx_lm* lm) {
+  vx_ctx* ctx = lm->ctx;
+  if (!(lm->cur_len < lm->max_length)) return fail(ctx, VX_ERR_KV_FULL, "KV cache is full");
+  VX_CUDA(ctx, cudaGraphLaunch(lm->bstep_exec, ctx->stream));
+  count_launch(lm->bstep_kernels);
+  lm->cur_len += 1;
+  return VX_OK;
+}
+
+const float* lm_batch_hidden(const vx_lm* lm) { return lm->bhid; }
+const int* lm_batch_tokens(const vx_lm* lm) { return lm->btokens; }
+int lm_max_batch(const vx_lm* lm) { return lm->max_batch; }
 
 // One graph-replayed decode step: consumes the last picked id at the device position,
 // writes the next id, the final-norm hidden (hid_norm) and advances the position.

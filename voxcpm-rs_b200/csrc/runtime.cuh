@@ -38,7 +38,11 @@ cudaError_t launch_tc_gemm(const float* X, int ldx, int M, int N, int K, const u
 cudaError_t launch_rmsnorm_residual(const float* x, const float* r, const float* w, float resid_scale, float eps,
                                     int rows, int hidden, float* h_out, float* y_out, cudaStream_t st);
 cudaError_t launch_rope_scatter(const float* qkv, int B, int S, int nh, int nkv, int d, const RopeParams* rope,
-                                int pos0, float* q_out, float* kcache, float* vcache, int s_max, cudaStream_t st);
+                                int pos0, float* q_out, float* kcache, float* vcache, int s_max, cudaStream_t st,
+                                const int* pos_ptr = nullptr);
+cudaError_t launch_argmax_rows(const float* logits, int B, int V, const int* step, int* tokens, int ld_tokens,
+                               const uint16_t* E, int H, float scale, float* next_x, cudaStream_t st);
+cudaError_t launch_advance(int* pos, int* step, bool inc_pos, cudaStream_t st);
 cudaError_t launch_rope_apply(float* x, int B, int H, int S, int d, const float* cos, const float* sin,
                               cudaStream_t st);
 cudaError_t launch_silu_mul(const float* gu, int M, int inter, float* act, cudaStream_t st);
@@ -136,6 +140,14 @@ int lm_hidden_size(const vx_lm* lm);
 const float* lm_hid_norm(const vx_lm* lm);
 int lm_greedy_begin(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps);
 int lm_greedy_step(vx_lm* lm);
+// Batched greedy decode (B rows in lockstep, equal prompt lengths): prefill + first pick, then
+// one graph-replayed step per call; the final-norm hiddens [B, H] and the ids
+// [step][max_batch] stay on the device.
+int lm_batch_begin(vx_lm* lm, const int32_t* prompt_ids, int B, int n_prompt, int n_steps);
+int lm_batch_step(vx_lm* lm);
+const float* lm_batch_hidden(const vx_lm* lm);
+const int* lm_batch_tokens(const vx_lm* lm);
+int lm_max_batch(const vx_lm* lm);
 // DiT / VAE accessors (dit.cu, vae.cu).
 vx_ctx* dit_ctx(vx_dit* d);
 int dit_in_channels(const vx_dit* d);

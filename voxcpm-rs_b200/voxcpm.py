@@ -85,3 +85,20 @@ class VoxCPM:
         check(lib().vx_generate(self.lm.h, self.dit.h, self.vae.h, ptr(ids), len(ids), C.byref(o), ptr(noise),
                                 ptr(wav), ptr(latent)), self.ctx.h)
         return (wav, latent) if return_latent else wav
+
+    def generate_batch(self, prompt_ids, opts: GenerateOptions, noise, return_latent=False):
+        """B utterances at once (``vx_generate_batch``): prompt_ids [B, n] (equal lengths),
+        noise [B, max_len, C, patch_size].  Returns wav [B, samples] (and latents
+        [B, C, max_len*patch_size]).  The LM needs max_batch >= B, the DiT max_rows >= 2B."""
+        ids = np.ascontiguousarray(prompt_ids, np.int32)
+        b, n = ids.shape
+        noise = np.ascontiguousarray(noise, np.float32)
+        c = self.dit.in_channels
+        frames = opts.max_len * opts.patch_size
+        hop = int(np.prod(self.vae.cfg.decoder_rates))
+        wav = np.empty((b, frames * hop), np.float32)
+        latent = np.empty((b, c, frames), np.float32) if return_latent else None
+        o = opts.to_c()
+        check(lib().vx_generate_batch(self.lm.h, self.dit.h, self.vae.h, ptr(ids), b, n, C.byref(o), ptr(noise),
+                                      ptr(wav), ptr(latent)), self.ctx.h)
+        return (wav, latent) if return_latent else wav
