@@ -208,11 +208,11 @@ int vx_lm_greedy(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps
  * counterpart beyond the VOXCPM_PROFILE timing split (voxcpm2/model.rs:316-372). */
 int vx_lm_profile_decode_step(vx_lm* lm, int pos, float* kernel_us, int n);
 /* One persistent decode step (the single-launch form vx_lm_greedy replays) at `pos` with its
- * phase trace on.  trace_out (host, n >= (num_hidden_layers*5 + 1) * grid * 8 entries)
- * receives, per phase p (qkv+rope, attention, o_proj, gate_up, down per layer; then the
- * head) and CTA c, the %globaltimer ns at [(p*grid + c)*8 + k]: k = 0 phase start, 1 inputs
- * ready, 2 phase published, 3 first operand copy issued, 4 last copy issued, 5 last unit
- * computed, 6 first stage available, 7 first unit computed (0 where the CTA had no work).
+ * phase trace on.  trace_out (host, n >= (num_hidden_layers*4 + 1) * grid * 8 entries)
+ * receives, per phase p (qkv+rope, attention, o_proj, MLP per layer; then the head) and
+ * CTA c, the %globaltimer ns at [(p*grid + c)*8 + k]: k = 0 phase start, 1 inputs ready,
+ * 2 phase published, 3 first operand copy issued, 4 last copy issued, 5 last unit computed,
+ * 6 first stage available, 7 first unit computed (0 where the CTA had no work).
  * *grid_out receives the grid.  Advances the position and greedy step
  * like a replayed step.  VX_ERR_CONFIG when the model runs the per-kernel step.
  * Instrumentation, no reference counterpart. */

@@ -126,6 +126,9 @@ int vx_ctx_create(int device, vx_ctx** out) {
   if (const char* s = getenv("VX_TC_GEMM")) ctx->tc_gemm = atoi(s) != 0;
   if (const char* s = getenv("VX_PERSIST")) ctx->persist = atoi(s) != 0;
   if (const char* s = getenv("VX_PERSIST_NST")) ctx->persist_nst = std::max(0, atoi(s));
+  if (const char* s = getenv("VX_PERSIST_GRID")) ctx->persist_grid = std::max(0, atoi(s));
+  if (const char* s = getenv("VX_PERSIST_PF")) ctx->persist_pf = std::max(0, std::min(256, atoi(s)));
+  if (const char* s = getenv("VX_PERSIST_EF")) ctx->persist_ef = atoi(s) != 0;
   if (cudaSetDevice(device) != cudaSuccess ||
       cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&ctx->counters, 4096 * sizeof(unsigned)) != cudaSuccess ||

@@ -132,6 +132,22 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// L2 policy that makes the lines a load touches the first to be evicted (data read once).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// bulk_g2s with an L2 cache-policy hint (e.g. l2_policy_evict_first()).
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
 // Bulk prefetch of a global range into L2 (TMA engine, no shared-memory destination).
 // addr 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {

@@ -86,6 +86,8 @@ struct vx_lm {
   PersistLayer* pk_layers = nullptr;   // device [L]
   unsigned* pk_cnt = nullptr;          // phase counters [5L + 2]
   float* pk_att_part = nullptr;        // attention split partials of the persistent step
+  float* pk_x0b = nullptr;             // its second residual-stream buffer [H]
+  uint16_t* pk_wdt = nullptr;          // its transposed down_proj weights [L][I][H]
   LinearWorkspace ws;  // tcgen05 few-row GEMM workspace (prefill, non-causal forward)
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
   float t_prefill_ms = 0.f, t_decode_ms = 0.f;
@@ -289,18 +291,18 @@ cudaError_t enqueue_persist_step(vx_lm* lm, cudaStream_t st, bool cooperative,
   a.step = lm->d_step;
   a.tokens = lm->d_tokens;
   a.x0 = lm->x;
+  a.x0b = lm->pk_x0b;
   a.x1 = lm->x_mid;
   a.q = lm->q;
-  a.attn = lm->attn;
-  a.act = lm->act;
   a.logits = lm->logits;
   a.hid_norm = lm->hid_norm;
   a.att_part = lm->pk_att_part;
-  a.att_cnt = lm->attn_counters;
   a.am_part = lm->argmax_partials;
   a.phase_cnt = lm->pk_cnt;
   a.err = lm->ctx->dev_err;
   a.trace = trace;
+  a.pf_stages = lm->ctx->persist_pf;
+  a.evict_first = lm->ctx->persist_ef;
   return launch_persist(a, lm->pk_grid, lm->ctx->persist_nst, st, cooperative);
 }
 
@@ -529,19 +531,21 @@ int vx_lm_create(vx_ctx* ctx, const vx_minicpm4_config* cfg, int max_batch, int 
                      std::max({lm->H, lm->I, lm->qs})) != VX_OK)
     return fail_free(VX_ERR_OOM, "linear workspace allocation failed");
   if (ctx->persist && lm->L > 0 && lm->embed &&
-      persist_supported(lm->H, lm->I, lm->nh, lm->nkv, d, lm->V, max_length)) {
-    const int grid = persist_configure(lm->H, lm->I, lm->nh, lm->nkv, d, max_length, ctx->persist_nst);
+      persist_supported(lm->L, lm->H, lm->I, lm->nh, lm->nkv, d, lm->V, max_length)) {
+    const int grid = persist_configure(lm->H, lm->I, lm->nh, lm->nkv, d, max_length, ctx->persist_nst, ctx->persist_grid);
     if (grid > 0) {
       std::vector<PersistLayer> pl(lm->L);
-      for (int l = 0; l < lm->L; ++l)
-        pl[l] = {lm->layers[l].wqkv, lm->layers[l].wo, lm->layers[l].wgu, lm->layers[l].wd, lm->layers[l].ln_in,
-                 lm->layers[l].ln_post};
       const size_t nc = persist_counter_count(lm->L);
-      ok = cudaMalloc(&lm->x_mid, H * 4) == cudaSuccess &&
+      ok = cudaMalloc(&lm->pk_wdt, (size_t)lm->L * I * H * 2) == cudaSuccess &&
+           cudaMalloc(&lm->pk_x0b, H * 4) == cudaSuccess;
+      for (int l = 0; ok && l < lm->L; ++l)
+        pl[l] = {lm->layers[l].wqkv, lm->layers[l].wo, lm->layers[l].wgu, lm->pk_wdt + (size_t)l * I * H,
+                 lm->layers[l].ln_in, lm->layers[l].ln_post};
+      ok = ok && cudaMalloc(&lm->x_mid, H * 4) == cudaSuccess &&
            cudaMalloc(&lm->pk_layers, sizeof(PersistLayer) * lm->L) == cudaSuccess &&
            cudaMemcpy(lm->pk_layers, pl.data(), sizeof(PersistLayer) * lm->L, cudaMemcpyHostToDevice) == cudaSuccess &&
            cudaMalloc(&lm->pk_cnt, nc * 4) == cudaSuccess && cudaMemset(lm->pk_cnt, 0, nc * 4) == cudaSuccess &&
-           cudaMalloc(&lm->pk_att_part, persist_att_part_floats(lm->nkv, lm->nh, d, lm->H, lm->I, max_length) * 4) ==
+           cudaMalloc(&lm->pk_att_part, persist_att_part_floats(lm->nkv, lm->nh, d) * 4) ==
                cudaSuccess;
       if (!ok) {
         cudaGetLastError();
@@ -571,7 +575,7 @@ void vx_lm_destroy(vx_lm* lm) {
                   lm->d_step, lm->d_tokens, lm->x, lm->hid_norm, lm->q, lm->attn, lm->act, lm->logits,
                   lm->attn_partials,
                   lm->attn_counters, lm->argmax_partials, lm->argmax_counter, lm->pf_ids,
-                  lm->x_mid,         lm->pk_layers, lm->pk_cnt, lm->pk_att_part};
+                  lm->x_mid,         lm->pk_layers, lm->pk_cnt, lm->pk_att_part, lm->pk_x0b, lm->pk_wdt};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   delete lm;
@@ -595,6 +599,9 @@ int vx_lm_load_layer(vx_lm* lm, int layer, const uint16_t* q, const uint16_t* k,
   VX_CUDA(ctx, cudaMemcpyAsync(w.wgu, gate, I * H * 2, cudaMemcpyDefault, st));
   VX_CUDA(ctx, cudaMemcpyAsync(w.wgu + I * H, up, I * H * 2, cudaMemcpyDefault, st));
   VX_CUDA(ctx, cudaMemcpyAsync(w.wd, down, H * I * 2, cudaMemcpyDefault, st));
+  // the persistent step streams down_proj as rows of its transpose (one contiguous 8-row
+  // group per MLP unit)
+  if (lm->pk_wdt) VX_CUDA(ctx, transpose_bf16(w.wd, lm->pk_wdt + (size_t)layer * I * H, (int)H, (int)I, st));
   VX_CUDA(ctx, cudaMemcpyAsync(w.ln_in, ln_in, H * 4, cudaMemcpyDefault, st));
   VX_CUDA(ctx, cudaMemcpyAsync(w.ln_post, ln_post, H * 4, cudaMemcpyDefault, st));
   VX_CUDA(ctx, cudaStreamSynchronize(st));

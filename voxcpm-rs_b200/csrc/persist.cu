@@ -1,27 +1,32 @@
 // Persistent batch-1 decode step (sm_100a): ONE launch per token runs every decoder layer
 // and the greedy head (reference MiniCpmModel::forward_step, src/minicpm4/model.rs:64-84).
 //
-// Why: the per-kernel decode step is 5 launches per layer; each streams a few MB of weights
-// and loses microseconds to its pipeline ramp and tail.  Here one CTA per SM stays resident
-// for the whole token and its producer warp streams ALL of that CTA's operand tiles, phase
-// after phase, through one shared-memory ring with 1-D bulk copies (the TMA engine).
+// Why: a per-kernel decode step is several launches per layer; each streams a few MB of
+// weights and loses microseconds to its pipeline ramp and tail.  Here one CTA per SM stays
+// resident for the whole token and its producer warp streams ALL of that CTA's operand tiles,
+// phase after phase, through one shared-memory ring with 1-D bulk copies (the TMA engine).
 // Weights never depend on activations, and neither do the KV-cache rows of earlier
 // positions, so while the consumer warps wait for the previous phase's result the producer
-// already fills the ring with the next phase's tiles: HBM stays busy across the phase
-// boundaries that cost a ramp and a tail per launch before.
+// already fills the ring with the next phase's tiles.  Every stage is ONE 32 KB bulk copy
+// (the TMA engine issues a bounded number of copies per SM per second, so smaller pieces
+// would cap the stream below the HBM rate).
 //
 // Phases per layer (the unit a CTA owns; units spread round-robin with a rotating offset so
 // every CTA streams about the same bytes per token):
 //   Q    input RMSNorm -> qkv_proj rows -> LongRoPE -> q buffer, k/v into the static cache
 //        (layer.rs:64-66, attention.rs:102-127); unit = a rotate_half pair of 8-row groups
 //   ATT  flash-decode over the cached prefix (attention.rs:129-150, 156-204); unit = one KV
-//        head's 8 query heads against a span of positions whose K/V rows arrive through the
-//        ring (the row of the current position, written by Q, is read after the wait); the
-//        last split to finish merges the online-softmax partials
-//   O    o_proj + residual into x1 (attention.rs:153, layer.rs:67); unit = 8 rows
-//   GU   post-attention RMSNorm -> gate|up rows -> silu(gate)*up (layer.rs:69-71,
-//        mlp.rs:29-33); unit = matching gate and up 8-row groups
-//   D    down_proj + residual into x0 (mlp.rs:33, layer.rs:72); unit = 8 rows
+//        head's 8 query heads against a run of 32-position tiles whose K/V rows arrive
+//        through the ring (the current position's row, written by Q, is read after the
+//        wait); each unit leaves its online-softmax partial (o, max, sum) in global memory
+//   O    merge of the attention partials -> o_proj + residual into x1 (attention.rs:153,
+//        layer.rs:67); unit = 8 rows.  Also seeds the next layer's residual buffer with x1.
+//   M    post-attention RMSNorm -> gate|up rows -> silu(gate)*up -> down_proj (mlp.rs:28-34,
+//        layer.rs:69-72); unit = 8 MLP channels j: their gate row, up row and down column
+//        (a row of the transposed down weight).  Each warp accumulates its slice of the
+//        2048 outputs across the CTA's units; at the end of the phase the CTA adds
+//        res_scale * its partial into the next layer's residual buffer with vector
+//        reductions.  Fusing the down projection removes a dependency round trip per layer.
 // then the greedy head: final norm -> tied-embedding logits -> argmax -> next input
 // embedding, position and step advanced on the device.
 //
@@ -33,7 +38,8 @@
 // reports VX_ERR_TIMEOUT.  The last CTA to leave zeroes the counters for the next launch.
 //
 // GEMV arithmetic per output row is the same as the per-kernel step's streamed GEMV (same
-// per-lane partial sums and warp tree), so the two paths agree to rounding in attention.
+// per-lane partial sums and warp tree).  The down projection sums its 148 CTA partials with
+// f32 reductions in arrival order, so its last bits can differ from run to run.
 #include <algorithm>
 #include <cfloat>
 #include <climits>
@@ -49,12 +55,20 @@ constexpr int PK_CWARPS = 8;
 constexpr int PK_CTHREADS = PK_CWARPS * 32;
 constexpr int PK_THREADS = PK_CTHREADS + 32;
 constexpr int PK_ROWS = 8;
-constexpr int PK_MAX_SMEM = 232448;  // 227 KB opt-in dynamic shared memory per CTA
-constexpr int PK_MISC_FLOATS = 64 + 64 + 64;  // rope tables, reduction scratch
-constexpr int PK_RES_UNITS = 4;      // residual rows preloaded per warp and phase
-constexpr int PK_XREG = 4;           // float4 per thread held by a normalising load_x (K <= 4096)
+constexpr int PK_MAX_LAYERS = 64;                  // layer-table entries held in shared memory
+constexpr int PK_MAX_SMEM = 232448 - PK_MAX_LAYERS * (int)sizeof(PersistLayer);  // 227 KB per CTA, less the table
+constexpr int PK_MISC_FLOATS = 64 + 64 + 64 + 16;  // rope tables, reduction scratch, MLP gate values
+constexpr int PK_RES_UNITS = 4;                    // residual rows preloaded per warp and phase
+constexpr int PK_XREG = 4;                         // float4 per thread held by a normalising load_x (K <= 4096)
+constexpr int NREP = 8;                            // query heads per KV head
 
-enum { PH_Q = 0, PH_ATT = 1, PH_O = 2, PH_GU = 3, PH_D = 4, PH_PER_LAYER = 5, PH_HEAD = 5 };
+enum { PH_Q = 0, PH_ATT = 1, PH_O = 2, PH_M = 3, PH_PER_LAYER = PERSIST_PHASES_PER_LAYER, PH_HEAD = 4 };
+static_assert(PH_PER_LAYER == 4, "phase kinds per layer");
+
+// The layer table, copied from a.layers at kernel start: the producer looks up weight
+// pointers at every phase change, and a global load there (about 1 us under a saturated HBM)
+// would stall the copy stream.
+__shared__ PersistLayer s_lay[PK_MAX_LAYERS];
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
@@ -80,6 +94,14 @@ __device__ __forceinline__ bool sync_or(bool v) {
 __device__ __forceinline__ void csync() { named_sync(1, PK_CTHREADS); }
 
 __device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float2 ldcg2(const float* p) { return __ldcg(reinterpret_cast<const float2*>(p)); }
+
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+__device__ __forceinline__ void red_add_v2(float* p, float a, float b) {
+  asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b) : "memory");
+}
 
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
@@ -91,23 +113,35 @@ __device__ __forceinline__ void trace_mark(const PersistArgs& a, int p, int k) {
   if (a.trace) a.trace[((size_t)p * gridDim.x + blockIdx.x) * PERSIST_TRACE_FIELDS + k] = gtimer();
 }
 
+// Residual-stream buffer that is the input of layer l (layer L: the head's input).
+__device__ __forceinline__ float* xbuf(const PersistArgs& a, int l) { return (l & 1) ? a.x0b : a.x0; }
+
 // flags[0]: consumers stopped (producer must stop too); flags[1]: last-arrival broadcast;
 // flags[2]: picked token broadcast; flags[3]: producer gave up.
 struct Smem {
   uint16_t* ring;
   float* xs;
+  float* parts;  // attention split partials of one layer, as in att_part
   float* ctab;  // [64]
   float* stab;  // [64]
   float* red;   // [64]: [0,8) group sums / merge, [16,32) per-warp argmax, [48,50) CTA argmax
+  float* mv;    // [16]: silu(gate)*up of the current MLP unit's 8 channels, double-buffered
   volatile int* flags;
   uint64_t* full;
   uint64_t* empty;
+  uint64_t* pbar;  // completion of the partials' bulk copies
 };
 
-// Attention split layout of this launch, the same in every CTA.
+// Attention geometry of this launch, the same in every CTA: `ntiles` tiles of `span`
+// positions cover [0, len); split sp of a KV head covers tiles [sp*tps, (sp+1)*tps).
 struct AttGeo {
-  int pos, len, span, nsplit, ns_max, items;
+  int pos, len, span, ntiles, nsplit, tps, items;
 };
+
+__device__ __forceinline__ int att_tiles(const AttGeo& at, int u) {
+  const int t0 = (u % at.nsplit) * at.tps;
+  return min(at.ntiles, t0 + at.tps) - t0;
+}
 
 // Bounded wait for a ring stage, by every consumer thread.  Returns false on failure.
 __device__ __forceinline__ bool wait_full(uint64_t* bar, uint32_t parity, int* err, volatile int* flags) {
@@ -148,7 +182,7 @@ __device__ bool dep_wait(const unsigned* cnt, unsigned target, int* err, bool ba
   return !sync_or(bad);
 }
 
-// Publish this CTA's completion of a phase (after all its stores).
+// Publish this CTA's completion of a phase (after all its stores and reductions).
 __device__ __forceinline__ void arrive(unsigned* cnt) {
   csync();
   if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
@@ -158,7 +192,7 @@ struct Geo {
   const uint16_t* W;
   int K;
   int U;    // units in the phase
-  int gpu;  // 8-row groups per unit
+  int gpu;  // 8-row groups per unit (attention: tiles per split)
   int kind;
 };
 
@@ -167,18 +201,17 @@ __device__ __forceinline__ int unit_row(const PersistArgs& a, int kind, int u, i
     const int hp = a.d / 16;
     return (u / hp) * a.d + (u % hp) * PK_ROWS + gi * (a.d / 2);
   }
-  if (kind == PH_GU) return gi * a.I + u * PK_ROWS;  // gate rows, then the matching up rows
+  if (kind == PH_M) return (gi == 1 ? a.I : 0) + u * PK_ROWS;  // gate rows, up rows, wdt rows
   return u * PK_ROWS;
 }
 
 __device__ __forceinline__ Geo geo_of(const PersistArgs& a, int l, int kind, const AttGeo& at) {
-  const PersistLayer& w = a.layers[l < a.L ? l : 0];
+  const PersistLayer& w = s_lay[l < a.L ? l : 0];
   switch (kind) {
     case PH_Q: return {w.wqkv, a.H, (a.nh + 2 * a.nkv) * a.d / 16, 2, PH_Q};
-    case PH_ATT: return {nullptr, 0, at.items, 1, PH_ATT};
+    case PH_ATT: return {nullptr, 0, at.items, at.tps, PH_ATT};
     case PH_O: return {w.wo, a.nh * a.d, a.H / PK_ROWS, 1, PH_O};
-    case PH_GU: return {w.wgu, a.H, a.I / PK_ROWS, 2, PH_GU};
-    case PH_D: return {w.wd, a.I, a.H / PK_ROWS, 1, PH_D};
+    case PH_M: return {w.wgu, a.H, a.I / PK_ROWS, 3, PH_M};
     default: return {a.embed, a.H, a.V / PK_ROWS, 1, PH_HEAD};
   }
 }
@@ -189,15 +222,19 @@ __device__ __forceinline__ int first_unit(int off, int G) {
 
 // ---------------------------------------------------------------- producer warp (lane 0)
 
-// Position in this CTA's stage sequence: phases in order (5 per layer, then the head), this
-// CTA's units of each phase, the 8-row groups of a unit, the K chunks of a group (an
-// attention unit is one stage).
+// Position in this CTA's stage sequence: phases in order (4 per layer, then the head), this
+// CTA's units of each phase, the 8-row groups (or attention tiles) of a unit, the K chunks of
+// a group.
 struct Cursor {
   int l, kind, off;
-  int u, gi, c, nch;
+  int u, gi, ngi, c, nch;
   Geo g;
   bool valid;
 };
+
+__device__ __forceinline__ int unit_groups(const Cursor& k, const AttGeo& at) {
+  return k.kind == PH_ATT ? att_tiles(at, k.u) : k.g.gpu;
+}
 
 template <int KC>
 __device__ void cursor_seek(const PersistArgs& a, Cursor& k, const AttGeo& at) {
@@ -210,6 +247,7 @@ __device__ void cursor_seek(const PersistArgs& a, Cursor& k, const AttGeo& at) {
       k.gi = 0;
       k.c = 0;
       k.nch = k.kind == PH_ATT ? 1 : k.g.K / KC;
+      k.ngi = unit_groups(k, at);
       k.valid = true;
       return;
     }
@@ -235,10 +273,13 @@ template <int KC>
 __device__ void cursor_next(const PersistArgs& a, Cursor& k, const AttGeo& at) {
   if (++k.c < k.nch) return;
   k.c = 0;
-  if (++k.gi < k.g.gpu) return;
+  if (++k.gi < k.ngi) return;
   k.gi = 0;
   k.u += gridDim.x;
-  if (k.u < k.g.U) return;
+  if (k.u < k.g.U) {
+    k.ngi = unit_groups(k, at);
+    return;
+  }
   k.off = (k.off + k.g.U) % gridDim.x;
   if (k.kind == PH_HEAD) {
     k.valid = false;
@@ -255,12 +296,57 @@ __device__ __forceinline__ int cursor_phase(const PersistArgs& a, const Cursor& 
   return k.kind == PH_HEAD ? a.L * PH_PER_LAYER : k.l * PH_PER_LAYER + k.kind;
 }
 
-// Streams this CTA's stages into the shared-memory ring (about 100 KB in flight per SM
-// already saturates HBM; deeper L2 prefetching measured slower).
+// K/V rows of positions [j0, min(j1, pos)) of tile gi of attention unit u: element offset
+// and bytes (the current position's row is written during this launch and patched in by the
+// consumers after the dependency wait).
+__device__ __forceinline__ uint32_t att_old_rows(const PersistArgs& a, const AttGeo& at, int l, int u, int gi,
+                                                 size_t* base) {
+  const int g = u / at.nsplit, t = (u % at.nsplit) * at.tps + gi;
+  const int j0 = t * at.span, j1 = min(at.len, j0 + at.span);
+  const int nold = max(0, min(j1, at.pos) - j0);
+  *base = (size_t)l * a.kv_layer_stride + ((size_t)g * a.s_max + j0) * a.d;
+  return (uint32_t)nold * a.d * 4;
+}
+
+
+// First row of the 8-row group at cursor k (rows are k.g.K elements apart) plus the chunk.
+template <int KC>
+__device__ __forceinline__ const uint16_t* group_src(const PersistArgs& a, const Cursor& k) {
+  const uint16_t* W = (k.kind == PH_M && k.gi == 2) ? s_lay[k.l].wdt : k.g.W;
+  return W + (size_t)unit_row(a, k.kind, k.u, k.gi) * k.g.K + (size_t)k.c * KC;
+}
+
+// L2 prefetch of the bytes of the stage at cursor k (nothing lands in shared memory).
+template <int KC>
+__device__ __forceinline__ void prefetch_stage(const PersistArgs& a, const Cursor& k, const AttGeo& at) {
+  if (k.kind == PH_ATT) {
+    size_t base;
+    const uint32_t bytes = att_old_rows(a, at, k.l, k.u, k.gi, &base);
+    if (bytes) {
+      bulk_prefetch_l2(a.kcache + base, bytes);
+      bulk_prefetch_l2(a.vcache + base, bytes);
+    }
+  } else {
+    const uint16_t* src = group_src<KC>(a, k);
+    if (k.nch == 1) {
+      bulk_prefetch_l2(src, PK_ROWS * KC * 2);
+    } else {
+      for (int r = 0; r < PK_ROWS; ++r) bulk_prefetch_l2(src + (size_t)r * k.g.K, KC * 2);
+    }
+  }
+}
+
+// Streams this CTA's stages into the shared-memory ring.  With a.pf_stages > 0 a second
+// cursor runs that many stages ahead of the newest ring copy and prefetches them into L2.
 template <int KC>
 __device__ void produce(const PersistArgs& a, const Smem& sm, int nst, const AttGeo& at) {
   Cursor cp;
   cursor_init<KC>(a, cp, at);
+  Cursor cq = cp;  // L2 prefetch cursor, stage index sq
+  int sq = 0;
+  if (a.pf_stages > 0)
+    for (; sq < nst && cq.valid; ++sq) cursor_next<KC>(a, cq, at);  // the first nst stages are copied at once
+  const uint64_t pol = a.evict_first ? l2_policy_evict_first() : 0ull;
   int s = 0, last_phase = -1;
   bool ok = true;
   while (cp.valid && ok) {
@@ -293,32 +379,38 @@ __device__ void produce(const PersistArgs& a, const Smem& sm, int nst, const Att
     }
     uint16_t* dst = sm.ring + (size_t)slot * PK_ROWS * KC;
     if (cp.kind == PH_ATT) {
-      // K/V rows of positions [j0, min(j1, pos)) of one KV head (the current position's row is
-      // written during this launch and read by the consumers after the dependency wait)
-      const int g = cp.u / at.nsplit, sp = cp.u % at.nsplit;
-      const int j0 = sp * at.span, j1 = min(at.len, j0 + at.span);
-      const int nold = max(0, min(j1, at.pos) - j0);
-      const uint32_t bytes = (uint32_t)nold * a.d * 4;
+      size_t base;
+      const uint32_t bytes = att_old_rows(a, at, cp.l, cp.u, cp.gi, &base);
       if (bytes == 0) {
         mbar_arrive(&sm.full[slot]);
       } else {
-        const size_t base = (size_t)cp.l * a.kv_layer_stride + ((size_t)g * a.s_max + j0) * a.d;
         mbar_arrive_expect_tx(&sm.full[slot], 2 * bytes);
         bulk_g2s(dst, a.kcache + base, bytes, &sm.full[slot]);
         bulk_g2s(reinterpret_cast<float*>(dst) + (size_t)at.span * a.d, a.vcache + base, bytes, &sm.full[slot]);
       }
     } else {
-      const int row0 = unit_row(a, cp.kind, cp.u, cp.gi);
+      const uint16_t* src = group_src<KC>(a, cp);
       mbar_arrive_expect_tx(&sm.full[slot], PK_ROWS * KC * 2);
       if (cp.nch == 1) {
-        bulk_g2s(dst, cp.g.W + (size_t)row0 * cp.g.K, PK_ROWS * KC * 2, &sm.full[slot]);
+        if (a.evict_first)
+          bulk_g2s_hint(dst, src, PK_ROWS * KC * 2, &sm.full[slot], pol);
+        else
+          bulk_g2s(dst, src, PK_ROWS * KC * 2, &sm.full[slot]);
       } else {
-        for (int r = 0; r < PK_ROWS; ++r)
-          bulk_g2s(dst + r * KC, cp.g.W + (size_t)(row0 + r) * cp.g.K + (size_t)cp.c * KC, KC * 2, &sm.full[slot]);
+        for (int r = 0; r < PK_ROWS; ++r) {
+          if (a.evict_first)
+            bulk_g2s_hint(dst + r * KC, src + (size_t)r * cp.g.K, KC * 2, &sm.full[slot], pol);
+          else
+            bulk_g2s(dst + r * KC, src + (size_t)r * cp.g.K, KC * 2, &sm.full[slot]);
+        }
       }
     }
     ++s;
     cursor_next<KC>(a, cp, at);
+    for (; a.pf_stages > 0 && cq.valid && sq < s + a.pf_stages; ++sq) {
+      prefetch_stage<KC>(a, cq, at);
+      cursor_next<KC>(a, cq, at);
+    }
   }
   if (last_phase >= 0) trace_mark(a, last_phase, 4);
   // Do not leave while a copy into this CTA's shared memory may still be in flight.
@@ -378,141 +470,197 @@ __device__ void load_x(const float* x, const float* norm_w, int K, float eps, co
   csync();
 }
 
+// The attention output [nh*D] -> xs: per query head, the merge of its KV head's split
+// partials (o unnormalised, max m, sum l): out = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s
+// with M the largest m_s (attention.rs:186-191 over the whole prefix).  One bulk copy per KV
+// head brings the partials into shared memory (one L2 round trip; they were written by other
+// CTAs' generic stores, hence the proxy fence), then the merge reads shared memory only.
+// `use` counts this CTA's earlier merges (the parity of sm.pbar).  Returns false on a failed
+// wait.
+template <int D>
+__device__ bool att_merge(const PersistArgs& a, const AttGeo& at, const Smem& sm, int use) {
+  const int nhd = a.nh * D, ns = at.nsplit;
+  const size_t gstride = (size_t)PERSIST_ATT_SPLITS * NREP * (D + 4);  // floats per KV head
+  if (threadIdx.x == 0) {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    const uint32_t bytes = (uint32_t)(ns * NREP * (D + 4) * 4);
+    mbar_arrive_expect_tx(sm.pbar, bytes * a.nkv);
+    for (int g = 0; g < a.nkv; ++g) bulk_g2s(sm.parts + g * gstride, a.att_part + g * gstride, bytes, sm.pbar);
+  }
+  const bool ok = wait_full(sm.pbar, use & 1, a.err, sm.flags);
+  if (ok) {
+    for (int e = threadIdx.x * 4; e < nhd; e += PK_CTHREADS * 4) {
+      const int h = e / D, dd = e % D;
+      const float* p0 = sm.parts + (size_t)(h / NREP) * gstride + (size_t)(h % NREP) * (D + 4);
+      const size_t ss = (size_t)NREP * (D + 4);
+      float M = p0[D];
+      for (int sp = 1; sp < ns; ++sp) M = fmaxf(M, p0[sp * ss + D]);
+      float Ls = 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int sp = 0; sp < ns; ++sp) {
+        const float* pp = p0 + sp * ss;
+        const float f = expf(pp[D] - M);
+        const float4 o = *reinterpret_cast<const float4*>(pp + dd);
+        Ls = fmaf(f, pp[D + 1], Ls);
+        acc.x = fmaf(f, o.x, acc.x);
+        acc.y = fmaf(f, o.y, acc.y);
+        acc.z = fmaf(f, o.z, acc.z);
+        acc.w = fmaf(f, o.w, acc.w);
+      }
+      float4 r;
+      r.x = acc.x / Ls;
+      r.y = acc.y / Ls;
+      r.z = acc.z / Ls;
+      r.w = acc.w / Ls;
+      *reinterpret_cast<float4*>(sm.xs + e) = r;
+    }
+  }
+  return !sync_or(!ok);
+}
+
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
 
-// One attention unit, K/V rows in ring slot `kv` (K [span][D] then V [span][D]): query heads
-// g*8..g*8+7 against positions [j0, j1) (attention.rs:129-150 for one split).  Warp r is query
-// head r, lane j scores position j0 + j (dims visited in a lane-rotated order so the row-per-
-// lane reads hit distinct banks).  Writes the normalised output directly when there is one
-// split, else the (o, m, l) partial; the last split to finish merges them.  Returns false if
-// the CTA must stop.
-template <int D>
-__device__ bool att_unit(const PersistArgs& a, const AttGeo& at, int l, int u, float* kv, bool lbad, const Smem& sm) {
-  constexpr int NC = D / 4, DPL = D / 32, NREP = 8;
+// Consumer state carried across phases (returned by value from the out-of-line phase bodies).
+struct CState {
+  int s;      // ring stages consumed
+  int bad;    // the step must stop
+  int merges; // attention merges done (parity of sm.pbar)
+};
+
+// One attention unit: query heads g*8..g*8+7 against the positions of its tiles
+// (attention.rs:129-150 for one split).  Warp r is query head r, lane j scores position
+// j0 + j of a tile (dims visited in a lane-rotated order so the row-per-lane reads hit
+// distinct banks); the softmax runs online across the unit's tiles.  Leaves the partial
+// (o, m, l) in att_part.  Returns false if the CTA must stop.
+template <int KC, int D>
+__device__ bool att_unit(const PersistArgs& a, const AttGeo& at, int l, int u, const Smem& sm, CState& st, int nst) {
+  constexpr int NC = D / 4, DPL = D / 32;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = u / at.nsplit, sp = u % at.nsplit;
-  const int j0 = sp * at.span, j1 = min(at.len, j0 + at.span), nt = j1 - j0;
-  float* Ks = kv;
-  float* Vs = kv + (size_t)at.span * D;
+  const int t0 = sp * at.tps, t1 = min(at.ntiles, t0 + at.tps);
   float* qs = sm.xs;  // [8][D]
-  // post-RoPE queries of this KV head's 8 query heads, and the current position's K/V row
-  for (int i = tid; i < NREP * NC; i += PK_CTHREADS)
-    *reinterpret_cast<float4*>(qs + i * 4) = ldcg4(a.q + (size_t)g * NREP * D + i * 4);
-  if (at.pos >= j0 && at.pos < j1 && tid < 2 * NC) {
-    const size_t src = (size_t)l * a.kv_layer_stride + ((size_t)g * a.s_max + at.pos) * D;
-    const int c = tid % NC;
-    float* dst = (tid < NC ? Ks : Vs) + (size_t)(at.pos - j0) * D + c * 4;
-    *reinterpret_cast<float4*>(dst) = ldcg4((tid < NC ? a.kcache : a.vcache) + src + c * 4);
-    // the slot is refilled by bulk copies (async proxy) once released
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  // the 8 query rows and the current position's K/V row (both written by this launch's Q
+  // phase) are fetched in one round trip; the row is patched into its tile's ring slot below
+  static_assert(NREP * NC <= 4 * PK_CTHREADS, "query rows per thread");
+  float4 qv[(NREP * NC + PK_CTHREADS - 1) / PK_CTHREADS];
+#pragma unroll
+  for (int i = 0; i < (NREP * NC + PK_CTHREADS - 1) / PK_CTHREADS; ++i)
+    if (tid + i * PK_CTHREADS < NREP * NC) qv[i] = ldcg4(a.q + (size_t)g * NREP * D + (tid + i * PK_CTHREADS) * 4);
+  const int tpos = at.pos / at.span;  // tile holding the current position
+  float4 cur = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (tpos >= t0 && tpos < t1 && tid < 2 * NC) {
+    const size_t src = (size_t)l * a.kv_layer_stride + ((size_t)g * a.s_max + at.pos) * D + (tid % NC) * 4;
+    cur = ldcg4((tid < NC ? a.kcache : a.vcache) + src);
   }
-  if (sync_or(lbad)) return false;
-  // scores q.k^T * scale (attention.rs:166)
-  float sc = 0.f;
-  if (lane < nt) {
-    const float* kr = Ks + (size_t)lane * D;
-    const float* qr = qs + warp * D;
-#pragma unroll 8
-    for (int ch = 0; ch < NC; ++ch) {
-      const int c = (ch + lane) & (NC - 1);
-      const float4 kk = *reinterpret_cast<const float4*>(kr + c * 4);
-      const float4 qq = *reinterpret_cast<const float4*>(qr + c * 4);
-      sc = fmaf(qq.x, kk.x, sc);
-      sc = fmaf(qq.y, kk.y, sc);
-      sc = fmaf(qq.z, kk.z, sc);
-      sc = fmaf(qq.w, kk.w, sc);
-    }
-  }
-  const bool valid = lane < nt;
-  const float sv = valid ? sc * a.attn_scale : -INFINITY;
-  const float m = warp_max(sv);
-  const float p = valid ? expf(sv - m) : 0.f;
-  const float lsum = warp_sum(p);
+#pragma unroll
+  for (int i = 0; i < (NREP * NC + PK_CTHREADS - 1) / PK_CTHREADS; ++i)
+    if (tid + i * PK_CTHREADS < NREP * NC) *reinterpret_cast<float4*>(qs + (tid + i * PK_CTHREADS) * 4) = qv[i];
+  float m = -INFINITY, lsum = 0.f;
   float o[DPL];
 #pragma unroll
   for (int e = 0; e < DPL; ++e) o[e] = 0.f;
-  for (int j = 0; j < nt; ++j) {
-    const float pj = __shfl_sync(0xffffffffu, p, j);
-    const float* vr = Vs + (size_t)j * D + lane * DPL;
+  for (int t = t0; t < t1; ++t) {
+    const int slot = st.s % nst;
+    bool lbad = !wait_full(&sm.full[slot], (st.s / nst) & 1, a.err, sm.flags);
+    float* Ks = reinterpret_cast<float*>(sm.ring + (size_t)slot * PK_ROWS * KC);
+    float* Vs = Ks + (size_t)at.span * D;
+    const int j0 = t * at.span, j1 = min(at.len, j0 + at.span), nt = j1 - j0;
+    if (!lbad && t == tpos && tid < 2 * NC) {
+      float* dst = (tid < NC ? Ks : Vs) + (size_t)(at.pos - j0) * D + (tid % NC) * 4;
+      *reinterpret_cast<float4*>(dst) = cur;
+      // the slot is refilled by bulk copies (async proxy) once released
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (sync_or(lbad)) return false;
+    // scores q.k^T * scale (attention.rs:166)
+    float sc = 0.f;
+    if (lane < nt) {
+      const float* kr = Ks + (size_t)lane * D;
+      const float* qr = qs + warp * D;
+#pragma unroll 8
+      for (int ch = 0; ch < NC; ++ch) {
+        const int c = (ch + lane) & (NC - 1);
+        const float4 kk = *reinterpret_cast<const float4*>(kr + c * 4);
+        const float4 qq = *reinterpret_cast<const float4*>(qr + c * 4);
+        sc = fmaf(qq.x, kk.x, sc);
+        sc = fmaf(qq.y, kk.y, sc);
+        sc = fmaf(qq.z, kk.z, sc);
+        sc = fmaf(qq.w, kk.w, sc);
+      }
+    }
+    const bool valid = lane < nt;
+    const float sv = valid ? sc * a.attn_scale : -INFINITY;
+    const float mn = fmaxf(m, warp_max(sv));
+    const float corr = expf(m - mn);  // 0 on the first tile (m = -inf)
+    const float p = valid ? expf(sv - mn) : 0.f;
+    lsum = lsum * corr + warp_sum(p);
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) o[e] = fmaf(pj, vr[e], o[e]);
-  }
-  __syncwarp();
-  float* outp = a.attn + (size_t)(g * NREP + warp) * D + lane * DPL;
-  if (at.nsplit == 1) {
+    for (int e = 0; e < DPL; ++e) o[e] *= corr;
+    for (int j = 0; j < nt; ++j) {
+      const float pj = __shfl_sync(0xffffffffu, p, j);
+      const float* vr = Vs + (size_t)j * D + lane * DPL;
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) outp[e] = o[e] / lsum;
-    return true;
+      for (int e = 0; e < DPL; ++e) o[e] = fmaf(pj, vr[e], o[e]);
+    }
+    m = mn;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[slot]);
+    ++st.s;
   }
-  float* pp = a.att_part + (((size_t)g * at.ns_max + sp) * NREP + warp) * (D + 2);
+  float* pp = a.att_part + (((size_t)g * PERSIST_ATT_SPLITS + sp) * NREP + warp) * (D + 4);
 #pragma unroll
   for (int e = 0; e < DPL; ++e) pp[lane * DPL + e] = o[e];
   if (lane == 0) {
     pp[D] = m;
     pp[D + 1] = lsum;
   }
-  csync();
-  if (tid == 0) {
-    __threadfence();
-    const unsigned prev = atomicAdd(&a.att_cnt[g], 1u);
-    sm.flags[1] = (prev == (unsigned)at.nsplit - 1) ? 1 : 0;
-  }
-  csync();
-  if (!sm.flags[1]) return true;
-  __threadfence();
-  // last split: merge the nsplit partials of head `warp` (m, l staged in shared memory)
-  const float* pb = a.att_part + ((size_t)g * at.ns_max * NREP + warp) * (D + 2);
-  const size_t sstride = (size_t)NREP * (D + 2);
-  float* fm = sm.xs + NREP * D + (size_t)warp * 2 * at.ns_max;
-  float M = -INFINITY;
-  for (int q = lane; q < at.nsplit; q += 32) {
-    const float mq = __ldcg(pb + q * sstride + D);
-    fm[q] = mq;
-    fm[at.ns_max + q] = __ldcg(pb + q * sstride + D + 1);
-    M = fmaxf(M, mq);
-  }
-  M = warp_max(M);
-  float Ls = 0.f;
-  for (int q = lane; q < at.nsplit; q += 32) {
-    const float f = expf(fm[q] - M);
-    fm[q] = f;
-    Ls = fmaf(f, fm[at.ns_max + q], Ls);
-  }
-  Ls = warp_sum(Ls);
-  __syncwarp();
-  float acc[DPL];
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) acc[e] = 0.f;
-#pragma unroll 4
-  for (int q = 0; q < at.nsplit; ++q) {
-    const float f = fm[q];
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) acc[e] = fmaf(f, __ldcg(pb + q * sstride + lane * DPL + e), acc[e]);
-  }
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) outp[e] = acc[e] / Ls;
-  if (tid == 0) a.att_cnt[g] = 0u;
   return true;
 }
 
-// Consumer state carried across phases (returned by value from the out-of-line phase bodies).
-struct CState {
-  int s;    // ring stages consumed
-  int bad;  // the step must stop
-};
+// This CTA's attention units of layer l (after the Q phase is published).
+template <int KC, int D>
+__device__ __forceinline__ CState att_units(const PersistArgs& a, const Smem& sm, CState st, int nst, const AttGeo& at,
+                                            int l, int first) {
+  for (int u = first; u < at.items; u += gridDim.x) {
+    const bool ok = att_unit<KC, D>(a, at, l, u, sm, st, nst);
+    csync();  // xs (queries) reused by the next unit
+    if (!ok) {
+      st.bad = 1;
+      break;
+    }
+  }
+  return st;
+}
 
-// This CTA's units of one GEMV phase (after its dependency is met): x -> xs (optional RMSNorm),
-// then the streamed dot products.  Warp w owns row w of every 8-row group, so each warp
-// applies its rows' epilogue itself (its rotate_half partner and its matching up row come from
-// the same warp) and the warps run through the ring independently: no CTA barrier per unit.
-// Shared by every phase kind from one call site, so one copy of the streaming loop stays hot
-// in the instruction cache.
-template <int KC>
+// CPL consecutive bf16 of shared memory -> f32.
+template <int CPL>
+__device__ __forceinline__ void load_bf16(const uint16_t* p, float* out) {
+  if constexpr (CPL == 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    out[0] = bf16lo(v.x); out[1] = bf16hi(v.x); out[2] = bf16lo(v.y); out[3] = bf16hi(v.y);
+    out[4] = bf16lo(v.z); out[5] = bf16hi(v.z); out[6] = bf16lo(v.w); out[7] = bf16hi(v.w);
+  } else if constexpr (CPL == 4) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    out[0] = bf16lo(v.x); out[1] = bf16hi(v.x); out[2] = bf16lo(v.y); out[3] = bf16hi(v.y);
+  } else if constexpr (CPL == 2) {
+    const uint32_t v = *reinterpret_cast<const uint32_t*>(p);
+    out[0] = bf16lo(v); out[1] = bf16hi(v);
+  } else {
+    out[0] = __uint_as_float(((uint32_t)*p) << 16);
+  }
+}
+
+// This CTA's units of a GEMV phase (Q, O, head) after its dependency is met: x -> xs
+// (optional RMSNorm; O: the attention merge), then the streamed dot products.  Warp w owns row
+// w of every 8-row group, so each warp applies its rows' epilogue itself (its rotate_half
+// partner comes from the same warp) and the warps run through the ring independently: no CTA
+// barrier per unit.
+template <int KC, int D>
 __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& sm, CState st, int nst, int kind, int l,
-                                          int pos, int U, int K, int gpu, int first, const float* xsrc,
-                                          const float* norm_w, const float* resid) {
+                                             int pos, int U, int K, int gpu, int first, const float* xsrc,
+                                             const float* norm_w, const float* resid, const AttGeo& at) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x;
   // residual of this warp's row in each of its first PK_RES_UNITS units, fetched together
@@ -523,18 +671,62 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
     const int u = first + k * G;
     resv[k] = (resid != nullptr && lane == 0 && u < U) ? __ldcg(resid + (size_t)u * PK_ROWS + warp) : 0.f;
   }
-  load_x(xsrc, norm_w, K, a.eps, sm);
+  if (kind == PH_O) {
+    if (!att_merge<D>(a, at, sm, st.merges++)) {
+      st.bad = 1;
+      return st;
+    }
+  } else {
+    load_x(xsrc, norm_w, K, a.eps, sm);
+  }
   if (tid == 0) trace_mark(a, kind == PH_HEAD ? a.L * PH_PER_LAYER : l * PH_PER_LAYER + kind, 1);
-  constexpr int NJ = KC / 256;
+  constexpr int NJ = KC / 256, CPL = KC / 256;
+  // MLP: this lane's CPL down_proj accumulators (output columns warp*KC/8 + lane*CPL..) live
+  // in shared memory, xs[H, 2H) being free in this phase
+  float* dacc = sm.xs + a.H + warp * (KC / 8) + lane * CPL;
+  if (kind == PH_M) {
+#pragma unroll
+    for (int e = 0; e < CPL; ++e) dacc[e] = 0.f;
+  }
   float xr[NJ * 8];
   const int nch = K / KC;
   bool lbad = false, first_stage = true;
   float bv = -FLT_MAX;  // head: this warp's running argmax
   int bi = INT_MAX;
+  float* xnext = xbuf(a, l + 1);
   int k = 0;
   for (int u = first; u < U; u += G, ++k) {
     float t[2] = {0.f, 0.f};
     for (int gi = 0; gi < gpu; ++gi) {
+      if (kind == PH_M && gi == 2) {
+        // down_proj column block (mlp.rs:33): every warp needs the unit's 8 silu(gate)*up
+        // values, then accumulates its KC/8 output columns over rows j0..j0+7 of wdt
+        float* mvb = sm.mv + (k & 1) * PK_ROWS;
+        if (lane == 0) mvb[warp] = silu(t[0]) * t[1];  // mlp.rs:31-33
+        csync();
+        const int slot = st.s % nst;
+        if (!lbad && !wait_full(&sm.full[slot], (st.s / nst) & 1, a.err, sm.flags)) lbad = true;
+        if (!lbad) {
+          const uint16_t* wr = sm.ring + (size_t)slot * PK_ROWS * KC + warp * (KC / 8) + lane * CPL;
+          float d[CPL];
+#pragma unroll
+          for (int e = 0; e < CPL; ++e) d[e] = dacc[e];
+#pragma unroll
+          for (int r = 0; r < PK_ROWS; ++r) {
+            const float mr = mvb[r];
+            float wv[CPL];
+            load_bf16<CPL>(wr + r * KC, wv);
+#pragma unroll
+            for (int e = 0; e < CPL; ++e) d[e] = fmaf(mr, wv[e], d[e]);
+          }
+#pragma unroll
+          for (int e = 0; e < CPL; ++e) dacc[e] = d[e];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.empty[slot]);
+        ++st.s;
+        continue;
+      }
       float acc0 = 0.f, acc1 = 0.f;
       for (int c = 0; c < nch; ++c) {
         if (nch > 1 || first_stage) {
@@ -567,7 +759,7 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
     }
     if (tid == 0 && k == 0) trace_mark(a, kind == PH_HEAD ? a.L * PH_PER_LAYER : l * PH_PER_LAYER + kind, 7);
     // ---- this warp's row epilogue (lane 0)
-    if (lbad || lane != 0) continue;
+    if (kind == PH_M || lbad || lane != 0) continue;
     const int row = unit_row(a, kind, u, 0) + warp;
     if (kind == PH_HEAD) {
       if (a.logits) a.logits[row] = t[0];
@@ -595,21 +787,39 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
         dst[ii] = isk ? oa : ya;
         dst[ii + half] = isk ? ob : yb;
       }
-    } else if (kind == PH_GU) {
-      a.act[row] = silu(t[0]) * t[1];  // mlp.rs:31-33
     } else {
-      // o_proj / down_proj + residual (layer.rs:33-38): x1 = x0 + s*o, x0 = x1 + s*down
+      // o_proj + residual (layer.rs:33-38): x1 = x0 + s*o; x1 also seeds the next layer's
+      // residual buffer, into which the MLP phase adds s*down
       float r = 0.f;
 #pragma unroll
       for (int q = 0; q < PK_RES_UNITS; ++q)
         if (q == k) r = resv[q];
       if (k >= PK_RES_UNITS) r = __ldcg(resid + row);
-      (kind == PH_O ? a.x1 : a.x0)[row] = r + t[0] * a.res_scale;
+      const float x1 = r + t[0] * a.res_scale;
+      a.x1[row] = x1;
+      xnext[row] = x1;
     }
   }
   if (kind == PH_HEAD && lane == 0) {
     sm.red[16 + warp] = bv;
     reinterpret_cast<int*>(sm.red)[24 + warp] = bi;
+  }
+  if (kind == PH_M && !lbad && k > 0) {
+    // this CTA's res_scale * down partial into the next layer's residual buffer (seeded with
+    // x1 by the O phase): x0' = x1 + s * down (layer.rs:33-38, 72)
+    float* dst = xnext + warp * (KC / 8) + lane * CPL;
+    const float sc = a.res_scale;
+    if constexpr (CPL >= 4) {
+#pragma unroll
+      for (int e = 0; e < CPL; e += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(dacc + e);
+        red_add_v4(dst + e, sc * v.x, sc * v.y, sc * v.z, sc * v.w);
+      }
+    } else if constexpr (CPL == 2) {
+      red_add_v2(dst, sc * dacc[0], sc * dacc[1]);
+    } else {
+      atomicAdd(dst, sc * dacc[0]);
+    }
   }
   if (sync_or(lbad)) st.bad = 1;
   if (kind == PH_HEAD && tid == 0) {  // CTA best over the warps (ties -> lowest id)
@@ -625,27 +835,6 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
   return st;
 }
 
-// This CTA's attention units of layer l (after the Q phase is published).
-template <int KC, int D>
-__device__ __forceinline__ CState att_units(const PersistArgs& a, const Smem& sm, CState st, int nst, const AttGeo& at,
-                                         int l, int first) {
-  const int lane = threadIdx.x & 31;
-  for (int u = first; u < at.items; u += gridDim.x) {
-    const int slot = st.s % nst;
-    const bool lbad = !wait_full(&sm.full[slot], (st.s / nst) & 1, a.err, sm.flags);
-    float* kv = reinterpret_cast<float*>(sm.ring + (size_t)slot * PK_ROWS * KC);
-    const bool ok = att_unit<D>(a, at, l, u, kv, lbad, sm);
-    if (lane == 0) mbar_arrive(&sm.empty[slot]);
-    ++st.s;
-    csync();  // xs (queries, merge scratch) reused by the next unit
-    if (!ok) {
-      st.bad = 1;
-      break;
-    }
-  }
-  return st;
-}
-
 template <int KC, int D>
 __global__ void __launch_bounds__(PK_THREADS, 1) persist_decode_kernel(const PersistArgs a, int nst, int xs_floats,
                                                                         int att_span) {
@@ -653,12 +842,15 @@ __global__ void __launch_bounds__(PK_THREADS, 1) persist_decode_kernel(const Per
   Smem sm;
   sm.ring = reinterpret_cast<uint16_t*>(smem_raw);
   sm.xs = reinterpret_cast<float*>(smem_raw + (size_t)nst * PK_ROWS * KC * 2);
-  sm.ctab = sm.xs + xs_floats;
+  sm.parts = sm.xs + xs_floats;
+  sm.ctab = sm.parts + persist_att_part_floats(a.nkv, a.nh, D);
   sm.stab = sm.ctab + 64;
   sm.red = sm.stab + 64;
-  sm.flags = reinterpret_cast<volatile int*>(sm.red + 64);
-  sm.full = reinterpret_cast<uint64_t*>(sm.red + 64 + 8);
+  sm.mv = sm.red + 64;
+  sm.flags = reinterpret_cast<volatile int*>(sm.mv + 16);
+  sm.full = reinterpret_cast<uint64_t*>(sm.mv + 16 + 8);
   sm.empty = sm.full + nst;
+  sm.pbar = sm.empty + nst;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int G = gridDim.x;
@@ -666,16 +858,21 @@ __global__ void __launch_bounds__(PK_THREADS, 1) persist_decode_kernel(const Per
   at.pos = *a.pos;  // position of the token being decoded (advanced by this launch)
   at.len = at.pos + 1;
   at.span = att_span;
-  at.nsplit = (at.len + att_span - 1) / att_span;
-  at.ns_max = (a.s_max + att_span - 1) / att_span;
+  at.ntiles = (at.len + att_span - 1) / att_span;
+  at.nsplit = min(at.ntiles, PERSIST_ATT_SPLITS);
+  at.tps = (at.ntiles + at.nsplit - 1) / at.nsplit;
+  at.nsplit = (at.ntiles + at.tps - 1) / at.tps;
   at.items = a.nkv * at.nsplit;
   const int pos = at.pos;
 
+  for (int i = tid; i < a.L * (int)(sizeof(PersistLayer) / 8); i += PK_THREADS)
+    reinterpret_cast<unsigned long long*>(s_lay)[i] = reinterpret_cast<const unsigned long long*>(a.layers)[i];
   if (tid == 0) {
     for (int i = 0; i < nst; ++i) {
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], PK_CWARPS);
     }
+    mbar_init(sm.pbar, 1);
     for (int i = 0; i < 8; ++i) sm.flags[i] = 0;
     sm.red[48] = -FLT_MAX;  // running argmax of the head (value, index)
     reinterpret_cast<int*>(sm.red)[49] = INT_MAX;
@@ -698,7 +895,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) persist_decode_kernel(const Per
     sm.stab[tid] = (float)(sd * a.rope->scaling_factor);
   }
 
-  CState st = {0, 0};
+  CState st = {0, 0, 0};
   int off = 0;
   const unsigned* prev_cnt = nullptr;
   unsigned prev_target = 0;
@@ -720,11 +917,12 @@ __global__ void __launch_bounds__(PK_THREADS, 1) persist_decode_kernel(const Per
         if (tid == 0) trace_mark(a, ph, 1);
         st = att_units<KC, D>(a, sm, st, nst, at, l, first);
       } else {
-        const PersistLayer* w = a.layers + (l < a.L ? l : 0);
-        const float* xsrc = kind == PH_O ? a.attn : kind == PH_GU ? a.x1 : kind == PH_D ? a.act : a.x0;
-        const float* norm_w = kind == PH_Q ? w->ln_in : kind == PH_GU ? w->ln_post : head ? a.final_norm : nullptr;
-        const float* resid = kind == PH_O ? a.x0 : kind == PH_D ? a.x1 : nullptr;
-        st = gemv_units<KC>(a, sm, st, nst, kind, l, pos, g.U, g.K, g.gpu, first, xsrc, norm_w, resid);
+        const PersistLayer* w = s_lay + (l < a.L ? l : 0);
+        // Q: the layer input; M: x1; head: the last layer's output (O merges attention)
+        const float* xsrc = kind == PH_M ? a.x1 : xbuf(a, l);
+        const float* norm_w = kind == PH_Q ? w->ln_in : kind == PH_M ? w->ln_post : head ? a.final_norm : nullptr;
+        const float* resid = kind == PH_O ? xbuf(a, l) : nullptr;
+        st = gemv_units<KC, D>(a, sm, st, nst, kind, l, pos, g.U, g.K, g.gpu, first, xsrc, norm_w, resid, at);
       }
       if (tid == 0) trace_mark(a, ph, 5);
       if (st.bad) break;
@@ -823,6 +1021,21 @@ __global__ void __launch_bounds__(PK_THREADS, 1) persist_decode_kernel(const Per
   }
 }
 
+__global__ void transpose_u16_kernel(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, int R, int C) {
+  __shared__ uint16_t tile[32][33];
+  const int c = blockIdx.x * 32 + threadIdx.x;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int r = blockIdx.y * 32 + i;
+    if (r < R && c < C) tile[i][threadIdx.x] = src[(size_t)r * C + c];
+  }
+  __syncthreads();
+  const int r2 = blockIdx.y * 32 + threadIdx.x;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int c2 = blockIdx.x * 32 + i;
+    if (c2 < C && r2 < R) dst[(size_t)c2 * R + r2] = tile[threadIdx.x][i];
+  }
+}
+
 int pick_kc(int H, int I, int qd) {
   for (int kc : {2048, 1024, 512, 256})
     if (H % kc == 0 && I % kc == 0 && qd % kc == 0) return kc;
@@ -834,18 +1047,26 @@ struct PkShape {
   size_t smem = 0;
 };
 
-PkShape shape_of(int H, int I, int nh, int d, int s_max, int nst_cap) {
+// Ring depth: about 128 KB of copies in flight per SM streams HBM fastest (4 x 32 KB measured
+// 7.4 TB/s over 148 SMs; 6 x 32 KB 6.9 TB/s).  nst_cap > 1 overrides it.
+constexpr int PK_RING_BYTES = 131072;
+
+PkShape shape_of(int H, int I, int nh, int nkv, int d, int nst_cap) {
   PkShape p;
   p.kc = pick_kc(H, I, nh * d);
   p.d = d;
-  if (!p.kc || d <= 0) return p;
+  if (!p.kc || d <= 0 || nkv <= 0) return p;
   p.span = std::min(32, 2 * p.kc / d);  // K and V rows of `span` positions fill one ring stage
-  const int ns_max = (s_max + p.span - 1) / p.span;
-  const int m = std::max(std::max(H, I), std::max(nh * d, 8 * d + 16 * ns_max));
+  // xs holds the largest input vector; the MLP phase also keeps its down_proj accumulators
+  // in xs[H, 2H)
+  const int m = std::max(std::max(2 * H, I), std::max(nh * d, NREP * d));
   p.xs_floats = (m + 3) & ~3;
-  const int fixed = p.xs_floats * 4 + PK_MISC_FLOATS * 4 + 32;
-  p.nst = std::min(nst_cap > 1 ? nst_cap : 64, (PK_MAX_SMEM - fixed) / (16 * p.kc + 16));
-  p.smem = (size_t)p.nst * 16 * p.kc + fixed + 16 * (size_t)p.nst;
+  const size_t fixed = (size_t)p.xs_floats * 4 + persist_att_part_floats(nkv, nh, d) * 4 + PK_MISC_FLOATS * 4 + 32 + 8;
+  const int stage = PK_ROWS * p.kc * 2;
+  const int want = nst_cap > 1 ? nst_cap : std::max(2, PK_RING_BYTES / stage);
+  const int fit = (int)(((size_t)PK_MAX_SMEM - fixed) / (stage + 16));
+  p.nst = std::min(want, fit);
+  p.smem = (size_t)p.nst * stage + fixed + 16 * (size_t)p.nst;
   return p;
 }
 
@@ -872,22 +1093,19 @@ KernelFn kernel_of(int kc, int d) {
 
 }  // namespace
 
-bool persist_supported(int H, int I, int nh, int nkv, int d, int V, int s_max) {
-  if (nkv <= 0 || nh != 8 * nkv || (d != 64 && d != 128) || V <= 0 || V % PK_ROWS != 0 || s_max <= 0) return false;
-  if (H > PK_XREG * PK_CTHREADS * 4) return false;  // normalised inputs are [H]
-  const PkShape p = shape_of(H, I, nh, d, s_max, 0);
-  return p.kc != 0 && p.nst >= 2 && p.span >= 1;
+bool persist_supported(int L, int H, int I, int nh, int nkv, int d, int V, int s_max) {
+  if (L <= 0 || L > PK_MAX_LAYERS) return false;
+  if (nkv <= 0 || nh != NREP * nkv || (d != 64 && d != 128) || V <= 0 || V % PK_ROWS != 0 || s_max <= 0) return false;
+  if (I % PK_ROWS != 0) return false;
+  static_assert(sizeof(PersistLayer) % 8 == 0, "layer table copied in 8-byte words");
+  const PkShape p = shape_of(H, I, nh, nkv, d, 0);
+  // the fused MLP phase keeps one K chunk of H per row: H must equal the chunk
+  return p.kc != 0 && p.kc == H && p.nst >= 2 && p.span >= 1;
 }
 
-size_t persist_att_part_floats(int nkv, int nh, int d, int H, int I, int s_max) {
-  const PkShape p = shape_of(H, I, nh, d, s_max, 0);
-  if (!p.span) return 0;
-  return (size_t)nkv * ((s_max + p.span - 1) / p.span) * (nh / nkv) * (d + 2);
-}
-
-int persist_configure(int H, int I, int nh, int nkv, int d, int s_max, int nst_cap) {
-  (void)nkv;
-  const PkShape p = shape_of(H, I, nh, d, s_max, nst_cap);
+int persist_configure(int H, int I, int nh, int nkv, int d, int s_max, int nst_cap, int grid_cap) {
+  (void)s_max;
+  const PkShape p = shape_of(H, I, nh, nkv, d, nst_cap);
   KernelFn fn = kernel_of(p.kc, d);
   if (!fn || p.nst < 2) return 0;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem) != cudaSuccess) {
@@ -902,11 +1120,12 @@ int persist_configure(int H, int I, int nh, int nkv, int d, int s_max, int nst_c
     return 0;
   }
   if (per_sm < 1) return 0;
-  return std::min(sms, 4096);  // one CTA per SM (am_part holds 4096 partials)
+  // one CTA per SM (am_part holds 4096 partials), at most grid_cap
+  return std::min(std::min(sms, 4096), grid_cap > 0 ? grid_cap : sms);
 }
 
 cudaError_t launch_persist(const PersistArgs& a, int grid, int nst_cap, cudaStream_t st, bool cooperative) {
-  const PkShape p = shape_of(a.H, a.I, a.nh, a.d, a.s_max, nst_cap);
+  const PkShape p = shape_of(a.H, a.I, a.nh, a.nkv, a.d, nst_cap);
   KernelFn fn = kernel_of(p.kc, a.d);
   if (!fn || grid <= 0) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
@@ -921,6 +1140,14 @@ cudaError_t launch_persist(const PersistArgs& a, int grid, int nst_cap, cudaStre
   cfg.numAttrs = cooperative ? 1 : 0;
   count_launch();
   return cudaLaunchKernelEx(&cfg, fn, a, p.nst, p.xs_floats, p.span);
+}
+
+cudaError_t transpose_bf16(const uint16_t* src, uint16_t* dst, int R, int C, cudaStream_t st) {
+  if (R <= 0 || C <= 0) return cudaErrorInvalidValue;
+  const dim3 grid((C + 31) / 32, (R + 31) / 32);
+  count_launch();
+  transpose_u16_kernel<<<grid, dim3(32, 8), 0, st>>>(src, dst, R, C);
+  return cudaGetLastError();
 }
 
 }  // namespace vx

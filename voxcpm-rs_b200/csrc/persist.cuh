@@ -14,10 +14,16 @@ struct PersistLayer {
   const uint16_t* wqkv;  // [(nh+2nkv)*d, H]
   const uint16_t* wo;    // [H, nh*d]
   const uint16_t* wgu;   // [2I, H]
-  const uint16_t* wd;    // [H, I]
+  const uint16_t* wdt;   // [I, H]: down_proj transposed (row j = the weights input j feeds)
   const float* ln_in;    // [H]
   const float* ln_post;  // [H]
 };
+
+// Phases per decoder layer: qkv+rope, attention, o_proj, MLP (gate|up + down); then the head.
+constexpr int PERSIST_PHASES_PER_LAYER = 4;
+// Attention splits per KV head (each split covers whole 32-position tiles); the O phase
+// stages all partials of a layer in shared memory.
+constexpr int PERSIST_ATT_SPLITS = 8;
 
 struct PersistArgs {
   int L, H, I, nh, nkv, d, V, s_max;
@@ -32,19 +38,23 @@ struct PersistArgs {
   int* pos;                    // device position of the token being decoded (incremented)
   int* step;                   // device greedy step index (incremented)
   int* tokens;                 // picked ids, tokens[*step]
-  float* x0;                   // residual stream [H]: input of each layer, output of its MLP
+  float* x0;                   // residual stream [H], buffer 0: input of even layers; receives
+                               // the next token's embedding
+  float* x0b;                  // residual stream [H], buffer 1: input of odd layers
   float* x1;                   // residual stream after attention [H]
   float* q;                    // post-RoPE queries [nh*d]
-  float* attn;                 // attention output [nh*d]
-  float* act;                  // silu(gate)*up [I]
   float* logits;               // optional [V]
   float* hid_norm;             // final-norm hidden [H]
-  float* att_part;             // [nkv][ceil(s_max/span)][nh/nkv][d+2] split partials
-  unsigned* att_cnt;           // [nkv] split arrival counters (self-resetting)
+  float* att_part;             // [nkv][PERSIST_ATT_SPLITS][nh/nkv][d+4] split partials (o, m, l)
   float2* am_part;             // [grid] per-CTA argmax partials
-  unsigned* phase_cnt;         // [5L + 2] phase arrival counters, zero between launches
+  unsigned* phase_cnt;         // [4L + 2] phase arrival counters, zero between launches
   int* err;                    // device error word
-  // Optional phase trace (nullptr: off): per phase p (5 per layer, then the head) and CTA c,
+  // L2 staging ahead of the shared-memory ring: the producer issues L2 prefetches for the
+  // stages pf_stages beyond its newest ring copy (0: off).  evict_first: weight copies into
+  // the ring mark their L2 lines evict-first.
+  int pf_stages;
+  int evict_first;
+  // Optional phase trace (nullptr: off): per phase p (4 per layer, then the head) and CTA c,
   // trace[(p * grid + c) * PERSIST_TRACE_FIELDS + k] = %globaltimer ns at k = 0 consumer
   // phase start, 1 inputs ready (dependency met, x loaded), 2 phase published, 3 producer's
   // first copy of the phase issued, 4 its last copy issued, 5 last unit computed, 6 first
@@ -54,18 +64,23 @@ struct PersistArgs {
 };
 
 constexpr int PERSIST_TRACE_FIELDS = 8;
-inline size_t persist_trace_entries(int L, int grid) { return ((size_t)5 * L + 1) * grid * PERSIST_TRACE_FIELDS; }
+inline size_t persist_phase_count(int L) { return (size_t)PERSIST_PHASES_PER_LAYER * L + 1; }
+inline size_t persist_trace_entries(int L, int grid) { return persist_phase_count(L) * grid * PERSIST_TRACE_FIELDS; }
 
 // Sizes of the device buffers the caller provides.
-inline size_t persist_counter_count(int L) { return (size_t)5 * L + 2; }
-size_t persist_att_part_floats(int nkv, int nh, int d, int H, int I, int s_max);
+inline size_t persist_counter_count(int L) { return (size_t)PERSIST_PHASES_PER_LAYER * L + 2; }
+__host__ __device__ inline size_t persist_att_part_floats(int nkv, int nh, int d) {
+  return (size_t)nkv * PERSIST_ATT_SPLITS * (nh / (nkv > 0 ? nkv : 1)) * (d + 4);
+}
 
 // Whether the persistent step supports this model shape (else the per-kernel step is used).
-bool persist_supported(int H, int I, int nh, int nkv, int d, int V, int s_max);
+bool persist_supported(int L, int H, int I, int nh, int nkv, int d, int V, int s_max);
 // Once per context, before capture: raise the kernel's shared-memory limit and return the
-// grid (one CTA per SM) or 0 when the device cannot hold it.  nst_cap (> 1) caps the ring
-// depth in stages (0: as deep as shared memory allows).
-int persist_configure(int H, int I, int nh, int nkv, int d, int s_max, int nst_cap);
+// grid (one CTA per SM, at most grid_cap when > 0) or 0 when the device cannot hold it.
+// nst_cap (> 1) sets the ring depth in stages (0: about 128 KB of stages).
+int persist_configure(int H, int I, int nh, int nkv, int d, int s_max, int nst_cap, int grid_cap);
 cudaError_t launch_persist(const PersistArgs& a, int grid, int nst_cap, cudaStream_t st, bool cooperative);
+// dst [C, R] = transpose of src [R, C] (bf16 bit patterns); used to lay down_proj out as wdt.
+cudaError_t transpose_bf16(const uint16_t* src, uint16_t* dst, int R, int C, cudaStream_t st);
 
 }  // namespace vx
