@@ -303,6 +303,8 @@ cudaError_t enqueue_persist_step(vx_lm* lm, cudaStream_t st, bool cooperative,
   a.trace = trace;
   a.pf_stages = lm->ctx->persist_pf;
   a.evict_first = lm->ctx->persist_ef;
+  a.inflight = lm->ctx->persist_inflight;
+  a.mlp_pf = lm->ctx->persist_mlp_pf;
   return launch_persist(a, lm->pk_grid, lm->ctx->persist_nst, st, cooperative);
 }
 

@@ -371,6 +371,29 @@ __device__ void produce(const PersistArgs& a, const Smem& sm, int nst, const Att
         if (!ok) break;
       }
     }
+    // Pacing: at most a.inflight copies issued and not yet landed, so the memory system stays
+    // near its unloaded latency and the other ring slots hold landed stages that carry the
+    // stream through the consumers' pauses (input loads, publish fences, merges).
+    if (a.inflight > 0 && s >= a.inflight) {
+      const int o = s - a.inflight;
+      if (!mbar_try_wait(&sm.full[o % nst], (o / nst) & 1)) {
+        const long long t0 = clock64();
+        while (true) {
+          if (sm.flags[0]) {
+            ok = false;
+            break;
+          }
+          if (mbar_try_wait(&sm.full[o % nst], (o / nst) & 1)) break;
+          if (clock64() - t0 > kWaitLimitCycles) {
+            record_error(a.err, VX_DEVICE_ERR_TIMEOUT);
+            sm.flags[3] = 1;
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
+      }
+    }
     const int ph = cursor_phase(a, cp);
     if (ph != last_phase) {
       if (last_phase >= 0) trace_mark(a, last_phase, 4);
@@ -652,6 +675,25 @@ __device__ __forceinline__ void load_bf16(const uint16_t* p, float* out) {
   }
 }
 
+// L2 line prefetches (load/store path, no data returned) of MLP stages [s0, s1) of this
+// CTA in layer l: stage q is unit first_m + (q / 3) * grid, group q % 3 (gate rows, up rows,
+// rows of the transposed down weight), 32 KB contiguous; each consumer thread takes one 128 B
+// line of each stage.  Issued while the warps wait on an earlier phase, so the MLP phase
+// finds most of its weights in L2 instead of waiting on HBM behind the ring.
+template <int KC>
+__device__ __forceinline__ void prefetch_mlp(const PersistArgs& a, int l, int first_m, int s0, int s1) {
+  const int U = a.I / PK_ROWS, G = gridDim.x;
+  for (int q = s0; q < s1; ++q) {
+    const int u = first_m + (q / 3) * G, gi = q % 3;
+    if (u >= U) break;
+    const uint16_t* W = gi == 2 ? s_lay[l].wdt : s_lay[l].wgu;
+    const char* src = reinterpret_cast<const char*>(W + (size_t)unit_row(a, PH_M, u, gi) * a.H);
+    const int lines = PK_ROWS * KC * 2 / 128;
+    for (int i = threadIdx.x; i < lines; i += PK_CTHREADS)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(src + (size_t)i * 128));
+  }
+}
+
 // This CTA's units of a GEMV phase (Q, O, head) after its dependency is met: x -> xs
 // (optional RMSNorm; O: the attention merge), then the streamed dot products.  Warp w owns row
 // w of every 8-row group, so each warp applies its rows' epilogue itself (its rotate_half
@@ -688,24 +730,33 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
 #pragma unroll
     for (int e = 0; e < CPL; ++e) dacc[e] = 0.f;
   }
+  // x slice of this lane (one K chunk per row: K == KC), loaded once for the phase
   float xr[NJ * 8];
-  const int nch = K / KC;
-  bool lbad = false, first_stage = true;
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const float4 v0 = *reinterpret_cast<const float4*>(sm.xs + j * 256 + lane * 8);
+    const float4 v1 = *reinterpret_cast<const float4*>(sm.xs + j * 256 + lane * 8 + 4);
+    xr[j * 8 + 0] = v0.x; xr[j * 8 + 1] = v0.y; xr[j * 8 + 2] = v0.z; xr[j * 8 + 3] = v0.w;
+    xr[j * 8 + 4] = v1.x; xr[j * 8 + 5] = v1.y; xr[j * 8 + 6] = v1.z; xr[j * 8 + 7] = v1.w;
+  }
+  (void)K;
+  int slot = st.s % nst;  // ring position, advanced incrementally
+  uint32_t par = (st.s / nst) & 1;
+  bool lbad = false;
   float bv = -FLT_MAX;  // head: this warp's running argmax
   int bi = INT_MAX;
   float* xnext = xbuf(a, l + 1);
   int k = 0;
   for (int u = first; u < U; u += G, ++k) {
-    float t[2] = {0.f, 0.f};
+    float t0 = 0.f, t1 = 0.f;
     for (int gi = 0; gi < gpu; ++gi) {
       if (kind == PH_M && gi == 2) {
         // down_proj column block (mlp.rs:33): every warp needs the unit's 8 silu(gate)*up
         // values, then accumulates its KC/8 output columns over rows j0..j0+7 of wdt
         float* mvb = sm.mv + (k & 1) * PK_ROWS;
-        if (lane == 0) mvb[warp] = silu(t[0]) * t[1];  // mlp.rs:31-33
+        if (lane == 0) mvb[warp] = silu(t0) * t1;  // mlp.rs:31-33
         csync();
-        const int slot = st.s % nst;
-        if (!lbad && !wait_full(&sm.full[slot], (st.s / nst) & 1, a.err, sm.flags)) lbad = true;
+        if (!lbad && !wait_full(&sm.full[slot], par, a.err, sm.flags)) lbad = true;
         if (!lbad) {
           const uint16_t* wr = sm.ring + (size_t)slot * PK_ROWS * KC + warp * (KC / 8) + lane * CPL;
           float d[CPL];
@@ -724,53 +775,59 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.empty[slot]);
+        if (++slot == nst) {
+          slot = 0;
+          par ^= 1u;
+        }
         ++st.s;
         continue;
       }
       float acc0 = 0.f, acc1 = 0.f;
-      for (int c = 0; c < nch; ++c) {
-        if (nch > 1 || first_stage) {
+      if (!lbad && !wait_full(&sm.full[slot], par, a.err, sm.flags)) lbad = true;
+      if (!lbad) {
+        const uint4* wr = reinterpret_cast<const uint4*>(sm.ring + (size_t)slot * PK_ROWS * KC + warp * KC);
 #pragma unroll
-          for (int j = 0; j < NJ; ++j) {
-            const float4 v0 = *reinterpret_cast<const float4*>(sm.xs + c * KC + j * 256 + lane * 8);
-            const float4 v1 = *reinterpret_cast<const float4*>(sm.xs + c * KC + j * 256 + lane * 8 + 4);
-            xr[j * 8 + 0] = v0.x; xr[j * 8 + 1] = v0.y; xr[j * 8 + 2] = v0.z; xr[j * 8 + 3] = v0.w;
-            xr[j * 8 + 4] = v1.x; xr[j * 8 + 5] = v1.y; xr[j * 8 + 6] = v1.z; xr[j * 8 + 7] = v1.w;
-          }
-          first_stage = false;
+        for (int j = 0; j < NJ; j += 2) {
+          acc0 = dot8(wr[j * 32 + lane], &xr[j * 8], acc0);
+          if (j + 1 < NJ) acc1 = dot8(wr[(j + 1) * 32 + lane], &xr[(j + 1) * 8], acc1);
         }
-        const int slot = st.s % nst;
-        if (!lbad && !wait_full(&sm.full[slot], (st.s / nst) & 1, a.err, sm.flags)) lbad = true;
-        if (tid == 0 && k == 0 && gi == 0 && c == 0)
-          trace_mark(a, kind == PH_HEAD ? a.L * PH_PER_LAYER : l * PH_PER_LAYER + kind, 6);
-        if (!lbad) {
-          const uint4* wr = reinterpret_cast<const uint4*>(sm.ring + (size_t)slot * PK_ROWS * KC + warp * KC);
-#pragma unroll
-          for (int j = 0; j < NJ; j += 2) {
-            acc0 = dot8(wr[j * 32 + lane], &xr[j * 8], acc0);
-            if (j + 1 < NJ) acc1 = dot8(wr[(j + 1) * 32 + lane], &xr[(j + 1) * 8], acc1);
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.empty[slot]);
-        ++st.s;
       }
-      t[gi] = warp_sum(acc0 + acc1);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.empty[slot]);
+      if (++slot == nst) {
+        slot = 0;
+        par ^= 1u;
+      }
+      ++st.s;
+      // the lane partials of a unit's two row groups (rotate_half pair, gate and up) are
+      // reduced together, two interleaved shuffle chains instead of two in a row
+      if (gi == 0) t0 = acc0 + acc1;
+      else t1 = acc0 + acc1;
+      if (gi == 1 || gpu == 1) {
+        if (gpu == 1) {
+          t0 = warp_sum(t0);
+        } else {
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            t0 += __shfl_xor_sync(0xffffffffu, t0, o);
+            t1 += __shfl_xor_sync(0xffffffffu, t1, o);
+          }
+        }
+      }
     }
-    if (tid == 0 && k == 0) trace_mark(a, kind == PH_HEAD ? a.L * PH_PER_LAYER : l * PH_PER_LAYER + kind, 7);
     // ---- this warp's row epilogue (lane 0)
     if (kind == PH_M || lbad || lane != 0) continue;
     const int row = unit_row(a, kind, u, 0) + warp;
     if (kind == PH_HEAD) {
-      if (a.logits) a.logits[row] = t[0];
-      if (better(t[0], row, bv, bi)) {
-        bv = t[0];
+      if (a.logits) a.logits[row] = t0;
+      if (better(t0, row, bv, bi)) {
+        bv = t0;
         bi = row;
       }
     } else if (kind == PH_Q) {
       // LongRoPE on q/k rows (rope.rs:76-95), post-RoPE k and v into the cache at `pos`
       const int head = row / a.d, ii = row % a.d, half = a.d / 2;
-      const float ya = t[0], yb = t[1];
+      const float ya = t0, yb = t1;
       float oa = ya, ob = yb;
       if (head < a.nh + a.nkv && a.rope != nullptr) {
         const float c = sm.ctab[ii], sn = sm.stab[ii];
@@ -795,7 +852,7 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
       for (int q = 0; q < PK_RES_UNITS; ++q)
         if (q == k) r = resv[q];
       if (k >= PK_RES_UNITS) r = __ldcg(resid + row);
-      const float x1 = r + t[0] * a.res_scale;
+      const float x1 = r + t0 * a.res_scale;
       a.x1[row] = x1;
       xnext[row] = x1;
     }
@@ -907,6 +964,14 @@ __global__ void __launch_bounds__(PK_THREADS, 1) persist_decode_kernel(const Per
     const Geo g = geo_of(a, l, kind, at);
     unsigned* cnt = a.phase_cnt + ph;
     const int first = first_unit(off, G);
+    // while this phase waits on the previous one, stage a share of the coming MLP phase's
+    // weights in L2 (Q, ATT, O phases each take the next a.mlp_pf stages after the ring's)
+    if (a.mlp_pf > 0 && !head && kind != PH_M) {
+      int off_m = off;
+      for (int k2 = kind; k2 < PH_M; ++k2) off_m += geo_of(a, l, k2, at).U;
+      const int s0 = nst + kind * a.mlp_pf;
+      prefetch_mlp<KC>(a, l, first_unit(off_m % G, G), s0, s0 + a.mlp_pf);
+    }
     if (first < g.U) {
       if (tid == 0) trace_mark(a, ph, 0);
       if (prev_cnt != nullptr && !dep_wait(prev_cnt, prev_target, a.err, false)) {
@@ -1057,9 +1122,9 @@ PkShape shape_of(int H, int I, int nh, int nkv, int d, int nst_cap) {
   p.d = d;
   if (!p.kc || d <= 0 || nkv <= 0) return p;
   p.span = std::min(32, 2 * p.kc / d);  // K and V rows of `span` positions fill one ring stage
-  // xs holds the largest input vector; the MLP phase also keeps its down_proj accumulators
-  // in xs[H, 2H)
-  const int m = std::max(std::max(2 * H, I), std::max(nh * d, NREP * d));
+  // xs holds an input vector (x, normalised x1, or the attention output); the MLP phase also
+  // keeps its down_proj accumulators in xs[H, 2H)
+  const int m = std::max(2 * H, std::max(nh * d, NREP * d));
   p.xs_floats = (m + 3) & ~3;
   const size_t fixed = (size_t)p.xs_floats * 4 + persist_att_part_floats(nkv, nh, d) * 4 + PK_MISC_FLOATS * 4 + 32 + 8;
   const int stage = PK_ROWS * p.kc * 2;
@@ -1099,8 +1164,9 @@ bool persist_supported(int L, int H, int I, int nh, int nkv, int d, int V, int s
   if (I % PK_ROWS != 0) return false;
   static_assert(sizeof(PersistLayer) % 8 == 0, "layer table copied in 8-byte words");
   const PkShape p = shape_of(H, I, nh, nkv, d, 0);
-  // the fused MLP phase keeps one K chunk of H per row: H must equal the chunk
-  return p.kc != 0 && p.kc == H && p.nst >= 2 && p.span >= 1;
+  // every row is one K chunk (the streaming loop keeps that chunk of x in registers): the
+  // chunk must equal H and the attention width nh*d
+  return p.kc != 0 && p.kc == H && nh * d == H && p.nst >= 2 && p.span >= 1;
 }
 
 int persist_configure(int H, int I, int nh, int nkv, int d, int s_max, int nst_cap, int grid_cap) {

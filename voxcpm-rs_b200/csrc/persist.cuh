@@ -54,6 +54,10 @@ struct PersistArgs {
   // the ring mark their L2 lines evict-first.
   int pf_stages;
   int evict_first;
+  // Ring copies in flight (issued, not landed) at most; 0: as many as there are free slots.
+  int inflight;
+  // MLP stages each of the Q, ATT and O phases prefetches into L2 for the layer's MLP phase.
+  int mlp_pf;
   // Optional phase trace (nullptr: off): per phase p (4 per layer, then the head) and CTA c,
   // trace[(p * grid + c) * PERSIST_TRACE_FIELDS + k] = %globaltimer ns at k = 0 consumer
   // phase start, 1 inputs ready (dependency met, x loaded), 2 phase published, 3 producer's

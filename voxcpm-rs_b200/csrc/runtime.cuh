@@ -77,6 +77,8 @@ struct vx_ctx {
   bool persist = true;               // batch-1 decode step as one persistent launch (env VX_PERSIST=0: 141 launches)
   int persist_nst = 0;               // its ring depth cap in stages, 0 = shared-memory limit (env VX_PERSIST_NST)
   int persist_grid = 0;              // its CTA count cap (env VX_PERSIST_GRID), 0 = one CTA per SM
+  int persist_inflight = 0;          // its ring copies in flight cap (env VX_PERSIST_INFLIGHT), 0 = none
+  int persist_mlp_pf = 0;            // its MLP stages staged in L2 per earlier phase (env VX_PERSIST_MLP_PF)
   int persist_pf = 0;                // its L2 prefetch distance beyond the ring, in stages (env VX_PERSIST_PF)
   int persist_ef = 0;                // its weight copies mark L2 lines evict-first (env VX_PERSIST_EF)
                                      // (env VX_L2_PREFETCH=1; measured: no gain with separate kernels)
