@@ -402,6 +402,57 @@ def run_lm_only(layers=LAYERS):
     return 0
 
 
+def run_phase_trace(pos=200, layers=LAYERS):
+    """Phase trace of one persistent decode step of the LM-decode model at position `pos`
+    (vx_lm_trace_decode_step): per phase kind, medians over layers 2..L-2 of the time after
+    the previous phase was published at which the median CTA had its inputs, finished its
+    last unit and published, and the phase duration (microseconds)."""
+    import numpy as np
+    import torch
+    from __graft_entry__ import load_package
+    load_package()
+    from voxcpm_rs_b200 import synth
+    from voxcpm_rs_b200._lib import check, lib
+    from voxcpm_rs_b200.minicpm4 import Context, MiniCpmModel
+    global LAYERS
+    LAYERS = layers
+    ctx = Context(0)
+    model = MiniCpmModel(ctx, lm_config(), None, max_length=MAX_LEN)
+    load_device_weights(model, device_weights(1234, "cuda:0"))
+    model.greedy(synth.prompt_ids(PROMPT, VOCAB, seed=0), 8)
+    torch.cuda.synchronize()
+    nph = 4 * layers + 1
+    n = nph * 4096 * 8
+    buf = (ctypes.c_ulonglong * n)()
+    grid = ctypes.c_int()
+    for _ in range(3):
+        check(lib().vx_lm_trace_decode_step(model.h, pos, buf, n, ctypes.byref(grid)), ctx.h)
+    G = grid.value
+    t = np.frombuffer(buf, dtype=np.uint64)[:nph * G * 8].reshape(nph, G, 8).astype(np.int64)
+    tt = np.where(t > 0, (t - t[t > 0].min()) / 1000.0, np.nan)
+    pub = [np.nanmax(tt[p, :, 2]) if p < nph - 1 else np.nanmax(tt[p, :, 5]) for p in range(nph)]
+    out = {}
+    for k, name in enumerate(["qkv_rope", "attention", "o_proj", "mlp", "head"]):
+        ps = [nph - 1] if name == "head" else [p for p in range(nph - 1) if p % 4 == k and 2 <= p // 4 < layers - 1]
+        rows = []
+        for p in ps:
+            a = tt[p]
+            has = ~np.isnan(a[:, 0])
+            prev = pub[p - 1]
+            rows.append([pub[p] - prev, np.median(a[has, 1] - prev), np.median(a[has, 5] - prev),
+                         np.max(a[has, 5] - prev), np.median(a[has, 2] - prev) if name != "head" else np.nan,
+                         int(has.sum())])
+        r = np.median(np.array(rows, dtype=np.float64), axis=0)
+        out[name] = {"duration_us": round(r[0], 2), "inputs_ready_us": round(r[1], 2),
+                     "last_unit_median_us": round(r[2], 2), "last_unit_max_us": round(r[3], 2),
+                     "published_us": None if name == "head" else round(r[4], 2), "ctas": int(r[5])}
+    print(json.dumps({"phase_trace": out, "position": pos, "grid": G, "layers": layers,
+                      "step_us": round(float(np.nanmax(tt)), 1)}))
+    model.close()
+    ctx.close()
+    return 0
+
+
 def run_cfm_only():
     """Small profiling case: the LocDiT CFM solve (8 layers, hidden 1024, CFG 2.0, 10 uniform
     Euler steps, B=1) run twice (the first call captures the solve graph)."""
@@ -446,11 +497,15 @@ def main():
                     help="profiling case: the LM-decode model, two greedy runs of 32 decode steps each")
     ap.add_argument("--lm-layers", type=int, default=LAYERS,
                     help="decoder layers of the --lm-only case (fewer for an ncu capture)")
+    ap.add_argument("--phase-trace", type=int, default=None, metavar="POS",
+                    help="print the phase trace of one persistent decode step at position POS")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
     if args.kernel_only:
         return run_kernel_only()
+    if args.phase_trace is not None:
+        return run_phase_trace(args.phase_trace, args.lm_layers)
     if args.lm_only:
         return run_lm_only(args.lm_layers)
     if args.cfm_only:
