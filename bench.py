@@ -34,6 +34,7 @@ sys.path.insert(0, ROOT)
 
 LAYERS, HIDDEN, INTER, NH, NKV, HD, VOCAB = 28, 2048, 6144, 16, 2, 128, 73448
 PROMPT, STEPS_PER_UTT, MAX_LEN = 64, 256, 4096
+SYN_B = 8  # utterances resident per GPU in the batched-synthesis side figure
 BASELINE_METRIC = "LM decode tok/s/GPU, audio-s/s at 1/2/4/8 B200; fused-op HBM GB/s vs peak"
 
 # Algorithmic bytes (the roofline basis): bf16 weights of one decoder layer, the tied
@@ -544,7 +545,8 @@ def main():
     ctx = Context(local)
     cfg = lm_config()
     w = device_weights(1234 + rank, device)
-    model = MiniCpmModel(ctx, cfg, None, max_batch=1, max_length=MAX_LEN)
+    # batch capacity for the batched-synthesis side figure; the headline decode uses row 0
+    model = MiniCpmModel(ctx, cfg, None, max_batch=1 if args.no_extras else SYN_B, max_length=MAX_LEN)
     load_device_weights(model, w)
     prompt = synth.prompt_ids(PROMPT, VOCAB, seed=rank)
     prompt_pinned = torch.from_numpy(prompt).pin_memory()
@@ -643,6 +645,21 @@ def main():
                                            "(rates 2,5,8,8; 16 kHz)",
                                "audio_seconds_per_utterance": audio_s, "wall_s": e2e_s,
                                "audio_s_per_s": world * audio_s / e2e_s, "n_gpus": world}
+        # the same synthesis for SYN_B utterances resident per GPU (vx_generate_batch: the LM
+        # decodes them as SYN_B rows of one step, each patch's CFM solve runs 2*SYN_B DiT rows)
+        rng_b = np.random.default_rng(200 + rank)
+        prompts_b = np.stack([synth.prompt_ids(PROMPT, VOCAB, seed=1000 + rank * SYN_B + b) for b in range(SYN_B)])
+        noise_b = rng_b.standard_normal((SYN_B, STEPS_PER_UTT, 64, 4), dtype=np.float32)
+        vox.generate_batch(prompts_b, GenerateOptions(max_len=4), noise_b[:, :4])
+        barrier()
+        t0 = time.perf_counter()
+        wav_b = vox.generate_batch(prompts_b, GenerateOptions(max_len=STEPS_PER_UTT), noise_b)
+        e2e_b = allmax(time.perf_counter() - t0)
+        extras["synthesis_batched"] = {
+            "workload": f"end-to-end synthesis, {SYN_B} utterances per GPU decoded together (vx_generate_batch), "
+                        "same LM / CFM / AudioVAE settings",
+            "utterances_per_gpu": SYN_B, "audio_seconds_per_utterance": wav_b.shape[1] / 16000.0, "wall_s": e2e_b,
+            "audio_s_per_s": world * SYN_B * (wav_b.shape[1] / 16000.0) / e2e_b, "n_gpus": world}
         vox.dit.close()
         vox.vae.close()
 
