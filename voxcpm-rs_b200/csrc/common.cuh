@@ -174,6 +174,24 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Launch configuration with programmatic dependent launch: the kernel may be scheduled while
+// its predecessor in the stream drains; it must call pdl_wait() before touching anything the
+// predecessor writes or reads.
+struct PdlLaunch {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  PdlLaunch(dim3 grid, dim3 block, size_t smem, cudaStream_t st) {
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+};
+
 // silu_stable: x * sigmoid(x) in f32 (reference src/minicpm4/mod.rs:29-33)
 __device__ __forceinline__ float silu(float x) { return x * (1.0f / (1.0f + expf(-x))); }
 

@@ -111,6 +111,8 @@ cudaError_t launch_rmsnorm_residual(const float* x, const float* r, const float*
 __global__ void rope_scatter_kernel(const float* __restrict__ qkv, int B, int S, int nh, int nkv, int d,
                                     const RopeParams* rope, int pos0, const int* pos_ptr, float* q_out, float* kcache,
                                     float* vcache, int s_max) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int half = d / 2;
   const int heads = nh + 2 * nkv;
   if (pos_ptr) pos0 = *pos_ptr;
@@ -153,9 +155,9 @@ cudaError_t launch_rope_scatter(const float* qkv, int B, int S, int nh, int nkv,
   const size_t total = (size_t)B * S * (nh + 2 * nkv) * (d / 2);
   const int grid = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
   count_launch();
-  rope_scatter_kernel<<<grid, 256, 0, st>>>(qkv, B, S, nh, nkv, d, rope, pos0, pos_ptr, q_out, kcache, vcache,
-                                            s_max);
-  return cudaGetLastError();
+  PdlLaunch l(dim3(grid), dim3(256), 0, st);
+  return cudaLaunchKernelEx(&l.cfg, rope_scatter_kernel, qkv, B, S, nh, nkv, d, rope, pos0, pos_ptr, q_out, kcache,
+                            vcache, s_max);
 }
 
 // ------------------------------------------------------------ RoPE apply on [B,H,S,D]
@@ -189,6 +191,8 @@ cudaError_t launch_rope_apply(float* x, int B, int H, int S, int d, const float*
 
 // ------------------------------------------------------------ SiLU gate * up (S rows)
 __global__ void silu_mul_kernel(const float* __restrict__ gu, int M, int inter, float* __restrict__ act) {
+  pdl_wait();
+  pdl_launch_dependents();
   const size_t total = (size_t)M * inter;
   for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
        idx += (size_t)gridDim.x * blockDim.x) {
@@ -202,8 +206,8 @@ cudaError_t launch_silu_mul(const float* gu, int M, int inter, float* act, cudaS
   const size_t total = (size_t)M * inter;
   const int grid = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
   count_launch();
-  silu_mul_kernel<<<grid, 256, 0, st>>>(gu, M, inter, act);
-  return cudaGetLastError();
+  PdlLaunch l(dim3(grid), dim3(256), 0, st);
+  return cudaLaunchKernelEx(&l.cfg, silu_mul_kernel, gu, M, inter, act);
 }
 
 // ------------------------------------------------------------ embedding gather

@@ -714,11 +714,11 @@ int vx_lm_forward(vx_lm* lm, const float* embeds, int B, int S, int causal, int 
       for (int b = 0; b < B; ++b) {
         AttnPrefillArgs ap = {lm->pf_q + (size_t)b * S * lm->qs, lm->kc(l, b), lm->vc(l, b), 1, S, lm->nh, lm->nkv,
                               lm->d, s_max, lm->attn_scale, causal, lm->pf_attn + (size_t)b * S * lm->qs};
-        VX_CUDA(ctx, launch_attn_prefill(ap, st, false));
+        VX_CUDA(ctx, launch_attn_prefill(ap, st, true));
       }
     } else {
       AttnPrefillArgs ap = {lm->pf_q, kd, vd, B, S, lm->nh, lm->nkv, lm->d, s_max, lm->attn_scale, causal, lm->pf_attn};
-      VX_CUDA(ctx, launch_attn_prefill(ap, st, false));
+      VX_CUDA(ctx, launch_attn_prefill(ap, st, true));
     }
     rc = linear(ctx, &lm->ws, lm->pf_attn, lm->qs, (int)M, H, lm->qs, w.wo, nullptr, lm->pf_x, lm->res_scale, lm->pf_x,
                 H, st);

@@ -148,6 +148,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // The weights never depend on the previous kernel: under programmatic dependent launch the
+  // producer issues the first stages' weight tiles before waiting for it, so they stream
+  // while the previous kernel drains; the activation tiles follow the wait.
+  const int pre = nkb < a.nstages ? nkb : a.nstages;
+  if (warp == 0 && lane == 0)
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&full[i], a_bytes + b_bytes);
+      tma_load_2d(base + i * stage_bytes, &tmW, (kb0 + i) * TC_BK, tile * TC_BM, &full[i]);
+    }
   pdl_wait();
   pdl_launch_dependents();
 
@@ -160,9 +169,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         break;
       }
       unsigned char* st = base + s * stage_bytes;
-      mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
       const int kx = (kb0 + i) * TC_BK;
-      tma_load_2d(st, &tmW, kx, tile * TC_BM, &full[s]);
+      if (i >= pre) {
+        mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
+        tma_load_2d(st, &tmW, kx, tile * TC_BM, &full[s]);
+      }
       tma_load_2d(st + a_bytes, &tmX, kx, 0, &full[s]);
     }
   } else if (warp == 1 && lane == 0) {
@@ -263,6 +274,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
 // X [M, K] f32 (row stride ldx) -> Xs [NB, K] bf16: rows 0..M hi, M..2M lo, the rest zero.
 __global__ void split_bf16_kernel(const float* __restrict__ X, int ldx, int M, int K, int NB, uint16_t* __restrict__ Xs) {
+  pdl_wait();
+  pdl_launch_dependents();
   const size_t total = (size_t)NB * K;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int r = (int)(i / K), k = (int)(i % K);
@@ -347,8 +360,10 @@ cudaError_t launch_tc_gemm(const float* X, int ldx, int M, int N, int K, const u
   uint16_t* Xs = static_cast<uint16_t*>(scratch);
   float* partials = reinterpret_cast<float*>(static_cast<char*>(scratch) + (((size_t)NB * K * 2 + 255) & ~(size_t)255));
   count_launch();
-  split_bf16_kernel<<<std::min(4096, (NB * K + 255) / 256), 256, 0, st>>>(X, ldx, M, K, NB, Xs);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  {
+    PdlLaunch l(dim3(std::min(4096, (NB * K + 255) / 256)), dim3(256), 0, st);
+    if ((e = cudaLaunchKernelEx(&l.cfg, split_bf16_kernel, X, ldx, M, K, NB, Xs)) != cudaSuccess) return e;
+  }
   CUtensorMap tmW, tmX;
   if ((e = make_map(&tmW, W, N, K, TC_BM)) != cudaSuccess) return e;
   if ((e = make_map(&tmX, Xs, NB, K, NB)) != cudaSuccess) return e;
@@ -371,8 +386,8 @@ cudaError_t launch_tc_gemm(const float* X, int ldx, int M, int N, int K, const u
   a.nstages = std::max(1, std::min({6, a.kblocks_per_split, (200 * 1024) / stage_bytes}));
   const int smem = 1024 + a.nstages * stage_bytes + 256;
   count_launch();
-  tc_gemm_kernel<<<dim3(tiles, splits), TC_THREADS, smem, st>>>(tmW, tmX, a);
-  return cudaGetLastError();
+  PdlLaunch l(dim3(tiles, splits), dim3(TC_THREADS), smem, st);
+  return cudaLaunchKernelEx(&l.cfg, tc_gemm_kernel, tmW, tmX, a);
 }
 
 }  // namespace vx
