@@ -25,8 +25,8 @@
 //        layer.rs:69-72); unit = 8 MLP channels j: their gate row, up row and down column
 //        (a row of the transposed down weight).  Each warp accumulates its slice of the
 //        2048 outputs across the CTA's units; at the end of the phase the CTA adds
-//        res_scale * its partial into the next layer's residual buffer with vector
-//        reductions.  Fusing the down projection removes a dependency round trip per layer.
+//        res_scale * its partial into the next layer's residual buffer with one bulk
+//        reduce-add.  Fusing the down projection removes a dependency round trip per layer.
 // then the greedy head: final norm -> tied-embedding logits -> argmax -> next input
 // embedding, position and step advanced on the device.
 //
@@ -94,14 +94,6 @@ __device__ __forceinline__ bool sync_or(bool v) {
 __device__ __forceinline__ void csync() { named_sync(1, PK_CTHREADS); }
 
 __device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
-__device__ __forceinline__ float2 ldcg2(const float* p) { return __ldcg(reinterpret_cast<const float2*>(p)); }
-
-__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
-}
-__device__ __forceinline__ void red_add_v2(float* p, float a, float b) {
-  asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b) : "memory");
-}
 
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
@@ -861,22 +853,29 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
     sm.red[16 + warp] = bv;
     reinterpret_cast<int*>(sm.red)[24 + warp] = bi;
   }
-  if (kind == PH_M && !lbad && k > 0) {
-    // this CTA's res_scale * down partial into the next layer's residual buffer (seeded with
-    // x1 by the O phase): x0' = x1 + s * down (layer.rs:33-38, 72)
-    float* dst = xnext + warp * (KC / 8) + lane * CPL;
-    const float sc = a.res_scale;
-    if constexpr (CPL >= 4) {
+  if (kind == PH_M) {
+    // this CTA's res_scale * down partial (xs[H, 2H), the warps' column slices side by side)
+    // into the next layer's residual buffer, seeded with x1 by the O phase: x0' = x1 + s * down
+    // (layer.rs:33-38, 72).  One bulk reduce-add through the TMA engine per CTA: 128-byte
+    // reductions at L2 instead of 16-byte ones from every lane.
+    const bool mine = !lbad && k > 0;
+    if (mine) {
 #pragma unroll
-      for (int e = 0; e < CPL; e += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(dacc + e);
-        red_add_v4(dst + e, sc * v.x, sc * v.y, sc * v.z, sc * v.w);
-      }
-    } else if constexpr (CPL == 2) {
-      red_add_v2(dst, sc * dacc[0], sc * dacc[1]);
-    } else {
-      atomicAdd(dst, sc * dacc[0]);
+      for (int e = 0; e < CPL; ++e) dacc[e] *= a.res_scale;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // read by the async proxy
     }
+    if (sync_or(lbad)) st.bad = 1;
+    if (mine && !st.bad && tid == 0) {
+      // the destination was seeded by other CTAs' generic stores (acquired at the phase start)
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(xnext),
+                   "r"(smem_u32(sm.xs + a.H)), "r"((uint32_t)a.H * 4u)
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+      asm volatile("fence.proxy.async.global;" ::: "memory");  // before the generic release
+    }
+    return st;
   }
   if (sync_or(lbad)) st.bad = 1;
   if (kind == PH_HEAD && tid == 0) {  // CTA best over the warps (ties -> lowest id)
