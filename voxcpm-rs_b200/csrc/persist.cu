@@ -590,7 +590,7 @@ __device__ bool att_unit(const PersistArgs& a, const AttGeo& at, int l, int u, c
     }
     if (sync_or(lbad)) return false;
     // scores q.k^T * scale (attention.rs:166)
-    float sc = 0.f;
+    float sc0 = 0.f, sc1 = 0.f, sc2 = 0.f, sc3 = 0.f;  // four independent FMA chains
     if (lane < nt) {
       const float* kr = Ks + (size_t)lane * D;
       const float* qr = qs + warp * D;
@@ -599,26 +599,32 @@ __device__ bool att_unit(const PersistArgs& a, const AttGeo& at, int l, int u, c
         const int c = (ch + lane) & (NC - 1);
         const float4 kk = *reinterpret_cast<const float4*>(kr + c * 4);
         const float4 qq = *reinterpret_cast<const float4*>(qr + c * 4);
-        sc = fmaf(qq.x, kk.x, sc);
-        sc = fmaf(qq.y, kk.y, sc);
-        sc = fmaf(qq.z, kk.z, sc);
-        sc = fmaf(qq.w, kk.w, sc);
+        sc0 = fmaf(qq.x, kk.x, sc0);
+        sc1 = fmaf(qq.y, kk.y, sc1);
+        sc2 = fmaf(qq.z, kk.z, sc2);
+        sc3 = fmaf(qq.w, kk.w, sc3);
       }
     }
     const bool valid = lane < nt;
-    const float sv = valid ? sc * a.attn_scale : -INFINITY;
+    const float sv = valid ? ((sc0 + sc1) + (sc2 + sc3)) * a.attn_scale : -INFINITY;
     const float mn = fmaxf(m, warp_max(sv));
     const float corr = expf(m - mn);  // 0 on the first tile (m = -inf)
     const float p = valid ? expf(sv - mn) : 0.f;
+    // the weights go through shared memory so the P.V loop below can run ahead of them
+    float* ps = sm.xs + NREP * D + warp * 32;
+    ps[lane] = p;
     lsum = lsum * corr + warp_sum(p);
 #pragma unroll
     for (int e = 0; e < DPL; ++e) o[e] *= corr;
+    __syncwarp();
+#pragma unroll 8
     for (int j = 0; j < nt; ++j) {
-      const float pj = __shfl_sync(0xffffffffu, p, j);
+      const float pj = ps[j];
       const float* vr = Vs + (size_t)j * D + lane * DPL;
 #pragma unroll
       for (int e = 0; e < DPL; ++e) o[e] = fmaf(pj, vr[e], o[e]);
     }
+    __syncwarp();  // ps is rewritten by the next tile
     m = mn;
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[slot]);
@@ -1123,7 +1129,7 @@ PkShape shape_of(int H, int I, int nh, int nkv, int d, int nst_cap) {
   p.span = std::min(32, 2 * p.kc / d);  // K and V rows of `span` positions fill one ring stage
   // xs holds an input vector (x, normalised x1, or the attention output); the MLP phase also
   // keeps its down_proj accumulators in xs[H, 2H)
-  const int m = std::max(2 * H, std::max(nh * d, NREP * d));
+  const int m = std::max(2 * H, std::max(nh * d, NREP * d + NREP * 32));  // attention: q rows + weights
   p.xs_floats = (m + 3) & ~3;
   const size_t fixed = (size_t)p.xs_floats * 4 + persist_att_part_floats(nkv, nh, d) * 4 + PK_MISC_FLOATS * 4 + 32 + 8;
   const int stage = PK_ROWS * p.kc * 2;
