@@ -403,25 +403,14 @@ def run_lm_only(layers=LAYERS):
     return 0
 
 
-def run_phase_trace(pos=200, layers=LAYERS):
-    """Phase trace of one persistent decode step of the LM-decode model at position `pos`
+def phase_trace(model, ctx, pos, layers):
+    """Phase trace of one persistent decode step of `model` at position `pos`
     (vx_lm_trace_decode_step): per phase kind, medians over layers 2..L-2 of the time after
     the previous phase was published at which the median CTA had its inputs, finished its
-    last unit and published, and the phase duration (microseconds)."""
+    last unit and published, and the phase duration (microseconds).  Advances the model's
+    position like a decode step."""
     import numpy as np
-    import torch
-    from __graft_entry__ import load_package
-    load_package()
-    from voxcpm_rs_b200 import synth
     from voxcpm_rs_b200._lib import check, lib
-    from voxcpm_rs_b200.minicpm4 import Context, MiniCpmModel
-    global LAYERS
-    LAYERS = layers
-    ctx = Context(0)
-    model = MiniCpmModel(ctx, lm_config(), None, max_length=MAX_LEN)
-    load_device_weights(model, device_weights(1234, "cuda:0"))
-    model.greedy(synth.prompt_ids(PROMPT, VOCAB, seed=0), 8)
-    torch.cuda.synchronize()
     nph = 4 * layers + 1
     n = nph * 4096 * 8
     buf = (ctypes.c_ulonglong * n)()
@@ -447,8 +436,26 @@ def run_phase_trace(pos=200, layers=LAYERS):
         out[name] = {"duration_us": round(r[0], 2), "inputs_ready_us": round(r[1], 2),
                      "last_unit_median_us": round(r[2], 2), "last_unit_max_us": round(r[3], 2),
                      "published_us": None if name == "head" else round(r[4], 2), "ctas": int(r[5])}
-    print(json.dumps({"phase_trace": out, "position": pos, "grid": G, "layers": layers,
-                      "step_us": round(float(np.nanmax(tt)), 1)}))
+    layer_us = [pub[p + 3] - pub[p - 1] for p in range(4, nph - 1, 4) if 2 <= p // 4 < layers - 1]
+    return {"phase_trace": out, "position": pos, "grid": G, "layers": layers,
+            "layer_us_median": round(float(np.median(layer_us)), 2), "step_us": round(float(np.nanmax(tt)), 1)}
+
+
+def run_phase_trace(pos=200, layers=LAYERS):
+    """--phase-trace: the LM-decode model after a 64-id prompt + 8 greedy steps, traced at `pos`."""
+    import torch
+    from __graft_entry__ import load_package
+    load_package()
+    from voxcpm_rs_b200 import synth
+    from voxcpm_rs_b200.minicpm4 import Context, MiniCpmModel
+    global LAYERS
+    LAYERS = layers
+    ctx = Context(0)
+    model = MiniCpmModel(ctx, lm_config(), None, max_length=MAX_LEN)
+    load_device_weights(model, device_weights(1234, "cuda:0"))
+    model.greedy(synth.prompt_ids(PROMPT, VOCAB, seed=0), 8)
+    torch.cuda.synchronize()
+    print(json.dumps(phase_trace(model, ctx, pos, layers)))
     model.close()
     ctx.close()
     return 0
@@ -626,6 +633,16 @@ def main():
         from voxcpm_rs_b200.voxcpm import GenerateOptions, VoxCPM
         extras["rmsnorm"] = measure_rmsnorm(ctx, device)
         extras["decoder_layer_step"] = measure_layer_step(model, device, peak)
+        if persistent:
+            # the same layer step inside the one-launch decode step (config 2's layer, p = 1000):
+            # median time from a layer's qkv phase start to its MLP publish, phase trace
+            tr = phase_trace(model, ctx, 1000, LAYERS)
+            lb = LAYER_WEIGHT_BYTES + 2 * NKV * 1001 * HD * 4
+            extras["decoder_layer_step_persistent"] = {
+                "workload": "one decoder layer of the persistent decode step at p=1000 (phase trace, median layer)",
+                "us_per_layer": tr["layer_us_median"], "gb_s": lb / (tr["layer_us_median"] * 1e-6) / 1e9,
+                "frac_of_hbm_peak": lb / (tr["layer_us_median"] * 1e-6) / 1e9 / peak, "algorithmic_bytes": lb,
+                "phases_us": {k: v["duration_us"] for k, v in tr["phase_trace"].items()}}
         dcfg = config.locdit_config(cfg)
         dit_w = synth.locdit_weights(dcfg, in_channels=64, seed=rank)
         extras["locdit_cfm"] = measure_cfm(ctx, device, dcfg, dit_w)

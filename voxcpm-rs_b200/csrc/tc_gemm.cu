@@ -25,7 +25,9 @@
 #include <cudaTypedefs.h>
 
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "common.cuh"
 #include "runtime.cuh"
@@ -49,7 +51,29 @@ struct TcGemmArgs {
   unsigned int* counters;  // [tiles], zero-initialised, reset by the last CTA
   int* err;
   int nstages;
+  int cluster;  // 1: the K splits of a tile form one thread-block cluster and sum through DSMEM
 };
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Shared-memory address of `p` in the CTA of cluster rank `rank` (DSMEM window).
+__device__ __forceinline__ uint32_t dsmem_addr(const void* p, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ int ld_dsmem_s32(uint32_t addr) {
+  int v;
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -119,6 +143,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* done = empty + a.nstages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort, [1] last-CTA
+  // cluster mode: this split's partial tile [M][128] f32, read by the cluster's other CTAs
+  float* spart = reinterpret_cast<float*>(base + a.nstages * stage_bytes + 1024);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
@@ -206,7 +232,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int n = tile * TC_BM + warp * 32 + lane;  // this thread's weight row
   if (!flags[0]) {
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-    float* part = a.splits > 1 ? a.partials + (((size_t)tile * a.splits + split) * a.M) * TC_BM : nullptr;
+    float* part = a.splits == 1 ? nullptr
+                  : a.cluster   ? spart
+                                : a.partials + (((size_t)tile * a.splits + split) * a.M) * TC_BM;
     for (int c0 = 0; c0 < a.M; c0 += 16) {
       float hi[16], lo[16];
       tmem_ld16(trow + c0, hi);
@@ -231,6 +259,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+  if (a.splits > 1 && a.cluster) {
+    // ---- split-K inside the cluster: every CTA of the tile reaches both cluster barriers (also
+    // after an abort); CTA r then sums output rows [r*ceil(M/S), ...) over the S partials in
+    // split order (deterministic), reading the other CTAs' partial tiles through DSMEM
+    cluster_sync_all();
+    const int S = a.splits;
+    bool any_abort = false;
+    for (int r = 0; r < S; ++r) any_abort |= ld_dsmem_s32(dsmem_addr(&flags[0], r)) != 0;
+    const int per = (a.M + S - 1) / S;
+    const int m0 = split * per, m1 = min(a.M, m0 + per);
+    if (!any_abort && n < a.N) {
+      const float bn = a.bias ? a.bias[n] : 0.f;
+      for (int m = m0; m < m1; ++m) {
+        const float* src = spart + (size_t)m * TC_BM + threadIdx.x;
+        float acc = 0.f;
+        for (int r = 0; r < S; ++r) acc += ld_dsmem_f32(dsmem_addr(src, r));
+        float y = acc + bn;
+        if (a.R) y = a.R[(size_t)m * a.ldy + n] + y * a.res_scale;
+        a.Y[(size_t)m * a.ldy + n] = y;
+      }
+    }
+    cluster_sync_all();  // the partial tiles stay alive until every CTA has read them
+    return;
+  }
   if (flags[0] || a.splits == 1) return;
   // ---- split-K: the last CTA of this tile sums the partials in split order
   __threadfence();
@@ -320,6 +372,32 @@ cudaError_t make_map(CUtensorMap* m, const void* ptr, int rows, int K, int box_r
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// Whether clusters of `splits` CTAs with `smem` bytes each can be resident (cached per shape).
+bool cluster_fits(int splits, int smem) {
+  static std::mutex mu;
+  static std::map<std::pair<int, int>, bool> memo;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_pair(splits, smem);
+  auto it = memo.find(key);
+  if (it != memo.end()) return it->second;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, splits);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = splits;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  const bool ok = cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel, &cfg) == cudaSuccess && n >= 1;
+  cudaGetLastError();
+  memo[key] = ok;
+  return ok;
+}
+
 }  // namespace
 
 // Raise the dynamic shared-memory limit on the current device; called once per context,
@@ -383,10 +461,23 @@ cudaError_t launch_tc_gemm(const float* X, int ldx, int M, int N, int K, const u
   a.counters = counters;
   a.err = err;
   const int stage_bytes = TC_BM * TC_BK * 2 + ((NB * TC_BK * 2 + 1023) & ~1023);
-  a.nstages = std::max(1, std::min({6, a.kblocks_per_split, (200 * 1024) / stage_bytes}));
-  const int smem = 1024 + a.nstages * stage_bytes + 256;
+  const int part_bytes = splits > 1 ? M * TC_BM * 4 : 0;  // the cluster reduction's partial tile
+  a.nstages = std::max(1, std::min({6, a.kblocks_per_split, (200 * 1024 - part_bytes) / stage_bytes}));
+  const int smem = 1024 + a.nstages * stage_bytes + 1024 + part_bytes + 256;
   count_launch();
   PdlLaunch l(dim3(tiles, splits), dim3(TC_THREADS), smem, st);
+  // the K splits of a tile as one cluster (DSMEM reduction) when the device can hold it
+  cudaLaunchAttribute attrs[2] = {l.attr[0], {}};
+  a.cluster = 0;
+  if (splits > 1 && cluster_fits(splits, smem)) {
+    attrs[1].id = cudaLaunchAttributeClusterDimension;
+    attrs[1].val.clusterDim.x = 1;
+    attrs[1].val.clusterDim.y = splits;
+    attrs[1].val.clusterDim.z = 1;
+    l.cfg.attrs = attrs;
+    l.cfg.numAttrs = 2;
+    a.cluster = 1;
+  }
   return cudaLaunchKernelEx(&l.cfg, tc_gemm_kernel, tmW, tmX, a);
 }
 
