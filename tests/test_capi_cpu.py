@@ -75,3 +75,33 @@ def test_null_arguments_rejected():
     from voxcpm_rs_b200._lib import VX_ERR_ARG, lib
     assert lib().vx_rmsnorm_residual(None, None, None, None, 1.0, 1e-6, 1, 4, None, None, None) == VX_ERR_ARG
     assert lib().vx_lm_greedy(None, None, 0, 0, None) == VX_ERR_ARG
+
+
+def test_context_close_destroys_its_objects_first(monkeypatch):
+    """Closing a Context destroys the library objects created on it before the context
+    itself, so an object that outlives its context (a failed test's local, a dropped
+    reference) never reaches a freed vx_ctx.  Runs on a recording stand-in for the library."""
+    from voxcpm_rs_b200 import _lib, audiovae, locdit, minicpm4
+
+    calls = []
+
+    class Fake:
+        def __getattr__(self, name):
+            def fn(*args):
+                calls.append(name)
+                return 0
+            return fn
+
+    fake = Fake()
+    for mod in (_lib, minicpm4, locdit, audiovae):
+        monkeypatch.setattr(mod, "lib", lambda: fake)
+    monkeypatch.setattr(_lib, "config_struct", lambda cfg: C.c_int(0))
+    ctx = minicpm4.Context(0)
+    ctx.h = C.c_void_p(1)
+    m = minicpm4.MiniCpmModel(ctx, cfg=None)
+    m.h = C.c_void_p(2)
+    ctx.close()
+    assert calls.index("vx_lm_destroy") < calls.index("vx_ctx_destroy")
+    assert m.h is None and ctx.h is None
+    m.close()  # a second close after the context is gone touches nothing
+    assert calls.count("vx_lm_destroy") == 1

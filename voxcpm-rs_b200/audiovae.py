@@ -25,6 +25,7 @@ class AudioVae:
         h = C.c_void_p()
         check(lib().vx_vae_create(ctx.h, C.byref(s), C.byref(h)), ctx.h)
         self.h = h
+        ctx._adopt(self)
         if weights is not None:
             self.load(weights)
 

@@ -19,6 +19,7 @@ class VoxCpmLocDiTV2:
         h = C.c_void_p()
         check(lib().vx_dit_create(ctx.h, C.byref(s), in_channels, max_rows, C.byref(h)), ctx.h)
         self.h = h
+        ctx._adopt(self)
         if weights is not None:
             self.load(weights)
 

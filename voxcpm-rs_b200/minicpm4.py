@@ -9,6 +9,7 @@ every computation is a call into the CUDA library.  Names follow the reference:
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 
 import numpy as np
 
@@ -31,6 +32,12 @@ class Context:
             raise _lib.VxError(rc, f"vx_ctx_create(device={device}) failed")
         self.h = h
         self.device = device
+        self._owned = weakref.WeakSet()
+
+    def _adopt(self, obj):
+        """Register a library object created on this context: closing the context closes it
+        first, so no native object outlives the context it points to."""
+        self._owned.add(obj)
 
     @property
     def stream(self):
@@ -51,6 +58,8 @@ class Context:
 
     def close(self):
         if getattr(self, "h", None):
+            for obj in list(getattr(self, "_owned", ())):
+                obj.close()
             lib().vx_ctx_destroy(self.h)
             self.h = None
 
@@ -177,6 +186,7 @@ class MiniCpmModel:
         h = C.c_void_p()
         check(lib().vx_lm_create(ctx.h, C.byref(s), max_batch, max_length, C.byref(h)), ctx.h)
         self.h = h
+        ctx._adopt(self)
         if weights is not None:
             self.load(weights)
 
