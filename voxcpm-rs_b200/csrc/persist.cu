@@ -57,7 +57,8 @@ constexpr int PK_THREADS = PK_CTHREADS + 32;
 constexpr int PK_ROWS = 8;
 constexpr int PK_MAX_LAYERS = 64;                  // layer-table entries held in shared memory
 constexpr int PK_MAX_SMEM = 232448 - PK_MAX_LAYERS * (int)sizeof(PersistLayer);  // 227 KB per CTA, less the table
-constexpr int PK_MISC_FLOATS = 64 + 64 + 64 + 16;  // rope tables, reduction scratch, MLP gate values
+constexpr int PK_KP_FLOATS = 2 * 2 * PK_ROWS * PK_CWARPS;  // per-warp row partials: 2 units x 2 row groups
+constexpr int PK_MISC_FLOATS = 64 + 64 + 64 + PK_KP_FLOATS;  // rope tables, reduction scratch, row partials
 constexpr int PK_RES_UNITS = 4;                    // residual rows preloaded per warp and phase
 constexpr int PK_XREG = 4;                         // float4 per thread held by a normalising load_x (K <= 4096)
 constexpr int NREP = 8;                            // query heads per KV head
@@ -117,7 +118,8 @@ struct Smem {
   float* ctab;  // [64]
   float* stab;  // [64]
   float* red;   // [64]: [0,8) group sums / merge, [16,32) per-warp argmax, [48,50) CTA argmax
-  float* mv;    // [16]: silu(gate)*up of the current MLP unit's 8 channels, double-buffered
+  float* kp;    // [2][2][PK_ROWS][PK_CWARPS]: each warp's K-slice sums of a unit's rows (row
+                // group, row, warp), double-buffered by unit parity
   volatile int* flags;
   uint64_t* full;
   uint64_t* empty;
@@ -655,6 +657,30 @@ __device__ __forceinline__ CState att_units(const PersistArgs& a, const Smem& sm
   return st;
 }
 
+// Sum over the warp's 32 lanes of eight per-lane values, one per row: three exchange steps that
+// each halve the rows a lane carries (lanes differing in bit 4, 3, 2 swap the halves they do
+// not keep), then two plain butterfly steps.  Lane l returns the sum of v[(l >> 2) & 7].
+__device__ __forceinline__ float warp_rows_sum(const float (&v)[PK_ROWS], int lane) {
+  const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
+  float b[4], c[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    b[i] = (h16 ? v[i + 4] : v[i]) + __shfl_xor_sync(0xffffffffu, h16 ? v[i] : v[i + 4], 16);
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    c[i] = (h8 ? b[i + 2] : b[i]) + __shfl_xor_sync(0xffffffffu, h8 ? b[i] : b[i + 2], 8);
+  float d = (h4 ? c[1] : c[0]) + __shfl_xor_sync(0xffffffffu, h4 ? c[0] : c[1], 4);
+  d += __shfl_xor_sync(0xffffffffu, d, 2);
+  d += __shfl_xor_sync(0xffffffffu, d, 1);
+  return d;
+}
+
+// Sum of 8 consecutive floats of shared memory, in index order.
+__device__ __forceinline__ float sum8(const float* p) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  return ((((((a.x + a.y) + a.z) + a.w) + b.x) + b.y) + b.z) + b.w;
+}
+
 // CPL consecutive bf16 of shared memory -> f32.
 template <int CPL>
 __device__ __forceinline__ void load_bf16(const uint16_t* p, float* out) {
@@ -692,11 +718,12 @@ __device__ __forceinline__ void prefetch_mlp(const PersistArgs& a, int l, int fi
   }
 }
 
-// This CTA's units of a GEMV phase (Q, O, head) after its dependency is met: x -> xs
-// (optional RMSNorm; O: the attention merge), then the streamed dot products.  Warp w owns row
-// w of every 8-row group, so each warp applies its rows' epilogue itself (its rotate_half
-// partner comes from the same warp) and the warps run through the ring independently: no CTA
-// barrier per unit.
+// This CTA's units of a GEMV phase (Q, O, MLP, head) after its dependency is met: x -> xs
+// (optional RMSNorm; O: the attention merge), then the streamed dot products.  Warp w owns the
+// K slice [w*KC/8, (w+1)*KC/8) of every row, so a lane holds only KC/256 input values and each
+// stage is 8 independent FMA chains per lane; the warps' row partials meet in sm.kp behind one
+// CTA barrier per unit, after which warp w applies row w's epilogue (Q: its rotate_half
+// partner is row w of the unit's second group).
 template <int KC, int D>
 __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& sm, CState st, int nst, int kind, int l,
                                              int pos, int U, int K, int gpu, int first, const float* xsrc,
@@ -720,23 +747,20 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
     load_x(xsrc, norm_w, K, a.eps, sm);
   }
   if (tid == 0) trace_mark(a, kind == PH_HEAD ? a.L * PH_PER_LAYER : l * PH_PER_LAYER + kind, 1);
-  constexpr int NJ = KC / 256, CPL = KC / 256;
-  // MLP: this lane's CPL down_proj accumulators (output columns warp*KC/8 + lane*CPL..) live
+  // Each warp owns a K slice of every row (columns warp*SL + lane*CPL ..), so a lane needs
+  // only CPL elements of the phase input; the warps' row partials meet in sm.kp.
+  constexpr int CPL = KC / 256, SL = KC / PK_CWARPS;
+  // MLP: this lane's CPL down_proj accumulators (output columns warp*SL + lane*CPL..) live
   // in shared memory, xs[H, 2H) being free in this phase
-  float* dacc = sm.xs + a.H + warp * (KC / 8) + lane * CPL;
+  float* dacc = sm.xs + a.H + warp * SL + lane * CPL;
   if (kind == PH_M) {
 #pragma unroll
     for (int e = 0; e < CPL; ++e) dacc[e] = 0.f;
   }
-  // x slice of this lane (one K chunk per row: K == KC), loaded once for the phase
-  float xr[NJ * 8];
+  // this lane's slice of the input (K == KC), loaded once for the phase
+  float xr[CPL];
 #pragma unroll
-  for (int j = 0; j < NJ; ++j) {
-    const float4 v0 = *reinterpret_cast<const float4*>(sm.xs + j * 256 + lane * 8);
-    const float4 v1 = *reinterpret_cast<const float4*>(sm.xs + j * 256 + lane * 8 + 4);
-    xr[j * 8 + 0] = v0.x; xr[j * 8 + 1] = v0.y; xr[j * 8 + 2] = v0.z; xr[j * 8 + 3] = v0.w;
-    xr[j * 8 + 4] = v1.x; xr[j * 8 + 5] = v1.y; xr[j * 8 + 6] = v1.z; xr[j * 8 + 7] = v1.w;
-  }
+  for (int e = 0; e < CPL; ++e) xr[e] = sm.xs[warp * SL + lane * CPL + e];
   (void)K;
   int slot = st.s % nst;  // ring position, advanced incrementally
   uint32_t par = (st.s / nst) & 1;
@@ -744,29 +768,29 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
   float bv = -FLT_MAX;  // head: this warp's running argmax
   int bi = INT_MAX;
   float* xnext = xbuf(a, l + 1);
+  float mvr[PK_ROWS];  // MLP: silu(gate) * up of the unit's 8 channels
+  const int rrow = (lane >> 2) & 7;  // the row whose warp sum this lane holds after a reduction
+  const int last_group = kind == PH_M ? 1 : gpu - 1;
   int k = 0;
   for (int u = first; u < U; u += G, ++k) {
+    float* kpb = sm.kp + (k & 1) * (2 * PK_ROWS * PK_CWARPS);
     float t0 = 0.f, t1 = 0.f;
     for (int gi = 0; gi < gpu; ++gi) {
       if (kind == PH_M && gi == 2) {
-        // down_proj column block (mlp.rs:33): every warp needs the unit's 8 silu(gate)*up
-        // values, then accumulates its KC/8 output columns over rows j0..j0+7 of wdt
-        float* mvb = sm.mv + (k & 1) * PK_ROWS;
-        if (lane == 0) mvb[warp] = silu(t0) * t1;  // mlp.rs:31-33
-        csync();
+        // down_proj column block (mlp.rs:33): accumulate this warp's SL output columns over
+        // rows j0..j0+7 of wdt, weighted by the unit's 8 silu(gate)*up values
         if (!lbad && !wait_full(&sm.full[slot], par, a.err, sm.flags)) lbad = true;
         if (!lbad) {
-          const uint16_t* wr = sm.ring + (size_t)slot * PK_ROWS * KC + warp * (KC / 8) + lane * CPL;
+          const uint16_t* wr = sm.ring + (size_t)slot * PK_ROWS * KC + warp * SL + lane * CPL;
           float d[CPL];
 #pragma unroll
           for (int e = 0; e < CPL; ++e) d[e] = dacc[e];
 #pragma unroll
           for (int r = 0; r < PK_ROWS; ++r) {
-            const float mr = mvb[r];
             float wv[CPL];
             load_bf16<CPL>(wr + r * KC, wv);
 #pragma unroll
-            for (int e = 0; e < CPL; ++e) d[e] = fmaf(mr, wv[e], d[e]);
+            for (int e = 0; e < CPL; ++e) d[e] = fmaf(mvr[r], wv[e], d[e]);
           }
 #pragma unroll
           for (int e = 0; e < CPL; ++e) dacc[e] = d[e];
@@ -780,14 +804,19 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
         ++st.s;
         continue;
       }
-      float acc0 = 0.f, acc1 = 0.f;
+      // the stage's 8 rows over this warp's K slice: 8 independent FMA chains
+      float acc[PK_ROWS];
+#pragma unroll
+      for (int r = 0; r < PK_ROWS; ++r) acc[r] = 0.f;
       if (!lbad && !wait_full(&sm.full[slot], par, a.err, sm.flags)) lbad = true;
       if (!lbad) {
-        const uint4* wr = reinterpret_cast<const uint4*>(sm.ring + (size_t)slot * PK_ROWS * KC + warp * KC);
+        const uint16_t* wr = sm.ring + (size_t)slot * PK_ROWS * KC + warp * SL + lane * CPL;
 #pragma unroll
-        for (int j = 0; j < NJ; j += 2) {
-          acc0 = dot8(wr[j * 32 + lane], &xr[j * 8], acc0);
-          if (j + 1 < NJ) acc1 = dot8(wr[(j + 1) * 32 + lane], &xr[(j + 1) * 8], acc1);
+        for (int r = 0; r < PK_ROWS; ++r) {
+          float wv[CPL];
+          load_bf16<CPL>(wr + r * KC, wv);
+#pragma unroll
+          for (int e = 0; e < CPL; ++e) acc[r] = fmaf(wv[e], xr[e], acc[r]);
         }
       }
       __syncwarp();
@@ -797,19 +826,20 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
         par ^= 1u;
       }
       ++st.s;
-      // the lane partials of a unit's two row groups (rotate_half pair, gate and up) are
-      // reduced together, two interleaved shuffle chains instead of two in a row
-      if (gi == 0) t0 = acc0 + acc1;
-      else t1 = acc0 + acc1;
-      if (gi == 1 || gpu == 1) {
-        if (gpu == 1) {
-          t0 = warp_sum(t0);
-        } else {
+      const float ws = warp_rows_sum(acc, lane);
+      if ((lane & 3) == 0) kpb[(gi * PK_ROWS + rrow) * PK_CWARPS + warp] = ws;
+      if (gi == last_group) {
+        // every warp's partials of the unit are in: row totals over the warps, in warp order
+        csync();
+        if (kind == PH_M) {
+          // lanes 0..7: silu(gate) * up of channel `lane` (mlp.rs:31-33), then to every lane
+          float m = 0.f;
+          if (lane < PK_ROWS) m = silu(sum8(kpb + lane * PK_CWARPS)) * sum8(kpb + (PK_ROWS + lane) * PK_CWARPS);
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-            t0 += __shfl_xor_sync(0xffffffffu, t0, o);
-            t1 += __shfl_xor_sync(0xffffffffu, t1, o);
-          }
+          for (int r = 0; r < PK_ROWS; ++r) mvr[r] = __shfl_sync(0xffffffffu, m, r);
+        } else if (lane == 0) {
+          t0 = sum8(kpb + warp * PK_CWARPS);
+          if (gpu == 2) t1 = sum8(kpb + (PK_ROWS + warp) * PK_CWARPS);
         }
       }
     }
@@ -908,9 +938,9 @@ __global__ void __launch_bounds__(PK_THREADS, 1) persist_decode_kernel(const Per
   sm.ctab = sm.parts + persist_att_part_floats(a.nkv, a.nh, D);
   sm.stab = sm.ctab + 64;
   sm.red = sm.stab + 64;
-  sm.mv = sm.red + 64;
-  sm.flags = reinterpret_cast<volatile int*>(sm.mv + 16);
-  sm.full = reinterpret_cast<uint64_t*>(sm.mv + 16 + 8);
+  sm.kp = sm.red + 64;
+  sm.flags = reinterpret_cast<volatile int*>(sm.kp + PK_KP_FLOATS);
+  sm.full = reinterpret_cast<uint64_t*>(sm.kp + PK_KP_FLOATS + 8);
   sm.empty = sm.full + nst;
   sm.pbar = sm.empty + nst;
 
