@@ -771,6 +771,10 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
   float mvr[PK_ROWS];  // MLP: silu(gate) * up of the unit's 8 channels
   const int rrow = (lane >> 2) & 7;  // the row whose warp sum this lane holds after a reduction
   const int last_group = kind == PH_M ? 1 : gpu - 1;
+  // head: the warps' row partials of all this CTA's units are kept in sm.parts (free in this
+  // phase) and summed once after the last unit, instead of a CTA barrier per unit
+  const bool defer = kind == PH_HEAD && (size_t)((U - first + G - 1) / G) * (PK_ROWS * PK_CWARPS) <=
+                                            persist_att_part_floats(a.nkv, a.nh, D);
   int k = 0;
   for (int u = first; u < U; u += G, ++k) {
     float* kpb = sm.kp + (k & 1) * (2 * PK_ROWS * PK_CWARPS);
@@ -827,6 +831,10 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
       }
       ++st.s;
       const float ws = warp_rows_sum(acc, lane);
+      if (defer) {
+        if ((lane & 3) == 0) sm.parts[(k * PK_ROWS + rrow) * PK_CWARPS + warp] = ws;
+        continue;
+      }
       if ((lane & 3) == 0) kpb[(gi * PK_ROWS + rrow) * PK_CWARPS + warp] = ws;
       if (gi == last_group) {
         // every warp's partials of the unit are in: row totals over the warps, in warp order
@@ -844,7 +852,7 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
       }
     }
     // ---- this warp's row epilogue (lane 0)
-    if (kind == PH_M || lbad || lane != 0) continue;
+    if (kind == PH_M || defer || lbad || lane != 0) continue;
     const int row = unit_row(a, kind, u, 0) + warp;
     if (kind == PH_HEAD) {
       if (a.logits) a.logits[row] = t0;
@@ -883,6 +891,28 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
       const float x1 = r + t0 * a.res_scale;
       a.x1[row] = x1;
       xnext[row] = x1;
+    }
+  }
+  if (defer) {
+    // the logits of this CTA's k units: thread t sums row t % 8 of its unit t / 8 over the warps
+    csync();
+    for (int t = tid; t < k * PK_ROWS; t += PK_CTHREADS) {
+      const int row = (first + (t / PK_ROWS) * G) * PK_ROWS + t % PK_ROWS;
+      const float v = sum8(sm.parts + t * PK_CWARPS);
+      if (a.logits) a.logits[row] = v;
+      if (better(v, row, bv, bi)) {
+        bv = v;
+        bi = row;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
     }
   }
   if (kind == PH_HEAD && lane == 0) {
