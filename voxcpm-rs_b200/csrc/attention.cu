@@ -226,7 +226,20 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnPrefillArgs
     }
   }
   if (!active) return;
-  float* orow = a.out + ((size_t)b * a.S + i) * a.nh * D + h * D;
+  const size_t orow_i = (size_t)b * a.S + i;
+  if (a.xs) {  // straight into the o_proj GEMM's split operand
+    const int M = a.B * a.S, K = a.nh * D;
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) {
+      const float v = o[e] / l;
+      const __nv_bfloat16 hb = __float2bfloat16_rn(v);
+      a.xs[orow_i * K + h * D + lane * DPL + e] = __bfloat16_as_ushort(hb);
+      a.xs[((size_t)M + orow_i) * K + h * D + lane * DPL + e] =
+          __bfloat16_as_ushort(__float2bfloat16_rn(v - __bfloat162float(hb)));
+    }
+    return;
+  }
+  float* orow = a.out + orow_i * a.nh * D + h * D;
 #pragma unroll
   for (int e = 0; e < DPL; ++e) orow[lane * DPL + e] = o[e] / l;
 }

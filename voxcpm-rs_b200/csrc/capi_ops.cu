@@ -73,6 +73,18 @@ int linear(vx_ctx* ctx, const LinearWorkspace* ws, const float* X, int ldx, int 
   return VX_OK;
 }
 
+bool presplit_ok(vx_ctx* ctx, const LinearWorkspace* ws, int M, int N, int K) {
+  return ctx->tc_gemm && ctx->presplit && ws && ws->scratch && M > 1 && M <= 128 && tc_gemm_supported(M, N, K) &&
+         tc_gemm_scratch_bytes(M, N, K, ctx->gemv_ctas) <= ws->bytes;
+}
+
+int linear_presplit(vx_ctx* ctx, const LinearWorkspace* ws, int M, int N, int K, const uint16_t* W, const float* bias,
+                    const float* R, float res_scale, float* Y, int ldy, cudaStream_t st) {
+  VX_CUDA(ctx, launch_tc_gemm_presplit(M, N, K, W, bias, R, res_scale, Y, ldy, ws->scratch, ws->counters,
+                                       ctx->dev_err, st, ctx->gemv_ctas));
+  return VX_OK;
+}
+
 int fill_rope_params(const vx_minicpm4_config& c, RopeParams* rp, std::string* err) {
   // MiniCpmLongRope::new (src/minicpm4/rope.rs:16-32), all in f64
   const int d = c.kv_channels > 0 ? c.kv_channels : c.hidden_size / c.num_attention_heads;
@@ -131,6 +143,7 @@ int vx_ctx_create(int device, vx_ctx** out) {
   if (const char* s = getenv("VX_PERSIST_MLP_PF")) ctx->persist_mlp_pf = std::max(0, std::min(64, atoi(s)));
   if (const char* s = getenv("VX_PERSIST_PF")) ctx->persist_pf = std::max(0, std::min(256, atoi(s)));
   if (const char* s = getenv("VX_PERSIST_EF")) ctx->persist_ef = atoi(s) != 0;
+  if (const char* s = getenv("VX_PRESPLIT")) ctx->presplit = atoi(s) != 0;
   if (cudaSetDevice(device) != cudaSuccess ||
       cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&ctx->counters, 4096 * sizeof(unsigned)) != cudaSuccess ||

@@ -7,6 +7,7 @@
 //   and lets the kernel return, so a lost arrival never hangs the GPU.
 #pragma once
 #include <cstdint>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #define VX_DEVICE_ERR_TIMEOUT 1
@@ -191,6 +192,24 @@ struct PdlLaunch {
     cfg.numAttrs = 1;
   }
 };
+
+// Four consecutive f32 activations (row r, columns k..k+3) stored as the tcgen05 GEMM's split
+// operand: bf16(v) in row r and bf16(v - bf16(v)) in row M + r of a [2M, K] bf16 buffer
+// (k a multiple of 4).
+__device__ __forceinline__ void store_split4(uint16_t* xs, int M, int K, size_t r, int k, float4 v) {
+  const float f[4] = {v.x, v.y, v.z, v.w};
+  uint16_t hi[4], lo[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(f[i]);
+    hi[i] = __bfloat16_as_ushort(h);
+    lo[i] = __bfloat16_as_ushort(__float2bfloat16_rn(f[i] - __bfloat162float(h)));
+  }
+  *reinterpret_cast<uint2*>(xs + r * K + k) =
+      make_uint2(hi[0] | ((uint32_t)hi[1] << 16), hi[2] | ((uint32_t)hi[3] << 16));
+  *reinterpret_cast<uint2*>(xs + ((size_t)M + r) * K + k) =
+      make_uint2(lo[0] | ((uint32_t)lo[1] << 16), lo[2] | ((uint32_t)lo[3] << 16));
+}
 
 // silu_stable: x * sigmoid(x) in f32 (reference src/minicpm4/mod.rs:29-33)
 __device__ __forceinline__ float silu(float x) { return x * (1.0f / (1.0f + expf(-x))); }

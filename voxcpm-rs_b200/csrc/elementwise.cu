@@ -20,7 +20,8 @@ template <int VPT>  // float4 per thread
 __global__ void __launch_bounds__(256) rmsnorm_residual_kernel(const float* __restrict__ x,
                                                                const float* __restrict__ r,
                                                                const float* __restrict__ w, float resid_scale,
-                                                               float eps, int hidden, float* h_out, float* y_out) {
+                                                               float eps, int hidden, float* h_out, float* y_out,
+                                                               uint16_t* xs) {
   __shared__ float red[8];
   pdl_wait();
   pdl_launch_dependents();
@@ -73,14 +74,15 @@ __global__ void __launch_bounds__(256) rmsnorm_residual_kernel(const float* __re
       y.y = (v[i].y * inv) * ww[i].y;
       y.z = (v[i].z * inv) * ww[i].z;
       y.w = (v[i].w * inv) * ww[i].w;
-      __stcs(reinterpret_cast<float4*>(y_out + row * hidden) + c, y);
+      if (y_out) __stcs(reinterpret_cast<float4*>(y_out + row * hidden) + c, y);
+      if (xs) store_split4(xs, gridDim.x, hidden, row, c * 4, y);
     }
   }
 }
 
 cudaError_t launch_rmsnorm_residual(const float* x, const float* r, const float* w, float resid_scale,
                                     float eps, int rows, int hidden, float* h_out, float* y_out,
-                                    cudaStream_t st) {
+                                    cudaStream_t st, uint16_t* xs) {
   if (hidden % 4 != 0 || hidden > 8192 || rows <= 0) return cudaErrorInvalidValue;
   const int n4 = hidden / 4;
   const int vpt = (n4 + 255) / 256;
@@ -97,10 +99,10 @@ cudaError_t launch_rmsnorm_residual(const float* x, const float* r, const float*
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (vpt <= 2)
-    return cudaLaunchKernelEx(&cfg, rmsnorm_residual_kernel<2>, x, r, w, resid_scale, eps, hidden, h_out, y_out);
+    return cudaLaunchKernelEx(&cfg, rmsnorm_residual_kernel<2>, x, r, w, resid_scale, eps, hidden, h_out, y_out, xs);
   if (vpt <= 4)
-    return cudaLaunchKernelEx(&cfg, rmsnorm_residual_kernel<4>, x, r, w, resid_scale, eps, hidden, h_out, y_out);
-  return cudaLaunchKernelEx(&cfg, rmsnorm_residual_kernel<8>, x, r, w, resid_scale, eps, hidden, h_out, y_out);
+    return cudaLaunchKernelEx(&cfg, rmsnorm_residual_kernel<4>, x, r, w, resid_scale, eps, hidden, h_out, y_out, xs);
+  return cudaLaunchKernelEx(&cfg, rmsnorm_residual_kernel<8>, x, r, w, resid_scale, eps, hidden, h_out, y_out, xs);
 }
 
 // ------------------------------------------------------------ RoPE + KV scatter (S rows)
@@ -190,9 +192,21 @@ cudaError_t launch_rope_apply(float* x, int B, int H, int S, int d, const float*
 }
 
 // ------------------------------------------------------------ SiLU gate * up (S rows)
-__global__ void silu_mul_kernel(const float* __restrict__ gu, int M, int inter, float* __restrict__ act) {
+__global__ void silu_mul_kernel(const float* __restrict__ gu, int M, int inter, float* __restrict__ act,
+                                uint16_t* __restrict__ xs) {
   pdl_wait();
   pdl_launch_dependents();
+  if (xs) {  // straight into the down projection's split operand, four channels per thread
+    const size_t total4 = (size_t)M * inter / 4;
+    for (size_t q = blockIdx.x * (size_t)blockDim.x + threadIdx.x; q < total4; q += (size_t)gridDim.x * blockDim.x) {
+      const size_t m = q / (inter / 4);
+      const int i = (int)(q % (inter / 4)) * 4;
+      const float4 g = *reinterpret_cast<const float4*>(gu + m * 2 * inter + i);
+      const float4 u = *reinterpret_cast<const float4*>(gu + m * 2 * inter + inter + i);
+      store_split4(xs, M, inter, m, i, make_float4(silu(g.x) * u.x, silu(g.y) * u.y, silu(g.z) * u.z, silu(g.w) * u.w));
+    }
+    return;
+  }
   const size_t total = (size_t)M * inter;
   for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
        idx += (size_t)gridDim.x * blockDim.x) {
@@ -202,12 +216,13 @@ __global__ void silu_mul_kernel(const float* __restrict__ gu, int M, int inter, 
   }
 }
 
-cudaError_t launch_silu_mul(const float* gu, int M, int inter, float* act, cudaStream_t st) {
-  const size_t total = (size_t)M * inter;
+cudaError_t launch_silu_mul(const float* gu, int M, int inter, float* act, cudaStream_t st, uint16_t* xs) {
+  if (xs && (inter % 4 != 0 || ((uintptr_t)gu & 15))) return cudaErrorInvalidValue;
+  const size_t total = xs ? (size_t)M * inter / 4 : (size_t)M * inter;
   const int grid = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
   count_launch();
   PdlLaunch l(dim3(grid), dim3(256), 0, st);
-  return cudaLaunchKernelEx(&l.cfg, silu_mul_kernel, gu, M, inter, act);
+  return cudaLaunchKernelEx(&l.cfg, silu_mul_kernel, gu, M, inter, act, xs);
 }
 
 // ------------------------------------------------------------ embedding gather

@@ -26,7 +26,8 @@ struct AttnPrefillArgs {
   int B, S, nh, nkv, d, s_max;
   float scale;
   int causal;
-  float* out;  // [B, S, nh*d]
+  float* out;    // [B, S, nh*d]
+  uint16_t* xs;  // optional: out written instead as the tcgen05 GEMM's split operand [2 B S, nh*d]
 };
 
 struct GemmArgs {

@@ -391,10 +391,17 @@ int enqueue_batch_step(vx_lm* lm, int B, cudaStream_t st) {
   const int H = lm->H, I = lm->I, qkvw = lm->qs + 2 * lm->ks;
   const float eps = lm->cfg.rms_norm_eps;
   int rc = VX_OK;
+  // the RMSNorm and SiLU*up kernels write the few-row GEMMs' split operand themselves
+  uint16_t* xs = lm->ws.scratch ? tc_gemm_presplit_buffer(lm->ws.scratch) : nullptr;
+  const bool ps_qkv = presplit_ok(ctx, &lm->ws, B, qkvw, H), ps_gu = presplit_ok(ctx, &lm->ws, B, 2 * I, H),
+             ps_d = presplit_ok(ctx, &lm->ws, B, H, I);
   for (int l = 0; l < lm->L; ++l) {
     const LmLayer& w = lm->layers[l];
-    VX_CUDA(ctx, launch_rmsnorm_residual(lm->bx, nullptr, w.ln_in, 1.f, eps, B, H, nullptr, lm->bxn, st));
-    if ((rc = linear(ctx, &lm->ws, lm->bxn, H, B, qkvw, H, w.wqkv, nullptr, nullptr, 1.f, lm->bqkv, qkvw, st))) return rc;
+    VX_CUDA(ctx, launch_rmsnorm_residual(lm->bx, nullptr, w.ln_in, 1.f, eps, B, H, nullptr, ps_qkv ? nullptr : lm->bxn,
+                                         st, ps_qkv ? xs : nullptr));
+    rc = ps_qkv ? linear_presplit(ctx, &lm->ws, B, qkvw, H, w.wqkv, nullptr, nullptr, 1.f, lm->bqkv, qkvw, st)
+                : linear(ctx, &lm->ws, lm->bxn, H, B, qkvw, H, w.wqkv, nullptr, nullptr, 1.f, lm->bqkv, qkvw, st);
+    if (rc) return rc;
     VX_CUDA(ctx, launch_rope_scatter(lm->bqkv, B, 1, lm->nh, lm->nkv, lm->d, lm->rope, 0, lm->bq, lm->kc(l, 0),
                                      lm->vc(l, 0), lm->max_length, st, lm->d_pos));
     AttnDecodeArgs ad = {lm->bq, lm->kc(l, 0), lm->vc(l, 0), B, lm->nh, lm->nkv, lm->d, lm->max_length, lm->d_pos, 0,
@@ -402,10 +409,15 @@ int enqueue_batch_step(vx_lm* lm, int B, cudaStream_t st) {
     VX_CUDA(ctx, launch_attn_decode(ad, st, false));
     if ((rc = linear(ctx, &lm->ws, lm->battn, lm->qs, B, H, lm->qs, w.wo, nullptr, lm->bx, lm->res_scale, lm->bx, H, st)))
       return rc;
-    VX_CUDA(ctx, launch_rmsnorm_residual(lm->bx, nullptr, w.ln_post, 1.f, eps, B, H, nullptr, lm->bxn, st));
-    if ((rc = linear(ctx, &lm->ws, lm->bxn, H, B, 2 * I, H, w.wgu, nullptr, nullptr, 1.f, lm->bgu, 2 * I, st))) return rc;
-    VX_CUDA(ctx, launch_silu_mul(lm->bgu, B, I, lm->bact, st));
-    if ((rc = linear(ctx, &lm->ws, lm->bact, I, B, H, I, w.wd, nullptr, lm->bx, lm->res_scale, lm->bx, H, st))) return rc;
+    VX_CUDA(ctx, launch_rmsnorm_residual(lm->bx, nullptr, w.ln_post, 1.f, eps, B, H, nullptr, ps_gu ? nullptr : lm->bxn,
+                                         st, ps_gu ? xs : nullptr));
+    rc = ps_gu ? linear_presplit(ctx, &lm->ws, B, 2 * I, H, w.wgu, nullptr, nullptr, 1.f, lm->bgu, 2 * I, st)
+               : linear(ctx, &lm->ws, lm->bxn, H, B, 2 * I, H, w.wgu, nullptr, nullptr, 1.f, lm->bgu, 2 * I, st);
+    if (rc) return rc;
+    VX_CUDA(ctx, launch_silu_mul(lm->bgu, B, I, lm->bact, st, ps_d ? xs : nullptr));
+    rc = ps_d ? linear_presplit(ctx, &lm->ws, B, H, I, w.wd, nullptr, lm->bx, lm->res_scale, lm->bx, H, st)
+              : linear(ctx, &lm->ws, lm->bact, I, B, H, I, w.wd, nullptr, lm->bx, lm->res_scale, lm->bx, H, st);
+    if (rc) return rc;
   }
   return enqueue_batch_head(lm, B, st, true);
 }
@@ -692,15 +704,23 @@ int vx_lm_forward(vx_lm* lm, const float* embeds, int B, int S, int causal, int 
   cudaStream_t st = ctx->stream;
   const int H = lm->H, I = lm->I, qkvw = lm->qs + 2 * lm->ks;
   VX_CUDA(ctx, cudaMemcpyAsync(lm->pf_x, embeds, M * H * 4, cudaMemcpyDefault, st));
+  // the RMSNorm, attention and SiLU*up kernels write the few-row GEMMs' split operand
+  // themselves when the rows fit one tcgen05 chunk (the attention only as one launch)
+  uint16_t* xs = lm->ws.scratch ? tc_gemm_presplit_buffer(lm->ws.scratch) : nullptr;
+  const int Mi = (int)M;
+  const bool ps_qkv = presplit_ok(ctx, &lm->ws, Mi, qkvw, H), ps_gu = presplit_ok(ctx, &lm->ws, Mi, 2 * I, H),
+             ps_d = presplit_ok(ctx, &lm->ws, Mi, H, I),
+             ps_o = presplit_ok(ctx, &lm->ws, Mi, H, lm->qs) && (!fill_cache || B == 1);
   for (int l = 0; l < lm->L; ++l) {
     const LmLayer& w = lm->layers[l];
     // K/V for this layer: the cache itself (prefill) or a [B, nkv, S, d] temporary
     float* kd = fill_cache ? lm->kc(l, 0) : lm->pf_k;
     float* vd = fill_cache ? lm->vc(l, 0) : lm->pf_v;
     const int s_max = fill_cache ? lm->max_length : S;
-    VX_CUDA(ctx, launch_rmsnorm_residual(lm->pf_x, nullptr, w.ln_in, 1.f, lm->cfg.rms_norm_eps, (int)M, H, nullptr,
-                                         lm->pf_xn, st));
-    rc = linear(ctx, &lm->ws, lm->pf_xn, H, (int)M, qkvw, H, w.wqkv, nullptr, nullptr, 1.f, lm->pf_qkv, qkvw, st);
+    VX_CUDA(ctx, launch_rmsnorm_residual(lm->pf_x, nullptr, w.ln_in, 1.f, lm->cfg.rms_norm_eps, Mi, H, nullptr,
+                                         ps_qkv ? nullptr : lm->pf_xn, st, ps_qkv ? xs : nullptr));
+    rc = ps_qkv ? linear_presplit(ctx, &lm->ws, Mi, qkvw, H, w.wqkv, nullptr, nullptr, 1.f, lm->pf_qkv, qkvw, st)
+                : linear(ctx, &lm->ws, lm->pf_xn, H, Mi, qkvw, H, w.wqkv, nullptr, nullptr, 1.f, lm->pf_qkv, qkvw, st);
     if (rc) return rc;
     if (fill_cache) {
       for (int b = 0; b < B; ++b)
@@ -713,22 +733,27 @@ int vx_lm_forward(vx_lm* lm, const float* embeds, int B, int S, int causal, int 
     if (fill_cache) {
       for (int b = 0; b < B; ++b) {
         AttnPrefillArgs ap = {lm->pf_q + (size_t)b * S * lm->qs, lm->kc(l, b), lm->vc(l, b), 1, S, lm->nh, lm->nkv,
-                              lm->d, s_max, lm->attn_scale, causal, lm->pf_attn + (size_t)b * S * lm->qs};
+                              lm->d, s_max, lm->attn_scale, causal, lm->pf_attn + (size_t)b * S * lm->qs,
+                              ps_o ? xs : nullptr};
         VX_CUDA(ctx, launch_attn_prefill(ap, st, true));
       }
     } else {
-      AttnPrefillArgs ap = {lm->pf_q, kd, vd, B, S, lm->nh, lm->nkv, lm->d, s_max, lm->attn_scale, causal, lm->pf_attn};
+      AttnPrefillArgs ap = {lm->pf_q,  kd,     vd,          B,           S, lm->nh, lm->nkv, lm->d, s_max, lm->attn_scale,
+                            causal, lm->pf_attn, ps_o ? xs : nullptr};
       VX_CUDA(ctx, launch_attn_prefill(ap, st, true));
     }
-    rc = linear(ctx, &lm->ws, lm->pf_attn, lm->qs, (int)M, H, lm->qs, w.wo, nullptr, lm->pf_x, lm->res_scale, lm->pf_x,
-                H, st);
+    rc = ps_o ? linear_presplit(ctx, &lm->ws, Mi, H, lm->qs, w.wo, nullptr, lm->pf_x, lm->res_scale, lm->pf_x, H, st)
+              : linear(ctx, &lm->ws, lm->pf_attn, lm->qs, Mi, H, lm->qs, w.wo, nullptr, lm->pf_x, lm->res_scale, lm->pf_x,
+                       H, st);
     if (rc) return rc;
-    VX_CUDA(ctx, launch_rmsnorm_residual(lm->pf_x, nullptr, w.ln_post, 1.f, lm->cfg.rms_norm_eps, (int)M, H, nullptr,
-                                         lm->pf_xn, st));
-    rc = linear(ctx, &lm->ws, lm->pf_xn, H, (int)M, 2 * I, H, w.wgu, nullptr, nullptr, 1.f, lm->pf_gu, 2 * I, st);
+    VX_CUDA(ctx, launch_rmsnorm_residual(lm->pf_x, nullptr, w.ln_post, 1.f, lm->cfg.rms_norm_eps, Mi, H, nullptr,
+                                         ps_gu ? nullptr : lm->pf_xn, st, ps_gu ? xs : nullptr));
+    rc = ps_gu ? linear_presplit(ctx, &lm->ws, Mi, 2 * I, H, w.wgu, nullptr, nullptr, 1.f, lm->pf_gu, 2 * I, st)
+               : linear(ctx, &lm->ws, lm->pf_xn, H, Mi, 2 * I, H, w.wgu, nullptr, nullptr, 1.f, lm->pf_gu, 2 * I, st);
     if (rc) return rc;
-    VX_CUDA(ctx, launch_silu_mul(lm->pf_gu, (int)M, I, lm->pf_act, st));
-    rc = linear(ctx, &lm->ws, lm->pf_act, I, (int)M, H, I, w.wd, nullptr, lm->pf_x, lm->res_scale, lm->pf_x, H, st);
+    VX_CUDA(ctx, launch_silu_mul(lm->pf_gu, Mi, I, lm->pf_act, st, ps_d ? xs : nullptr));
+    rc = ps_d ? linear_presplit(ctx, &lm->ws, Mi, H, I, w.wd, nullptr, lm->pf_x, lm->res_scale, lm->pf_x, H, st)
+              : linear(ctx, &lm->ws, lm->pf_act, I, Mi, H, I, w.wd, nullptr, lm->pf_x, lm->res_scale, lm->pf_x, H, st);
     if (rc) return rc;
   }
   VX_CUDA(ctx, launch_rmsnorm_residual(lm->pf_x, nullptr, lm->norm_w, 1.f, lm->cfg.rms_norm_eps, (int)M, H, nullptr,

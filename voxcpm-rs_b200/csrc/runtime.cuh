@@ -35,8 +35,17 @@ size_t tc_gemm_scratch_bytes(int M, int N, int K, int target_ctas);
 cudaError_t launch_tc_gemm(const float* X, int ldx, int M, int N, int K, const uint16_t* W, const float* bias,
                            const float* R, float res_scale, float* Y, int ldy, void* scratch, unsigned* counters,
                            int* err, cudaStream_t st, int target_ctas);
+// The same GEMM with its activations already split by their producer into the buffer
+// tc_gemm_presplit_buffer(scratch): rows [0, M) bf16(x), rows [M, 2M) bf16(x - bf16(x)),
+// row stride K (no split kernel launch).
+uint16_t* tc_gemm_presplit_buffer(void* scratch);
+cudaError_t launch_tc_gemm_presplit(int M, int N, int K, const uint16_t* W, const float* bias, const float* R,
+                                    float res_scale, float* Y, int ldy, void* scratch, unsigned* counters, int* err,
+                                    cudaStream_t st, int target_ctas);
+// xs: also (y_out may be null: instead) store y as the tcgen05 GEMM's split operand [2 rows, hidden]
 cudaError_t launch_rmsnorm_residual(const float* x, const float* r, const float* w, float resid_scale, float eps,
-                                    int rows, int hidden, float* h_out, float* y_out, cudaStream_t st);
+                                    int rows, int hidden, float* h_out, float* y_out, cudaStream_t st,
+                                    uint16_t* xs = nullptr);
 cudaError_t launch_rope_scatter(const float* qkv, int B, int S, int nh, int nkv, int d, const RopeParams* rope,
                                 int pos0, float* q_out, float* kcache, float* vcache, int s_max, cudaStream_t st,
                                 const int* pos_ptr = nullptr);
@@ -45,7 +54,8 @@ cudaError_t launch_argmax_rows(const float* logits, int B, int V, const int* ste
 cudaError_t launch_advance(int* pos, int* step, bool inc_pos, cudaStream_t st);
 cudaError_t launch_rope_apply(float* x, int B, int H, int S, int d, const float* cos, const float* sin,
                               cudaStream_t st);
-cudaError_t launch_silu_mul(const float* gu, int M, int inter, float* act, cudaStream_t st);
+// xs: write silu(gate)*up as the tcgen05 GEMM's split operand [2M, inter] instead of act
+cudaError_t launch_silu_mul(const float* gu, int M, int inter, float* act, cudaStream_t st, uint16_t* xs = nullptr);
 cudaError_t launch_embed(const uint16_t* E, const int* ids, int n, int H, int V, float scale, float* out,
                          cudaStream_t st);
 cudaError_t launch_fsq_quant(float* h, size_t n, float scale, cudaStream_t st);
@@ -73,6 +83,7 @@ struct vx_ctx {
   bool pdl = true;                   // programmatic dependent launch between decode kernels
   int gemv_ctas = 296;               // target GEMV grid (CTAs); env VX_GEMV_CTAS overrides
   bool tc_gemm = true;               // tcgen05 path for few-row GEMMs (env VX_TC_GEMM=0: CUDA cores)
+  bool presplit = true;              // producers write the tcgen05 GEMM's split operand (env VX_PRESPLIT=0: a split kernel)
   bool l2_prefetch = false;          // decode kernels prefetch the next kernel's weights into L2
   bool persist = true;               // batch-1 decode step as one persistent launch (env VX_PERSIST=0: 141 launches)
   int persist_nst = 0;               // its ring depth cap in stages, 0 = shared-memory limit (env VX_PERSIST_NST)
@@ -134,6 +145,11 @@ void workspace_free(LinearWorkspace* ws);
 // M == 1: streamed GEMV; 2..128-row chunks: tcgen05 GEMM; otherwise the CUDA-core GEMM.
 int linear(vx_ctx* ctx, const LinearWorkspace* ws, const float* X, int ldx, int M, int N, int K, const uint16_t* W,
            const float* bias, const float* R, float res_scale, float* Y, int ldy, cudaStream_t st);
+// Whether linear() over M rows takes the tcgen05 path as one chunk, so that the producer of X
+// may write it split (tc_gemm_presplit_buffer(ws->scratch)) and linear_presplit() run the GEMM.
+bool presplit_ok(vx_ctx* ctx, const LinearWorkspace* ws, int M, int N, int K);
+int linear_presplit(vx_ctx* ctx, const LinearWorkspace* ws, int M, int N, int K, const uint16_t* W, const float* bias,
+                    const float* R, float res_scale, float* Y, int ldy, cudaStream_t st);
 
 // Greedy LM decoding, split for the synthesis loop (lm.cu).
 vx_ctx* lm_ctx(vx_lm* lm);

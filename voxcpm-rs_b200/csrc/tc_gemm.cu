@@ -421,12 +421,15 @@ size_t tc_gemm_scratch_bytes(int M, int N, int K, int target_ctas) {
 }
 
 // scratch: >= tc_gemm_scratch_bytes; counters: >= N/128 zeroed words (reset by the kernel).
-cudaError_t launch_tc_gemm(const float* X, int ldx, int M, int N, int K, const uint16_t* W, const float* bias,
-                           const float* R, float res_scale, float* Y, int ldy, void* scratch, unsigned* counters,
-                           int* err, cudaStream_t st, int target_ctas) {
-  if (!tc_gemm_supported(M, N, K)) return cudaErrorInvalidValue;
-  cudaError_t e = get_encoder();
-  if (e != cudaSuccess) return e;
+namespace {
+
+// The GEMM proper over the split activations at the start of `scratch`: rows [0, M) bf16(x),
+// rows [M, 2M) bf16(x - bf16(x)); the tensor map covers `x_rows` rows (2M: the TMA box's
+// rows past them read as zeros; NB: the split kernel wrote the zero rows).
+cudaError_t tc_gemm_core(int M, int N, int K, int x_rows, const uint16_t* W, const float* bias, const float* R,
+                         float res_scale, float* Y, int ldy, void* scratch, unsigned* counters, int* err,
+                         cudaStream_t st, int target_ctas) {
+  cudaError_t e;
   const int NB = ((2 * M + 15) / 16) * 16;
   const int tiles = N / TC_BM, kblocks = K / TC_BK;
   // K splits: the largest divisor of the K blocks (at most TC_MAX_SPLITS) keeping the grid
@@ -435,16 +438,11 @@ cudaError_t launch_tc_gemm(const float* X, int ldx, int M, int N, int K, const u
   const int cap = std::max(tiles, target_ctas / 2);
   for (int s = 1; s <= std::min(TC_MAX_SPLITS, kblocks); ++s)
     if (kblocks % s == 0 && tiles * s <= cap) splits = s;
-  uint16_t* Xs = static_cast<uint16_t*>(scratch);
+  const uint16_t* Xs = static_cast<const uint16_t*>(scratch);
   float* partials = reinterpret_cast<float*>(static_cast<char*>(scratch) + (((size_t)NB * K * 2 + 255) & ~(size_t)255));
-  count_launch();
-  {
-    PdlLaunch l(dim3(std::min(4096, (NB * K + 255) / 256)), dim3(256), 0, st);
-    if ((e = cudaLaunchKernelEx(&l.cfg, split_bf16_kernel, X, ldx, M, K, NB, Xs)) != cudaSuccess) return e;
-  }
   CUtensorMap tmW, tmX;
   if ((e = make_map(&tmW, W, N, K, TC_BM)) != cudaSuccess) return e;
-  if ((e = make_map(&tmX, Xs, NB, K, NB)) != cudaSuccess) return e;
+  if ((e = make_map(&tmX, Xs, x_rows, K, NB)) != cudaSuccess) return e;
   TcGemmArgs a = {};
   a.M = M;
   a.N = N;
@@ -479,6 +477,36 @@ cudaError_t launch_tc_gemm(const float* X, int ldx, int M, int N, int K, const u
     a.cluster = 1;
   }
   return cudaLaunchKernelEx(&l.cfg, tc_gemm_kernel, tmW, tmX, a);
+}
+
+}  // namespace
+
+cudaError_t launch_tc_gemm(const float* X, int ldx, int M, int N, int K, const uint16_t* W, const float* bias,
+                           const float* R, float res_scale, float* Y, int ldy, void* scratch, unsigned* counters,
+                           int* err, cudaStream_t st, int target_ctas) {
+  if (!tc_gemm_supported(M, N, K)) return cudaErrorInvalidValue;
+  cudaError_t e = get_encoder();
+  if (e != cudaSuccess) return e;
+  const int NB = ((2 * M + 15) / 16) * 16;
+  count_launch();
+  {
+    PdlLaunch l(dim3(std::min(4096, (NB * K + 255) / 256)), dim3(256), 0, st);
+    if ((e = cudaLaunchKernelEx(&l.cfg, split_bf16_kernel, X, ldx, M, K, NB, static_cast<uint16_t*>(scratch))) !=
+        cudaSuccess)
+      return e;
+  }
+  return tc_gemm_core(M, N, K, NB, W, bias, R, res_scale, Y, ldy, scratch, counters, err, st, target_ctas);
+}
+
+uint16_t* tc_gemm_presplit_buffer(void* scratch) { return static_cast<uint16_t*>(scratch); }
+
+cudaError_t launch_tc_gemm_presplit(int M, int N, int K, const uint16_t* W, const float* bias, const float* R,
+                                    float res_scale, float* Y, int ldy, void* scratch, unsigned* counters, int* err,
+                                    cudaStream_t st, int target_ctas) {
+  if (!tc_gemm_supported(M, N, K)) return cudaErrorInvalidValue;
+  cudaError_t e = get_encoder();
+  if (e != cudaSuccess) return e;
+  return tc_gemm_core(M, N, K, 2 * M, W, bias, R, res_scale, Y, ldy, scratch, counters, err, st, target_ctas);
 }
 
 }  // namespace vx
