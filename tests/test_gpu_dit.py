@@ -86,3 +86,32 @@ def test_cfm_solve_full(ctx, full_dit, sway, zero_star):
     assert_close(got, want, **TOL, what="cfm solve")
     assert np.abs(got - want).max() < 2e-3
     dit.close()
+
+
+def test_dit_forward_producer_split_is_exact(full_dit):
+    """The RMSNorm, attention and SiLU*up kernels write the few-row GEMMs' split operand
+    themselves (default); VX_PRESPLIT=0 runs the separate split kernel instead.  The two
+    paths do the same arithmetic, so the LocDiT forward must match bit for bit."""
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    from voxcpm_rs_b200.minicpm4 import Context
+    dcfg, w, _ = full_dit
+    rng = np.random.default_rng(22)
+    x = rng.standard_normal((2, 64, 4), dtype=np.float32)
+    mu = rng.standard_normal((2, 2048), dtype=np.float32)
+    cond = rng.standard_normal((2, 64, 4), dtype=np.float32)
+    outs = []
+    for flag in ("0", "1"):
+        old_env = os.environ.get("VX_PRESPLIT")
+        os.environ["VX_PRESPLIT"] = flag
+        try:
+            c = Context(0)
+        finally:
+            if old_env is None:
+                del os.environ["VX_PRESPLIT"]
+            else:
+                os.environ["VX_PRESPLIT"] = old_env
+        dit = VoxCpmLocDiTV2(c, dcfg, w)
+        outs.append(dit.forward(_t(x), _t(mu), [0.4, 0.4], _t(cond), [0.0, 0.0]).cpu().numpy())
+        dit.close()
+        c.close()
+    assert np.array_equal(outs[0], outs[1]), np.abs(outs[0] - outs[1]).max()
