@@ -190,9 +190,15 @@ struct Geo {
   int kind;
 };
 
+// Q phase: units [0, q_pair_units) are rotate_half pairs of 8-row groups of the q and k
+// heads (two stages each); the v rows follow as plain 8-row units (one stage each), so the
+// phase's 2.16 stages per CTA spread as at most 3 instead of two whole pair units (4).
+__device__ __forceinline__ int q_pair_units(const PersistArgs& a) { return (a.nh + a.nkv) * a.d / 16; }
+
 __device__ __forceinline__ int unit_row(const PersistArgs& a, int kind, int u, int gi) {
   if (kind == PH_Q) {  // rotate_half pair: rows j*8.. of the first and second half of a head
-    const int hp = a.d / 16;
+    const int hp = a.d / 16, up = q_pair_units(a);
+    if (u >= up) return (a.nh + a.nkv) * a.d + (u - up) * PK_ROWS;
     return (u / hp) * a.d + (u % hp) * PK_ROWS + gi * (a.d / 2);
   }
   if (kind == PH_M) return (gi == 1 ? a.I : 0) + u * PK_ROWS;  // gate rows, up rows, wdt rows
@@ -202,7 +208,7 @@ __device__ __forceinline__ int unit_row(const PersistArgs& a, int kind, int u, i
 __device__ __forceinline__ Geo geo_of(const PersistArgs& a, int l, int kind, const AttGeo& at) {
   const PersistLayer& w = s_lay[l < a.L ? l : 0];
   switch (kind) {
-    case PH_Q: return {w.wqkv, a.H, (a.nh + 2 * a.nkv) * a.d / 16, 2, PH_Q};
+    case PH_Q: return {w.wqkv, a.H, q_pair_units(a) + a.nkv * a.d / PK_ROWS, 2, PH_Q};
     case PH_ATT: return {nullptr, 0, at.items, at.tps, PH_ATT};
     case PH_O: return {w.wo, a.nh * a.d, a.H / PK_ROWS, 1, PH_O};
     case PH_M: return {w.wgu, a.H, a.I / PK_ROWS, 3, PH_M};
@@ -226,7 +232,8 @@ struct Cursor {
   bool valid;
 };
 
-__device__ __forceinline__ int unit_groups(const Cursor& k, const AttGeo& at) {
+__device__ __forceinline__ int unit_groups(const PersistArgs& a, const Cursor& k, const AttGeo& at) {
+  if (k.kind == PH_Q && k.u >= q_pair_units(a)) return 1;
   return k.kind == PH_ATT ? att_tiles(at, k.u) : k.g.gpu;
 }
 
@@ -241,7 +248,7 @@ __device__ void cursor_seek(const PersistArgs& a, Cursor& k, const AttGeo& at) {
       k.gi = 0;
       k.c = 0;
       k.nch = k.kind == PH_ATT ? 1 : k.g.K / KC;
-      k.ngi = unit_groups(k, at);
+      k.ngi = unit_groups(a, k, at);
       k.valid = true;
       return;
     }
@@ -271,7 +278,7 @@ __device__ void cursor_next(const PersistArgs& a, Cursor& k, const AttGeo& at) {
   k.gi = 0;
   k.u += gridDim.x;
   if (k.u < k.g.U) {
-    k.ngi = unit_groups(k, at);
+    k.ngi = unit_groups(a, k, at);
     return;
   }
   k.off = (k.off + k.g.U) % gridDim.x;
@@ -770,7 +777,7 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
   float* xnext = xbuf(a, l + 1);
   float mvr[PK_ROWS];  // MLP: silu(gate) * up of the unit's 8 channels
   const int rrow = (lane >> 2) & 7;  // the row whose warp sum this lane holds after a reduction
-  const int last_group = kind == PH_M ? 1 : gpu - 1;
+  const int qpu = q_pair_units(a);
   // head: the warps' row partials of all this CTA's units are kept in sm.parts (free in this
   // phase) and summed once after the last unit, instead of a CTA barrier per unit
   const bool defer = kind == PH_HEAD && (size_t)((U - first + G - 1) / G) * (PK_ROWS * PK_CWARPS) <=
@@ -779,7 +786,9 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
   for (int u = first; u < U; u += G, ++k) {
     float* kpb = sm.kp + (k & 1) * (2 * PK_ROWS * PK_CWARPS);
     float t0 = 0.f, t1 = 0.f;
-    for (int gi = 0; gi < gpu; ++gi) {
+    const int ng = (kind == PH_Q && u >= qpu) ? 1 : gpu;  // Q: v rows are one group
+    const int last_group = kind == PH_M ? 1 : ng - 1;
+    for (int gi = 0; gi < ng; ++gi) {
       if (kind == PH_M && gi == 2) {
         // down_proj column block (mlp.rs:33): accumulate this warp's SL output columns over
         // rows j0..j0+7 of wdt, weighted by the unit's 8 silu(gate)*up values
@@ -847,7 +856,7 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
           for (int r = 0; r < PK_ROWS; ++r) mvr[r] = __shfl_sync(0xffffffffu, m, r);
         } else if (lane == 0) {
           t0 = sum8(kpb + warp * PK_CWARPS);
-          if (gpu == 2) t1 = sum8(kpb + (PK_ROWS + warp) * PK_CWARPS);
+          if (ng == 2) t1 = sum8(kpb + (PK_ROWS + warp) * PK_CWARPS);
         }
       }
     }
@@ -860,8 +869,12 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
         bv = t0;
         bi = row;
       }
+    } else if (kind == PH_Q && ng == 1) {
+      // a v row: straight into the cache at `pos`
+      const int head = row / a.d, ii = row % a.d;
+      a.vcache[(size_t)l * a.kv_layer_stride + ((size_t)(head - a.nh - a.nkv) * a.s_max + pos) * a.d + ii] = t0;
     } else if (kind == PH_Q) {
-      // LongRoPE on q/k rows (rope.rs:76-95), post-RoPE k and v into the cache at `pos`
+      // LongRoPE on q/k rows (rope.rs:76-95), post-RoPE q and k into the cache at `pos`
       const int head = row / a.d, ii = row % a.d, half = a.d / 2;
       const float ya = t0, yb = t1;
       float oa = ya, ob = yb;
@@ -874,11 +887,9 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
         a.q[head * a.d + ii] = oa;
         a.q[head * a.d + ii + half] = ob;
       } else {
-        const bool isk = head < a.nh + a.nkv;
-        float* dst = (isk ? a.kcache : a.vcache) + (size_t)l * a.kv_layer_stride +
-                     ((size_t)(head - a.nh - (isk ? 0 : a.nkv)) * a.s_max + pos) * a.d;
-        dst[ii] = isk ? oa : ya;
-        dst[ii + half] = isk ? ob : yb;
+        float* dst = a.kcache + (size_t)l * a.kv_layer_stride + ((size_t)(head - a.nh) * a.s_max + pos) * a.d;
+        dst[ii] = oa;
+        dst[ii + half] = ob;
       }
     } else {
       // o_proj + residual (layer.rs:33-38): x1 = x0 + s*o; x1 also seeds the next layer's
