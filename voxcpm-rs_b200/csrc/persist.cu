@@ -15,6 +15,7 @@
 // every CTA streams about the same bytes per token):
 //   Q    input RMSNorm -> qkv_proj rows -> LongRoPE -> q buffer, k/v into the static cache
 //        (layer.rs:64-66, attention.rs:102-127); unit = a rotate_half pair of 8-row groups
+//        of the q / k heads, then 8 v rows
 //   ATT  flash-decode over the cached prefix (attention.rs:129-150, 156-204); unit = one KV
 //        head's 8 query heads against a run of 32-position tiles whose K/V rows arrive
 //        through the ring (the current position's row, written by Q, is read after the
@@ -37,9 +38,11 @@
 // elsewhere the CTA records it, stops cleanly (all in-flight copies landed) and the host
 // reports VX_ERR_TIMEOUT.  The last CTA to leave zeroes the counters for the next launch.
 //
-// GEMV arithmetic per output row is the same as the per-kernel step's streamed GEMV (same
-// per-lane partial sums and warp tree).  The down projection sums its 148 CTA partials with
-// f32 reductions in arrival order, so its last bits can differ from run to run.
+// Every GEMV output row is summed in a fixed order: each lane's run of KC/256 products, the
+// lane butterfly within a warp, then the 8 warps' K slices in warp order.  The per-kernel
+// step's GEMV sums in another order, so the two agree to rounding, not bit for bit.  The down
+// projection sums its 148 CTA partials with f32 reductions in arrival order, so its last
+// bits can differ from run to run.
 #include <algorithm>
 #include <cfloat>
 #include <climits>
