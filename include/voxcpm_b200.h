@@ -131,7 +131,9 @@ int vx_attention_decode(vx_ctx* ctx, const float* q, const float* kcache, const 
  * array of 1 MiB plus 64 counters, held by every GPU that loads the library until exit, so
  * it accepts B * nkv <= 64 and B * nkv * 16 * 8 * (head_dim + 2) * 4 <= 1 MiB (else
  * VX_ERR_SHAPE).  The first call on a device looks up the array's device address; make that
- * call before any stream capture.  All calls share the array: calls that overlap on the GPU
+ * call before any stream capture.  The address is kept for the life of the process: it does
+ * not survive cudaDeviceReset, so do not call this after resetting a device the library has
+ * already used.  All calls share the array: calls that overlap on the GPU
  * race and must be serialised by the caller.  Returns a status code only (no context, so no
  * message).  Same arguments and results as vx_attention_decode; `stream` NULL = the legacy
  * default stream.  No counterpart in the reference. */

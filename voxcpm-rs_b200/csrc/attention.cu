@@ -289,6 +289,8 @@ static __device__ __align__(256) unsigned int g_static_counters[kStaticCounters]
 
 // Device addresses of the two arrays, looked up once per device.  In host code the array
 // names are host-side stand-ins, not device addresses, so they are never passed to a kernel.
+// The cached addresses belong to the device's primary context: after a cudaDeviceReset the
+// module is loaded again and they are stale (documented for callers in the header).
 struct StaticScratchAddr {
   float* partials = nullptr;
   unsigned int* counters = nullptr;

@@ -131,7 +131,8 @@ int vx_ctx_create(int device, vx_ctx** out) {
   if (device < 0 || device >= n) return VX_ERR_ARG;
   vx_ctx* ctx = new vx_ctx();
   ctx->device = device;
-  // tuning knobs (documented in DESIGN.md): GEMV grid target and programmatic dependent launch
+  // tuning knobs read from the environment: GEMV grid target, programmatic dependent launch,
+  // the tcgen05 few-row GEMM and the persistent decode step's ring / grid / prefetch settings
   if (const char* s = getenv("VX_GEMV_CTAS")) ctx->gemv_ctas = std::max(1, atoi(s));
   if (const char* s = getenv("VX_PDL")) ctx->pdl = atoi(s) != 0;
   if (const char* s = getenv("VX_L2_PREFETCH")) ctx->l2_prefetch = atoi(s) != 0;

@@ -86,7 +86,7 @@ struct vx_lm {
   PersistLayer* pk_layers = nullptr;   // device [L]
   unsigned* pk_cnt = nullptr;          // phase counters [5L + 2]
   float* pk_att_part = nullptr;        // attention split partials of the persistent step
-  float* pk_x0b = nullptr;             // its second residual-stream buffer [H]
+  long long* pk_xacc = nullptr;        // its fixed-point residual accumulators [2][H]
   uint16_t* pk_wdt = nullptr;          // its transposed down_proj weights [L][I][H]
   LinearWorkspace ws;  // tcgen05 few-row GEMM workspace (prefill, non-causal forward)
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
@@ -291,7 +291,7 @@ cudaError_t enqueue_persist_step(vx_lm* lm, cudaStream_t st, bool cooperative,
   a.step = lm->d_step;
   a.tokens = lm->d_tokens;
   a.x0 = lm->x;
-  a.x0b = lm->pk_x0b;
+  a.xacc = lm->pk_xacc;
   a.x1 = lm->x_mid;
   a.q = lm->q;
   a.logits = lm->logits;
@@ -309,7 +309,7 @@ cudaError_t enqueue_persist_step(vx_lm* lm, cudaStream_t st, bool cooperative,
 }
 
 int capture_step(vx_lm* lm, int mode, cudaGraphExec_t* exec) {
-  // mode 0: per-kernel step; 1: persistent, cooperative launch; 2: persistent, plain launch
+  // mode 0: per-kernel step; 1: persistent, cooperative launch
   vx_ctx* ctx = lm->ctx;
   cudaGraph_t graph = nullptr;
   const unsigned long long before = g_launches;
@@ -342,9 +342,12 @@ int capture_step(vx_lm* lm, int mode, cudaGraphExec_t* exec) {
 int build_step_graph(vx_lm* lm) {
   if (lm->step_exec) return VX_OK;
   if (lm->pk_grid > 0) {
-    for (int mode : {1, 2})
-      if (capture_step(lm, mode, &lm->step_exec) == VX_OK) return VX_OK;
-    lm->pk_grid = 0;  // neither launch form captures: use the per-kernel step
+    // The persistent step's CTAs wait on one another, so it needs a cooperative launch (every
+    // CTA resident at once).  If that cannot be captured, use the per-kernel step: a plain
+    // launch could leave CTAs unscheduled behind other work and end in VX_ERR_TIMEOUT.
+    if (capture_step(lm, 1, &lm->step_exec) == VX_OK) return VX_OK;
+    cudaGetLastError();
+    lm->pk_grid = 0;
   }
   return capture_step(lm, 0, &lm->step_exec);
 }
@@ -551,7 +554,7 @@ int vx_lm_create(vx_ctx* ctx, const vx_minicpm4_config* cfg, int max_batch, int 
       std::vector<PersistLayer> pl(lm->L);
       const size_t nc = persist_counter_count(lm->L);
       ok = cudaMalloc(&lm->pk_wdt, (size_t)lm->L * I * H * 2) == cudaSuccess &&
-           cudaMalloc(&lm->pk_x0b, H * 4) == cudaSuccess;
+           cudaMalloc(&lm->pk_xacc, 2 * H * 8) == cudaSuccess;
       for (int l = 0; ok && l < lm->L; ++l)
         pl[l] = {lm->layers[l].wqkv, lm->layers[l].wo, lm->layers[l].wgu, lm->pk_wdt + (size_t)l * I * H,
                  lm->layers[l].ln_in, lm->layers[l].ln_post};
@@ -589,7 +592,7 @@ void vx_lm_destroy(vx_lm* lm) {
                   lm->d_step, lm->d_tokens, lm->x, lm->hid_norm, lm->q, lm->attn, lm->act, lm->logits,
                   lm->attn_partials,
                   lm->attn_counters, lm->argmax_partials, lm->argmax_counter, lm->pf_ids,
-                  lm->x_mid,         lm->pk_layers, lm->pk_cnt, lm->pk_att_part, lm->pk_x0b, lm->pk_wdt};
+                  lm->x_mid,         lm->pk_layers, lm->pk_cnt, lm->pk_att_part, lm->pk_xacc, lm->pk_wdt};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   delete lm;

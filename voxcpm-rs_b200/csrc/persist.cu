@@ -21,13 +21,15 @@
 //        through the ring (the current position's row, written by Q, is read after the
 //        wait); each unit leaves its online-softmax partial (o, max, sum) in global memory
 //   O    merge of the attention partials -> o_proj + residual into x1 (attention.rs:153,
-//        layer.rs:67); unit = 8 rows.  Also seeds the next layer's residual buffer with x1.
+//        layer.rs:67); unit = 8 rows.  Also seeds the next layer's residual accumulator
+//        with x1 (fixed point, below).
 //   M    post-attention RMSNorm -> gate|up rows -> silu(gate)*up -> down_proj (mlp.rs:28-34,
 //        layer.rs:69-72); unit = 8 MLP channels j: their gate row, up row and down column
 //        (a row of the transposed down weight).  Each warp accumulates its slice of the
 //        2048 outputs across the CTA's units; at the end of the phase the CTA adds
-//        res_scale * its partial into the next layer's residual buffer with one bulk
-//        reduce-add.  Fusing the down projection removes a dependency round trip per layer.
+//        res_scale * its partial into the next layer's residual accumulator with one bulk
+//        integer reduce-add.  Fusing the down projection removes a dependency round trip
+//        per layer.
 // then the greedy head: final norm -> tied-embedding logits -> argmax -> next input
 // embedding, position and step advanced on the device.
 //
@@ -41,8 +43,11 @@
 // Every GEMV output row is summed in a fixed order: each lane's run of KC/256 products, the
 // lane butterfly within a warp, then the 8 warps' K slices in warp order.  The per-kernel
 // step's GEMV sums in another order, so the two agree to rounding, not bit for bit.  The down
-// projection sums its 148 CTA partials with f32 reductions in arrival order, so its last
-// bits can differ from run to run.
+// projection's CTA partials arrive in any order, so the residual stream of layers 1..L is
+// kept in fixed point (x * 2^32 in int64; |x| < 2^31 / grid): each partial is rounded once
+// to that grid and the integer sum is exact, hence independent of the arrival order, and
+// readers convert it back to f32 with one rounding.  The whole step is deterministic: the
+// same inputs give the same bits, run after run.
 #include <algorithm>
 #include <cfloat>
 #include <climits>
@@ -109,8 +114,28 @@ __device__ __forceinline__ void trace_mark(const PersistArgs& a, int p, int k) {
   if (a.trace) a.trace[((size_t)p * gridDim.x + blockIdx.x) * PERSIST_TRACE_FIELDS + k] = gtimer();
 }
 
-// Residual-stream buffer that is the input of layer l (layer L: the head's input).
-__device__ __forceinline__ float* xbuf(const PersistArgs& a, int l) { return (l & 1) ? a.x0b : a.x0; }
+// Fixed point of the residual accumulators: value x 2^32 in int64.
+__device__ __forceinline__ long long to_fix(float v) { return __float2ll_rn(v * 4294967296.0f); }
+__device__ __forceinline__ float from_fix(long long v) { return __ll2float_rn(v) * 2.3283064365386963e-10f; }
+
+// The input of layer l (layer L: the head's input): layer 0 reads the f32 embedding buffer,
+// later layers the fixed-point accumulator the previous layer's O and M phases wrote.
+struct XIn {
+  const float* f;
+  const long long* i;
+};
+__device__ __forceinline__ XIn xin_of(const PersistArgs& a, int l) {
+  return l == 0 ? XIn{a.x0, nullptr} : XIn{nullptr, a.xacc + (size_t)(l & 1) * a.H};
+}
+__device__ __forceinline__ float4 ldx4(const XIn& x, int k) {
+  if (x.i == nullptr) return __ldcg(reinterpret_cast<const float4*>(x.f + k));
+  const longlong2 p = __ldcg(reinterpret_cast<const longlong2*>(x.i + k));
+  const longlong2 q = __ldcg(reinterpret_cast<const longlong2*>(x.i + k + 2));
+  return make_float4(from_fix(p.x), from_fix(p.y), from_fix(q.x), from_fix(q.y));
+}
+__device__ __forceinline__ float ldx1(const XIn& x, int k) {
+  return x.i == nullptr ? __ldcg(x.f + k) : from_fix(__ldcg(x.i + k));
+}
 
 // flags[0]: consumers stopped (producer must stop too); flags[1]: last-arrival broadcast;
 // flags[2]: picked token broadcast; flags[3]: producer gave up.
@@ -453,11 +478,11 @@ __device__ void produce(const PersistArgs& a, const Smem& sm, int nst, const Att
 // x (f32 [K], produced in this launch or the previous one) -> xs, optionally RMS-normalised
 // exactly as MiniCpmRmsNorm::forward (src/minicpm4/mod.rs:62-67).  With a norm, x and the
 // norm weight are fetched in one round trip and held in registers (K <= 4096).
-__device__ void load_x(const float* x, const float* norm_w, int K, float eps, const Smem& sm) {
+__device__ void load_x(const XIn& x, const float* norm_w, int K, float eps, const Smem& sm) {
   const int tid = threadIdx.x;
   if (norm_w == nullptr) {
 #pragma unroll 4
-    for (int k = tid * 4; k < K; k += PK_CTHREADS * 4) *reinterpret_cast<float4*>(sm.xs + k) = ldcg4(x + k);
+    for (int k = tid * 4; k < K; k += PK_CTHREADS * 4) *reinterpret_cast<float4*>(sm.xs + k) = ldx4(x, k);
     csync();
     return;
   }
@@ -467,7 +492,7 @@ __device__ void load_x(const float* x, const float* norm_w, int K, float eps, co
   for (int i = 0; i < PK_XREG; ++i) {
     const int k = (tid + i * PK_CTHREADS) * 4;
     if (k < K) {
-      v[i] = ldcg4(x + k);
+      v[i] = ldx4(x, k);
       w[i] = __ldg(reinterpret_cast<const float4*>(norm_w + k));
     }
   }
@@ -736,8 +761,8 @@ __device__ __forceinline__ void prefetch_mlp(const PersistArgs& a, int l, int fi
 // partner is row w of the unit's second group).
 template <int KC, int D>
 __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& sm, CState st, int nst, int kind, int l,
-                                             int pos, int U, int K, int gpu, int first, const float* xsrc,
-                                             const float* norm_w, const float* resid, const AttGeo& at) {
+                                             int pos, int U, int K, int gpu, int first, const XIn xsrc,
+                                             const float* norm_w, const XIn resid, const AttGeo& at) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x;
   // residual of this warp's row in each of its first PK_RES_UNITS units, fetched together
@@ -746,7 +771,7 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
 #pragma unroll
   for (int k = 0; k < PK_RES_UNITS; ++k) {
     const int u = first + k * G;
-    resv[k] = (resid != nullptr && lane == 0 && u < U) ? __ldcg(resid + (size_t)u * PK_ROWS + warp) : 0.f;
+    resv[k] = (kind == PH_O && lane == 0 && u < U) ? ldx1(resid, u * PK_ROWS + warp) : 0.f;
   }
   if (kind == PH_O) {
     if (!att_merge<D>(a, at, sm, st.merges++)) {
@@ -777,7 +802,7 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
   bool lbad = false;
   float bv = -FLT_MAX;  // head: this warp's running argmax
   int bi = INT_MAX;
-  float* xnext = xbuf(a, l + 1);
+  long long* xnext = a.xacc + (size_t)((l + 1) & 1) * a.H;  // the next layer's accumulator
   float mvr[PK_ROWS];  // MLP: silu(gate) * up of the unit's 8 channels
   const int rrow = (lane >> 2) & 7;  // the row whose warp sum this lane holds after a reduction
   const int qpu = q_pair_units(a);
@@ -896,15 +921,15 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
       }
     } else {
       // o_proj + residual (layer.rs:33-38): x1 = x0 + s*o; x1 also seeds the next layer's
-      // residual buffer, into which the MLP phase adds s*down
+      // accumulator, into which the MLP phase adds s*down
       float r = 0.f;
 #pragma unroll
       for (int q = 0; q < PK_RES_UNITS; ++q)
         if (q == k) r = resv[q];
-      if (k >= PK_RES_UNITS) r = __ldcg(resid + row);
+      if (k >= PK_RES_UNITS) r = ldx1(resid, row);
       const float x1 = r + t0 * a.res_scale;
       a.x1[row] = x1;
-      xnext[row] = x1;
+      xnext[row] = to_fix(x1);
     }
   }
   if (defer) {
@@ -935,21 +960,28 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
   }
   if (kind == PH_M) {
     // this CTA's res_scale * down partial (xs[H, 2H), the warps' column slices side by side)
-    // into the next layer's residual buffer, seeded with x1 by the O phase: x0' = x1 + s * down
-    // (layer.rs:33-38, 72).  One bulk reduce-add through the TMA engine per CTA: 128-byte
-    // reductions at L2 instead of 16-byte ones from every lane.
+    // into the next layer's accumulator, seeded with x1 by the O phase: x0' = x1 + s * down
+    // (layer.rs:33-38, 72).  The partial is rounded to the accumulator's fixed point in
+    // xs[0, 2H) viewed as int64 [H] (the phase input there is no longer read: each lane holds
+    // its slice in registers), then one bulk integer reduce-add through the TMA engine per
+    // CTA: 128-byte reductions at L2, exact in any arrival order.
     const bool mine = !lbad && k > 0;
-    if (mine) {
+    float dv[CPL];
 #pragma unroll
-      for (int e = 0; e < CPL; ++e) dacc[e] *= a.res_scale;
+    for (int e = 0; e < CPL; ++e) dv[e] = dacc[e] * a.res_scale;
+    csync();  // every lane's accumulators are in registers before the int64 image overwrites xs
+    if (mine) {
+      long long* fx = reinterpret_cast<long long*>(sm.xs) + warp * SL + lane * CPL;
+#pragma unroll
+      for (int e = 0; e < CPL; ++e) fx[e] = to_fix(dv[e]);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // read by the async proxy
     }
     if (sync_or(lbad)) st.bad = 1;
     if (mine && !st.bad && tid == 0) {
       // the destination was seeded by other CTAs' generic stores (acquired at the phase start)
       asm volatile("fence.proxy.async.global;" ::: "memory");
-      asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(xnext),
-                   "r"(smem_u32(sm.xs + a.H)), "r"((uint32_t)a.H * 4u)
+      asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.u64 [%0], [%1], %2;" ::"l"(xnext),
+                   "r"(smem_u32(sm.xs)), "r"((uint32_t)a.H * 8u)
                    : "memory");
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -1063,9 +1095,9 @@ __global__ void __launch_bounds__(PK_THREADS, 1) persist_decode_kernel(const Per
       } else {
         const PersistLayer* w = s_lay + (l < a.L ? l : 0);
         // Q: the layer input; M: x1; head: the last layer's output (O merges attention)
-        const float* xsrc = kind == PH_M ? a.x1 : xbuf(a, l);
+        const XIn xsrc = kind == PH_M ? XIn{a.x1, nullptr} : xin_of(a, l);
         const float* norm_w = kind == PH_Q ? w->ln_in : kind == PH_M ? w->ln_post : head ? a.final_norm : nullptr;
-        const float* resid = kind == PH_O ? xbuf(a, l) : nullptr;
+        const XIn resid = xin_of(a, l);
         st = gemv_units<KC, D>(a, sm, st, nst, kind, l, pos, g.U, g.K, g.gpu, first, xsrc, norm_w, resid, at);
       }
       if (tid == 0) trace_mark(a, ph, 5);

@@ -38,9 +38,11 @@ struct PersistArgs {
   int* pos;                    // device position of the token being decoded (incremented)
   int* step;                   // device greedy step index (incremented)
   int* tokens;                 // picked ids, tokens[*step]
-  float* x0;                   // residual stream [H], buffer 0: input of even layers; receives
-                               // the next token's embedding
-  float* x0b;                  // residual stream [H], buffer 1: input of odd layers
+  float* x0;                   // layer 0's input [H]: receives the next token's embedding
+  long long* xacc;             // [2][H] residual stream of layers 1..L in fixed point (value x
+                               // 2^32, int64): layer l >= 1 reads xacc[l & 1].  Integer sums
+                               // are exact, so the order in which the CTAs' down-projection
+                               // partials arrive cannot change a bit of the result.
   float* x1;                   // residual stream after attention [H]
   float* q;                    // post-RoPE queries [nh*d]
   float* logits;               // optional [V]

@@ -188,10 +188,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer
+    int issued = pre;  // stages whose copies have been issued
+    bool aborted = false;
     for (int i = 0; i < nkb; ++i) {
       const int s = i % a.nstages;
       if (i >= a.nstages && !mbar_wait(&empty[s], ((i / a.nstages) - 1) & 1, a.err)) {
         atomicExch(&flags[0], 1);
+        aborted = true;
         break;
       }
       unsigned char* st = base + s * stage_bytes;
@@ -201,6 +204,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tma_load_2d(st, &tmW, kx, tile * TC_BM, &full[s]);
       }
       tma_load_2d(st + a_bytes, &tmX, kx, 0, &full[s]);
+      issued = i + 1 > issued ? i + 1 : issued;
+    }
+    if (aborted || *reinterpret_cast<volatile int*>(&flags[0])) {
+      // do not let the CTA leave while a copy into its shared memory may still land: wait
+      // (bounded) for the stages issued and not yet known to be consumed
+      for (int j = issued > a.nstages ? issued - a.nstages : 0; j < issued; ++j) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&full[j % a.nstages], (j / a.nstages) & 1))
+          if (clock64() - t0 > kWaitLimitCycles) break;
+      }
     }
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer

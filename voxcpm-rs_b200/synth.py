@@ -27,8 +27,11 @@ def bf16_bits(a) -> np.ndarray:
 
 
 def bf16_to_f32(bits) -> np.ndarray:
-    """Exact upcast of bf16 bit patterns to f32."""
-    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(F32)
+    """Exact upcast of bf16 bit patterns to f32 (torch's multi-threaded cast: the bits are
+    moved into the high half of each f32, nothing is rounded)."""
+    import torch
+    b = np.ascontiguousarray(bits, dtype=np.uint16)
+    return torch.from_numpy(b.view(np.int16)).view(torch.bfloat16).float().numpy()
 
 
 def _rng(seed, *tags):
@@ -91,16 +94,19 @@ def minicpm_weights(cfg, seed=0, std=0.02, prefix="lm"):
 def minicpm_f32_view(w):
     """f32 model-layout view (q|k|v and gate|up fused along ``out``, as
     ``src/weights.rs:648-772`` fuses them) for an f32 restatement."""
-    return {
-        "embed": None if w["embed"] is None else bf16_to_f32(w["embed"]),
-        "norm": w["norm"],
-        "layers": [{
+    def layer(l):
+        return {
             "wqkv": bf16_to_f32(np.concatenate([l["q"], l["k"], l["v"]], 0)),
             "wo": bf16_to_f32(l["o"]),
             "wgu": bf16_to_f32(np.concatenate([l["gate"], l["up"]], 0)),
             "wd": bf16_to_f32(l["down"]),
             "ln_in": l["ln_in"], "ln_post": l["ln_post"],
-        } for l in w["layers"]],
+        }
+    got = _parallel([(i, lambda l=l: layer(l)) for i, l in enumerate(w["layers"])])
+    return {
+        "embed": None if w["embed"] is None else bf16_to_f32(w["embed"]),
+        "norm": w["norm"],
+        "layers": [got[i] for i in range(len(w["layers"]))],
     }
 
 
