@@ -339,6 +339,68 @@ int vx_generate(vx_lm* lm, vx_dit* dit, vx_vae* vae, const int32_t* prompt_ids, 
 int vx_generate_batch(vx_lm* lm, vx_dit* dit, vx_vae* vae, const int32_t* prompt_ids, int B, int n_prompt,
                       const vx_generate_options* opts, const float* noise, float* wav_out, float* latent_out);
 
+/* ----------------------------------------------------------------- VoxCPM2 model */
+
+/* VoxCpm2Model (voxcpm2/model.rs:22-37) over model objects created on one context: the base
+ * LM (MiniCpmModel with its tied vocabulary, max_batch 1), the residual LM (vocab_size 0,
+ * VoxCpm2Config::residual_lm_config, config.rs:421-427), the local encoder's MiniCPM-4
+ * (vocab_size 0, encoder_lm_config, config.rs:430-440) and the LocDiT (dit_lm_config).  The
+ * model keeps pointers to them; destroy it before them.  feat_dim D and patch_size P
+ * (config.rs:318-321), scalar-quantization latent / scale (config.rs:326-329); max_len caps
+ * the AR steps of one inference call. */
+typedef struct vx_voxcpm2 vx_voxcpm2;
+
+/* The projection weights of VoxCpm2Model::new (model.rs:41-100), bf16 [out, in] bit
+ * patterns and f32 vectors (host or device pointers). */
+typedef struct {
+  const float* special_token;   /* VoxCpmLocEnc.special_token [enc_hidden] (locenc.rs:11) */
+  const uint16_t* enc_in_w;     /* VoxCpmLocEnc.in_proj [enc_hidden, D] */
+  const float* enc_in_b;
+  const uint16_t* enc_to_lm_w;  /* [lm_hidden, enc_hidden] */
+  const float* enc_to_lm_b;
+  const uint16_t* lm_to_dit_w;  /* [dit_hidden, lm_hidden] */
+  const float* lm_to_dit_b;
+  const uint16_t* res_to_dit_w; /* [dit_hidden, lm_hidden] */
+  const float* res_to_dit_b;
+  const uint16_t* fusion_w;     /* fusion_concat_proj [lm_hidden, 2 * lm_hidden] */
+  const float* fusion_b;
+  const uint16_t* stop_proj_w;  /* [lm_hidden, lm_hidden] */
+  const float* stop_proj_b;
+  const uint16_t* stop_head_w;  /* [2, lm_hidden], no bias */
+  const uint16_t* fsq_in_w;     /* ScalarQuantizationLayer.in_proj [latent, lm_hidden] (fsq.rs:17) */
+  const float* fsq_in_b;
+  const uint16_t* fsq_out_w;    /* ScalarQuantizationLayer.out_proj [lm_hidden, latent] */
+  const float* fsq_out_b;
+} vx_voxcpm2_weights;
+
+int vx_voxcpm2_create(vx_lm* base_lm, vx_lm* residual_lm, vx_lm* encoder, vx_dit* dit, int feat_dim, int patch_size,
+                      int sq_latent_dim, int sq_scale, int max_len, vx_voxcpm2** out);
+void vx_voxcpm2_destroy(vx_voxcpm2* m);
+int vx_voxcpm2_load(vx_voxcpm2* m, const vx_voxcpm2_weights* w);
+/* VoxCpmLocEnc::forward (locenc.rs:32-44) for N patches: feat [N, P, D] (device) -> the cls
+ * rows out [N, enc_hidden] (device).  Synchronises. */
+int vx_locenc_forward(vx_voxcpm2* m, const float* feat, int N, float* out);
+/* VoxCpm2Model::inference (model.rs:301-375) for one sequence: prefill (model.rs:128-207)
+ * over text_token [S] ids, text_mask / feat_mask [S] (0 or 1) and feat [S, P, D], then
+ * dit_step / lm_step (model.rs:215-279) until the stop head fires at a step i > min_len or
+ * max_len patches exist.  noise [max_len, D, P] is each step's CFM noise z (the reference
+ * draws it from the backend RNG, unified_cfm.rs:47-52); the CFM runs with sway 1 and
+ * CFG-zero-star as dit_step passes them.  latent_out receives [D, n * P] (stack_pred_feats,
+ * model.rs:283-287) with n written to *n_patches; stop_logits_out (optional) [n, 2].  The
+ * stop flag stays on the device: the host reads step i's flag after queueing step i + 1.
+ * vx_cancel is polled every step (model.rs:323-328).  Inputs may be host or device memory. */
+int vx_voxcpm2_inference(vx_voxcpm2* m, const int32_t* text_token, const float* text_mask, const float* feat,
+                         const float* feat_mask, int S, int min_len, int max_len, int inference_timesteps,
+                         float cfg_value, const float* noise, float* latent_out, int* n_patches,
+                         float* stop_logits_out);
+/* VoxCPM::generate (wrapper.rs:401-423) without the tokenizer: vx_voxcpm2_inference, then
+ * decode_latent_to_samples (wrapper.rs:616-629) through the VAE.  wav_out (host or device)
+ * must hold max_len * P * prod(rates) samples; *n_samples receives the count written. */
+int vx_voxcpm2_generate(vx_voxcpm2* m, vx_vae* vae, const int32_t* text_token, const float* text_mask,
+                        const float* feat, const float* feat_mask, int S, int min_len, int max_len,
+                        int inference_timesteps, float cfg_value, const float* noise, float* wav_out,
+                        int* n_samples);
+
 #ifdef __cplusplus
 }
 #endif

@@ -74,3 +74,37 @@ def test_generate_batch_small(ctx):
                                              inference_timesteps=4)
         assert_close(lat[b], want_lat, **TOL, what=f"latent[{b}]")
         assert_close(wav[b], want_wav, **TOL, what=f"wav[{b}]")
+
+
+@pytest.mark.slow
+def test_generate_full_width(ctx):
+    """vx_generate at the end-to-end workload's widths: a 4-layer LM of the decode workload
+    (hidden 2048, 16/2 heads, SwiGLU 6144, vocab 73448), the 8-layer hidden-1024 LocDiT, the
+    2048-wide AudioVAE with rates [2,5,8,8]; 64-id prompt, 8 patches, 10 Euler steps with
+    the reference-default sampler (sway 1, CFG-zero-star, CFG 2)."""
+    from voxcpm_rs_b200 import config, synth
+    from voxcpm_rs_b200.audiovae import AudioVae
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    from voxcpm_rs_b200.minicpm4 import MiniCpmModel
+    from voxcpm_rs_b200.voxcpm import GenerateOptions, VoxCPM
+    lm_cfg = config.lm_decode_config(layers=4)
+    lm_w = synth.minicpm_weights(lm_cfg, seed=11)
+    dcfg, vcfg = config.locdit_config(lm_cfg), config.vae_config()
+    dit_w = synth.locdit_weights(dcfg, in_channels=64, seed=12)
+    vae_w = synth.vae_weights(vcfg, seed=13)
+    prompt = synth.prompt_ids(64, lm_cfg.vocab_size, seed=14)
+    steps = 8
+    noise = np.random.default_rng(15).standard_normal((steps, 64, 4), dtype=np.float32)
+    opts = GenerateOptions(max_len=steps, inference_timesteps=10)
+    vox = VoxCPM(ctx, MiniCpmModel(ctx, lm_cfg, lm_w, max_length=128), VoxCpmLocDiTV2(ctx, dcfg, dit_w),
+                 AudioVae(ctx, vcfg, vae_w))
+    wav, lat = vox.generate(prompt, opts, noise, return_latent=True)
+    vox.dit.close()
+    vox.vae.close()
+    vox.lm.close()
+    want_wav, want_lat, _ = ovx.generate(lm_cfg, synth.minicpm_f32_view(lm_w), dcfg, synth.locdit_f32_view(dit_w),
+                                         vcfg, synth.vae_f32_view(vae_w), prompt, steps, noise,
+                                         inference_timesteps=10)
+    assert wav.shape == (steps * 4 * 640,)
+    assert_close(lat, want_lat, **TOL, what="latent")
+    assert_close(wav, want_wav, **TOL, what="wav")

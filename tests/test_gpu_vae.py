@@ -67,3 +67,20 @@ def test_vae_causal_prefix(ctx, c5_vae):
     part = vae.decode(_t(z[:, :, :12])).cpu().numpy()
     assert np.array_equal(part, full[:, :, :12 * 640])
     vae.close()
+
+
+@pytest.mark.slow
+def test_vae_decode_c5_t256(ctx, c5_vae):
+    """The end-to-end workload's decoder at T = 256 latent frames (163,840 samples): the
+    full channel ladder 2048 -> 1024 -> 512 -> 256 -> 128 at a length where every block's
+    tiles run many times over."""
+    from voxcpm_rs_b200.audiovae import AudioVae
+    vcfg, w, fw = c5_vae
+    z = np.random.default_rng(256).standard_normal((1, 64, 256), dtype=np.float32)
+    want = oav.decoder_forward(vcfg, fw, z)
+    vae = AudioVae(ctx, vcfg, w)
+    got = vae.decode(_t(z)).cpu().numpy()
+    vae.close()
+    assert got.shape == (1, 1, 256 * 640)
+    assert_close(got, want, **TOL, what="VAE decode T=256")
+    assert np.abs(got - want).max() < 2e-3

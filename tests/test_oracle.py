@@ -180,3 +180,23 @@ def test_scalar_quantization_vs_torch():
     q = torch.sign(lat) * torch.floor(lat.abs() + 0.5) / 9
     want = torch.nn.functional.linear(q, t(w_out), t(b_out)).numpy()
     np.testing.assert_allclose(got, want, atol=1e-5, rtol=1e-5)
+
+
+def test_voxcpm2_loop_semantics():
+    """oracle.voxcpm2.inference follows model.rs:318-347: the stop head only ends the loop at
+    a step i > min_len, the patch of the stopping step is kept, and with min_len >= max_len
+    every step runs; the stacked latent's prefix does not depend on min_len."""
+    import numpy as np
+    from oracle import voxcpm2 as ov2
+    from tests.test_gpu_voxcpm2 import inputs, oracle_cfgs, small_voxcpm2
+    from voxcpm_rs_b200 import synth
+    v = small_voxcpm2()
+    fw = synth.voxcpm2_f32_view(synth.voxcpm2_weights(v, seed=2, std=0.05))
+    ids, tm, feat, fm, noise = inputs(2)
+    lat, lg = ov2.inference(oracle_cfgs(v), fw, ids, tm, feat, fm, 2, 12, 10, 2.0, noise)
+    n = lat.shape[1] // 4
+    stops = lg[:, 1] > lg[:, 0]
+    assert stops[n - 1] and n - 1 > 2 and not any(stops[3:n - 1])
+    lat_all, lg_all = ov2.inference(oracle_cfgs(v), fw, ids, tm, feat, fm, 12, 12, 10, 2.0, noise)
+    assert lat_all.shape[1] == 48
+    assert np.array_equal(lat_all[:, :4 * n], lat)

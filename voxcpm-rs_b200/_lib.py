@@ -62,6 +62,13 @@ class VaeBlockWeightsC(C.Structure):
                 ("res_b1", P * 3), ("res_alpha2", P * 3), ("res_w2", P * 3), ("res_b2", P * 3),
                 ("sr_scale", P), ("sr_bias", P)]
 
+class VoxCpm2WeightsC(C.Structure):
+    _fields_ = [(n, P) for n in ("special_token", "enc_in_w", "enc_in_b", "enc_to_lm_w", "enc_to_lm_b",
+                                 "lm_to_dit_w", "lm_to_dit_b", "res_to_dit_w", "res_to_dit_b", "fusion_w",
+                                 "fusion_b", "stop_proj_w", "stop_proj_b", "stop_head_w", "fsq_in_w", "fsq_in_b",
+                                 "fsq_out_w", "fsq_out_b")]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "vx_version": (I32, []),
@@ -117,6 +124,12 @@ SIGNATURES = {
     "vx_generate": (I32, [P, P, P, P, I32, C.POINTER(GenerateOptionsC), P, P, P]),
     "vx_generate_batch": (I32, [P, P, P, P, I32, I32, C.POINTER(GenerateOptionsC), P, P, P]),
     "vx_lm_last_logits": (I32, [P, P]),
+    "vx_voxcpm2_create": (I32, [P, P, P, P, I32, I32, I32, I32, I32, C.POINTER(P)]),
+    "vx_voxcpm2_destroy": (None, [P]),
+    "vx_voxcpm2_load": (I32, [P, C.POINTER(VoxCpm2WeightsC)]),
+    "vx_locenc_forward": (I32, [P, P, I32, P]),
+    "vx_voxcpm2_inference": (I32, [P, P, P, P, P, I32, I32, I32, I32, F32, P, P, C.POINTER(I32), P]),
+    "vx_voxcpm2_generate": (I32, [P, P, P, P, P, P, I32, I32, I32, I32, F32, P, P, C.POINTER(I32)]),
 }
 
 _lib = None

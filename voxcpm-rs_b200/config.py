@@ -62,6 +62,50 @@ class VoxCpmDitConfig:
     dit_mean_mode: bool = False
 
 
+@dataclass
+class VoxCpmEncoderConfig:
+    """``VoxCpmEncoderConfig`` (``src/config.rs:158-184``)."""
+    hidden_dim: int = 1024
+    ffn_dim: int = 4096
+    num_heads: int = 16
+    num_layers: int = 4
+    kv_channels: Optional[int] = None
+
+
+@dataclass
+class VoxCpm2Config:
+    """``VoxCpm2Config`` (``src/config.rs:316-341``) fields the model uses, with the
+    reference defaults, and its derivation helpers (``config.rs:421-453``).  ``dit_rope``
+    / ``enc_rope`` override the inherited LongRoPE factors when a head_dim needs vectors of
+    another length (``rope.rs:32``)."""
+    lm_config: MiniCpm4Config
+    encoder_config: VoxCpmEncoderConfig
+    dit_config: VoxCpmDitConfig
+    patch_size: int = 4
+    feat_dim: int = 64
+    residual_lm_num_layers: int = 8
+    residual_lm_no_rope: bool = False
+    scalar_quantization_latent_dim: int = 512
+    scalar_quantization_scale: int = 9
+    max_length: int = 8192
+    enc_rope: Optional[RopeScalingConfig] = None
+    dit_rope: Optional[RopeScalingConfig] = None
+
+    def residual_lm_config(self) -> MiniCpm4Config:
+        return self.lm_config.derive(num_hidden_layers=self.residual_lm_num_layers, vocab_size=0,
+                                     no_rope=self.residual_lm_no_rope)
+
+    def encoder_lm_config(self) -> MiniCpm4Config:
+        e = self.encoder_config
+        return self.lm_config.derive(hidden_size=e.hidden_dim, intermediate_size=e.ffn_dim,
+                                     num_attention_heads=e.num_heads, num_hidden_layers=e.num_layers,
+                                     kv_channels=e.kv_channels, vocab_size=0,
+                                     rope_scaling=self.enc_rope or copy.deepcopy(self.lm_config.rope_scaling))
+
+    def dit_lm_config(self) -> MiniCpm4Config:
+        return dit_lm_config(self.lm_config, self.dit_config, self.dit_rope)
+
+
 def dit_lm_config(lm: MiniCpm4Config, d: VoxCpmDitConfig,
                   rope_scaling: Optional[RopeScalingConfig] = None) -> MiniCpm4Config:
     """``VoxCpm2Config::dit_lm_config`` (``src/config.rs:443-453``): the LM config with the
@@ -140,3 +184,13 @@ def vae_config(**kw) -> AudioVaeConfig:
                 sample_rate=16000, out_sample_rate=16000)
     base.update(kw)
     return AudioVaeConfig(**base)
+
+
+def voxcpm2_config(base: MiniCpm4Config, residual_layers=8, enc=None, dit=None, enc_rope=None, dit_rope=None,
+                   latent=512, scale=9, feat_dim=64, patch_size=4) -> VoxCpm2Config:
+    """A ``VoxCpm2Config`` over a base LM config (encoder / DiT default to the reference's
+    1024-wide, 16-head stacks: 4 encoder layers, DiT layers as given)."""
+    return VoxCpm2Config(lm_config=base, encoder_config=enc or VoxCpmEncoderConfig(),
+                         dit_config=dit or VoxCpmDitConfig(), patch_size=patch_size, feat_dim=feat_dim,
+                         residual_lm_num_layers=residual_layers, scalar_quantization_latent_dim=latent,
+                         scalar_quantization_scale=scale, enc_rope=enc_rope, dit_rope=dit_rope)

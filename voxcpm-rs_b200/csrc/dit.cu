@@ -406,6 +406,21 @@ int vx_dit_forward(vx_dit* d, const float* x, const float* mu, const float* t, c
 
 int vx_cfm_solve(vx_dit* d, const float* mu, const float* cond, const float* z, int B, int C_mu, int T, int Tc,
                  int n_timesteps, float cfg_value, float sway_sampling_coef, int use_cfg_zero_star, float* x_out) {
+  const int rc = vx::cfm_solve_enqueue(d, mu, cond, z, B, C_mu, T, Tc, n_timesteps, cfg_value, sway_sampling_coef,
+                                       use_cfg_zero_star, x_out);
+  if (rc) return rc;
+  return vx_ctx_synchronize(d->ctx);
+}
+
+}  // extern "C"
+
+namespace vx {
+
+// vx_cfm_solve without the final synchronisation: the solve is queued on the context stream
+// (inputs staged, the captured graph launched, the result copied to x_out).
+int cfm_solve_enqueue(vx_dit* d, const float* mu, const float* cond, const float* z, int B, int C_mu, int T, int Tc,
+                      int n_timesteps, float cfg_value, float sway_sampling_coef, int use_cfg_zero_star,
+                      float* x_out) {
   if (!d || !mu || !cond || !z || !x_out) return VX_ERR_ARG;
   vx_ctx* ctx = d->ctx;
   const int H = d->H, C = d->C, N = 2 * B;
@@ -451,12 +466,10 @@ int vx_cfm_solve(vx_dit* d, const float* mu, const float* cond, const float* z, 
   VX_CUDA(ctx, cudaGraphLaunch(d->solve_exec, st));
   count_launch(d->solve_kernels);
   VX_CUDA(ctx, cudaMemcpyAsync(x_out, d->xw, (size_t)B * C * T * 4, cudaMemcpyDefault, st));
-  return vx_ctx_synchronize(ctx);
+  return VX_OK;
 }
 
-}  // extern "C"
-
-namespace vx {
 vx_ctx* dit_ctx(vx_dit* d) { return d->ctx; }
 int dit_in_channels(const vx_dit* d) { return d->C; }
+int dit_hidden_size(const vx_dit* d) { return d->H; }
 }  // namespace vx

@@ -910,6 +910,8 @@ int lm_batch_step(vx_lm* lm) {
 const float* lm_batch_hidden(const vx_lm* lm) { return lm->bhid; }
 const int* lm_batch_tokens(const vx_lm* lm) { return lm->btokens; }
 int lm_max_batch(const vx_lm* lm) { return lm->max_batch; }
+int lm_vocab_size(const vx_lm* lm) { return lm->V; }
+int lm_max_length(const vx_lm* lm) { return lm->max_length; }
 
 // One graph-replayed decode step: consumes the last picked id at the device position,
 // writes the next id, the final-norm hidden (hid_norm) and advances the position.

@@ -143,6 +143,40 @@ def locdit_f32_view(w):
     return f
 
 
+# ----------------------------------------------------------------------- VoxCPM2
+
+def voxcpm2_weights(vcfg, seed=0, std=0.02):
+    """Random-init ``VoxCpm2Model`` (``src/voxcpm2/model.rs:41-100``): base LM (with the tied
+    vocabulary), residual LM, local encoder (MiniCPM-4 + in_proj + special token ~N(0,1),
+    ``src/locenc.rs:17-28``), LocDiT, FSQ and the projection layers (biased except
+    ``stop_head``)."""
+    base = vcfg.lm_config
+    H, D = base.hidden_size, vcfg.feat_dim
+    ecfg, dcfg = vcfg.encoder_lm_config(), vcfg.dit_lm_config()
+    He, Hd, Lq = ecfg.hidden_size, dcfg.hidden_size, vcfg.scalar_quantization_latent_dim
+    w = {"base": minicpm_weights(base, seed, std, prefix="base"),
+         "residual": minicpm_weights(vcfg.residual_lm_config(), seed, std, prefix="residual"),
+         "encoder": minicpm_weights(ecfg, seed, std, prefix="encoder"),
+         "dit": locdit_weights(dcfg, in_channels=D, seed=seed, std=std)}
+    w["special"] = bf16_to_f32(normal_bf16(seed, (He,), 1.0, 0.0, "vox", "special"))
+    for name, out_f, in_f in (("enc_in", He, D), ("enc_to_lm", H, He), ("lm_to_dit", Hd, H), ("res_to_dit", Hd, H),
+                              ("fusion", H, 2 * H), ("stop_proj", H, H), ("fsq_in", Lq, H), ("fsq_out", H, Lq)):
+        w[name + "_w"], w[name + "_b"] = _lin(seed, out_f, in_f, std, "vox", name)
+    w["stop_head_w"] = normal_bf16(seed, (2, H), std, 0.0, "vox", "stop_head")
+    return w
+
+
+def voxcpm2_f32_view(w):
+    """f32 view of ``voxcpm2_weights`` for the restatement (``oracle/voxcpm2.py``)."""
+    f = {k: (bf16_to_f32(v) if k.endswith("_w") else v) for k, v in w.items()
+         if k.endswith("_w") or k.endswith("_b") or k == "special"}
+    f["base"] = minicpm_f32_view(w["base"])
+    f["residual"] = minicpm_f32_view(w["residual"])
+    f["encoder"] = minicpm_f32_view(w["encoder"])
+    f["dit"] = locdit_f32_view(w["dit"])
+    return f
+
+
 # ---------------------------------------------------------------------- AudioVAE
 
 def vae_weights(vcfg, seed=0):

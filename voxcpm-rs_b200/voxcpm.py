@@ -102,3 +102,98 @@ class VoxCPM:
         check(lib().vx_generate_batch(self.lm.h, self.dit.h, self.vae.h, ptr(ids), b, n, C.byref(o), ptr(noise),
                                       ptr(wav), ptr(latent)), self.ctx.h)
         return (wav, latent) if return_latent else wav
+
+
+class VoxCpm2Model:
+    """``VoxCpm2Model`` (reference ``src/voxcpm2/model.rs``): base LM, residual LM, local
+    encoder, LocDiT, FSQ and projection layers on one context (``vx_voxcpm2``).  ``inference``
+    is ``VoxCpm2Model::inference`` with the per-step CFM noise given; ``generate`` adds the
+    AudioVAE decode (``VoxCPM::generate`` without the tokenizer)."""
+
+    def __init__(self, ctx, vcfg, weights=None, max_len=64, max_length=None):
+        from .locdit import VoxCpmLocDiTV2
+        from .minicpm4 import MiniCpmModel
+        self.ctx, self.cfg = ctx, vcfg
+        max_length = max_length or vcfg.max_length
+        self.base = MiniCpmModel(ctx, vcfg.lm_config, None, max_length=max_length)
+        self.residual = MiniCpmModel(ctx, vcfg.residual_lm_config(), None, max_length=max_length)
+        self.encoder = MiniCpmModel(ctx, vcfg.encoder_lm_config(), None, max_length=vcfg.patch_size + 1)
+        self.dit = VoxCpmLocDiTV2(ctx, vcfg.dit_lm_config(), None, in_channels=vcfg.feat_dim, max_rows=2)
+        h = C.c_void_p()
+        check(lib().vx_voxcpm2_create(self.base.h, self.residual.h, self.encoder.h, self.dit.h, vcfg.feat_dim,
+                                      vcfg.patch_size, vcfg.scalar_quantization_latent_dim,
+                                      vcfg.scalar_quantization_scale, max_len, C.byref(h)), ctx.h)
+        self.h = h
+        ctx._adopt(self)
+        self.max_len = max_len
+        if weights is not None:
+            self.load(weights)
+
+    def load(self, w):
+        """Weights from ``synth.voxcpm2_weights``."""
+        self.base.load(w["base"])
+        self.residual.load(w["residual"])
+        self.encoder.load(w["encoder"])
+        self.dit.load(w["dit"])
+        names = [f for f, _ in _lib.VoxCpm2WeightsC._fields_]
+        src = {"special_token": w["special"]}
+        src.update({n: w[n] for n in names if n != "special_token"})
+        keep = {n: np.ascontiguousarray(v, dtype=np.float32 if v.dtype != np.uint16 else np.uint16)
+                for n, v in src.items()}
+        s = _lib.VoxCpm2WeightsC(*[ptr(keep[n]) for n in names])
+        check(lib().vx_voxcpm2_load(self.h, C.byref(s)), self.ctx.h)
+
+    def locenc(self, feat):
+        """``VoxCpmLocEnc::forward`` of N patches: feat [N, P, D] -> [N, enc_hidden]."""
+        import torch
+        x = torch.as_tensor(np.ascontiguousarray(feat, np.float32)).cuda(self.ctx.device)
+        out = torch.empty(x.shape[0], self.encoder.cfg.hidden_size, device=x.device)
+        torch.cuda.synchronize()
+        check(lib().vx_locenc_forward(self.h, ptr(x), x.shape[0], ptr(out)), self.ctx.h)
+        return out.cpu().numpy()
+
+    def inference(self, text_token, text_mask, feat, feat_mask, min_len, max_len, inference_timesteps, cfg_value,
+                  noise):
+        """Returns ``(latent [D, n*P], stop logits [n, 2])``."""
+        ids = np.ascontiguousarray(text_token, np.int32)
+        tm = np.ascontiguousarray(text_mask, np.float32)
+        fm = np.ascontiguousarray(feat_mask, np.float32)
+        feat = np.ascontiguousarray(feat, np.float32)
+        noise = np.ascontiguousarray(noise, np.float32)
+        D, P = self.cfg.feat_dim, self.cfg.patch_size
+        lat = np.empty((D, max_len * P), np.float32)
+        logits = np.empty((max_len, 2), np.float32)
+        n = C.c_int()
+        check(lib().vx_voxcpm2_inference(self.h, ptr(ids), ptr(tm), ptr(feat), ptr(fm), len(ids), min_len, max_len,
+                                         inference_timesteps, cfg_value, ptr(noise), ptr(lat), C.byref(n),
+                                         ptr(logits)), self.ctx.h)
+        k = n.value
+        return np.ascontiguousarray(lat.reshape(-1)[:D * k * P].reshape(D, k * P)), logits[:k]
+
+    def generate(self, vae, text_token, text_mask, feat, feat_mask, min_len, max_len, inference_timesteps,
+                 cfg_value, noise):
+        ids = np.ascontiguousarray(text_token, np.int32)
+        noise = np.ascontiguousarray(noise, np.float32)
+        hop = int(np.prod(vae.cfg.decoder_rates))
+        wav = np.empty(max_len * self.cfg.patch_size * hop, np.float32)
+        n = C.c_int()
+        check(lib().vx_voxcpm2_generate(self.h, vae.h, ptr(ids), ptr(np.ascontiguousarray(text_mask, np.float32)),
+                                        ptr(np.ascontiguousarray(feat, np.float32)),
+                                        ptr(np.ascontiguousarray(feat_mask, np.float32)), len(ids), min_len, max_len,
+                                        inference_timesteps, cfg_value, ptr(noise), ptr(wav), C.byref(n)),
+              self.ctx.h)
+        return wav[:n.value]
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().vx_voxcpm2_destroy(self.h)
+            self.h = None
+        for m in ("dit", "encoder", "residual", "base"):
+            if getattr(self, m, None) is not None:
+                getattr(self, m).close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
