@@ -319,6 +319,62 @@ def measure_cfm(ctx, device, dcfg, dit_w):
     return out
 
 
+
+
+def vae_flops(vcfg, T):
+    """Algorithmic FLOPs of one AudioVAE decode of T latent frames: the causal transposed
+    convs (2 * C_out * 2 C_in per output sample), the pointwise convs (2 * C^2 per sample, 3
+    per block), the first pointwise conv, the depthwise k7 convs and the last k7 conv."""
+    f = 2.0 * vcfg.decoder_dim * vcfg.latent_dim * T + 2.0 * 7 * vcfg.latent_dim * T
+    t, c = T, vcfg.decoder_dim
+    for s in vcfg.decoder_rates:
+        co = c // 2
+        t *= s
+        f += 2.0 * co * 2 * c * t + 3 * (2.0 * co * co * t + 2.0 * 7 * co * t)
+        c = co
+    return f + 2.0 * 7 * c * t
+
+
+def measure_vae(ctx, device, rank):
+    """AudioVAE decoder of the end-to-end workload (latent 64, decoder_dim 2048, rates
+    [2,5,8,8], 16 kHz) on T = 1024 latent frames (one 40.96 s utterance): device time per
+    decode (CUDA events on the context stream, 5 calls after 2 warm-up), algorithmic TFLOP/s
+    against the measured sustained bf16 peak."""
+    import numpy as np
+    import torch
+    from voxcpm_rs_b200 import config, synth
+    from voxcpm_rs_b200._lib import check, lib, ptr
+    from voxcpm_rs_b200.audiovae import AudioVae
+    vcfg = config.vae_config()
+    vae = AudioVae(ctx, vcfg, synth.vae_weights(vcfg, seed=rank))
+    z = torch.from_numpy(np.random.default_rng(1).standard_normal((1, 64, 1024), dtype=np.float32)).to(device)
+    wav = torch.empty(1, 1, 1024 * 640, device=device)
+    L = lib()
+    for _ in range(2):
+        check(L.vx_vae_decode(vae.h, ptr(z), 1, 1024, ptr(wav)), ctx.h)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(5):
+        check(L.vx_vae_decode(vae.h, ptr(z), 1, 1024, ptr(wav)), ctx.h)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / 5
+    vae.close()
+    flops = vae_flops(vcfg, 1024)
+    try:
+        peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops_sustained"])
+        kind = "measured (MEASURED_PEAKS.json bf16_tflops_sustained)"
+    except Exception:
+        peak, kind = 1400.0, "fallback"
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"workload": "AudioVAE decode, latent 64 x 1024 frames -> 655,360 samples (rates 2,5,8,8; channels "
+                        "2048 -> 128)", "ms": ms, "algorithmic_gflop": flops / 1e9, "tflops": tf,
+            "peak_tflops": peak, "peak_kind": kind, "frac_of_tensor_peak": tf / peak,
+            "math": "pointwise and transposed convs on tcgen05 (bf16 weights x bf16 hi/lo activations, f32 TMEM "
+                    "accumulators); depthwise k7 convs on CUDA cores"}
+
+
 def gemv_graph_us(ctx, weights, x, reps):
     """Average device time of one streamed-GEMV launch over ``weights`` (each [N, K] bf16
     bits), measured by replaying a CUDA graph of one launch per weight ``reps`` times between
@@ -461,6 +517,30 @@ def run_phase_trace(pos=200, layers=LAYERS):
     return 0
 
 
+def run_vae_only():
+    """Small profiling case: the end-to-end workload's AudioVAE decoder on 1024 latent frames,
+    two decodes (the first allocates its buffers)."""
+    import numpy as np
+    import torch
+    from __graft_entry__ import load_package
+    load_package()
+    from voxcpm_rs_b200 import config, synth
+    from voxcpm_rs_b200.audiovae import AudioVae
+    from voxcpm_rs_b200.minicpm4 import Context
+    ctx = Context(0)
+    vcfg = config.vae_config()
+    vae = AudioVae(ctx, vcfg, synth.vae_weights(vcfg, seed=0))
+    z = torch.from_numpy(np.random.default_rng(1).standard_normal((1, 64, 1024), dtype=np.float32)).cuda()
+    for _ in range(2):
+        t0 = time.perf_counter()
+        vae.decode(z)
+        torch.cuda.synchronize()
+        print(json.dumps({"vae_decode_ms": (time.perf_counter() - t0) * 1e3}))
+    vae.close()
+    ctx.close()
+    return 0
+
+
 def run_cfm_only():
     """Small profiling case: the LocDiT CFM solve (8 layers, hidden 1024, CFG 2.0, 10 uniform
     Euler steps, B=1) run twice (the first call captures the solve graph)."""
@@ -501,6 +581,8 @@ def main():
                     help="profiling case: only the gate|up GEMV over 4 distinct 50 MB weights")
     ap.add_argument("--cfm-only", action="store_true",
                     help="profiling case: two CFM solves of the LocDiT workload (B=1, 10 Euler steps)")
+    ap.add_argument("--vae-only", action="store_true",
+                    help="profiling case: two AudioVAE decodes of 1024 latent frames")
     ap.add_argument("--lm-only", action="store_true",
                     help="profiling case: the LM-decode model, two greedy runs of 32 decode steps each")
     ap.add_argument("--lm-layers", type=int, default=LAYERS,
@@ -518,6 +600,8 @@ def main():
         return run_lm_only(args.lm_layers)
     if args.cfm_only:
         return run_cfm_only()
+    if args.vae_only:
+        return run_vae_only()
     args.warmup = max(3, args.warmup)
 
     import numpy as np
@@ -646,6 +730,7 @@ def main():
         dcfg = config.locdit_config(cfg)
         dit_w = synth.locdit_weights(dcfg, in_channels=64, seed=rank)
         extras["locdit_cfm"] = measure_cfm(ctx, device, dcfg, dit_w)
+        extras["vae"] = measure_vae(ctx, device, rank)
         # end-to-end synthesis: one utterance per GPU (LM 64-id prompt + 256 steps, a CFM solve
         # per step with the reference-default sampler, AudioVAE 16 kHz); weak scaling
         vcfg = config.vae_config()

@@ -150,7 +150,8 @@ int vx_ctx_create(int device, vx_ctx** out) {
       cudaMalloc(&ctx->counters, 4096 * sizeof(unsigned)) != cudaSuccess ||
       cudaMemset(ctx->counters, 0, 4096 * sizeof(unsigned)) != cudaSuccess ||
       cudaMalloc(&ctx->dev_err, 64) != cudaSuccess || cudaMemset(ctx->dev_err, 0, 64) != cudaSuccess ||
-      gemv_configure() != cudaSuccess || tc_gemm_configure() != cudaSuccess) {
+      gemv_configure() != cudaSuccess || tc_gemm_configure() != cudaSuccess ||
+      vae_tc_configure() != cudaSuccess) {
     cudaGetLastError();
     delete ctx;
     return VX_ERR_CUDA;

@@ -157,6 +157,16 @@ const LinearWorkspace* lm_workspace(const vx_lm* lm);
 // Grow the forward() work buffers to `rows` token rows (so a later capture allocates nothing).
 int lm_prepare_rows(vx_lm* lm, size_t rows);
 cudaError_t tc_gemm_configure();
+// AudioVAE convolutions on tcgen05 (vae_tc.cu).  launch_vae_split writes X [B, C, T] (after
+// the optional SR conditioning and snake) as the bf16 hi / lo operand xs [2][B][T][C];
+// launch_vae_tc_conv runs a pointwise conv (s = 1, A = W [Cout, Cin]) or a causal transposed
+// conv (stride s, A = the phase-folded weight [vae_tc_rows(Cout, s), 2 Cin]) over it.
+cudaError_t vae_tc_configure();
+int vae_tc_rows(int cout, int s);
+cudaError_t launch_vae_split(const float* X, int B, int C, int T, const float* alpha, const float* sr_scale,
+                             const float* sr_bias, uint16_t* xs, cudaStream_t st);
+cudaError_t launch_vae_tc_conv(const uint16_t* xs, int B, int T_in, int Cin, int Cout, int s, const uint16_t* A,
+                               const float* bias, const float* R, float* Y, int* err, cudaStream_t st);
 int lm_hidden_size(const vx_lm* lm);
 const float* lm_hid_norm(const vx_lm* lm);
 int lm_greedy_begin(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps);

@@ -13,7 +13,9 @@
 //     operand loader applies SampleRateConditionLayer (layers.rs:213-220) and the block's
 //     Snake1d to the input on the fly, so neither is a separate pass.
 //   * last_conv_kernel: snake_out -> CausalConv1d(C -> 1, k=7) -> tanh (decoder.rs:164-166).
-// First version on CUDA cores (f32 FMA on bf16-valued weights); a tcgen05 path is planned.
+// conv_gemm_kernel is the CUDA-core (f32 FMA) form of the same GEMMs; the decoder runs the
+// pointwise and transposed convs on tcgen05 (vae_tc.cu) and keeps conv_gemm_kernel for a
+// latent width that is not a multiple of 64 and for A/B timing (env VX_VAE_TC=0).
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -210,7 +212,8 @@ struct VaeUnit {
 struct VaeBlock {
   int cin = 0, cout = 0, stride = 0;
   float* alpha = nullptr;
-  uint16_t* up_w = nullptr;  // [stride][cout][2*cin] per-phase GEMM layout
+  uint16_t* up_w = nullptr;   // [stride][cout][2*cin] per-phase GEMM layout (CUDA-core path)
+  uint16_t* up_wt = nullptr;  // [vae_tc_rows(cout, stride)][2*cin] phase-folded layout (tcgen05 path)
   float* up_b = nullptr;
   VaeUnit res[3];
   float* sr_scale = nullptr;  // [cin] for the configured output sample rate (or null)
@@ -229,6 +232,9 @@ struct vx_vae {
   std::vector<void*> allocs;
   size_t buf_elems = 0;
   float *buf0 = nullptr, *buf1 = nullptr, *buf2 = nullptr;
+  bool tc = true;             // convolutions on tcgen05 (env VX_VAE_TC=0: CUDA-core FMA)
+  uint16_t* xs = nullptr;     // split operand of the tcgen05 convs [2][B][T][C]
+  size_t xs_elems = 0;
 
   template <typename T>
   T* alloc(size_t n) {
@@ -240,6 +246,19 @@ struct vx_vae {
 };
 
 namespace {
+
+int vae_split_buffer(vx_vae* v, size_t elems) {
+  if (elems <= v->xs_elems) return VX_OK;
+  if (v->xs) cudaFree(v->xs);
+  v->xs = nullptr;
+  v->xs_elems = 0;
+  if (cudaMalloc(&v->xs, elems * 2) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(v->ctx, VX_ERR_OOM, "VAE split operand (%zu bf16) allocation failed", elems);
+  }
+  v->xs_elems = elems;
+  return VX_OK;
+}
 
 int vae_buffers(vx_vae* v, size_t elems) {
   if (elems <= v->buf_elems) return VX_OK;
@@ -293,6 +312,7 @@ int vx_vae_create(vx_ctx* ctx, const vx_vae_config* cfg, vx_vae** out) {
   v->depthwise = cfg->depthwise;
   v->nblocks = cfg->n_rates;
   v->out_sr = cfg->out_sample_rate;
+  if (const char* e = getenv("VX_VAE_TC")) v->tc = atoi(e) != 0;
   for (int i = 0; i < cfg->n_rates; ++i) v->rates.push_back(cfg->rates[i]);
   // sr_bucket (layers.rs:225-228)
   if (cfg->n_sr_boundaries > 0) {
@@ -318,6 +338,7 @@ int vx_vae_create(vx_ctx* ctx, const vx_vae_config* cfg, vx_vae** out) {
     }
     ok = (bl.alpha = v->alloc<float>(bl.cin)) &&
          (bl.up_w = v->alloc<uint16_t>((size_t)bl.stride * bl.cout * 2 * bl.cin)) &&
+         (bl.up_wt = v->alloc<uint16_t>((size_t)vae_tc_rows(bl.cout, bl.stride) * 2 * bl.cin)) &&
          (bl.up_b = v->alloc<float>(bl.cout));
     for (int u = 0; ok && u < 3; ++u) {
       VaeUnit& r = bl.res[u];
@@ -347,6 +368,7 @@ void vx_vae_destroy(vx_vae* v) {
   for (void* p : v->allocs) cudaFree(p);
   for (float* p : {v->buf0, v->buf1, v->buf2})
     if (p) cudaFree(p);
+  if (v->xs) cudaFree(v->xs);
   delete v;
 }
 
@@ -381,6 +403,21 @@ int vx_vae_load_block(vx_vae* v, int i, const vx_vae_block_weights* w) {
         for (int c = 0; c < ci; ++c)
           dst[((size_t)r * co + o) * 2 * ci + (size_t)k * ci + c] = src[((size_t)c * co + o) * 2 * s + r + k * s];
   VX_CUDA(ctx, cudaMemcpy(bl.up_w, dst.data(), dst.size() * 2, cudaMemcpyHostToDevice));
+  // the tcgen05 path folds the phases into 128-row tiles of cpt = 128 / s channels: row
+  // tile * 128 + q * s + r holds phase r of channel tile * cpt + q; rows past cpt * s are zero
+  {
+    const int cpt = 128 / s, rows = vae_tc_rows(co, s);
+    std::vector<uint16_t> ft((size_t)rows * 2 * ci, 0);
+    for (int row = 0; row < rows; ++row) {
+      const int tile = row / 128, i = row % 128;
+      const int o = tile * cpt + i / s, r = i % s;
+      if (i >= cpt * s || o >= co) continue;
+      for (int k = 0; k < 2; ++k)
+        for (int c = 0; c < ci; ++c)
+          ft[(size_t)row * 2 * ci + (size_t)k * ci + c] = src[((size_t)c * co + o) * 2 * s + r + k * s];
+    }
+    VX_CUDA(ctx, cudaMemcpy(bl.up_wt, ft.data(), ft.size() * 2, cudaMemcpyHostToDevice));
+  }
   for (int u = 0; u < 3; ++u) {
     if (!w->res_alpha1[u] || !w->res_w1[u] || !w->res_b1[u] || !w->res_alpha2[u] || !w->res_w2[u] || !w->res_b2[u])
       return VX_ERR_ARG;
@@ -428,19 +465,41 @@ int vx_vae_decode(vx_vae* v, const float* z, int B, int T, float* wav) {
   elems *= B;
   int rc = vae_buffers(v, elems);
   if (rc) return rc;
+  // the split operand of the tcgen05 convs: two bf16 planes of the largest conv input
+  size_t xs_elems = (size_t)v->latent * T;
+  t = T;
+  for (int i = 0; i < v->nblocks; ++i) {
+    xs_elems = std::max(xs_elems, (size_t)v->blocks[i].cin * t);
+    t *= v->rates[i];
+    xs_elems = std::max(xs_elems, (size_t)v->blocks[i].cout * t);
+  }
+  const bool tc_first = v->tc && v->latent % 64 == 0;
+  if (v->tc && (rc = vae_split_buffer(v, 2 * xs_elems * B))) return rc;
   float *h = v->buf0, *y = v->buf1, *tmp = v->buf2;
   // first conv: depthwise k7 over the latent channels, then pointwise latent -> dim (decoder.rs:83-89)
   VX_CUDA(ctx, launch_dw(z, B, v->latent, T, v->first_dw_w, v->first_dw_b, 1, nullptr, nullptr, y, st));
-  ConvGemmArgs f = {v->first_pw_w, v->first_pw_b, y, nullptr, h, B, v->dim, v->latent, v->latent, T, 1,
-                    nullptr, nullptr, nullptr};
-  VX_CUDA(ctx, launch_conv_gemm(f, st));
+  if (tc_first) {
+    VX_CUDA(ctx, launch_vae_split(y, B, v->latent, T, nullptr, nullptr, nullptr, v->xs, st));
+    VX_CUDA(ctx, launch_vae_tc_conv(v->xs, B, T, v->latent, v->dim, 1, v->first_pw_w, v->first_pw_b, nullptr, h,
+                                    ctx->dev_err, st));
+  } else {
+    ConvGemmArgs f = {v->first_pw_w, v->first_pw_b, y, nullptr, h, B, v->dim, v->latent, v->latent, T, 1,
+                      nullptr, nullptr, nullptr};
+    VX_CUDA(ctx, launch_conv_gemm(f, st));
+  }
   int tl = T;
   for (int i = 0; i < v->nblocks; ++i) {
     VaeBlock& bl = v->blocks[i];
     // SR cond -> snake -> causal transposed conv (decoder.rs:158-162, 45-47)
-    ConvGemmArgs up = {bl.up_w, bl.up_b, h, nullptr, tmp, B, bl.cout, 2 * bl.cin, bl.cin, tl, bl.stride,
-                       bl.alpha, bl.sr_scale, bl.sr_bias};
-    VX_CUDA(ctx, launch_conv_gemm(up, st));
+    if (v->tc) {
+      VX_CUDA(ctx, launch_vae_split(h, B, bl.cin, tl, bl.alpha, bl.sr_scale, bl.sr_bias, v->xs, st));
+      VX_CUDA(ctx, launch_vae_tc_conv(v->xs, B, tl, bl.cin, bl.cout, bl.stride, bl.up_wt, bl.up_b, nullptr, tmp,
+                                      ctx->dev_err, st));
+    } else {
+      ConvGemmArgs up = {bl.up_w, bl.up_b, h, nullptr, tmp, B, bl.cout, 2 * bl.cin, bl.cin, tl, bl.stride,
+                         bl.alpha, bl.sr_scale, bl.sr_bias};
+      VX_CUDA(ctx, launch_conv_gemm(up, st));
+    }
     tl *= bl.stride;
     std::swap(h, tmp);
     const int dils[3] = {1, 3, 9};
@@ -448,8 +507,13 @@ int vx_vae_decode(vx_vae* v, const float* z, int B, int T, float* wav) {
       const VaeUnit& r = bl.res[u];
       // CausalResidualUnit: x + conv1x1(snake(dwconv7_dil(snake(x))))  (layers.rs:150-156)
       VX_CUDA(ctx, launch_dw(h, B, bl.cout, tl, r.w1, r.b1, dils[u], r.alpha1, r.alpha2, y, st));
-      ConvGemmArgs pw = {r.w2, r.b2, y, h, h, B, bl.cout, bl.cout, bl.cout, tl, 1, nullptr, nullptr, nullptr};
-      VX_CUDA(ctx, launch_conv_gemm(pw, st));
+      if (v->tc) {
+        VX_CUDA(ctx, launch_vae_split(y, B, bl.cout, tl, nullptr, nullptr, nullptr, v->xs, st));
+        VX_CUDA(ctx, launch_vae_tc_conv(v->xs, B, tl, bl.cout, bl.cout, 1, r.w2, r.b2, h, h, ctx->dev_err, st));
+      } else {
+        ConvGemmArgs pw = {r.w2, r.b2, y, h, h, B, bl.cout, bl.cout, bl.cout, tl, 1, nullptr, nullptr, nullptr};
+        VX_CUDA(ctx, launch_conv_gemm(pw, st));
+      }
     }
   }
   const int cl = v->dim >> v->nblocks;
