@@ -35,7 +35,9 @@ sys.path.insert(0, ROOT)
 LAYERS, HIDDEN, INTER, NH, NKV, HD, VOCAB = 28, 2048, 6144, 16, 2, 128, 73448
 PROMPT, STEPS_PER_UTT, MAX_LEN = 64, 256, 4096
 SYN_B = 8  # utterances resident per GPU in the batched-synthesis side figure
-BASELINE_METRIC = "LM decode tok/s/GPU, audio-s/s at 1/2/4/8 B200; fused-op HBM GB/s vs peak"
+WORKLOAD = ("MiniCPM-4 LM greedy decode: 28 layers, hidden 2048, 16/2 heads, head_dim 128, SwiGLU 6144, tied vocab "
+            "73448, bf16 weights ~N(0,0.02) (seed 0), 64-id prompt + 256 greedy steps, KV capacity 4096, batch 1 per GPU")
+HEADLINE_METRICS = "LM decode tok/s/GPU, audio-s/s at 1/2/4/8 B200; fused-op HBM GB/s vs peak"
 
 # Algorithmic bytes (the roofline basis): bf16 weights of one decoder layer, the tied
 # embedding read by the greedy head, and the KV rows read by attention at position p.
@@ -148,20 +150,6 @@ def load_device_weights(model, w):
     check(L.vx_lm_load_embed(model.h, ptr(w["embed"])), model.ctx.h)
 
 
-def oracle_weights_from_device(w):
-    """f32 model-layout copy of the device weights for the CPU restatement."""
-    import numpy as np
-    import torch
-
-    def f(t):
-        return t.view(torch.bfloat16).float().cpu().numpy()
-    return {"embed": f(w["embed"]), "norm": w["norm"].cpu().numpy(),
-            "layers": [{"wqkv": np.concatenate([f(l["q"]), f(l["k"]), f(l["v"])]), "wo": f(l["o"]),
-                        "wgu": np.concatenate([f(l["gate"]), f(l["up"])]), "wd": f(l["down"]),
-                        "ln_in": l["ln_in"].cpu().numpy(), "ln_post": l["ln_post"].cpu().numpy()}
-                       for l in w["layers"]]}
-
-
 # ------------------------------------------------------------------ CPU restatement timing
 def cpu_threads():
     """All host cores for the CPU arms: torch and the BLAS pool numpy uses (torchrun sets
@@ -172,6 +160,24 @@ def cpu_threads():
     torch.set_num_threads(n)
     threadpool_limits(limits=n)
     return n
+
+
+def cpu_model():
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_rate_1thread(fw, prompt, n_steps):
+    """The same greedy decode on one host thread (BLAS pool limited to 1)."""
+    from threadpoolctl import threadpool_limits
+    with threadpool_limits(limits=1):
+        r, _, _ = cpu_decode_rate(fw, prompt, n_steps, warm=1)
+    return r
 
 
 def cpu_decode_rate(fw, prompt, n_steps, warm=1):
@@ -223,10 +229,11 @@ def run_reference(args):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000.0 * per_step / value, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (random-init weights, seeded prompt)",
-            "config": {"workload": "MiniCPM-4 28-layer greedy LM decode, 64-id prompt, batch 1",
+            "config": {"workload": WORKLOAD,
                        "sample": f"{per_step} timed greedy decode steps per step, after a 64-id prefill "
                                  f"and one untimed decode step"},
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                             "cpu_model": cpu_model(), "value_1_thread": cpu_rate_1thread(fw, prompt, 1),
                              "sample": f"{per_step} decode steps per step, numpy f32 restatement "
                                        f"(oracle/) with {threads} BLAS threads"},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -635,10 +642,11 @@ def main():
     device = f"cuda:{local}"
     ctx = Context(local)
     cfg = lm_config()
-    w = device_weights(1234 + rank, device)
+    # the same seeded checkpoint-layout weights on every rank and in the CPU arms (host bf16
+    # bits, uploaded once); each rank decodes its own prompt
+    w = synth.minicpm_weights(cfg, seed=0)
     # batch capacity for the batched-synthesis side figure; the headline decode uses row 0
-    model = MiniCpmModel(ctx, cfg, None, max_batch=1 if args.no_extras else SYN_B, max_length=MAX_LEN)
-    load_device_weights(model, w)
+    model = MiniCpmModel(ctx, cfg, w, max_batch=1 if args.no_extras else SYN_B, max_length=MAX_LEN)
     prompt = synth.prompt_ids(PROMPT, VOCAB, seed=rank)
     prompt_pinned = torch.from_numpy(prompt).pin_memory()
     tokens_pinned = torch.empty(STEPS_PER_UTT + 1, dtype=torch.int32).pin_memory()
@@ -701,7 +709,7 @@ def main():
             traffic = None
     # the per-kernel step's dominant kernel, live: the streamed GEMV on the 28 gate|up weights
     # (50 MB each, 1.4 GB rotation > L2), graph-replayed between CUDA events
-    gu = [torch.cat([l["gate"], l["up"]], 0) for l in w["layers"]]
+    gu = [torch.from_numpy(np.concatenate([l["gate"], l["up"]], 0).view(np.int16)).to(device) for l in w["layers"]]
     xs = torch.randn(1, HIDDEN, device=device)
     gemv_us = gemv_graph_us(ctx, gu, xs, 5)
     gemv_gbs = GATE_UP_BYTES / (gemv_us * 1e-6) / 1e9
@@ -750,34 +758,52 @@ def main():
                                            "(rates 2,5,8,8; 16 kHz)",
                                "audio_seconds_per_utterance": audio_s, "wall_s": e2e_s, "wall_s_runs": runs,
                                "audio_s_per_s": world * audio_s / e2e_s, "n_gpus": world}
-        # the same synthesis for SYN_B utterances resident per GPU (vx_generate_batch: the LM
-        # decodes them as SYN_B rows of one step, each patch's CFM solve runs 2*SYN_B DiT rows)
-        rng_b = np.random.default_rng(200 + rank)
-        prompts_b = np.stack([synth.prompt_ids(PROMPT, VOCAB, seed=1000 + rank * SYN_B + b) for b in range(SYN_B)])
-        noise_b = rng_b.standard_normal((SYN_B, STEPS_PER_UTT, 64, 4), dtype=np.float32)
-        vox.generate_batch(prompts_b, GenerateOptions(max_len=4), noise_b[:, :4])
-        runs_b = []
-        for _ in range(3):  # median of three, as for one utterance
-            barrier()
-            t0 = time.perf_counter()
-            wav_b = vox.generate_batch(prompts_b, GenerateOptions(max_len=STEPS_PER_UTT), noise_b)
-            runs_b.append(allmax(time.perf_counter() - t0))
-        e2e_b = sorted(runs_b)[1]
-        extras["synthesis_batched"] = {
-            "workload": f"end-to-end synthesis, {SYN_B} utterances per GPU decoded together (vx_generate_batch), "
-                        "same LM / CFM / AudioVAE settings",
-            "utterances_per_gpu": SYN_B, "audio_seconds_per_utterance": wav_b.shape[1] / 16000.0, "wall_s": e2e_b,
-            "wall_s_runs": runs_b,
-            "audio_s_per_s": world * SYN_B * (wav_b.shape[1] / 16000.0) / e2e_b, "n_gpus": world}
+        # the end-to-end synthesis workload: 64 independent utterances partitioned over the ranks
+        # (contiguous blocks of 64/N), each rank decoding its block in waves of SYN_B
+        # utterances (vx_generate_batch: the LM runs SYN_B rows per step, each patch's CFM solve
+        # 2*SYN_B DiT rows); whole-job audio-s/s = 64 x 40.96 s over the slowest rank's wall time
+        n_utt = 64
+
+        def work_batch(ids):
+            prompts = np.stack([synth.prompt_ids(PROMPT, VOCAB, seed=1000 + u) for u in ids])
+            noise = np.stack([np.random.default_rng(2000 + u).standard_normal((STEPS_PER_UTT, 64, 4),
+                                                                                 dtype=np.float32) for u in ids])
+            wav = vox.generate_batch(prompts, GenerateOptions(max_len=STEPS_PER_UTT), noise)
+            return [w.shape[0] for w in wav]
+        warm_ids = list(range(SYN_B))
+        vox.generate_batch(np.stack([synth.prompt_ids(PROMPT, VOCAB, seed=1000 + u) for u in warm_ids]),
+                           GenerateOptions(max_len=4), np.zeros((SYN_B, 4, 64, 4), np.float32))
+        torch.cuda.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        got = vxd.run_partitioned(list(range(n_utt)), work_batch, batch=SYN_B)
+        torch.cuda.synchronize()
+        part_s = time.perf_counter() - t0
+        part_max = allmax(part_s)
+        samples = sum(got.values())
+        total_samples = samples
+        if dist is not None:
+            t = torch.tensor([float(samples)], dtype=torch.float64, device=device)
+            dist.all_reduce(t)
+            total_samples = float(t.item())
+        extras["synthesis_partitioned"] = {
+            "workload": f"end-to-end synthesis of {n_utt} utterances partitioned over {world} GPU(s) ({n_utt // world} "
+                        f"per GPU, waves of {SYN_B} decoded together): LM 64-id prompt + 256 greedy steps, a CFM solve "
+                        "per step (sway 1, zero-star, CFG 2, 10 steps), AudioVAE (rates 2,5,8,8; 16 kHz)",
+            "metric": "audio-s/s", "value": total_samples / 16000.0 / part_max, "unit": "audio-s/s",
+            "utterances": n_utt, "utterances_per_gpu": n_utt // world, "wave": SYN_B, "wall_s": part_max,
+            "audio_seconds": total_samples / 16000.0, "n_gpus": world, "scaling": "strong (64 utterances in total)",
+            "timing": "wall clock around every rank's waves (barrier before, max over ranks)"}
         vox.dit.close()
         vox.vae.close()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = cpu_threads()
-        fw = oracle_weights_from_device(w)
+        fw = synth.minicpm_f32_view(w)
         rate, n, secs = cpu_decode_rate(fw, prompt, args.cpu_steps)
-        cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
+        cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "cpu_model": cpu_model(),
+               "value_1_thread": cpu_rate_1thread(fw, prompt, 2),
                "sample": f"{n} greedy decode steps of the same 28-layer model after a 64-id prefill "
                          f"({secs:.1f} s), numpy f32 restatement (oracle/), {threads} BLAS threads"}
         del fw
@@ -788,10 +814,8 @@ def main():
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": total_ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32 (bf16 weights)", "data": "synthetic (random-init weights, seeded prompt)",
-            "baseline_metric": BASELINE_METRIC,
-            "config": {"workload": "MiniCPM-4 LM greedy decode: 28 layers, hidden 2048, 16/2 heads, head_dim 128, "
-                                   "SwiGLU 6144, tied vocab 73448, 64-id prompt + 256 greedy steps, KV capacity 4096, "
-                                   "batch 1 per GPU",
+            "headline_metrics": HEADLINE_METRICS,
+            "config": {"workload": WORKLOAD,
                        "global_batch": world, "seq_len": PROMPT + STEPS_PER_UTT, "parallelism": f"replicas x{world}",
                        "l2": "inputs larger than L2 (2.94 GB of weights read per decode step)",
                        "value_scope": "256 decode steps per step, device time; prefill excluded (see prefill_ms)"},

@@ -38,7 +38,18 @@ def _worker(rank, world, port, q, mode):
             if mode == "item7_bad" and x == 7:
                 raise RuntimeError("simulated failure of item 7")
             return x * x
-        done = vxd.run_partitioned(items, work)
+        if mode.startswith("waves"):
+            # 20 utterances in waves of up to 4 per rank; in "waves_bad" the wave holding
+            # utterance 13 raises on rank 1, so its 4 utterances are re-queued to rank 0
+
+            def work_batch(xs):
+                if mode == "waves_bad" and rank == 1 and 13 in xs:
+                    raise RuntimeError("simulated failure of a wave")
+                assert len(xs) <= 4
+                return [x * x for x in xs]
+            done = vxd.run_partitioned(list(range(20)), work_batch, batch=4)
+        else:
+            done = vxd.run_partitioned(items, work)
         q.put((rank, rate, done))
     finally:
         dist.destroy_process_group()
@@ -55,7 +66,15 @@ def test_partition_covers_everything():
         assert max(map(len, parts)) - min(map(len, parts)) <= 1
 
 
-@pytest.mark.parametrize("mode", ["ok", "rank1_down", "item7_bad"])
+def test_waves():
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from voxcpm_rs_b200 import dist as vxd
+    assert vxd.waves(list(range(10)), 4) == [[0, 1, 2, 3], [4, 5, 6, 7], [8, 9]]
+    assert vxd.waves([], 8) == []
+
+
+@pytest.mark.parametrize("mode", ["ok", "rank1_down", "item7_bad", "waves", "waves_bad"])
 def test_two_rank_partition_and_requeue(mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -74,6 +93,10 @@ def test_two_rank_partition_and_requeue(mode):
         for k, v in done.items():
             assert k not in merged
             merged[k] = v
+    if mode.startswith("waves"):
+        # every utterance completes exactly once; a failed wave is retried by a healthy rank
+        assert merged == {i: i * i for i in range(20)}
+        return
     if mode == "item7_bad":
         # item 7 fails on every rank: everything else completes exactly once
         assert merged == {i: i * i for i in range(9) if i != 7}

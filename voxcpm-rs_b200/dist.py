@@ -38,21 +38,39 @@ def aggregate_rate(local_units: float, local_seconds: float, group=None, device=
     return float(t.item()) / allmax(local_seconds, group, device)
 
 
-def run_partitioned(items: Sequence, work: Callable[[object], object], group=None) -> dict:
+def waves(indices: Sequence[int], size: int) -> List[List[int]]:
+    """Consecutive groups of at most ``size`` indices (the utterances decoded together)."""
+    return [list(indices[i:i + size]) for i in range(0, len(indices), size)]
+
+
+def run_partitioned(items: Sequence, work: Callable[[object], object], group=None, batch: int = 1) -> dict:
     """Process this rank's share of ``items`` with ``work``; items whose work raised are
     gathered from every rank and re-run round-robin by the ranks that did not fail (a rank
     that failed once gets no retries).  Returns ``{item_index: result}`` for the items this
-    rank completed.  Every rank takes the same collective steps in the same order."""
+    rank completed.  Every rank takes the same collective steps in the same order.
+
+    With ``batch > 1`` the rank's share runs in waves of up to ``batch`` items: ``work``
+    receives a list of items and returns one result per item; a wave that raised re-queues
+    all of its items (retried one wave per healthy rank, in waves of ``batch`` again)."""
     import torch.distributed as dist
     dist_on = dist.is_available() and dist.is_initialized()
     world = dist.get_world_size(group) if dist_on else 1
     rank = dist.get_rank(group) if dist_on else 0
-    done, failed = {}, []
-    for i in partition(len(items), world, rank):
+
+    def run(idx: List[int], done: dict, failed: list):
         try:
-            done[i] = work(items[i])
+            if batch > 1:
+                res = work([items[i] for i in idx])
+                for i, r in zip(idx, res):
+                    done[i] = r
+            else:
+                done[idx[0]] = work(items[idx[0]])
         except Exception:
-            failed.append(i)
+            failed.extend(idx)
+
+    done, failed = {}, []
+    for wv in waves(partition(len(items), world, rank), max(1, batch)):
+        run(wv, done, failed)
     if not dist_on:
         return done
     gathered: List[Iterable[int]] = [None] * world  # type: ignore[list-item]
@@ -60,10 +78,7 @@ def run_partitioned(items: Sequence, work: Callable[[object], object], group=Non
     healthy = [r for r in range(world) if not gathered[r]]
     retry = sorted(i for lst in gathered for i in lst)
     if healthy:
-        for j, i in enumerate(retry):
+        for j, wv in enumerate(waves(retry, max(1, batch))):
             if healthy[j % len(healthy)] == rank:
-                try:
-                    done[i] = work(items[i])
-                except Exception:
-                    pass  # failed twice: reported as missing from every rank's result
+                run(wv, done, [])  # failed twice: reported as missing from every rank's result
     return done
