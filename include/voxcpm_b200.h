@@ -401,6 +401,55 @@ int vx_voxcpm2_generate(vx_voxcpm2* m, vx_vae* vae, const int32_t* text_token, c
                         int inference_timesteps, float cfg_value, const float* noise, float* wav_out,
                         int* n_samples);
 
+/* ----------------------------------------------------------------- checkpoints */
+
+/* Element types of checkpoint tensors (safetensors dtypes / torch storage types). */
+enum { VX_DT_F32 = 0, VX_DT_F16 = 1, VX_DT_BF16 = 2, VX_DT_F64 = 3, VX_DT_I64 = 4, VX_DT_I32 = 5, VX_DT_I16 = 6,
+       VX_DT_I8 = 7, VX_DT_U8 = 8, VX_DT_BOOL = 9 };
+
+/* A checkpoint file opened on the host (load_single / load_single_pth, weights.rs:264-367):
+ * a .safetensors file, or a PyTorch zip checkpoint (.pth / .pt, torch.save) whose nested
+ * dicts are flattened with '.' and whose "state_dict." / "model_state_dict." / "module."
+ * prefixes are stripped (strip_pth_top_level, weights.rs:400-411).  The file is
+ * memory-mapped until vx_weights_close.  Errors are reported by vx_weights_last_error
+ * (this thread's last failure). */
+typedef struct vx_weights vx_weights;
+int vx_weights_open(const char* path, vx_weights** out);
+void vx_weights_close(vx_weights* w);
+const char* vx_weights_last_error(void);
+int vx_weights_count(const vx_weights* w);
+const char* vx_weights_name(const vx_weights* w, int i);
+int vx_weights_find(const vx_weights* w, const char* name);
+/* dtype and shape of tensor i; returns its rank (-1 if i is out of range). */
+int vx_weights_info(const vx_weights* w, int i, int* dtype, int64_t* shape, int max_dims);
+/* Tensor `name` converted to out_dtype (VX_DT_F32, or VX_DT_BF16 rounded to nearest even)
+ * into host memory of n_elems elements.  A "<stem>.weight" that the file stores as a
+ * weight_norm pair (<stem>.weight_g, <stem>.weight_v) is materialised:
+ * w[o, ...] = g[o] * v[o, ...] / max(||v[o, :]||, 1e-12) (materialize_weight_norm,
+ * weights.rs:447-471). */
+int vx_weights_read(const vx_weights* w, const char* name, int out_dtype, void* out, size_t n_elems);
+
+/* Model loaders over the upstream checkpoint key layout (the reference's module paths,
+ * weights.rs:56-133): <prefix>layers.<i>.self_attn.{q,k,v,o}_proj.weight (or a fused
+ * qkv_proj), mlp.{gate,up,down}_proj.weight (or gate_up_proj), input_layernorm /
+ * post_attention_layernorm, <prefix>norm.weight, <prefix>embed_tokens.weight (with a
+ * vocabulary).  Shapes are checked against the model (VX_ERR_SHAPE). */
+int vx_lm_load_weights(vx_lm* lm, const vx_weights* w, const char* prefix);
+/* VoxCpmLocDiTV2 (local_dit.rs:58-67): <prefix>{in,cond,out}_proj, time_mlp / delta_time_mlp
+ * .linear_{1,2}, decoder.*  (VoxCPM2: prefix "feat_decoder.estimator."). */
+int vx_dit_load_weights(vx_dit* dit, const vx_weights* w, const char* prefix);
+/* AudioVAE decoder from the checkpoint's nn.Sequential keys (remap_audiovae_key,
+ * weights.rs:140-262) under <prefix>decoder.: model.0 / model.1 (first depthwise / pointwise
+ * conv), model.<2+i>.block.{0: snake, 1: transposed conv, 2-4: residual units with block.0-3
+ * = snake1, conv1, snake2, conv2}, model.<2+n> snake_out, model.<3+n> last conv,
+ * sr_cond_model.<2+i>.{scale,bias}_embed.weight; weight_norm pairs are materialised. */
+int vx_vae_load_weights(vx_vae* vae, const vx_weights* w, const char* prefix);
+/* The whole VoxCpm2Model (model.rs:22-37) from model.safetensors / model.pth: base_lm.,
+ * residual_lm., feat_encoder.{special_token, in_proj, encoder.}, feat_decoder.estimator.,
+ * fsq_layer.{in,out}_proj, enc_to_lm_proj, lm_to_dit_proj, res_to_dit_proj,
+ * fusion_concat_proj, stop_proj, stop_head. */
+int vx_voxcpm2_load_weights(vx_voxcpm2* m, const vx_weights* w);
+
 #ifdef __cplusplus
 }
 #endif

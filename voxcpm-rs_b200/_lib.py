@@ -130,6 +130,18 @@ SIGNATURES = {
     "vx_locenc_forward": (I32, [P, P, I32, P]),
     "vx_voxcpm2_inference": (I32, [P, P, P, P, P, I32, I32, I32, I32, F32, P, P, C.POINTER(I32), P]),
     "vx_voxcpm2_generate": (I32, [P, P, P, P, P, P, I32, I32, I32, I32, F32, P, P, C.POINTER(I32)]),
+    "vx_weights_open": (I32, [C.c_char_p, C.POINTER(P)]),
+    "vx_weights_close": (None, [P]),
+    "vx_weights_last_error": (C.c_char_p, []),
+    "vx_weights_count": (I32, [P]),
+    "vx_weights_name": (C.c_char_p, [P, I32]),
+    "vx_weights_find": (I32, [P, C.c_char_p]),
+    "vx_weights_info": (I32, [P, I32, C.POINTER(I32), P, I32]),
+    "vx_weights_read": (I32, [P, C.c_char_p, I32, P, C.c_size_t]),
+    "vx_lm_load_weights": (I32, [P, P, C.c_char_p]),
+    "vx_dit_load_weights": (I32, [P, P, C.c_char_p]),
+    "vx_vae_load_weights": (I32, [P, P, C.c_char_p]),
+    "vx_voxcpm2_load_weights": (I32, [P, P]),
 }
 
 _lib = None

@@ -472,4 +472,9 @@ int cfm_solve_enqueue(vx_dit* d, const float* mu, const float* cond, const float
 vx_ctx* dit_ctx(vx_dit* d) { return d->ctx; }
 int dit_in_channels(const vx_dit* d) { return d->C; }
 int dit_hidden_size(const vx_dit* d) { return d->H; }
+vx_lm* dit_decoder(vx_dit* d, int* H, int* C) {
+  *H = d->H;
+  *C = d->C;
+  return d->dec;
+}
 }  // namespace vx

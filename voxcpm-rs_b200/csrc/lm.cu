@@ -911,6 +911,14 @@ const float* lm_batch_hidden(const vx_lm* lm) { return lm->bhid; }
 const int* lm_batch_tokens(const vx_lm* lm) { return lm->btokens; }
 int lm_max_batch(const vx_lm* lm) { return lm->max_batch; }
 int lm_vocab_size(const vx_lm* lm) { return lm->V; }
+void lm_dims(const vx_lm* lm, int* L, int* H, int* I, int* qs, int* ks, int* V) {
+  *L = lm->L;
+  *H = lm->H;
+  *I = lm->I;
+  *qs = lm->qs;
+  *ks = lm->ks;
+  *V = lm->V;
+}
 int lm_max_length(const vx_lm* lm) { return lm->max_length; }
 
 // One graph-replayed decode step: consumes the last picked id at the device position,

@@ -180,12 +180,19 @@ const float* lm_batch_hidden(const vx_lm* lm);
 const int* lm_batch_tokens(const vx_lm* lm);
 int lm_max_batch(const vx_lm* lm);
 int lm_vocab_size(const vx_lm* lm);
+void lm_dims(const vx_lm* lm, int* L, int* H, int* I, int* qs, int* ks, int* V);
 int lm_max_length(const vx_lm* lm);
 // DiT / VAE accessors (dit.cu, vae.cu).
 int cfm_solve_enqueue(vx_dit* d, const float* mu, const float* cond, const float* z, int B, int C_mu, int T, int Tc,
                       int n_timesteps, float cfg_value, float sway_sampling_coef, int use_cfg_zero_star,
                       float* x_out);
 int dit_hidden_size(const vx_dit* d);
+vx_lm* dit_decoder(vx_dit* d, int* H, int* C);
+struct VaeDims {
+  int latent, dim, nblocks, rates[8], n_buckets;  // n_buckets 0: no sample-rate conditioning
+};
+void vae_dims(const vx_vae* v, VaeDims* out);
+void voxcpm2_parts(vx_voxcpm2* m, vx_lm** base, vx_lm** res, vx_lm** enc, vx_dit** dit, int dims[6]);
 vx_ctx* dit_ctx(vx_dit* d);
 int dit_in_channels(const vx_dit* d);
 vx_ctx* vae_ctx(vx_vae* v);

@@ -224,7 +224,7 @@ struct VaeBlock {
 
 struct vx_vae {
   vx_ctx* ctx = nullptr;
-  int latent = 0, dim = 0, depthwise = 1, nblocks = 0, sr_idx = -1, out_sr = 0;
+  int latent = 0, dim = 0, depthwise = 1, nblocks = 0, sr_idx = -1, out_sr = 0, n_buckets = 0;
   std::vector<int> rates;
   float *first_dw_b = nullptr, *first_pw_b = nullptr, *alpha_out = nullptr, *last_b = nullptr;
   uint16_t *first_dw_w = nullptr, *first_pw_w = nullptr, *last_w = nullptr;
@@ -323,6 +323,7 @@ int vx_vae_create(vx_ctx* ctx, const vx_vae_config* cfg, vx_vae** out) {
         break;
       }
     v->sr_idx = idx;
+    v->n_buckets = cfg->n_sr_boundaries + 1;
   }
   const int L = v->latent, D = v->dim;
   bool ok = (v->first_dw_w = v->alloc<uint16_t>((size_t)L * 7)) && (v->first_dw_b = v->alloc<float>(L)) &&
@@ -529,6 +530,13 @@ int vx_vae_decode(vx_vae* v, const float* z, int B, int T, float* wav) {
 namespace vx {
 vx_ctx* vae_ctx(vx_vae* v) { return v->ctx; }
 int vae_latent(const vx_vae* v) { return v->latent; }
+void vae_dims(const vx_vae* v, VaeDims* out) {
+  out->latent = v->latent;
+  out->dim = v->dim;
+  out->nblocks = v->nblocks;
+  for (int i = 0; i < 8; ++i) out->rates[i] = i < v->nblocks ? v->rates[i] : 0;
+  out->n_buckets = v->n_buckets;
+}
 int vae_hop(const vx_vae* v) {
   int h = 1;
   for (int r : v->rates) h *= r;

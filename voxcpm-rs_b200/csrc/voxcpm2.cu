@@ -577,3 +577,18 @@ int vx_voxcpm2_generate(vx_voxcpm2* m, vx_vae* vae, const int32_t* text_token, c
 }
 
 }  // extern "C"
+
+namespace vx {
+void voxcpm2_parts(vx_voxcpm2* m, vx_lm** base, vx_lm** res, vx_lm** enc, vx_dit** dit, int dims[6]) {
+  *base = m->base;
+  *res = m->res;
+  *enc = m->enc;
+  *dit = m->dit;
+  dims[0] = m->H;
+  dims[1] = m->He;
+  dims[2] = m->Hd;
+  dims[3] = m->D;
+  dims[4] = m->P;
+  dims[5] = m->Lq;
+}
+}  // namespace vx
