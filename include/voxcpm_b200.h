@@ -46,6 +46,7 @@ typedef struct vx_ctx vx_ctx;
 typedef struct vx_lm vx_lm;
 typedef struct vx_dit vx_dit;
 typedef struct vx_vae vx_vae;
+typedef struct vx_vae_stream vx_vae_stream;
 typedef void* vx_stream;
 
 /* MiniCpm4Config + RopeScalingConfig (src/config.rs:42-84).  Factor arrays are host
@@ -307,6 +308,21 @@ int vx_vae_load_out(vx_vae* vae, const float* alpha_out, const uint16_t* last_w,
  * device pointers.  Synchronises. */
 int vx_vae_decode(vx_vae* vae, const float* z, int B, int T, float* wav);
 
+/* Stateful chunked decode for B utterances, the counterpart of generate_stream's per-chunk
+ * decode (voxcpm2/wrapper.rs:669-724), which re-decodes the whole accumulated latent every
+ * chunk: here every causal layer keeps the tail of its input (the first depthwise conv's
+ * last 6 latent frames, each transposed conv's last input frame, each residual unit's last
+ * 6 x dilation inputs, the last conv's last 6), so vx_vae_stream_decode of a chunk of T new
+ * latent frames costs T frames of work and writes exactly the T * prod(rates) samples that
+ * decoding the whole latent would give for them (bit for bit).  Needs the tcgen05 convs
+ * (latent a multiple of 64).  vx_vae_stream_reset starts a new utterance.  z [B, latent, T]
+ * and wav [B, 1, T * prod(rates)] are device pointers; the call synchronises.  One stream per
+ * VAE at a time: decodes share the VAE's work buffers. */
+int vx_vae_stream_create(vx_vae* vae, int B, vx_vae_stream** out);
+void vx_vae_stream_destroy(vx_vae_stream* s);
+int vx_vae_stream_reset(vx_vae_stream* s);
+int vx_vae_stream_decode(vx_vae_stream* s, const float* z, int T, float* wav);
+
 /* ----------------------------------------------------------------- synthesis */
 
 /* GenerateOptions (voxcpm2/wrapper.rs:146-187) as this library's synthesis loop uses them. */
@@ -393,6 +409,16 @@ int vx_voxcpm2_inference(vx_voxcpm2* m, const int32_t* text_token, const float* 
                          const float* feat_mask, int S, int min_len, int max_len, int inference_timesteps,
                          float cfg_value, const float* noise, float* latent_out, int* n_patches,
                          float* stop_logits_out);
+/* The inference loop in steps, for streaming (VoxCPM::generate_stream, wrapper.rs:456-492,
+ * 680-724): vx_voxcpm2_begin runs the prefill with the same arguments as
+ * vx_voxcpm2_inference; each vx_voxcpm2_advance runs up to max_patches more AR steps and
+ * writes the new patches' latent [D, n_new * P] (host or device) to latent_out; *finished
+ * becomes 1 once the stop head fired at a step i > min_len or max_len patches exist.  The
+ * concatenated latents equal vx_voxcpm2_inference's. */
+int vx_voxcpm2_begin(vx_voxcpm2* m, const int32_t* text_token, const float* text_mask, const float* feat,
+                     const float* feat_mask, int S, int min_len, int max_len, int inference_timesteps,
+                     float cfg_value, const float* noise);
+int vx_voxcpm2_advance(vx_voxcpm2* m, int max_patches, float* latent_out, int* n_new, int* finished);
 /* VoxCPM::generate (wrapper.rs:401-423) without the tokenizer: vx_voxcpm2_inference, then
  * decode_latent_to_samples (wrapper.rs:616-629) through the VAE.  wav_out (host or device)
  * must hold max_len * P * prod(rates) samples; *n_samples receives the count written. */

@@ -84,3 +84,28 @@ def test_vae_decode_c5_t256(ctx, c5_vae):
     assert got.shape == (1, 1, 256 * 640)
     assert_close(got, want, **TOL, what="VAE decode T=256")
     assert np.abs(got - want).max() < 2e-3
+
+
+@pytest.mark.parametrize("chunks", [[5, 3, 7, 1, 4], [1] * 10, [16]])
+def test_vae_stream_bit_exact(ctx, c5_vae, chunks):
+    """Stateful chunked decode (vx_vae_stream_decode) reproduces the one-shot decode bit for
+    bit, whatever the chunking (generate_stream's chunks, voxcpm2/wrapper.rs:669-724), for two
+    utterances at once; reset starts over."""
+    from voxcpm_rs_b200.audiovae import AudioVae, AudioVaeStream
+    vcfg, w, _ = c5_vae
+    T = sum(chunks)
+    z = np.random.default_rng(77).standard_normal((2, 64, T), dtype=np.float32)
+    vae = AudioVae(ctx, vcfg, w)
+    full = vae.decode(_t(z)).cpu().numpy()
+    st = AudioVaeStream(vae, B=2)
+    for rep in range(2):
+        parts, t0 = [], 0
+        for c in chunks:
+            parts.append(st.decode(_t(z[:, :, t0:t0 + c])).cpu().numpy())
+            t0 += c
+        got = np.concatenate(parts, axis=2)
+        assert got.shape == full.shape
+        assert np.array_equal(got, full), f"max diff {np.abs(got - full).max()}"
+        st.reset()
+    st.close()
+    vae.close()

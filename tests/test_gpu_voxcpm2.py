@@ -153,3 +153,25 @@ def test_cancel_and_bad_inputs(ctx, model):
         ctx.cancel_reset()
     lat, _ = m.inference(ids, tm, feat, fm, 2, 12, 10, 2.0, noise)
     assert lat.shape[1] > 0
+
+
+@pytest.mark.parametrize("chunk", [1, 3, 5])
+def test_generate_stream_matches_generate(ctx, model, chunk):
+    """VoxCPM::generate_stream (wrapper.rs:456-492, 680-724): AR steps in chunks of `chunk`
+    patches, each chunk decoded by the stateful AudioVAE stream; the concatenated audio equals
+    generate's waveform bit for bit, and the stop step is the same."""
+    from voxcpm_rs_b200 import config, synth
+    from voxcpm_rs_b200.audiovae import AudioVae
+    _, _, _, m = model
+    vcfg = config.vae_config(decoder_dim=256, decoder_rates=[2, 2])
+    vae = AudioVae(ctx, vcfg, synth.vae_weights(vcfg, seed=1))
+    try:
+        ids, tm, feat, fm, noise = inputs(2)
+        want = m.generate(vae, ids, tm, feat, fm, 2, 12, 10, 2.0, noise)
+        parts = list(m.generate_stream(vae, ids, tm, feat, fm, 2, 12, 10, 2.0, noise, chunk_patches=chunk))
+        got = np.concatenate(parts)
+        assert got.shape == want.shape
+        assert np.array_equal(got, want)
+        assert all(len(p) == chunk * 4 * 4 for p in parts[:-1])
+    finally:
+        vae.close()

@@ -130,6 +130,12 @@ SIGNATURES = {
     "vx_locenc_forward": (I32, [P, P, I32, P]),
     "vx_voxcpm2_inference": (I32, [P, P, P, P, P, I32, I32, I32, I32, F32, P, P, C.POINTER(I32), P]),
     "vx_voxcpm2_generate": (I32, [P, P, P, P, P, P, I32, I32, I32, I32, F32, P, P, C.POINTER(I32)]),
+    "vx_voxcpm2_begin": (I32, [P, P, P, P, P, I32, I32, I32, I32, F32, P]),
+    "vx_voxcpm2_advance": (I32, [P, I32, P, C.POINTER(I32), C.POINTER(I32)]),
+    "vx_vae_stream_create": (I32, [P, I32, C.POINTER(P)]),
+    "vx_vae_stream_destroy": (None, [P]),
+    "vx_vae_stream_reset": (I32, [P]),
+    "vx_vae_stream_decode": (I32, [P, P, I32, P]),
     "vx_weights_open": (I32, [C.c_char_p, C.POINTER(P)]),
     "vx_weights_close": (None, [P]),
     "vx_weights_last_error": (C.c_char_p, []),

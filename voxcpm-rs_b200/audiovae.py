@@ -76,3 +76,40 @@ class AudioVae:
             self.close()
         except Exception:
             pass
+
+
+class AudioVaeStream:
+    """Stateful chunked decoding of B utterances (``vx_vae_stream``): each ``decode`` of T new
+    latent frames returns exactly the samples that decoding the whole latent would give for
+    them; ``reset`` starts new utterances."""
+
+    def __init__(self, vae, B=1):
+        self.vae, self.ctx, self.B = vae, vae.ctx, B
+        h = C.c_void_p()
+        check(lib().vx_vae_stream_create(vae.h, B, C.byref(h)), self.ctx.h)
+        self.h = h
+        self.ctx._adopt(self)
+
+    def reset(self):
+        check(lib().vx_vae_stream_reset(self.h), self.ctx.h)
+
+    def decode(self, z):
+        """z [B, latent, T] (torch CUDA f32) -> wav [B, 1, T * prod(rates)]."""
+        import torch
+        b, _, t = z.shape
+        hop = int(np.prod(self.vae._rates))
+        out = torch.empty(b, 1, t * hop, device=z.device, dtype=torch.float32)
+        torch.cuda.synchronize()
+        check(lib().vx_vae_stream_decode(self.h, ptr(z.contiguous()), t, ptr(out)), self.ctx.h)
+        return out
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().vx_vae_stream_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -163,10 +163,13 @@ cudaError_t tc_gemm_configure();
 // conv (stride s, A = the phase-folded weight [vae_tc_rows(Cout, s), 2 Cin]) over it.
 cudaError_t vae_tc_configure();
 int vae_tc_rows(int cout, int s);
+// hist (streaming, transposed-conv inputs only): the previous chunk's last frame [B, C],
+// written as row 0 ahead of the chunk; the conv then reads with row_off = 1.
 cudaError_t launch_vae_split(const float* X, int B, int C, int T, const float* alpha, const float* sr_scale,
-                             const float* sr_bias, uint16_t* xs, cudaStream_t st);
+                             const float* sr_bias, uint16_t* xs, cudaStream_t st, const float* hist = nullptr);
 cudaError_t launch_vae_tc_conv(const uint16_t* xs, int B, int T_in, int Cin, int Cout, int s, const uint16_t* A,
-                               const float* bias, const float* R, float* Y, int* err, cudaStream_t st);
+                               const float* bias, const float* R, float* Y, int* err, cudaStream_t st,
+                               int row_off = 0);
 int lm_hidden_size(const vx_lm* lm);
 const float* lm_hid_norm(const vx_lm* lm);
 int lm_greedy_begin(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps);

@@ -40,18 +40,23 @@ constexpr int DW_TT = 1024;  // outputs per CTA
 __global__ void __launch_bounds__(256) dw_conv_kernel(const float* __restrict__ x, int C, int T,
                                                       const uint16_t* __restrict__ w, const float* __restrict__ bias,
                                                       int dil, const float* __restrict__ a_pre,
-                                                      const float* __restrict__ a_post, float* __restrict__ y) {
+                                                      const float* __restrict__ a_post, float* __restrict__ y,
+                                                      const float* __restrict__ hist) {
   __shared__ float xs[DW_TT + 6 * 9];
   const int c = blockIdx.y, b = blockIdx.z;
   const int t0 = blockIdx.x * DW_TT;
   const int halo = 6 * dil;
   const float* xr = x + ((size_t)b * C + c) * T;
+  const float* hr = hist ? hist + ((size_t)b * C + c) * halo : nullptr;  // the last `halo` inputs before x
   const float ap = a_pre ? a_pre[c] : 0.f;
   for (int i = threadIdx.x; i < DW_TT + halo; i += 256) {
     const int t = t0 - halo + i;
     float v = 0.f;  // causal left padding: zeros after the pre-snake (layers.rs:46-48)
     if (t >= 0 && t < T) {
       v = xr[t];
+      if (a_pre) v = snake(v, ap);
+    } else if (t < 0 && hr) {  // streaming: the previous chunk's inputs
+      v = hr[halo + t];
       if (a_pre) v = snake(v, ap);
     }
     xs[i] = v;
@@ -174,7 +179,8 @@ constexpr int LC_TT = 1024;
 // wav[b, t] = tanh(bias + sum_c sum_j w[c, j] * snake(h[b, c, t + j - 6], alpha[c]))
 __global__ void __launch_bounds__(256) last_conv_kernel(const float* __restrict__ h, int C, int T,
                                                         const float* __restrict__ alpha, const uint16_t* __restrict__ w,
-                                                        const float* __restrict__ bias, float* __restrict__ wav) {
+                                                        const float* __restrict__ bias, float* __restrict__ wav,
+                                                        const float* __restrict__ hist) {
   __shared__ float xs[LC_TT + 6];
   const int b = blockIdx.y, t0 = blockIdx.x * LC_TT;
   float acc[LC_TT / 256] = {};
@@ -182,9 +188,10 @@ __global__ void __launch_bounds__(256) last_conv_kernel(const float* __restrict_
     const float* hr = h + ((size_t)b * C + c) * T;
     const float al = alpha[c];
     __syncthreads();
+    const float* hh = hist ? hist + ((size_t)b * C + c) * 6 : nullptr;
     for (int i = threadIdx.x; i < LC_TT + 6; i += 256) {
       const int t = t0 - 6 + i;
-      xs[i] = (t >= 0 && t < T) ? snake(hr[t], al) : 0.f;
+      xs[i] = (t >= 0 && t < T) ? snake(hr[t], al) : (t < 0 && hh) ? snake(hh[6 + t], al) : 0.f;
     }
     __syncthreads();
     float wk[7];
@@ -201,6 +208,21 @@ __global__ void __launch_bounds__(256) last_conv_kernel(const float* __restrict_
   for (int q = 0; q < LC_TT / 256; ++q) {
     const int t = t0 + threadIdx.x + q * 256;
     if (t < T) wav[(size_t)b * T + t] = tanhf(acc[q] + bias[0]);
+  }
+}
+
+// Streaming state: hist[b, c, 0..H) <- the last H samples of [hist | x[b, c, 0..T)] (one
+// block per row; the old row is read before any of it is overwritten).
+__global__ void __launch_bounds__(64) hist_update_kernel(float* __restrict__ hist, const float* __restrict__ x,
+                                                         int T, int H) {
+  __shared__ float old[64];
+  const size_t row = blockIdx.x;
+  const int k = threadIdx.x;
+  if (k < H) old[k] = hist[row * H + k];
+  __syncthreads();
+  if (k < H) {
+    const int src = T - H + k;
+    hist[row * H + k] = src >= 0 ? x[row * T + src] : old[k + T];
   }
 }
 
@@ -285,12 +307,125 @@ cudaError_t launch_conv_gemm(const ConvGemmArgs& a, cudaStream_t st) {
 }
 
 cudaError_t launch_dw(const float* x, int B, int C, int T, const uint16_t* w, const float* bias, int dil,
-                      const float* a_pre, const float* a_post, float* y, cudaStream_t st) {
+                      const float* a_pre, const float* a_post, float* y, cudaStream_t st,
+                      const float* hist = nullptr) {
   if (dil < 1 || dil > 9) return cudaErrorInvalidValue;
   dim3 grid((T + DW_TT - 1) / DW_TT, C, B);
   count_launch();
-  dw_conv_kernel<<<grid, 256, 0, st>>>(x, C, T, w, bias, dil, a_pre, a_post, y);
+  dw_conv_kernel<<<grid, 256, 0, st>>>(x, C, T, w, bias, dil, a_pre, a_post, y, hist);
   return cudaGetLastError();
+}
+
+cudaError_t launch_hist_update(float* hist, const float* x, int rows, int T, int H, cudaStream_t st) {
+  if (H > 64) return cudaErrorInvalidValue;
+  count_launch();
+  hist_update_kernel<<<rows, 64, 0, st>>>(hist, x, T, H);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// Streaming decode state: the last inputs of every causal layer (vx_vae_stream_*).
+struct vx_vae_stream {
+  vx_vae* v = nullptr;
+  int B = 0;
+  bool started = false;  // false: the next chunk is an utterance's first (zero padding)
+  float* first = nullptr;                 // [B, latent, 6]: first depthwise conv input
+  float* up[8] = {};                      // [B, C_in]: each transposed conv's last input frame
+  float* unit[8][3] = {};                 // [B, C_out, 6 * dilation]: residual-unit depthwise inputs
+  float* last = nullptr;                  // [B, C_last, 6]: last conv input
+  std::vector<float*> allocs;
+  std::vector<size_t> alloc_bytes;
+};
+
+namespace {
+
+// AudioVae::decode (vae.rs:55-59) of z [B, latent, T].  With a stream state whose utterance
+// has started, every causal layer reads the previous chunk's inputs as its left context instead
+// of zero padding, and the state then takes this chunk's tail: chunk by chunk, the samples are
+// identical to decoding the whole latent at once (the decoder is causal).
+int vae_run(vx_vae* v, const float* z, int B, int T, float* wav, vx_vae_stream* sst) {
+  vx_ctx* ctx = v->ctx;
+  if (B <= 0 || T <= 0) return fail(ctx, VX_ERR_SHAPE, "vae_decode: empty input");
+  cudaSetDevice(ctx->device);
+  cudaStream_t st = ctx->stream;
+  const bool hist = sst && sst->started;
+  // largest activation: max over stages of C * T_stage
+  size_t elems = (size_t)std::max(v->latent, v->dim) * T;
+  size_t t = T;
+  for (int i = 0; i < v->nblocks; ++i) {
+    t *= v->rates[i];
+    elems = std::max(elems, (size_t)v->blocks[i].cout * t);
+  }
+  elems *= B;
+  int rc = vae_buffers(v, elems);
+  if (rc) return rc;
+  // the split operand of the tcgen05 convs: two bf16 planes of the largest conv input (one row
+  // of history ahead of a streamed chunk)
+  size_t xs_elems = (size_t)v->latent * T;
+  t = T;
+  for (int i = 0; i < v->nblocks; ++i) {
+    xs_elems = std::max(xs_elems, (size_t)v->blocks[i].cin * (t + 1));
+    t *= v->rates[i];
+    xs_elems = std::max(xs_elems, (size_t)v->blocks[i].cout * t);
+  }
+  const bool tc_first = v->tc && v->latent % 64 == 0;
+  if (v->tc && (rc = vae_split_buffer(v, 2 * xs_elems * B))) return rc;
+  float *h = v->buf0, *y = v->buf1, *tmp = v->buf2;
+  // first conv: depthwise k7 over the latent channels, then pointwise latent -> dim (decoder.rs:83-89)
+  VX_CUDA(ctx, launch_dw(z, B, v->latent, T, v->first_dw_w, v->first_dw_b, 1, nullptr, nullptr, y, st,
+                         hist ? sst->first : nullptr));
+  if (sst) VX_CUDA(ctx, launch_hist_update(sst->first, z, B * v->latent, T, 6, st));
+  if (tc_first) {
+    VX_CUDA(ctx, launch_vae_split(y, B, v->latent, T, nullptr, nullptr, nullptr, v->xs, st));
+    VX_CUDA(ctx, launch_vae_tc_conv(v->xs, B, T, v->latent, v->dim, 1, v->first_pw_w, v->first_pw_b, nullptr, h,
+                                    ctx->dev_err, st));
+  } else {
+    ConvGemmArgs f = {v->first_pw_w, v->first_pw_b, y, nullptr, h, B, v->dim, v->latent, v->latent, T, 1,
+                      nullptr, nullptr, nullptr};
+    VX_CUDA(ctx, launch_conv_gemm(f, st));
+  }
+  int tl = T;
+  for (int i = 0; i < v->nblocks; ++i) {
+    VaeBlock& bl = v->blocks[i];
+    // SR cond -> snake -> causal transposed conv (decoder.rs:158-162, 45-47)
+    if (v->tc) {
+      VX_CUDA(ctx, launch_vae_split(h, B, bl.cin, tl, bl.alpha, bl.sr_scale, bl.sr_bias, v->xs, st,
+                                    hist ? sst->up[i] : nullptr));
+      if (sst) VX_CUDA(ctx, launch_hist_update(sst->up[i], h, B * bl.cin, tl, 1, st));
+      VX_CUDA(ctx, launch_vae_tc_conv(v->xs, B, tl, bl.cin, bl.cout, bl.stride, bl.up_wt, bl.up_b, nullptr, tmp,
+                                      ctx->dev_err, st, hist ? 1 : 0));
+    } else {
+      ConvGemmArgs up = {bl.up_w, bl.up_b, h, nullptr, tmp, B, bl.cout, 2 * bl.cin, bl.cin, tl, bl.stride,
+                         bl.alpha, bl.sr_scale, bl.sr_bias};
+      VX_CUDA(ctx, launch_conv_gemm(up, st));
+    }
+    tl *= bl.stride;
+    std::swap(h, tmp);
+    const int dils[3] = {1, 3, 9};
+    for (int u = 0; u < 3; ++u) {
+      const VaeUnit& r = bl.res[u];
+      // CausalResidualUnit: x + conv1x1(snake(dwconv7_dil(snake(x))))  (layers.rs:150-156)
+      VX_CUDA(ctx, launch_dw(h, B, bl.cout, tl, r.w1, r.b1, dils[u], r.alpha1, r.alpha2, y, st,
+                             hist ? sst->unit[i][u] : nullptr));
+      if (sst) VX_CUDA(ctx, launch_hist_update(sst->unit[i][u], h, B * bl.cout, tl, 6 * dils[u], st));
+      if (v->tc) {
+        VX_CUDA(ctx, launch_vae_split(y, B, bl.cout, tl, nullptr, nullptr, nullptr, v->xs, st));
+        VX_CUDA(ctx, launch_vae_tc_conv(v->xs, B, tl, bl.cout, bl.cout, 1, r.w2, r.b2, h, h, ctx->dev_err, st));
+      } else {
+        ConvGemmArgs pw = {r.w2, r.b2, y, h, h, B, bl.cout, bl.cout, bl.cout, tl, 1, nullptr, nullptr, nullptr};
+        VX_CUDA(ctx, launch_conv_gemm(pw, st));
+      }
+    }
+  }
+  const int cl = v->dim >> v->nblocks;
+  dim3 grid((tl + LC_TT - 1) / LC_TT, B);
+  count_launch();
+  last_conv_kernel<<<grid, 256, 0, st>>>(h, cl, tl, v->alpha_out, v->last_w, v->last_b, wav,
+                                         hist ? sst->last : nullptr);
+  VX_CUDA(ctx, cudaGetLastError());
+  if (sst) VX_CUDA(ctx, launch_hist_update(sst->last, h, B * cl, tl, 6, st));
+  return VX_OK;
 }
 
 }  // namespace
@@ -452,77 +587,73 @@ int vx_vae_load_out(vx_vae* v, const float* alpha_out, const uint16_t* last_w, c
 
 int vx_vae_decode(vx_vae* v, const float* z, int B, int T, float* wav) {
   if (!v || !z || !wav) return VX_ERR_ARG;
+  const int rc = vae_run(v, z, B, T, wav, nullptr);
+  return rc ? rc : vx_ctx_synchronize(v->ctx);
+}
+
+int vx_vae_stream_create(vx_vae* v, int B, vx_vae_stream** out) {
+  if (!v || !out || B <= 0) return VX_ERR_ARG;
+  *out = nullptr;
   vx_ctx* ctx = v->ctx;
-  if (B <= 0 || T <= 0) return fail(ctx, VX_ERR_SHAPE, "vae_decode: empty input");
+  if (!v->tc || v->latent % 64)
+    return fail(ctx, VX_ERR_CONFIG, "streaming decode needs the tcgen05 convolutions (latent multiple of 64)");
   cudaSetDevice(ctx->device);
-  cudaStream_t st = ctx->stream;
-  // largest activation: max over stages of C * T_stage
-  size_t elems = (size_t)std::max(v->latent, v->dim) * T;
-  size_t t = T;
-  for (int i = 0; i < v->nblocks; ++i) {
-    t *= v->rates[i];
-    elems = std::max(elems, (size_t)v->blocks[i].cout * t);
-  }
-  elems *= B;
-  int rc = vae_buffers(v, elems);
-  if (rc) return rc;
-  // the split operand of the tcgen05 convs: two bf16 planes of the largest conv input
-  size_t xs_elems = (size_t)v->latent * T;
-  t = T;
-  for (int i = 0; i < v->nblocks; ++i) {
-    xs_elems = std::max(xs_elems, (size_t)v->blocks[i].cin * t);
-    t *= v->rates[i];
-    xs_elems = std::max(xs_elems, (size_t)v->blocks[i].cout * t);
-  }
-  const bool tc_first = v->tc && v->latent % 64 == 0;
-  if (v->tc && (rc = vae_split_buffer(v, 2 * xs_elems * B))) return rc;
-  float *h = v->buf0, *y = v->buf1, *tmp = v->buf2;
-  // first conv: depthwise k7 over the latent channels, then pointwise latent -> dim (decoder.rs:83-89)
-  VX_CUDA(ctx, launch_dw(z, B, v->latent, T, v->first_dw_w, v->first_dw_b, 1, nullptr, nullptr, y, st));
-  if (tc_first) {
-    VX_CUDA(ctx, launch_vae_split(y, B, v->latent, T, nullptr, nullptr, nullptr, v->xs, st));
-    VX_CUDA(ctx, launch_vae_tc_conv(v->xs, B, T, v->latent, v->dim, 1, v->first_pw_w, v->first_pw_b, nullptr, h,
-                                    ctx->dev_err, st));
-  } else {
-    ConvGemmArgs f = {v->first_pw_w, v->first_pw_b, y, nullptr, h, B, v->dim, v->latent, v->latent, T, 1,
-                      nullptr, nullptr, nullptr};
-    VX_CUDA(ctx, launch_conv_gemm(f, st));
-  }
-  int tl = T;
-  for (int i = 0; i < v->nblocks; ++i) {
-    VaeBlock& bl = v->blocks[i];
-    // SR cond -> snake -> causal transposed conv (decoder.rs:158-162, 45-47)
-    if (v->tc) {
-      VX_CUDA(ctx, launch_vae_split(h, B, bl.cin, tl, bl.alpha, bl.sr_scale, bl.sr_bias, v->xs, st));
-      VX_CUDA(ctx, launch_vae_tc_conv(v->xs, B, tl, bl.cin, bl.cout, bl.stride, bl.up_wt, bl.up_b, nullptr, tmp,
-                                      ctx->dev_err, st));
-    } else {
-      ConvGemmArgs up = {bl.up_w, bl.up_b, h, nullptr, tmp, B, bl.cout, 2 * bl.cin, bl.cin, tl, bl.stride,
-                         bl.alpha, bl.sr_scale, bl.sr_bias};
-      VX_CUDA(ctx, launch_conv_gemm(up, st));
+  vx_vae_stream* s = new vx_vae_stream();
+  s->v = v;
+  s->B = B;
+  auto alloc = [&](size_t n) {
+    float* p = nullptr;
+    if (cudaMalloc(&p, n * 4) != cudaSuccess) {
+      cudaGetLastError();
+      return (float*)nullptr;
     }
-    tl *= bl.stride;
-    std::swap(h, tmp);
-    const int dils[3] = {1, 3, 9};
-    for (int u = 0; u < 3; ++u) {
-      const VaeUnit& r = bl.res[u];
-      // CausalResidualUnit: x + conv1x1(snake(dwconv7_dil(snake(x))))  (layers.rs:150-156)
-      VX_CUDA(ctx, launch_dw(h, B, bl.cout, tl, r.w1, r.b1, dils[u], r.alpha1, r.alpha2, y, st));
-      if (v->tc) {
-        VX_CUDA(ctx, launch_vae_split(y, B, bl.cout, tl, nullptr, nullptr, nullptr, v->xs, st));
-        VX_CUDA(ctx, launch_vae_tc_conv(v->xs, B, tl, bl.cout, bl.cout, 1, r.w2, r.b2, h, h, ctx->dev_err, st));
-      } else {
-        ConvGemmArgs pw = {r.w2, r.b2, y, h, h, B, bl.cout, bl.cout, bl.cout, tl, 1, nullptr, nullptr, nullptr};
-        VX_CUDA(ctx, launch_conv_gemm(pw, st));
-      }
-    }
+    s->allocs.push_back(p);
+    s->alloc_bytes.push_back(n * 4);
+    return p;
+  };
+  const int dils[3] = {1, 3, 9};
+  bool ok = (s->first = alloc((size_t)B * v->latent * 6)) != nullptr;
+  for (int i = 0; ok && i < v->nblocks; ++i) {
+    const VaeBlock& bl = v->blocks[i];
+    ok = (s->up[i] = alloc((size_t)B * bl.cin)) != nullptr;
+    for (int u = 0; ok && u < 3; ++u) ok = (s->unit[i][u] = alloc((size_t)B * bl.cout * 6 * dils[u])) != nullptr;
   }
-  const int cl = v->dim >> v->nblocks;
-  dim3 grid((tl + LC_TT - 1) / LC_TT, B);
-  count_launch();
-  last_conv_kernel<<<grid, 256, 0, st>>>(h, cl, tl, v->alpha_out, v->last_w, v->last_b, wav);
-  VX_CUDA(ctx, cudaGetLastError());
+  ok = ok && (s->last = alloc((size_t)B * (v->dim >> v->nblocks) * 6)) != nullptr;
+  if (!ok) {
+    vx_vae_stream_destroy(s);
+    return fail(ctx, VX_ERR_OOM, "VAE stream state allocation failed");
+  }
+  *out = s;
+  return vx_vae_stream_reset(s);
+}
+
+void vx_vae_stream_destroy(vx_vae_stream* s) {
+  if (!s) return;
+  cudaSetDevice(s->v->ctx->device);
+  cudaStreamSynchronize(s->v->ctx->stream);
+  for (float* p : s->allocs) cudaFree(p);
+  delete s;
+}
+
+int vx_vae_stream_reset(vx_vae_stream* s) {
+  if (!s) return VX_ERR_ARG;
+  // the next chunk starts an utterance: histories of zeros are the causal zero padding (the
+  // depthwise and last convs apply Snake1d to them, and snake(0) = 0); the transposed convs,
+  // whose input transform does not map 0 to 0, read no history until a chunk has run
+  s->started = false;
+  vx_ctx* ctx = s->v->ctx;
+  cudaSetDevice(ctx->device);
+  for (size_t i = 0; i < s->allocs.size(); ++i)
+    VX_CUDA(ctx, cudaMemsetAsync(s->allocs[i], 0, s->alloc_bytes[i], ctx->stream));
   return vx_ctx_synchronize(ctx);
+}
+
+int vx_vae_stream_decode(vx_vae_stream* s, const float* z, int T, float* wav) {
+  if (!s || !z || !wav) return VX_ERR_ARG;
+  const int rc = vae_run(s->v, z, s->B, T, wav, s);
+  if (rc) return rc;
+  s->started = true;
+  return vx_ctx_synchronize(s->v->ctx);
 }
 
 }  // extern "C"

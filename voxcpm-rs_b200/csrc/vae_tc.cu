@@ -44,6 +44,7 @@ constexpr int VT_STAGE = VT_A_BYTES + 2 * VT_B_BYTES;
 
 struct VaeTcArgs {
   int B, T_in, Cin, Cout, s, taps, cpt, kchunks, nstages;
+  int row_off;        // rows of history ahead of the chunk in the activation operand (0 or 1)
   const float* bias;  // [Cout]
   const float* R;     // residual [B, Cout, T_out] or null (may alias Y)
   float* Y;           // [B, Cout, T_out]
@@ -57,23 +58,27 @@ __device__ __forceinline__ float snake_f(float x, float alpha) {
   return x + inv * (s * s);
 }
 
-// X [B, C, T] f32 -> xs [2][B][T][C] bf16 (plane 0: hi, plane 1: lo), after the optional
-// SR conditioning (x * scale[c] + bias[c], layers.rs:213-220) and Snake1d (alpha[c]).
-// Tile of 64 channels x 32 time samples per block, transposed through shared memory.
+// X [B, C, T] f32 -> xs [2][B][lead + T][C] bf16 (plane 0: hi, plane 1: lo), after the
+// optional SR conditioning (x * scale[c] + bias[c], layers.rs:213-220) and Snake1d (alpha[c]).
+// lead = 1 puts the previous chunk's last input frame hist[B, C] in row 0 (streaming decode:
+// the transposed conv's j - 1 tap of the chunk's first frame).  Tile of 64 channels x 32
+// rows per block, transposed through shared memory.
 __global__ void __launch_bounds__(256) vae_split_kernel(const float* __restrict__ X, int B, int C, int T,
                                                         const float* __restrict__ alpha,
                                                         const float* __restrict__ sc, const float* __restrict__ sb,
-                                                        uint16_t* __restrict__ xs) {
+                                                        uint16_t* __restrict__ xs, const float* __restrict__ hist,
+                                                        int lead) {
   __shared__ float tile[64][33];
   const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 64, b = blockIdx.z;
   const int tid = threadIdx.x;
+  const int rows = T + lead;
   {
     const int tt = tid & 31, cr = tid >> 5;  // 8 channel rows per pass
     for (int c = cr; c < 64; c += 8) {
       const int ch = c0 + c, t = t0 + tt;
       float v = 0.f;
-      if (ch < C && t < T) {
-        v = X[((size_t)b * C + ch) * T + t];
+      if (ch < C && t < rows) {
+        v = t < lead ? hist[(size_t)b * C + ch] : X[((size_t)b * C + ch) * T + t - lead];
         if (sc) v = v * sc[ch] + sb[ch];
         if (alpha) v = snake_f(v, alpha[ch]);
       }
@@ -85,16 +90,16 @@ __global__ void __launch_bounds__(256) vae_split_kernel(const float* __restrict_
   const int cp = tid & 31, tr = tid >> 5;
   for (int t = tr; t < 32; t += 8) {
     const int tg = t0 + t, ch = c0 + 2 * cp;
-    if (tg >= T || ch >= C) continue;
+    if (tg >= rows || ch >= C) continue;
     const float v0 = tile[2 * cp][t], v1 = tile[2 * cp + 1][t];
     const __nv_bfloat16 h0 = __float2bfloat16_rn(v0), h1 = __float2bfloat16_rn(v1);
     const __nv_bfloat16 l0 = __float2bfloat16_rn(v0 - __bfloat162float(h0));
     const __nv_bfloat16 l1 = __float2bfloat16_rn(v1 - __bfloat162float(h1));
-    const size_t row = ((size_t)b * T + tg) * C + ch;
+    const size_t row = ((size_t)b * rows + tg) * C + ch;
     const uint32_t hw = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
     const uint32_t lw = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
     *reinterpret_cast<uint32_t*>(xs + row) = hw;
-    *reinterpret_cast<uint32_t*>(xs + (size_t)B * T * C + row) = lw;
+    *reinterpret_cast<uint32_t*>(xs + (size_t)B * rows * C + row) = lw;
   }
 }
 
@@ -150,8 +155,8 @@ __global__ void __launch_bounds__(VT_THREADS, 1)
       unsigned char* st = base + s * VT_STAGE;
       mbar_arrive_expect_tx(&full[s], VT_STAGE);
       tma_load_2d(st, &tmA, tap * a.Cin + kc * TC_BK, mt * TC_BM, &full[s]);
-      tma_load_3d(st + VT_A_BYTES, &tmX, kc * TC_BK, j0 - tap, b, &full[s]);
-      tma_load_3d(st + VT_A_BYTES + VT_B_BYTES, &tmX, kc * TC_BK, j0 - tap, a.B + b, &full[s]);
+      tma_load_3d(st + VT_A_BYTES, &tmX, kc * TC_BK, j0 + a.row_off - tap, b, &full[s]);
+      tma_load_3d(st + VT_A_BYTES + VT_B_BYTES, &tmX, kc * TC_BK, j0 + a.row_off - tap, a.B + b, &full[s]);
       issued = it + 1;
     }
     if (aborted || *reinterpret_cast<volatile int*>(&flags[0])) {
@@ -247,23 +252,26 @@ int vae_tc_rows(int cout, int s) {
 }
 
 cudaError_t launch_vae_split(const float* X, int B, int C, int T, const float* alpha, const float* sr_scale,
-                             const float* sr_bias, uint16_t* xs, cudaStream_t st) {
+                             const float* sr_bias, uint16_t* xs, cudaStream_t st, const float* hist) {
   if (C % 2) return cudaErrorInvalidValue;
-  dim3 grid((T + 31) / 32, (C + 63) / 64, B);
+  const int lead = hist ? 1 : 0;
+  dim3 grid((T + lead + 31) / 32, (C + 63) / 64, B);
   count_launch();
-  vae_split_kernel<<<grid, 256, 0, st>>>(X, B, C, T, alpha, sr_scale, sr_bias, xs);
+  vae_split_kernel<<<grid, 256, 0, st>>>(X, B, C, T, alpha, sr_scale, sr_bias, xs, hist, lead);
   return cudaGetLastError();
 }
 
 cudaError_t launch_vae_tc_conv(const uint16_t* xs, int B, int T_in, int Cin, int Cout, int s, const uint16_t* A,
-                               const float* bias, const float* R, float* Y, int* err, cudaStream_t st) {
-  if (Cin % TC_BK || s < 1 || s > TC_BM || T_in <= 0 || B <= 0) return cudaErrorInvalidValue;
+                               const float* bias, const float* R, float* Y, int* err, cudaStream_t st,
+                               int row_off) {
+  if (Cin % TC_BK || s < 1 || s > TC_BM || T_in <= 0 || B <= 0 || row_off < 0 || row_off > 1)
+    return cudaErrorInvalidValue;
   const int taps = s > 1 ? 2 : 1, cpt = TC_BM / s;
   const int a_rows = s > 1 ? vae_tc_rows(Cout, s) : Cout;
   CUtensorMap tmA, tmX;
   cudaError_t e;
   if ((e = tc_map_2d(&tmA, A, a_rows, taps * Cin, TC_BM)) != cudaSuccess) return e;
-  if ((e = tc_map_3d(&tmX, xs, 2 * B, T_in, Cin, VT_N)) != cudaSuccess) return e;
+  if ((e = tc_map_3d(&tmX, xs, 2 * B, T_in + row_off, Cin, VT_N)) != cudaSuccess) return e;
   VaeTcArgs a = {};
   a.B = B;
   a.T_in = T_in;
@@ -274,6 +282,7 @@ cudaError_t launch_vae_tc_conv(const uint16_t* xs, int B, int T_in, int Cin, int
   a.cpt = cpt;
   a.kchunks = Cin / TC_BK;
   a.nstages = std::max(1, std::min(4, taps * a.kchunks));
+  a.row_off = row_off;
   a.bias = bias;
   a.R = R;
   a.Y = Y;

@@ -138,6 +138,11 @@ struct vx_voxcpm2 {
   float *enc_seq = nullptr, *enc_out = nullptr;  // [rows, He] LocEnc rows
   size_t enc_rows = 0;
   cudaEvent_t ev[2] = {nullptr, nullptr};
+  // the generation in progress (vx_voxcpm2_begin / advance): next patch index, the CFM's
+  // current condition buffer, the options, and whether the loop has ended
+  int s_i = 0, s_cur = 0, s_min_len = 0, s_max_len = 0, s_steps = 0;
+  float s_cfg = 0.f;
+  bool s_finished = true, s_active = false;
   // prefill buffers (grown to S rows)
   int pf_cap = 0;
   int* pf_ids = nullptr;
@@ -476,18 +481,17 @@ int vx_locenc_forward(vx_voxcpm2* m, const float* feat, int N, float* out) {
   return vx_ctx_synchronize(ctx);
 }
 
-int vx_voxcpm2_inference(vx_voxcpm2* m, const int32_t* text_token, const float* text_mask, const float* feat,
-                         const float* feat_mask, int S, int min_len, int max_len, int inference_timesteps,
-                         float cfg_value, const float* noise, float* latent_out, int* n_patches,
-                         float* stop_logits_out) {
-  if (!m || !text_token || !text_mask || !feat || !feat_mask || !noise || !latent_out || !n_patches) return VX_ERR_ARG;
+int vx_voxcpm2_begin(vx_voxcpm2* m, const int32_t* text_token, const float* text_mask, const float* feat,
+                     const float* feat_mask, int S, int min_len, int max_len, int inference_timesteps,
+                     float cfg_value, const float* noise) {
+  if (!m || !text_token || !text_mask || !feat || !feat_mask || !noise) return VX_ERR_ARG;
   vx_ctx* ctx = m->ctx;
-  *n_patches = 0;
+  m->s_active = false;
   if (S <= 0 || max_len <= 0 || max_len > m->max_len || min_len < 0 || inference_timesteps < 1)
-    return fail(ctx, VX_ERR_SHAPE, "voxcpm2_inference: S=%d, max_len=%d (<= %d), steps=%d", S, max_len, m->max_len,
+    return fail(ctx, VX_ERR_SHAPE, "voxcpm2: S=%d, max_len=%d (<= %d), steps=%d", S, max_len, m->max_len,
                 inference_timesteps);
   if (S + max_len > lm_max_length(m->base) || S + max_len > lm_max_length(m->res))
-    return fail(ctx, VX_ERR_KV_FULL, "voxcpm2_inference: %d positions + %d steps exceed the KV cache", S, max_len);
+    return fail(ctx, VX_ERR_KV_FULL, "voxcpm2: %d positions + %d steps exceed the KV cache", S, max_len);
   cudaSetDevice(ctx->device);
   cudaStream_t st = ctx->stream;
   const size_t DP = (size_t)m->D * m->P;
@@ -502,43 +506,120 @@ int vx_voxcpm2_inference(vx_voxcpm2* m, const int32_t* text_token, const float* 
   }
   VX_CUDA(ctx, cudaMemcpyAsync(m->noise, noise, DP * max_len * 4, cudaMemcpyDefault, st));
   VX_CUDA(ctx, cudaMemcpyAsync(m->patch[0], last.data(), DP * 4, cudaMemcpyHostToDevice, st));
-  int rc = prefill(m, text_token, text_mask, feat_mask, feat, S);
-  if (rc) return rc;
-  // the loop (model.rs:318-347): dit_step(i); stop if i > min_len and the head fires; else
-  // lm_step.  The flag of step i is read after step i + 1 is queued.
-  int n = max_len, cur = 0;
-  for (int i = 0; i < max_len; ++i) {
-    if (ctx->cancel.load(std::memory_order_relaxed)) {  // model.rs:323-328
-      cudaStreamSynchronize(st);
-      return fail(ctx, VX_ERR_CANCELLED, "generation cancelled");
-    }
-    rc = dit_step(m, i, cur, inference_timesteps, cfg_value);
-    if (rc) break;
-    if (i > 0) {
-      VX_CUDA(ctx, cudaEventSynchronize(m->ev[(i - 1) & 1]));
-      if (i - 1 > min_len && m->h_flags[i - 1]) {
-        n = i;  // step i - 1 stopped: its patch is the last one; step i's work is discarded
-        break;
-      }
-    }
-    if (i == max_len - 1) break;
-    rc = lm_step(m, cur ^ 1);
-    if (rc) break;
-    cur ^= 1;
-  }
+  const int rc = prefill(m, text_token, text_mask, feat_mask, feat, S);
   if (rc) {
     cudaStreamSynchronize(st);
     return rc;
   }
-  if (n == max_len) {  // the last step's own stop flag cannot shorten the output further
-    VX_CUDA(ctx, cudaEventSynchronize(m->ev[(max_len - 1) & 1]));
+  m->s_i = 0;
+  m->s_cur = 0;
+  m->s_min_len = min_len;
+  m->s_max_len = max_len;
+  m->s_steps = inference_timesteps;
+  m->s_cfg = cfg_value;
+  m->s_finished = false;
+  m->s_active = true;
+  return VX_OK;
+}
+
+// Up to `budget` more AR steps of the loop of model.rs:318-347: dit_step(i); stop if
+// i > min_len and the head fires; else lm_step.  Inside a call, the flag of step i is read
+// after step i + 1 is queued (step i + 1's work is discarded if step i stopped); the last step
+// of a call reads its own flag before deciding on its lm_step.  Returns the patches produced
+// through *n_new; they start at patch index *first.
+static int advance(vx_voxcpm2* m, int budget, int* first, int* n_new) {
+  vx_ctx* ctx = m->ctx;
+  cudaStream_t st = ctx->stream;
+  *first = m->s_i;
+  *n_new = 0;
+  int rc = VX_OK;
+  for (int j = 0; j < budget && !m->s_finished; ++j) {
+    const int i = m->s_i;
+    if (i >= m->s_max_len) {
+      m->s_finished = true;
+      break;
+    }
+    if (ctx->cancel.load(std::memory_order_relaxed)) {  // model.rs:323-328
+      cudaStreamSynchronize(st);
+      m->s_active = false;
+      return fail(ctx, VX_ERR_CANCELLED, "generation cancelled");
+    }
+    rc = dit_step(m, i, m->s_cur, m->s_steps, m->s_cfg);
+    if (rc) break;
+    if (j > 0) {
+      VX_CUDA(ctx, cudaEventSynchronize(m->ev[(i - 1) & 1]));
+      if (i - 1 > m->s_min_len && m->h_flags[i - 1]) {
+        m->s_finished = true;  // step i - 1 was the last; step i is discarded
+        break;
+      }
+    }
+    m->s_i = i + 1;
+    *n_new += 1;
+    if (i == m->s_max_len - 1) {
+      m->s_finished = true;
+      break;
+    }
+    if (j == budget - 1) {  // the call's last step: decide its lm_step on its own flag
+      VX_CUDA(ctx, cudaEventSynchronize(m->ev[i & 1]));
+      if (i > m->s_min_len && m->h_flags[i]) {
+        m->s_finished = true;
+        break;
+      }
+    }
+    rc = lm_step(m, m->s_cur ^ 1);
+    if (rc) break;
+    m->s_cur ^= 1;
   }
+  if (rc) {
+    cudaStreamSynchronize(st);
+    m->s_active = false;
+    return rc;
+  }
+  // a step past the stopping one was queued and discarded: it is not part of the output
+  if (m->s_finished && *first + *n_new > 0) {
+    const int lastp = *first + *n_new - 1;
+    VX_CUDA(ctx, cudaEventSynchronize(m->ev[lastp & 1]));
+  }
+  return VX_OK;
+}
+
+int vx_voxcpm2_advance(vx_voxcpm2* m, int max_patches, float* latent_out, int* n_new, int* finished) {
+  if (!m || !latent_out || !n_new || !finished || max_patches <= 0) return VX_ERR_ARG;
+  *n_new = 0;
+  *finished = 1;
+  if (!m->s_active) return fail(m->ctx, VX_ERR_ARG, "voxcpm2_advance: no generation begun");
+  int first = 0, n = 0;
+  const int rc = advance(m, max_patches, &first, &n);
+  if (rc) return rc;
+  const size_t frames = (size_t)n * m->P;
+  if (n > 0)
+    VX_CUDA(m->ctx, cudaMemcpy2DAsync(latent_out, frames * 4, m->latent + (size_t)first * m->P,
+                                      (size_t)m->max_len * m->P * 4, frames * 4, m->D, cudaMemcpyDefault,
+                                      m->ctx->stream));
+  *n_new = n;
+  *finished = m->s_finished ? 1 : 0;
+  return vx_ctx_synchronize(m->ctx);
+}
+
+int vx_voxcpm2_inference(vx_voxcpm2* m, const int32_t* text_token, const float* text_mask, const float* feat,
+                         const float* feat_mask, int S, int min_len, int max_len, int inference_timesteps,
+                         float cfg_value, const float* noise, float* latent_out, int* n_patches,
+                         float* stop_logits_out) {
+  if (!m || !latent_out || !n_patches) return VX_ERR_ARG;
+  *n_patches = 0;
+  int rc = vx_voxcpm2_begin(m, text_token, text_mask, feat, feat_mask, S, min_len, max_len, inference_timesteps,
+                            cfg_value, noise);
+  if (rc) return rc;
+  int first = 0, n = 0;
+  rc = advance(m, max_len, &first, &n);
+  if (rc) return rc;
+  vx_ctx* ctx = m->ctx;
   *n_patches = n;
   const size_t frames = (size_t)n * m->P;
   VX_CUDA(ctx, cudaMemcpy2DAsync(latent_out, frames * 4, m->latent, (size_t)m->max_len * m->P * 4, frames * 4, m->D,
-                                 cudaMemcpyDefault, st));
+                                 cudaMemcpyDefault, ctx->stream));
   if (stop_logits_out)
-    VX_CUDA(ctx, cudaMemcpyAsync(stop_logits_out, m->stop_logits, (size_t)n * 2 * 4, cudaMemcpyDefault, st));
+    VX_CUDA(ctx, cudaMemcpyAsync(stop_logits_out, m->stop_logits, (size_t)n * 2 * 4, cudaMemcpyDefault, ctx->stream));
   return vx_ctx_synchronize(ctx);
 }
 

@@ -184,6 +184,35 @@ class VoxCpm2Model:
               self.ctx.h)
         return wav[:n.value]
 
+    def generate_stream(self, vae, text_token, text_mask, feat, feat_mask, min_len, max_len, inference_timesteps,
+                        cfg_value, noise, chunk_patches=5):
+        """``VoxCPM::generate_stream`` (``wrapper.rs:456-492, 680-724``): yields mono audio
+        chunks as AR steps complete, ``chunk_patches`` patches at a time; each chunk is decoded
+        by a stateful AudioVAE stream (only the new frames), so the concatenated chunks equal
+        ``generate``'s waveform."""
+        import torch
+        from .audiovae import AudioVaeStream
+        ids = np.ascontiguousarray(text_token, np.int32)
+        noise = np.ascontiguousarray(noise, np.float32)
+        check(lib().vx_voxcpm2_begin(self.h, ptr(ids), ptr(np.ascontiguousarray(text_mask, np.float32)),
+                                     ptr(np.ascontiguousarray(feat, np.float32)),
+                                     ptr(np.ascontiguousarray(feat_mask, np.float32)), len(ids), min_len, max_len,
+                                     inference_timesteps, cfg_value, ptr(noise)), self.ctx.h)
+        D, P = self.cfg.feat_dim, self.cfg.patch_size
+        stream = AudioVaeStream(vae, 1)
+        try:
+            lat = torch.empty(D * chunk_patches * P, device=f"cuda:{self.ctx.device}")
+            n, fin = C.c_int(), C.c_int(0)
+            while not fin.value:
+                torch.cuda.synchronize()
+                check(lib().vx_voxcpm2_advance(self.h, chunk_patches, ptr(lat), C.byref(n), C.byref(fin)),
+                      self.ctx.h)
+                if n.value:
+                    z = lat[:D * n.value * P].reshape(1, D, n.value * P)
+                    yield stream.decode(z).reshape(-1).cpu().numpy()
+        finally:
+            stream.close()
+
     def close(self):
         if getattr(self, "h", None):
             lib().vx_voxcpm2_destroy(self.h)
