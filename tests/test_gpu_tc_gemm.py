@@ -13,7 +13,9 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("m,n,k,bias", [(2, 1024, 64, True), (3, 128, 128, False), (16, 1024, 1024, True),
                                         (22, 1280, 1024, False), (22, 8192, 1024, False), (22, 1024, 4096, True),
-                                        (64, 2560, 2048, False), (100, 2048, 6144, False), (128, 12288, 2048, True)])
+                                        (64, 2560, 2048, False), (100, 2048, 6144, False), (128, 12288, 2048, True),
+                                        (129, 1024, 1024, False), (176, 1280, 1024, True), (176, 1024, 4096, False),
+                                        (256, 2048, 2048, True), (300, 1024, 1024, False)])
 def test_tc_linear(ctx, m, n, k, bias):
     import torch
     from voxcpm_rs_b200 import synth
