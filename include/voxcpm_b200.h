@@ -240,6 +240,11 @@ int vx_dit_load(vx_dit* dit, const uint16_t* in_w, const float* in_b, const uint
                 const uint16_t* out_w, const float* out_b, const uint16_t* t1_w, const float* t1_b,
                 const uint16_t* t2_w, const float* t2_b, const uint16_t* dt1_w, const float* dt1_b,
                 const uint16_t* dt2_w, const float* dt2_b);
+/* Profiling: with VX_DIT_TRACE=1 set when the DiT first runs, the persistent decoder forward
+ * records %globaltimer on every CTA of its last launch at each of its phases (8 per layer + 1):
+ * [phase][CTA][4] = phase start, first segment's MMAs done (GEMM phases), CTA's work done, 0.
+ * Copies phases * grid * 4 values into out (n entries at least). */
+int vx_dit_trace(vx_dit* dit, unsigned long long* out, int n, int* grid, int* phases);
 /* Decoder layer / final norm weights (as vx_lm_load_layer / vx_lm_load_norm). */
 int vx_dit_load_layer(vx_dit* dit, int layer, const uint16_t* q, const uint16_t* k, const uint16_t* v,
                       const uint16_t* o, const uint16_t* gate, const uint16_t* up, const uint16_t* down,

@@ -115,3 +115,56 @@ def test_dit_forward_producer_split_is_exact(full_dit):
         dit.close()
         c.close()
     assert np.array_equal(outs[0], outs[1]), np.abs(outs[0] - outs[1]).max()
+
+
+def _dit_with_env(ctx, dcfg, w, persist):
+    """A DiT whose decoder forward policy is fixed by VX_DIT_PERSIST (read at creation)."""
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    old_env = os.environ.get("VX_DIT_PERSIST")
+    os.environ["VX_DIT_PERSIST"] = persist
+    try:
+        return VoxCpmLocDiTV2(ctx, dcfg, w)
+    finally:
+        if old_env is None:
+            del os.environ["VX_DIT_PERSIST"]
+        else:
+            os.environ["VX_DIT_PERSIST"] = old_env
+
+
+@pytest.mark.parametrize("persist", ["1", "0"])
+def test_dit_forward_full_both_paths(ctx, full_dit, persist):
+    """The full-width LocDiT forward through the persistent one-launch decoder (forced at two
+    sequences) and through the per-kernel decoder, each against the oracle."""
+    dcfg, w, fw = full_dit
+    rng = np.random.default_rng(23)
+    x = rng.standard_normal((2, 64, 4), dtype=np.float32)
+    mu = rng.standard_normal((2, 2048), dtype=np.float32)
+    cond = rng.standard_normal((2, 64, 4), dtype=np.float32)
+    t = np.array([0.6, 0.2], np.float32)
+    dt = np.array([0.0, 0.3], np.float32)
+    want = old.dit_forward(dcfg, fw, x, mu, t, cond, dt)
+    dit = _dit_with_env(ctx, dcfg, w, persist)
+    got = dit.forward(_t(x), _t(mu), t, _t(cond), dt).cpu().numpy()
+    assert_close(got, want, **TOL, what=f"dit forward (VX_DIT_PERSIST={persist})")
+    dit.close()
+
+
+def test_cfm_solve_batch8(ctx, full_dit):
+    """The CFM solve for 8 patches at once (16 CFG sequences, 176 decoder rows: the persistent
+    decoder by default) against the oracle, and bit-identical when run twice (the split-K
+    partials are summed in a fixed order)."""
+    dcfg, w, fw = full_dit
+    rng = np.random.default_rng(24)
+    B = 8
+    mu = rng.standard_normal((B, 2048), dtype=np.float32)
+    cond = (0.5 * rng.standard_normal((B, 64, 4))).astype(np.float32)
+    z = rng.standard_normal((B, 64, 4), dtype=np.float32)
+    want = old.cfm_forward(dcfg, fw, mu, 10, cond, z, 2.0, 1.0, True)
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    dit = VoxCpmLocDiTV2(ctx, dcfg, w)
+    got = dit.cfm_forward(_t(mu), 10, _t(cond), _t(z), 2.0, 1.0, True).cpu().numpy()
+    again = dit.cfm_forward(_t(mu), 10, _t(cond), _t(z), 2.0, 1.0, True).cpu().numpy()
+    assert_close(got, want, **TOL, what="cfm solve B=8")
+    assert np.abs(got - want).max() < 2e-3
+    assert np.array_equal(got, again)
+    dit.close()

@@ -1,0 +1,791 @@
+// Persistent forward of a non-causal MiniCPM-4 stack over a few token rows on the tensor cores
+// (sm_100a): the LocDiT decoder of every CFM Euler step (reference MiniCpmModel::forward with
+// is_causal = false, src/minicpm4/model.rs:43-62, as VoxCpmLocDiTV2::forward_cached runs it,
+// src/locdit/local_dit.rs:138-159).  One cooperative launch runs all layers; per layer
+//
+//   RES_A   x = x1 + s * down (layer 0: the input rows); x_n = RMSNorm(x)   -> split operand
+//   QKV     qkv = W_qkv x_n                                                  (tcgen05 GEMM)
+//   ATT     LongRoPE on q, k; softmax(q k^T / sqrt(d)) v per sequence and
+//           KV head (GQA, no mask)                                           -> split operand
+//   O       o = W_o attn                                                     (tcgen05 GEMM)
+//   RES_B   x1 = x + s * o; x1_n = RMSNorm(x1)                               -> split operand
+//   GU      [g | u] = W_gu x1_n                                              (tcgen05 GEMM)
+//   ACT     a = silu(g) * u                                                  -> split operand
+//   DOWN    down = W_d a                                                     (tcgen05 GEMM)
+//
+// and a final phase writes RMSNorm(x1 + s * down) (layer.rs:57-73, mlp.rs:28-34,
+// attention.rs:55-88, mod.rs:54-68).  Phases are separated by a grid barrier (release /
+// acquire counters; all CTAs are resident).
+//
+// GEMM phases: the weights are the A operand (128-row tiles x 64-element K chunks, TMA,
+// SWIZZLE_128B, no multicast); the activations are the B operand: the row phase before wrote
+// them as two bf16 planes x = hi + lo ([2][Rpad][K], token-major), so each K chunk is two MMAs
+// (hi, lo) into one f32 TMEM accumulator of Rpad columns.  A phase's (tile, K chunk) pairs are
+// dealt to its CTAs in contiguous runs, so a tile's K range may be split over CTAs: each run
+// inside one tile (a segment) stores its f32 partial tile into its own slot of the partial
+// buffer with plain stores, and the phase that consumes the GEMM sums a tile's slots in slot
+// order.  No atomics: the sum, and so the forward, does not depend on the order in which CTAs
+// finish (deterministic).  Warp 4 issues the TMA loads, warp 5 the MMAs, warps 0-3 read TMEM;
+// the row phases run on warps 0-7 (RES) or all twelve warps (attention, SiLU*up): their partial
+// sums are L2 reads, whose rate grows with the loads in flight per SM.  Weight tiles of the next
+// GEMM phase stream into the ring during the row phase before it.  Every wait is bounded; a
+// timeout records an error and the CTA stops cleanly.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cfloat>
+
+#include "common.cuh"
+#include "runtime.cuh"
+#include "dit_persist.cuh"
+#include "tc_common.cuh"
+
+namespace vx {
+
+namespace {
+
+constexpr int DP_WARPS = 12;
+constexpr int DP_THREADS = DP_WARPS * 32;
+constexpr int DP_EPI_THREADS = 128;  // warps 0-3: GEMM epilogue (TMEM lanes 0-127)
+constexpr int DP_RES_THREADS = 256;  // warps 0-7: RES rows, one float4 group of a row each (H <= 1024)
+constexpr int DP_A_BYTES = TC_BM * TC_BK * 2;
+constexpr int DP_SMAX = 16;          // tokens per sequence
+constexpr int DP_QS = 68;            // shared-memory row stride of q, k, v (floats; float4 aligned)
+constexpr int DP_SEGTAB_MAX = 2048;  // ints of segment tables held in shared memory
+constexpr int DP_HPU = 2;            // most query heads per attention unit
+constexpr int DP_ATT_FLOATS = (DP_HPU + 2) * DP_SMAX * DP_QS + DP_HPU * (DP_SMAX * DP_SMAX + DP_SMAX);
+enum { PH_RES_A, PH_QKV, PH_ATT, PH_O, PH_RES_B, PH_GU, PH_ACT, PH_DOWN, PH_N };
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+struct Sm {
+  unsigned char* stages;  // [nst][A 16 KB | B hi Rpad*128 | B lo Rpad*128]
+  float* att;             // attention scratch: q, k, v [16][DP_QS], scores [16][16], 1/sum [16]
+  float* red;             // [32] block reductions
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* seg_done;
+  uint64_t* acc_free;
+  uint64_t* fin;          // the MMA thread's last commit before TMEM is freed
+  uint32_t* tmem_slot;
+  volatile int* flags;    // [0] abort
+  int* segtab;            // copy of the segment tables
+};
+
+// Named barriers: 1 = warps 0-3 (epilogue), 2 = the whole CTA, 3 = warps 0-7 (RES rows); every
+// lane of a warp reaches them together (__syncwarp first: a lane may come from a longer run of
+// a per-thread loop).
+
+// Barrier 1 that ORs a per-thread flag, so every epilogue thread takes the same decision.
+__device__ __forceinline__ bool epi_or(bool v) {
+  int r;
+  __syncwarp();
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((int)v), "r"(DP_EPI_THREADS)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void res_sync() {
+  __syncwarp();
+  named_sync(3, DP_RES_THREADS);
+}
+__device__ __forceinline__ void cta_sync() {
+  __syncwarp();
+  named_sync(2, DP_THREADS);
+}
+
+// Grid barrier: thread 0 waits (bounded) for `target` arrivals on cnt, then the CTA syncs.
+__device__ bool grid_wait(const DitPersistArgs& a, const unsigned* cnt, unsigned target, const Sm& sm) {
+  if (threadIdx.x == 0) {
+    bool bad = sm.flags[0] != 0;
+    if (!bad && ld_acquire(cnt) < target) {
+      const long long t0 = clock64();
+      int n = 0;
+      while (ld_acquire(cnt) < target) {
+        if ((++n & 63) == 0) {
+          if (*reinterpret_cast<volatile int*>(a.err) != 0 || clock64() - t0 > kWaitLimitCycles) {
+            record_error(a.err, VX_DEVICE_ERR_TIMEOUT);
+            bad = true;
+            break;
+          }
+        }
+      }
+    }
+    if (bad) sm.flags[0] = 1;
+    // data written through the generic proxy by other CTAs is read by this CTA's TMA loads
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+  }
+  cta_sync();
+  return sm.flags[0] == 0;
+}
+
+__device__ void grid_arrive(unsigned* cnt) {
+  cta_sync();
+  if (threadIdx.x == 0) {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ partial sums
+
+__device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+
+// The partial slots of one GEMM output: slot k of (row r, channels c..c+3) is b[k * stride].
+struct PRange {
+  const float* b;
+  int n;
+};
+
+struct Parts {
+  const float* p;        // [segments][Rpad][128]
+  const int* seg_off;    // [tiles + 1], in shared memory (plain loads: not the global-only __ldg)
+  size_t stride;         // Rpad * 128
+  __device__ PRange at(int r, int c) const {
+    const int t = c >> 7, s0 = seg_off[t];
+    return {p + (size_t)s0 * stride + (size_t)r * 128 + (c & 127), seg_off[t + 1] - s0};
+  }
+};
+
+// o[k] = sum over the slots of x[k] in slot order; NR ranges x BT slots of loads in flight.
+template <int NR, int BT>
+__device__ __forceinline__ void psum(const PRange* x, size_t stride, float4* o) {
+  int nmax = 0;
+#pragma unroll
+  for (int k = 0; k < NR; ++k) {
+    o[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    nmax = max(nmax, x[k].n);
+  }
+  for (int s = 0; s < nmax; s += BT) {
+    float4 v[NR][BT];
+#pragma unroll
+    for (int k = 0; k < NR; ++k)
+#pragma unroll
+      for (int i = 0; i < BT; ++i)
+        v[k][i] = s + i < x[k].n ? ldcg4(x[k].b + (size_t)(s + i) * stride) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < NR; ++k)
+#pragma unroll
+      for (int i = 0; i < BT; ++i)
+        if (s + i < x[k].n) o[k] = add4(o[k], v[k][i]);
+  }
+}
+
+__device__ __forceinline__ Parts parts_of(const DitPersistArgs& a, const Sm& sm, int kind) {
+  return Parts{a.part, sm.segtab + a.tab_off[kind], (size_t)a.Rpad * 128};
+}
+
+// Optional timeline: %globaltimer into trace [phase][CTA][4] (0: phase start, 1: first segment's
+// MMAs done, 2: this CTA's work done).
+__device__ __forceinline__ void trace_at(const DitPersistArgs& a, int ph, int slot) {
+  if (a.trace) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    a.trace[((size_t)ph * gridDim.x + blockIdx.x) * 4 + slot] = t;
+  }
+}
+
+// ------------------------------------------------------------------ row phases
+
+// Per-row sums over the DP_RES_THREADS RES threads (fixed order).
+__device__ void res_sum2(float& v0, float& v1, float* red) {
+  v0 = warp_sum(v0);
+  v1 = warp_sum(v1);
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    red[w] = v0;
+    red[8 + w] = v1;
+  }
+  res_sync();
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < DP_RES_THREADS / 32; ++i) {
+    s0 += red[i];
+    s1 += red[8 + i];
+  }
+  res_sync();
+  v0 = s0;
+  v1 = s1;
+}
+
+__device__ __forceinline__ void split1(float v, uint16_t& h, uint16_t& l) {
+  const __nv_bfloat16 bh = __float2bfloat16_rn(v);
+  h = __bfloat16_as_ushort(bh);
+  l = __bfloat16_as_ushort(__float2bfloat16_rn(v - __bfloat162float(bh)));
+}
+
+__device__ __forceinline__ void store_split(uint16_t* xs, size_t plane, size_t idx, float v) {
+  uint16_t h, l;
+  split1(v, h, l);
+  xs[idx] = h;
+  xs[plane + idx] = l;
+}
+
+// Four consecutive elements (idx % 4 == 0) into the split operand.
+__device__ __forceinline__ void store_split4(uint16_t* xs, size_t plane, size_t idx, float4 v) {
+  uint16_t h[4], l[4];
+  split1(v.x, h[0], l[0]);
+  split1(v.y, h[1], l[1]);
+  split1(v.z, h[2], l[2]);
+  split1(v.w, h[3], l[3]);
+  *reinterpret_cast<uint2*>(xs + idx) = make_uint2(h[0] | ((unsigned)h[1] << 16), h[2] | ((unsigned)h[3] << 16));
+  *reinterpret_cast<uint2*>(xs + plane + idx) =
+      make_uint2(l[0] | ((unsigned)l[1] << 16), l[2] | ((unsigned)l[3] << 16));
+}
+
+// RES rows: v = base[r] + s * (the GEMM output, summed from its partials; none for the input
+// rows), optionally stored to `store`; then RMSNorm(v) * w into the split operand (K = H), or
+// into final_out.  Run by the DP_RES_THREADS threads: thread t holds channels 4t..4t+3 of two
+// rows at a time (rows r and r + grid), so both rows' partial loads are in flight together.
+__device__ void res_norm_rows(const DitPersistArgs& a, const float* base, const Parts* q, float* store,
+                              const float* w, uint16_t* xs, float* final_out, const Sm& sm) {
+  const int H = a.H, G = gridDim.x;
+  const size_t plane = (size_t)a.Rpad * H;
+  const int c = threadIdx.x * 4;
+  const bool on = c < H;
+  for (int r0 = blockIdx.x; r0 < a.R; r0 += 2 * G) {
+    const int rr[2] = {r0, r0 + G};
+    const bool live[2] = {on, on && r0 + G < a.R};
+    float4 v[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+      v[k] = live[k] ? ldcg4(base + (size_t)rr[k] * H + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (q) {
+      PRange x[2] = {live[0] ? q->at(rr[0], c) : PRange{nullptr, 0}, live[1] ? q->at(rr[1], c) : PRange{nullptr, 0}};
+      float4 o[2];
+      psum<2, 4>(x, q->stride, o);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        v[k].x += o[k].x * a.res_scale;
+        v[k].y += o[k].y * a.res_scale;
+        v[k].z += o[k].z * a.res_scale;
+        v[k].w += o[k].w * a.res_scale;
+      }
+    }
+    float ss[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      ss[k] = 0.f;
+      if (!live[k]) continue;
+      if (store) *reinterpret_cast<float4*>(store + (size_t)rr[k] * H + c) = v[k];
+      ss[k] = fmaf(v[k].x, v[k].x, ss[k]);
+      ss[k] = fmaf(v[k].y, v[k].y, ss[k]);
+      ss[k] = fmaf(v[k].z, v[k].z, ss[k]);
+      ss[k] = fmaf(v[k].w, v[k].w, ss[k]);
+    }
+    res_sum2(ss[0], ss[1], sm.red);
+    const float4 g = on ? __ldg(reinterpret_cast<const float4*>(w + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      if (!live[k]) continue;
+      const float inv = 1.0f / sqrtf(ss[k] / (float)H + a.eps);
+      const float4 y = make_float4((v[k].x * inv) * g.x, (v[k].y * inv) * g.y, (v[k].z * inv) * g.z,
+                                   (v[k].w * inv) * g.w);
+      if (final_out)
+        *reinterpret_cast<float4*>(final_out + (size_t)rr[k] * H + c) = y;
+      else
+        store_split4(xs, plane, (size_t)rr[k] * H + c, y);
+    }
+  }
+}
+
+// LongRoPE cos / sin (x scaling factor) at positions 0..S-1 (rope.rs:76-95), f64 as the
+// reference computes them, into rope_tab [2][16][64] (grid-stride over the RES threads).
+__device__ void rope_table(const DitPersistArgs& a) {
+  const int half = a.d / 2;
+  for (int i = blockIdx.x * DP_RES_THREADS + threadIdx.x; i < a.S * half; i += gridDim.x * DP_RES_THREADS) {
+    const int p = i / half, j = i % half;
+    const double f = ((double)p * a.rope->inv_freq[j]) / a.rope->ext[j];
+    double sd, cd;
+    sincos(f, &sd, &cd);
+    a.rope_tab[p * 64 + j] = (float)(cd * a.rope->scaling_factor);
+    a.rope_tab[DP_SMAX * 64 + p * 64 + j] = (float)(sd * a.rope->scaling_factor);
+  }
+}
+
+// Attention for one sequence n and hpu query heads h0.. of one KV head g (GQA, no mask) over the
+// S keys of sequence n: q, k, v summed from the QKV partials, LongRoPE on q and k, softmax with
+// the max subtracted (attention.rs:186-191); output into the split operand (K = nh * d).  Run
+// by all DP_THREADS threads of the CTA.
+__device__ void att_unit(const DitPersistArgs& a, const Parts& q, int n, int h0, int hpu, int ph, const Sm& sm) {
+  const int S = a.S, d = a.d, half = d / 2, d4 = d / 4, g = h0 / (a.nh / a.nkv);
+  float* qs = sm.att;                               // [hpu][16][DP_QS]
+  float* ks = qs + hpu * DP_SMAX * DP_QS;           // [16][DP_QS]
+  float* vs = ks + DP_SMAX * DP_QS;                 // [16][DP_QS]
+  float* sc = sm.att + (DP_HPU + 2) * DP_SMAX * DP_QS;  // [hpu][16][16]
+  float* inv = sc + DP_HPU * DP_SMAX * DP_SMAX;     // [hpu][16]
+  const int tid = threadIdx.x, rows = (hpu + 2) * S, cells = rows * d4;
+  // q, k, v rows: two float4 cells per thread, eight slots each in flight
+  for (int i0 = tid; i0 < cells; i0 += 2 * DP_THREADS) {
+    PRange x[2];
+    int dst[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = i0 + k * DP_THREADS;
+      x[k] = PRange{nullptr, 0};
+      dst[k] = -1;
+      if (i < cells) {
+        const int which = i / (S * d4), rem = i % (S * d4), s = rem / d4, e = (rem % d4) * 4;
+        const int cb = which < hpu ? (h0 + which) * d : which == hpu ? (a.nh + g) * d : (a.nh + a.nkv + g) * d;
+        x[k] = q.at(n * S + s, cb + e);
+        dst[k] = (which * DP_SMAX + s) * DP_QS + e;
+      }
+    }
+    float4 o[2];
+    psum<2, 8>(x, q.stride, o);
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+      if (dst[k] >= 0) *reinterpret_cast<float4*>(qs + dst[k]) = o[k];
+  }
+  cta_sync();
+  if (threadIdx.x == 0 && n * (a.nh / hpu) + h0 / hpu == (int)blockIdx.x) trace_at(a, ph, 1);
+  if (a.rope) {  // rows 0..hpu S-1 are q, rows hpu S.. are k (one rotation pair per thread)
+    for (int i = tid; i < (hpu + 1) * S * half; i += DP_THREADS) {
+      const int row = i / half, j = i % half, s = row % S;
+      float* v = qs + ((row / S) * DP_SMAX + s) * DP_QS;
+      const float c = __ldcg(a.rope_tab + s * 64 + j), si = __ldcg(a.rope_tab + DP_SMAX * 64 + s * 64 + j);
+      const float x1 = v[j], x2 = v[j + half];
+      v[j] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(-x2, si));
+      v[j + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, si));
+    }
+    cta_sync();
+  }
+  if (threadIdx.x == 0 && n * (a.nh / hpu) + h0 / hpu == (int)blockIdx.x) trace_at(a, ph, 3);
+  for (int i = tid; i < hpu * S * S; i += DP_THREADS) {
+    const int hh = i / (S * S), s = (i / S) % S, t = i % S;
+    const float4* qr = reinterpret_cast<const float4*>(qs + (hh * DP_SMAX + s) * DP_QS);
+    const float4* kr = reinterpret_cast<const float4*>(ks + t * DP_QS);
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int e = 0; e < d4; ++e) {
+      const float4 x = qr[e], y = kr[e];
+      a0 = fmaf(x.x, y.x, a0);
+      a1 = fmaf(x.y, y.y, a1);
+      a2 = fmaf(x.z, y.z, a2);
+      a3 = fmaf(x.w, y.w, a3);
+    }
+    sc[(hh * DP_SMAX + s) * DP_SMAX + t] = ((a0 + a1) + (a2 + a3)) * a.attn_scale;
+  }
+  cta_sync();
+  if (tid < hpu * S) {
+    float* row = sc + ((tid / S) * DP_SMAX + tid % S) * DP_SMAX;
+    float mx = -FLT_MAX;
+    for (int t = 0; t < S; ++t) mx = fmaxf(mx, row[t]);
+    float den = 0.f;
+    for (int t = 0; t < S; ++t) {
+      const float e = expf(row[t] - mx);
+      row[t] = e;
+      den += e;
+    }
+    inv[(tid / S) * DP_SMAX + tid % S] = 1.0f / den;
+  }
+  cta_sync();
+  const size_t plane = (size_t)a.Rpad * a.nh * d;
+  for (int i = tid; i < hpu * S * d4; i += DP_THREADS) {
+    const int hh = i / (S * d4), s = (i / d4) % S, e = (i % d4) * 4;
+    const float* p = sc + (hh * DP_SMAX + s) * DP_SMAX;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int t = 0; t < S; ++t) {
+      const float pt = p[t];
+      const float4 v = *reinterpret_cast<const float4*>(vs + t * DP_QS + e);
+      o.x = fmaf(pt, v.x, o.x);
+      o.y = fmaf(pt, v.y, o.y);
+      o.z = fmaf(pt, v.z, o.z);
+      o.w = fmaf(pt, v.w, o.w);
+    }
+    const float iv = inv[hh * DP_SMAX + s];
+    store_split4(a.xs, plane, (size_t)(n * S + s) * a.nh * d + (h0 + hh) * d + e,
+                 make_float4(o.x * iv, o.y * iv, o.z * iv, o.w * iv));
+  }
+  cta_sync();  // the scratch is free for the next unit
+}
+
+// ACT: silu(gate) * up, both summed from the GU partials, into the split operand (K = I);
+// two groups of four elements per thread in flight; run by all DP_THREADS threads.
+__device__ void act_rows(const DitPersistArgs& a, const Parts& q) {
+  const int I = a.I, i4 = I / 4;
+  const size_t plane = (size_t)a.Rpad * I, n = (size_t)a.R * i4;
+  const size_t step = (size_t)gridDim.x * DP_THREADS;
+  for (size_t i0 = (size_t)blockIdx.x * DP_THREADS + threadIdx.x; i0 < n; i0 += 2 * step) {
+    PRange x[4];
+    int rr[2], jj[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const size_t i = i0 + k * step;
+      rr[k] = -1;
+      x[2 * k] = x[2 * k + 1] = PRange{nullptr, 0};
+      if (i < n) {
+        rr[k] = (int)(i / i4);
+        jj[k] = (int)(i % i4) * 4;
+        x[2 * k] = q.at(rr[k], jj[k]);
+        x[2 * k + 1] = q.at(rr[k], I + jj[k]);
+      }
+    }
+    float4 o[4];
+    psum<4, 4>(x, q.stride, o);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      if (rr[k] < 0) continue;
+      const float4 gt = o[2 * k], up = o[2 * k + 1];
+      store_split4(a.xs_i, plane, (size_t)rr[k] * I + jj[k],
+                   make_float4(silu(gt.x) * up.x, silu(gt.y) * up.y, silu(gt.z) * up.z, silu(gt.w) * up.w));
+    }
+  }
+}
+
+// ------------------------------------------------------------------ the kernel
+
+// Static description of one GEMM phase (kind PH_QKV / PH_O / PH_GU / PH_DOWN of layer l) and
+// the contiguous run [c0, c1) of its (tile, K chunk) pairs this CTA takes.
+struct GemmPh {
+  int n_out, kch, gk, c0, c1;
+  const CUtensorMap* wmap;
+  const CUtensorMap* xmap;
+};
+
+__device__ GemmPh gemm_phase(const DitPersistArgs& a, int kind, int l) {
+  GemmPh g;
+  int K, wi;
+  if (kind == PH_QKV) { g.n_out = (a.nh + 2 * a.nkv) * a.d; K = a.H; wi = 0; g.gk = DP_KIND_QKV; g.xmap = &a.xmaps[0]; }
+  else if (kind == PH_O) { g.n_out = a.H; K = a.nh * a.d; wi = 1; g.gk = DP_KIND_O; g.xmap = &a.xmaps[0]; }
+  else if (kind == PH_GU) { g.n_out = 2 * a.I; K = a.H; wi = 2; g.gk = DP_KIND_GU; g.xmap = &a.xmaps[0]; }
+  else { g.n_out = a.H; K = a.I; wi = 3; g.gk = DP_KIND_DOWN; g.xmap = &a.xmaps[1]; }
+  g.wmap = &a.wmaps[l * 4 + wi];
+  g.kch = K / TC_BK;
+  const int total = (g.n_out / TC_BM) * g.kch, nc = a.ncta[g.gk], b = blockIdx.x;
+  g.c0 = b < nc ? (int)((long long)b * total / nc) : 0;
+  g.c1 = b < nc ? (int)((long long)(b + 1) * total / nc) : 0;
+  return g;
+}
+
+__global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPersistArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int plane_bytes = a.Rpad * TC_BK * 2;
+  const int stage_bytes = DP_A_BYTES + 2 * plane_bytes;
+  Sm sm;
+  sm.stages = base;
+  sm.att = reinterpret_cast<float*>(base + (size_t)a.nst * stage_bytes);
+  sm.red = sm.att + DP_ATT_FLOATS;
+  sm.full = reinterpret_cast<uint64_t*>(sm.red + 32);
+  sm.empty = sm.full + a.nst;
+  sm.seg_done = sm.empty + a.nst;
+  sm.acc_free = sm.seg_done + 1;
+  sm.fin = sm.acc_free + 1;
+  sm.tmem_slot = reinterpret_cast<uint32_t*>(sm.fin + 1);
+  sm.flags = reinterpret_cast<volatile int*>(sm.tmem_slot + 2);
+  sm.segtab = const_cast<int*>(reinterpret_cast<volatile int*>(sm.flags + 2));
+  for (int i = threadIdx.x; i < a.tab_len; i += DP_THREADS) sm.segtab[i] = __ldg(a.segtab + i);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t ncols = 32;
+  while ((int)ncols < a.Rpad) ncols <<= 1;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.nst; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    mbar_init(sm.seg_done, 1);
+    mbar_init(sm.acc_free, DP_EPI_THREADS);
+    mbar_init(sm.fin, 1);
+    sm.flags[0] = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    __syncwarp();
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(sm.tmem_slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *sm.tmem_slot;
+
+  // per-role persistent state: ring position (producer, MMA), segments done
+  int prod_i = 0, mma_i = 0, seg_g = 0;
+  int pre_n = 0, pre_kind = 0, pre_l = 0;  // producer: weight tiles of the next GEMM phase already armed
+  bool ok = true;
+  const int G = gridDim.x;
+  const int nph = a.L * PH_N + 1;
+
+  for (int ph = 0; ph < nph && ok; ++ph) {
+    if (ph > 0 && !grid_wait(a, a.bar + ph - 1, (unsigned)G, sm)) {
+      ok = false;
+      break;
+    }
+    if (threadIdx.x == 0) trace_at(a, ph, 0);
+    const int l = ph / PH_N, kind = ph == nph - 1 ? -1 : ph % PH_N;
+    const DitPersistLayer* w = a.layers + (l < a.L ? l : 0);
+    const bool gemm = kind == PH_QKV || kind == PH_O || kind == PH_GU || kind == PH_DOWN;
+    if (!gemm) {
+      if (warp == 4 && lane == 0 && kind >= 0) {
+        // the next phase is a GEMM: its first weight tiles do not depend on this phase, so they
+        // stream into the (free) ring during it; the activation planes follow after the barrier
+        const GemmPh g = gemm_phase(a, kind + 1, l);
+        pre_kind = kind + 1;
+        pre_l = l;
+        pre_n = 0;
+        for (int j = 0; j < std::min(a.nst, g.c1 - g.c0); ++j) {
+          const int pi = prod_i + j, s = pi % a.nst, c = g.c0 + j;
+          if (pi >= a.nst && !mbar_wait(&sm.empty[s], ((pi / a.nst) - 1) & 1, a.err)) {
+            sm.flags[0] = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&sm.full[s], stage_bytes);
+          tma_load_2d(sm.stages + (size_t)s * stage_bytes, g.wmap, (c % g.kch) * TC_BK, (c / g.kch) * TC_BM,
+                      &sm.full[s]);
+          pre_n = j + 1;
+        }
+      }
+      if (kind == PH_ATT) {  // all warps; two heads per unit when one per unit would not fit the grid
+        const Parts q = parts_of(a, sm, DP_KIND_QKV);
+        const int hpu = a.N * a.nh > G && (a.nh / a.nkv) % DP_HPU == 0 ? DP_HPU : 1, per = a.nh / hpu;
+        for (int u = blockIdx.x; u < a.N * per; u += G) att_unit(a, q, u / per, (u % per) * hpu, hpu, ph, sm);
+      } else if (kind == PH_ACT) {  // all warps
+        act_rows(a, parts_of(a, sm, DP_KIND_GU));
+      } else if (threadIdx.x < DP_RES_THREADS) {
+        if (kind == -1) {  // final: RMSNorm(x1 + s * down) with the final norm weight
+          const Parts q = parts_of(a, sm, DP_KIND_DOWN);
+          res_norm_rows(a, a.x1, &q, nullptr, a.final_norm, nullptr, a.out, sm);
+        } else if (kind == PH_RES_A) {
+          if (l == 0) {
+            if (a.rope) rope_table(a);
+            res_norm_rows(a, a.x_in, nullptr, a.x, w->ln_in, a.xs, nullptr, sm);
+          } else {
+            const Parts q = parts_of(a, sm, DP_KIND_DOWN);
+            res_norm_rows(a, a.x1, &q, a.x, w->ln_in, a.xs, nullptr, sm);
+          }
+        } else {  // PH_RES_B
+          const Parts q = parts_of(a, sm, DP_KIND_O);
+          res_norm_rows(a, a.x, &q, a.x1, w->ln_post, a.xs, nullptr, sm);
+        }
+      }
+      if (threadIdx.x == 0) trace_at(a, ph, 2);
+      if (ph < nph - 1) grid_arrive(a.bar + ph);
+      else cta_sync();
+      if (sm.flags[0]) ok = false;
+      continue;
+    }
+    // ---- GEMM phase
+    const GemmPh g = gemm_phase(a, kind, l);
+    const int n_out = g.n_out, kch = g.kch, gk = g.gk, c0 = g.c0, c1 = g.c1, b = blockIdx.x, nc = a.ncta[gk];
+    const CUtensorMap* wmap = g.wmap;
+    const CUtensorMap* xmap = g.xmap;
+    if (warp == 4) {
+      if (lane == 0) {  // TMA producer
+        // the activation operand was written by other CTAs' generic stores before the barrier
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        for (int c = c0; c < c1; ++c, ++prod_i) {
+          const int s = prod_i % a.nst;
+          unsigned char* st = sm.stages + (size_t)s * stage_bytes;
+          const int kx = (c % kch) * TC_BK, tile = c / kch;
+          if (c - c0 >= pre_n) {  // not armed in the phase before
+            if (prod_i >= a.nst && !mbar_wait(&sm.empty[s], ((prod_i / a.nst) - 1) & 1, a.err)) {
+              sm.flags[0] = 1;
+              break;
+            }
+            mbar_arrive_expect_tx(&sm.full[s], stage_bytes);
+            tma_load_2d(st, wmap, kx, tile * TC_BM, &sm.full[s]);
+          }
+          tma_load_3d(st + DP_A_BYTES, xmap, kx, 0, 0, &sm.full[s]);
+          tma_load_3d(st + DP_A_BYTES + plane_bytes, xmap, kx, 0, 1, &sm.full[s]);
+        }
+        pre_n = 0;
+      }
+    } else if (warp == 5) {
+      if (lane == 0) {  // MMA issuer
+        const uint32_t idesc = tc_idesc(a.Rpad);
+        int seg_local = seg_g;
+        for (int c = c0; c < c1; ++c, ++mma_i) {
+          const bool first = c == c0 || c % kch == 0;
+          if (first && seg_local > 0 && !mbar_wait(sm.acc_free, (seg_local - 1) & 1, a.err)) {
+            sm.flags[0] = 1;
+            break;
+          }
+          const int s = mma_i % a.nst;
+          if (!mbar_wait(&sm.full[s], (mma_i / a.nst) & 1, a.err)) {
+            sm.flags[0] = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(sm.stages + (size_t)s * stage_bytes);
+          const uint32_t sh = sa + DP_A_BYTES, sl = sh + plane_bytes;
+#pragma unroll
+          for (int kk = 0; kk < TC_BK / 16; ++kk) {
+            tc_mma(tmem, sw128_desc(sa + kk * 32), sw128_desc(sh + kk * 32), idesc, (!first || kk > 0) ? 1 : 0);
+            tc_mma(tmem, sw128_desc(sa + kk * 32), sw128_desc(sl + kk * 32), idesc, 1);
+          }
+          tc_commit(&sm.empty[s]);
+          if (c == c1 - 1 || (c + 1) % kch == 0) {
+            tc_commit(sm.seg_done);  // the segment's accumulator is complete once its MMAs finish
+            ++seg_local;
+          }
+        }
+      }
+    } else if (warp < 4) {
+      // ---- epilogue (warps 0-3): each segment's partial tile into its slot, rows < R
+      const Parts q = parts_of(a, sm, gk);
+      int seg = b < nc ? sm.segtab[a.tab_off[gk] + n_out / TC_BM + 1 + b] : 0;
+      const int ch = warp * 32 + lane;
+      for (int c = c0; c < c1; ++seg) {
+        const int tile = c / kch, cend = std::min(c1, (tile + 1) * kch);
+        const bool good = mbar_wait(sm.seg_done, seg_g & 1, a.err);
+        tc_fence_after();
+        if (!good) sm.flags[0] = 1;
+        if (epi_or(!good || sm.flags[0] != 0)) break;  // uniform over the four warps
+        if (threadIdx.x == 0 && c == c0) trace_at(a, ph, 1);
+        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+        float* dst = a.part + (size_t)seg * q.stride + ch;
+        for (int sl = 0; sl < a.Rpad / 32; ++sl) {
+          float v[32];
+          tmem_ld16(trow + sl * 32, v);
+          tmem_ld16(trow + sl * 32 + 16, v + 16);
+          if (sl == a.Rpad / 32 - 1) {  // last TMEM read of the segment: the MMA warp may reuse it
+            tc_fence_before();
+            mbar_arrive(sm.acc_free);
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (sl * 32 + j < a.R) __stcg(dst + (size_t)(sl * 32 + j) * 128, v[j]);
+        }
+        ++seg_g;
+        c = cend;
+      }
+      if (threadIdx.x == 0) trace_at(a, ph, 2);
+    }
+    // the MMA thread counts this phase's segments too (its seg_g drives the acc_free parity)
+    if (warp == 5) {
+      for (int c = c0; c < c1;) {
+        c = std::min(c1, (c / kch + 1) * kch);
+        ++seg_g;
+      }
+    }
+    if (ph < nph - 1) grid_arrive(a.bar + ph);
+    else cta_sync();
+    // read after the CTA barrier, where no thread of the CTA still writes the flag
+    if (sm.flags[0]) ok = false;
+  }
+
+  // ---- leave: no MMA may still be writing TMEM and no copy still landing in shared memory;
+  // free TMEM; the last CTA out resets the barrier counters.  Stages armed for a GEMM phase that
+  // never ran (abort) get their activation planes too, so the drain below sees them complete.
+  if (warp == 4 && lane == 0 && pre_n > 0) {
+    const GemmPh g = gemm_phase(a, pre_kind, pre_l);
+    for (int j = 0; j < pre_n; ++j, ++prod_i) {
+      unsigned char* st = sm.stages + (size_t)(prod_i % a.nst) * stage_bytes;
+      const int kx = ((g.c0 + j) % g.kch) * TC_BK;
+      tma_load_3d(st + DP_A_BYTES, g.xmap, kx, 0, 0, &sm.full[prod_i % a.nst]);
+      tma_load_3d(st + DP_A_BYTES + plane_bytes, g.xmap, kx, 0, 1, &sm.full[prod_i % a.nst]);
+    }
+    pre_n = 0;
+  }
+  if (warp == 5 && lane == 0) {
+    tc_commit(sm.fin);
+    const long long t0 = clock64();
+    while (!mbar_try_wait(sm.fin, 0))
+      if (clock64() - t0 > kWaitLimitCycles) break;
+  }
+  if (warp == 4 && lane == 0) {
+    for (int j = prod_i > a.nst ? prod_i - a.nst : 0; j < prod_i; ++j) {
+      const long long t0 = clock64();
+      while (!mbar_try_wait(&sm.full[j % a.nst], (j / a.nst) & 1))
+        if (clock64() - t0 > kWaitLimitCycles) break;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(a.bar + nph, 1u);
+    if (prev == (unsigned)G - 1) {
+      for (int i = 0; i <= nph; ++i) a.bar[i] = 0u;
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace
+
+int dit_persist_segments(int tiles, int kch, int ncta, int* tab) {
+  const int total = tiles * kch;
+  int* seg_off = tab;
+  int* first = tab + tiles + 1;
+  for (int t = 0; t <= tiles; ++t) seg_off[t] = 0;
+  int seg = 0;
+  for (int b = 0; b < ncta; ++b) {
+    const int c0 = (int)((long long)b * total / ncta), c1 = (int)((long long)(b + 1) * total / ncta);
+    first[b] = seg;
+    for (int c = c0; c < c1;) {
+      const int t = c / kch;
+      ++seg_off[t + 1];
+      ++seg;
+      c = std::min(c1, (t + 1) * kch);
+    }
+  }
+  for (int t = 0; t < tiles; ++t) seg_off[t + 1] += seg_off[t];
+  return seg;
+}
+
+size_t dit_persist_smem(int rpad, int* nst) {
+  const int stage = TC_BM * TC_BK * 2 + 2 * rpad * TC_BK * 2;
+  const size_t fixed = 1024 + (DP_ATT_FLOATS + 32) * 4 + 8 * 32 + 128 + DP_SEGTAB_MAX * 4;
+  const int n = (int)std::min<size_t>(6, (227 * 1024 - fixed) / stage);
+  *nst = n;
+  return fixed + (size_t)n * stage;
+}
+
+cudaError_t dit_persist_configure() {
+  return cudaFuncSetAttribute(dit_persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
+
+int dit_persist_grid() {
+  int dev = 0, sms = 0, per = 0;
+  int nst = 0;
+  const size_t smem = dit_persist_smem(256, &nst);
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, dit_persist_kernel, DP_THREADS, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return per >= 1 ? sms : 0;
+}
+
+cudaError_t launch_dit_persist(const DitPersistArgs& a, int grid, cudaStream_t st) {
+  int nst = 0;
+  const size_t smem = dit_persist_smem(a.Rpad, &nst);
+  DitPersistArgs b = a;
+  b.nst = nst;
+  if (nst < 2 || grid <= 0) return cudaErrorInvalidValue;
+  for (int k = 0; k < DP_KINDS; ++k)
+    if (a.ncta[k] < 1 || a.ncta[k] > grid) return cudaErrorInvalidValue;
+  if (a.tab_len < 1 || a.tab_len > DP_SEGTAB_MAX) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(DP_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  count_launch();
+  return cudaLaunchKernelEx(&cfg, dit_persist_kernel, b);
+}
+
+}  // namespace vx

@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "dit_persist.cuh"
 #include "persist.cuh"
 #include "runtime.cuh"
 
@@ -911,6 +912,24 @@ const float* lm_batch_hidden(const vx_lm* lm) { return lm->bhid; }
 const int* lm_batch_tokens(const vx_lm* lm) { return lm->btokens; }
 int lm_max_batch(const vx_lm* lm) { return lm->max_batch; }
 int lm_vocab_size(const vx_lm* lm) { return lm->V; }
+void lm_stack_view(const vx_lm* lm, LmStackView* v) {
+  v->L = lm->L;
+  v->H = lm->H;
+  v->I = lm->I;
+  v->nh = lm->nh;
+  v->nkv = lm->nkv;
+  v->d = lm->d;
+  v->eps = lm->cfg.rms_norm_eps;
+  v->res_scale = lm->res_scale;
+  v->attn_scale = lm->attn_scale;
+  v->rope = lm->rope;
+  v->norm_w = lm->norm_w;
+  v->layers.resize(lm->L);
+  for (int l = 0; l < lm->L; ++l) {
+    const LmLayer& w = lm->layers[l];
+    v->layers[l] = {w.wqkv, w.wo, w.wgu, w.wd, w.ln_in, w.ln_post};
+  }
+}
 void lm_dims(const vx_lm* lm, int* L, int* H, int* I, int* qs, int* ks, int* V) {
   *L = lm->L;
   *H = lm->H;

@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "../../include/voxcpm_b200.h"
+#include "dit_persist.cuh"
 #include "gemv.cuh"
 #include "kernels.cuh"
 
@@ -183,6 +184,15 @@ const float* lm_batch_hidden(const vx_lm* lm);
 const int* lm_batch_tokens(const vx_lm* lm);
 int lm_max_batch(const vx_lm* lm);
 int lm_vocab_size(const vx_lm* lm);
+// A model's stack as the persistent DiT-forward kernel sees it (dit_persist.cuh).
+struct LmStackView {
+  int L, H, I, nh, nkv, d;
+  float eps, res_scale, attn_scale;
+  const RopeParams* rope;
+  const float* norm_w;
+  std::vector<DitPersistLayer> layers;
+};
+void lm_stack_view(const vx_lm* lm, LmStackView* v);
 void lm_dims(const vx_lm* lm, int* L, int* H, int* I, int* qs, int* ks, int* V);
 int lm_max_length(const vx_lm* lm);
 // DiT / VAE accessors (dit.cu, vae.cu).
@@ -190,6 +200,7 @@ int cfm_solve_enqueue(vx_dit* d, const float* mu, const float* cond, const float
                       int n_timesteps, float cfg_value, float sway_sampling_coef, int use_cfg_zero_star,
                       float* x_out);
 int dit_hidden_size(const vx_dit* d);
+int dit_trace_copy(vx_dit* d, unsigned long long* out, int n, int* grid, int* phases);
 vx_lm* dit_decoder(vx_dit* d, int* H, int* C);
 struct VaeDims {
   int latent, dim, nblocks, rates[8], n_buckets;  // n_buckets 0: no sample-rate conditioning
