@@ -333,6 +333,19 @@ def measure_cfm(ctx, device, dcfg, dit_w):
             dit.cfm_forward(mu, 10, cond, z, 2.0, sway, zs)
         dt = (time.perf_counter() - t0) / 20
         out[f"patches_per_s_{name}"] = 1.0 / dt
+    # the batched synthesis solves 8 patches at once (16 CFG sequences, 176 decoder rows), which
+    # runs the persistent decoder forward
+    mu8 = torch.from_numpy(rng.standard_normal((8, 2048), dtype=np.float32)).to(device)
+    cond8 = torch.zeros(8, 64, 4, device=device)
+    z8 = torch.from_numpy(rng.standard_normal((8, 64, 4), dtype=np.float32)).to(device)
+    for _ in range(3):
+        dit.cfm_forward(mu8, 10, cond8, z8, 2.0, 1.0, True)
+    t0 = time.perf_counter()
+    for _ in range(20):
+        dit.cfm_forward(mu8, 10, cond8, z8, 2.0, 1.0, True)
+    dt = (time.perf_counter() - t0) / 20
+    out["batch8_ms_per_solve"] = dt * 1e3
+    out["patches_per_s_batch8"] = 8.0 / dt
     dit.close()
     return out
 
@@ -559,9 +572,66 @@ def run_vae_only():
     return 0
 
 
-def run_cfm_only():
+def run_dit_trace(batch=8):
+    """--dit-trace B: timeline of the persistent LocDiT decoder forward inside a CFM solve of B
+    patches (2B sequences of 11 rows; forced onto the persistent path): per phase kind, the
+    median over layers of the phase time (last CTA through the grid barrier to the next), the
+    slowest CTA's work and the barrier wait; GEMM phases also report when the slowest CTA's first
+    segment finished its MMAs."""
+    import ctypes
+    import numpy as np
+    import torch
+    os.environ["VX_DIT_TRACE"] = "1"
+    os.environ["VX_DIT_PERSIST"] = "1"
+    from __graft_entry__ import load_package
+    load_package()
+    from voxcpm_rs_b200 import config, synth
+    from voxcpm_rs_b200._lib import lib
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    from voxcpm_rs_b200.minicpm4 import Context
+    ctx = Context(0)
+    dcfg = config.locdit_config(lm_config())
+    dit = VoxCpmLocDiTV2(ctx, dcfg, synth.locdit_weights(dcfg, in_channels=64, seed=0))
+    rng = np.random.default_rng(0)
+    mu = torch.from_numpy(rng.standard_normal((batch, 2048), dtype=np.float32)).cuda()
+    cond = torch.zeros(batch, 64, 4, device="cuda")
+    z = torch.from_numpy(rng.standard_normal((batch, 64, 4), dtype=np.float32)).cuda()
+    for _ in range(3):
+        dit.cfm_forward(mu, 10, cond, z, 2.0, 0.0, False)
+    torch.cuda.synchronize()
+    n = (8 * dcfg.num_hidden_layers + 1) * 1024 * 4
+    buf = (ctypes.c_ulonglong * n)()
+    grid, phases = ctypes.c_int(), ctypes.c_int()
+    rc = lib().vx_dit_trace(dit.h, buf, n, ctypes.byref(grid), ctypes.byref(phases))
+    if rc:
+        raise SystemExit(f"vx_dit_trace: {rc}")
+    P, G = phases.value, grid.value
+    t = np.frombuffer(buf, dtype=np.uint64)[:P * G * 4].reshape(P, G, 4).astype(np.int64)
+    t0 = t[:, :, 0][t[:, :, 0] > 0].min()
+    t = np.where(t > 0, t - t0, -1) / 1000.0
+    start = t[:, :, 0].max(axis=1)
+    names = ["RES_A", "QKV", "ATT", "O", "RES_B", "GU", "ACT", "DOWN"]
+    res = {}
+    for p in range(P - 1):
+        d = res.setdefault(names[p % 8], {"phase_us": [], "work_us": [], "first_mma_us": [], "barrier_us": []})
+        work = t[p, :, 2]
+        wmax = work[work >= 0].max() if (work >= 0).any() else start[p]
+        m = t[p, :, 1]
+        d["phase_us"].append(start[p + 1] - start[p])
+        d["work_us"].append(wmax - start[p])
+        d["first_mma_us"].append(m[m >= 0].max() - start[p] if (m >= 0).any() and names[p % 8] in ("QKV", "O", "GU", "DOWN") else 0.0)
+        d["barrier_us"].append(start[p + 1] - wmax)
+    out = {k: {kk: round(float(np.median(vv)), 2) for kk, vv in v.items()} for k, v in res.items()}
+    print(json.dumps({"dit_trace": {"patches": batch, "rows": 2 * batch * 11, "grid": G,
+                                    "forward_us": round(float(start[-1]), 1), "phases": out}}))
+    dit.close()
+    ctx.close()
+    return 0
+
+
+def run_cfm_only(batch=1):
     """Small profiling case: the LocDiT CFM solve (8 layers, hidden 1024, CFG 2.0, 10 uniform
-    Euler steps, B=1) run twice (the first call captures the solve graph)."""
+    Euler steps, `batch` patches) run twice (the first call captures the solve graph)."""
     import numpy as np
     import torch
     from __graft_entry__ import load_package
@@ -573,13 +643,13 @@ def run_cfm_only():
     dcfg = config.locdit_config(lm_config())
     dit = VoxCpmLocDiTV2(ctx, dcfg, synth.locdit_weights(dcfg, in_channels=64, seed=0))
     rng = np.random.default_rng(0)
-    mu = torch.from_numpy(rng.standard_normal((1, 2048), dtype=np.float32)).cuda()
-    cond = torch.zeros(1, 64, 4, device="cuda")
-    z = torch.from_numpy(rng.standard_normal((1, 64, 4), dtype=np.float32)).cuda()
+    mu = torch.from_numpy(rng.standard_normal((batch, 2048), dtype=np.float32)).cuda()
+    cond = torch.zeros(batch, 64, 4, device="cuda")
+    z = torch.from_numpy(rng.standard_normal((batch, 64, 4), dtype=np.float32)).cuda()
     for _ in range(2):
         t0 = time.perf_counter()
         dit.cfm_forward(mu, 10, cond, z, 2.0, 0.0, False)
-        print(json.dumps({"cfm_solve_ms": (time.perf_counter() - t0) * 1e3}))
+        print(json.dumps({"cfm_solve_ms": (time.perf_counter() - t0) * 1e3, "batch": batch}))
     dit.close()
     ctx.close()
     return 0
@@ -598,7 +668,10 @@ def main():
     ap.add_argument("--kernel-only", action="store_true",
                     help="profiling case: only the gate|up GEMV over 4 distinct 50 MB weights")
     ap.add_argument("--cfm-only", action="store_true",
-                    help="profiling case: two CFM solves of the LocDiT workload (B=1, 10 Euler steps)")
+                    help="profiling case: two CFM solves of the LocDiT workload (10 Euler steps)")
+    ap.add_argument("--cfm-batch", type=int, default=1, help="patches per solve of --cfm-only")
+    ap.add_argument("--dit-trace", type=int, default=None, metavar="B",
+                    help="phase timeline of the persistent LocDiT forward in a CFM solve of B patches")
     ap.add_argument("--vae-only", action="store_true",
                     help="profiling case: two AudioVAE decodes of 1024 latent frames")
     ap.add_argument("--lm-only", action="store_true",
@@ -617,7 +690,9 @@ def main():
     if args.lm_only:
         return run_lm_only(args.lm_layers)
     if args.cfm_only:
-        return run_cfm_only()
+        return run_cfm_only(args.cfm_batch)
+    if args.dit_trace is not None:
+        return run_dit_trace(args.dit_trace)
     if args.vae_only:
         return run_vae_only()
     args.warmup = max(3, args.warmup)
