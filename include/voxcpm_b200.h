@@ -245,6 +245,9 @@ int vx_dit_load(vx_dit* dit, const uint16_t* in_w, const float* in_b, const uint
  * [phase][CTA][4] = phase start, first segment's MMAs done (GEMM phases), CTA's work done, 0.
  * Copies phases * grid * 4 values into out (n entries at least). */
 int vx_dit_trace(vx_dit* dit, unsigned long long* out, int n, int* grid, int* phases);
+/* The same timeline for the batched greedy step's persistent decoder layers (VX_LM_BATCH_TRACE=1
+ * set when the LM is created; the last batched step). */
+int vx_lm_batch_trace(vx_lm* lm, unsigned long long* out, int n, int* grid, int* phases);
 /* Decoder layer / final norm weights (as vx_lm_load_layer / vx_lm_load_norm). */
 int vx_dit_load_layer(vx_dit* dit, int layer, const uint16_t* q, const uint16_t* k, const uint16_t* v,
                       const uint16_t* o, const uint16_t* gate, const uint16_t* up, const uint16_t* down,

@@ -108,3 +108,52 @@ def test_generate_full_width(ctx):
     assert wav.shape == (steps * 4 * 640,)
     assert_close(lat, want_lat, **TOL, what="latent")
     assert_close(wav, want_wav, **TOL, what="wav")
+
+
+@pytest.mark.slow
+def test_generate_batch_full_width(ctx):
+    """vx_generate_batch at the end-to-end workload's widths (a 4-layer LM of the decode
+    workload, the 8-layer LocDiT, the 2048-wide AudioVAE): 4 utterances, 3 patches.  The
+    batched LM step runs as one persistent launch (decode attention over the static cache);
+    two utterances are checked against the oracle's single-utterance loop, and the whole run
+    against the per-kernel LM step (VX_LM_BATCH_PERSIST=0)."""
+    import os
+    from voxcpm_rs_b200 import config, synth
+    from voxcpm_rs_b200.audiovae import AudioVae
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    from voxcpm_rs_b200.minicpm4 import MiniCpmModel
+    from voxcpm_rs_b200.voxcpm import GenerateOptions, VoxCPM
+    B, n, steps = 4, 64, 3
+    lm_cfg = config.lm_decode_config(layers=4)
+    lm_w = synth.minicpm_weights(lm_cfg, seed=21)
+    dcfg, vcfg = config.locdit_config(lm_cfg), config.vae_config()
+    dit_w = synth.locdit_weights(dcfg, in_channels=64, seed=22)
+    vae_w = synth.vae_weights(vcfg, seed=23)
+    prompts = np.stack([synth.prompt_ids(n, lm_cfg.vocab_size, seed=30 + b) for b in range(B)])
+    noise = np.random.default_rng(24).standard_normal((B, steps, 64, 4), dtype=np.float32)
+    opts = GenerateOptions(max_len=steps, inference_timesteps=10)
+    outs = []
+    for flag in (None, "0"):
+        old_env = os.environ.get("VX_LM_BATCH_PERSIST")
+        if flag is not None:
+            os.environ["VX_LM_BATCH_PERSIST"] = flag
+        try:
+            lm = MiniCpmModel(ctx, lm_cfg, lm_w, max_batch=B, max_length=128)
+        finally:
+            if old_env is None:
+                os.environ.pop("VX_LM_BATCH_PERSIST", None)
+            else:
+                os.environ["VX_LM_BATCH_PERSIST"] = old_env
+        vox = VoxCPM(ctx, lm, VoxCpmLocDiTV2(ctx, dcfg, dit_w, max_rows=2 * B), AudioVae(ctx, vcfg, vae_w))
+        outs.append(vox.generate_batch(prompts, opts, noise, return_latent=True))
+        vox.dit.close()
+        vox.vae.close()
+        vox.lm.close()
+    (wav, lat), (wav0, lat0) = outs
+    assert_close(lat, lat0, atol=2e-3, rtol=2e-3, what="latent: persistent vs per-kernel batched LM step")
+    fl, fd, fv = synth.minicpm_f32_view(lm_w), synth.locdit_f32_view(dit_w), synth.vae_f32_view(vae_w)
+    for b in (0, 3):
+        want_wav, want_lat, _ = ovx.generate(lm_cfg, fl, dcfg, fd, vcfg, fv, prompts[b], steps, noise[b],
+                                             inference_timesteps=10)
+        assert_close(lat[b], want_lat, **TOL, what=f"latent[{b}]")
+        assert_close(wav[b], want_wav, **TOL, what=f"wav[{b}]")

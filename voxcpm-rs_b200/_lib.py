@@ -114,6 +114,7 @@ SIGNATURES = {
     "vx_dit_load_layer": (I32, [P, I32, P, P, P, P, P, P, P, P, P]),
     "vx_dit_load_norm": (I32, [P, P]),
     "vx_dit_trace": (I32, [P, P, I32, C.POINTER(I32), C.POINTER(I32)]),
+    "vx_lm_batch_trace": (I32, [P, P, I32, C.POINTER(I32), C.POINTER(I32)]),
     "vx_dit_forward": (I32, [P, P, P, P, P, P, I32, I32, I32, I32, P]),
     "vx_cfm_solve": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F32, F32, I32, P]),
     "vx_vae_create": (I32, [P, C.POINTER(VaeConfigC), C.POINTER(P)]),

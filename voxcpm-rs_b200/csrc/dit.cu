@@ -134,22 +134,7 @@ struct vx_dit {
   unsigned long long solve_kernels = 0;
   // persistent decoder forward (dit_persist.cu): one cooperative launch per DiT forward
   int dp_mode = -1;              // env VX_DIT_PERSIST: 0 never, 1 always, unset: above kDpMinRows rows
-  int dp_grid = -1;              // -1: not configured yet; 0: unsupported shape or device
-  int dp_rmax = 0;               // rows the buffers below hold (activation rows rounded up to 32)
-  DitPersistLayer* dp_layers = nullptr;
-  CUtensorMap* dp_maps = nullptr;  // device [4 L]: the layers' weight maps
-  std::map<int, CUtensorMap*> dp_xmaps;  // device [2] activation maps per padded row count
-  float *dp_x = nullptr, *dp_x1 = nullptr;
-  uint16_t *dp_xs = nullptr, *dp_xsi = nullptr;
-  float* dp_part = nullptr;      // GEMM segment partials [segments][rmax][128]
-  float* dp_rope = nullptr;      // [2][16][64] rope table
-  int* dp_segtab = nullptr;      // segment tables of the four GEMM kinds
-  int dp_tab_off[DP_KINDS] = {};
-  int dp_ncta[DP_KINDS] = {};
-  int dp_tab_len = 0;
-  unsigned* dp_bar = nullptr;
-  unsigned long long* dp_trace = nullptr;  // optional phase trace (vx_dit_trace)
-  LmStackView dp_view;
+  PersistStack dp;               // persistent decoder forward state (dit_persist.cu)
 };
 
 namespace {
@@ -212,19 +197,6 @@ int launch_time_mlp(vx_dit* d, const uint16_t* w1, const float* b1, const uint16
   return VX_OK;
 }
 
-void dp_free(vx_dit* d) {
-  for (void* p : {(void*)d->dp_x, (void*)d->dp_x1, (void*)d->dp_xs, (void*)d->dp_xsi, (void*)d->dp_part,
-                  (void*)d->dp_rope, (void*)d->dp_segtab, (void*)d->dp_maps})
-    if (p) cudaFree(p);
-  for (auto& kv : d->dp_xmaps) cudaFree(kv.second);
-  d->dp_xmaps.clear();
-  d->dp_x = d->dp_x1 = nullptr;
-  d->dp_xs = d->dp_xsi = nullptr;
-  d->dp_part = d->dp_rope = nullptr;
-  d->dp_segtab = nullptr;
-  d->dp_maps = nullptr;
-}
-
 // Prepare the persistent forward for N sequences of S tokens (outside any capture): check the
 // shape once, allocate its buffers once for the most rows this DiT can take (so a captured graph
 // never sees them move), and build the activation tensor maps for this row count (kept per
@@ -235,93 +207,15 @@ bool dp_wanted(const vx_dit* d, int N, int S) {
 
 bool dp_prepare(vx_dit* d, int N, int S) {
   if (!dp_wanted(d, N, S)) return false;
-  vx_ctx* ctx = d->ctx;
-  if (d->dp_grid < 0) {
-    d->dp_grid = 0;
-    lm_stack_view(d->dec, &d->dp_view);
-    const LmStackView& v = d->dp_view;
-    const bool shape_ok = v.L > 0 && v.L <= 64 && v.H <= 1024 && v.H % 128 == 0 && v.nh * v.d == v.H && v.d <= 64 &&
-                          v.d % 4 == 0 && v.nkv > 0 && v.nh % v.nkv == 0 && ((v.nh + 2 * v.nkv) * v.d) % 128 == 0 &&
-                          (2 * v.I) % 128 == 0 && v.I % 64 == 0;
-    if (shape_ok && dit_persist_configure() == cudaSuccess) d->dp_grid = dit_persist_grid();
-    cudaGetLastError();
-    if (d->dp_grid > 0) {
-      const size_t H = v.H, I = v.I, qkv = (size_t)(v.nh + 2 * v.nkv) * v.d;
-      const int rmax = std::min(256, (d->max_rows * 16 + 31) / 32 * 32);
-      d->dp_rmax = rmax;
-      // segment tables: each GEMM kind deals its (tile, K chunk) pairs to ncta CTAs, at least
-      // `min_pairs` pairs each (env VX_DIT_PAIRS="qkv,o,gu,down" overrides the minimums)
-      const int tiles[DP_KINDS] = {(int)(qkv / 128), v.H / 128, (int)(2 * I / 128), v.H / 128};
-      const int kchs[DP_KINDS] = {v.H / 64, v.nh * v.d / 64, v.H / 64, (int)(I / 64)};
-      int min_pairs[DP_KINDS] = {2, 2, 1, 4};
-      if (const char* e = getenv("VX_DIT_PAIRS"))
-        sscanf(e, "%d,%d,%d,%d", &min_pairs[0], &min_pairs[1], &min_pairs[2], &min_pairs[3]);
-      std::vector<int> tab;
-      int max_segs = 0;
-      for (int k = 0; k < DP_KINDS; ++k) {
-        const int total = tiles[k] * kchs[k];
-        d->dp_ncta[k] = std::max(1, std::min(d->dp_grid, total / std::max(1, min_pairs[k])));
-        d->dp_tab_off[k] = (int)tab.size();
-        tab.resize(tab.size() + tiles[k] + 1 + d->dp_ncta[k]);
-        d->dp_tab_len = (int)tab.size();
-        max_segs = std::max(max_segs, dit_persist_segments(tiles[k], kchs[k], d->dp_ncta[k],
-                                                           tab.data() + d->dp_tab_off[k]));
-      }
-      std::vector<CUtensorMap> maps(4 * v.L);
-      bool ok = cudaMalloc(&d->dp_layers, sizeof(DitPersistLayer) * v.L) == cudaSuccess &&
-                cudaMemcpy(d->dp_layers, v.layers.data(), sizeof(DitPersistLayer) * v.L, cudaMemcpyHostToDevice) ==
-                    cudaSuccess &&
-                cudaMalloc(&d->dp_bar, (8 * v.L + 2) * sizeof(unsigned)) == cudaSuccess &&
-                cudaMemset(d->dp_bar, 0, (8 * v.L + 2) * sizeof(unsigned)) == cudaSuccess &&
-                cudaMalloc(&d->dp_x, (size_t)rmax * H * 4) == cudaSuccess &&
-                cudaMalloc(&d->dp_x1, (size_t)rmax * H * 4) == cudaSuccess &&
-                cudaMalloc(&d->dp_xs, 2 * (size_t)rmax * H * 2) == cudaSuccess &&
-                cudaMalloc(&d->dp_xsi, 2 * (size_t)rmax * I * 2) == cudaSuccess &&
-                cudaMemset(d->dp_xs, 0, 2 * (size_t)rmax * H * 2) == cudaSuccess &&
-                cudaMemset(d->dp_xsi, 0, 2 * (size_t)rmax * I * 2) == cudaSuccess &&
-                cudaMalloc(&d->dp_part, (size_t)max_segs * rmax * 128 * 4) == cudaSuccess &&
-                cudaMalloc(&d->dp_rope, 2 * 16 * 64 * 4) == cudaSuccess &&
-                cudaMalloc(&d->dp_segtab, tab.size() * 4) == cudaSuccess &&
-                cudaMemcpy(d->dp_segtab, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
-                cudaMalloc(&d->dp_maps, sizeof(CUtensorMap) * 4 * v.L) == cudaSuccess;
-      for (int l = 0; ok && l < v.L; ++l) {
-        const DitPersistLayer& w = v.layers[l];
-        ok = tc_map_2d(&maps[4 * l + 0], w.wqkv, (int)qkv, (int)H, 128) == cudaSuccess &&
-             tc_map_2d(&maps[4 * l + 1], w.wo, (int)H, v.nh * v.d, 128) == cudaSuccess &&
-             tc_map_2d(&maps[4 * l + 2], w.wgu, (int)(2 * I), (int)H, 128) == cudaSuccess &&
-             tc_map_2d(&maps[4 * l + 3], w.wd, (int)H, (int)I, 128) == cudaSuccess;
-      }
-      ok = ok && cudaMemcpy(d->dp_maps, maps.data(), sizeof(CUtensorMap) * maps.size(), cudaMemcpyHostToDevice) ==
-                     cudaSuccess;
-      if (ok && getenv("VX_DIT_TRACE"))
-        ok = cudaMalloc(&d->dp_trace, (size_t)(8 * v.L + 1) * d->dp_grid * 4 * 8) == cudaSuccess &&
-             cudaMemset(d->dp_trace, 0, (size_t)(8 * v.L + 1) * d->dp_grid * 4 * 8) == cudaSuccess;
-      if (!ok) {
-        cudaGetLastError();
-        dp_free(d);
-        d->dp_grid = 0;
-        fail(ctx, VX_ERR_OOM, "persistent DiT buffers: allocation or tensor maps failed");
-      }
-    }
+  if (d->dp.grid < 0) {
+    LmStackView v;
+    lm_stack_view(d->dec, &v);
+    bool oom = false;
+    persist_stack_prepare(d->dp, v, d->max_rows * 16, getenv("VX_DIT_TRACE") != nullptr, &oom);
+    if (oom) fail(d->ctx, VX_ERR_OOM, "persistent DiT buffers: allocation or tensor maps failed");
   }
-  const int R = N * S;
-  if (d->dp_grid <= 0 || S > 16 || R > d->dp_rmax) return false;
-  const int rpad = (R + 31) / 32 * 32;
-  if (d->dp_xmaps.count(rpad)) return true;
-  const LmStackView& v = d->dp_view;
-  CUtensorMap xm[2];
-  CUtensorMap* dev = nullptr;
-  const bool ok = tc_map_3d(&xm[0], d->dp_xs, 2, rpad, v.H, rpad) == cudaSuccess &&
-                  tc_map_3d(&xm[1], d->dp_xsi, 2, rpad, v.I, rpad) == cudaSuccess &&
-                  cudaMalloc(&dev, sizeof(xm)) == cudaSuccess &&
-                  cudaMemcpy(dev, xm, sizeof(xm), cudaMemcpyHostToDevice) == cudaSuccess;
-  if (!ok) {
-    cudaGetLastError();
-    if (dev) cudaFree(dev);
-    return false;
-  }
-  d->dp_xmaps[rpad] = dev;
-  return true;
+  if (d->dp.grid <= 0 || !d->dp.seq_ok || N * S > d->dp.rmax) return false;
+  return persist_stack_rows(d->dp, (N * S + 31) / 32 * 32);
 }
 
 // The decoder stack (MiniCpmModel::forward, non-causal) over N sequences of S rows of `in`,
@@ -330,46 +224,9 @@ bool dp_prepare(vx_dit* d, int N, int S) {
 int dit_decoder_forward(vx_dit* d, const float* in, int N, int S, float* out, cudaStream_t st) {
   vx_ctx* ctx = d->ctx;
   const int R = N * S;
-  const auto xm = d->dp_grid > 0 && dp_wanted(d, N, S) ? d->dp_xmaps.find((R + 31) / 32 * 32) : d->dp_xmaps.end();
-  if (xm != d->dp_xmaps.end()) {
-    const LmStackView& v = d->dp_view;
-    DitPersistArgs a = {};
-    a.L = v.L;
-    a.H = v.H;
-    a.I = v.I;
-    a.nh = v.nh;
-    a.nkv = v.nkv;
-    a.d = v.d;
-    a.S = S;
-    a.N = N;
-    a.R = R;
-    a.Rpad = xm->first;
-    a.eps = v.eps;
-    a.res_scale = v.res_scale;
-    a.attn_scale = v.attn_scale;
-    a.layers = d->dp_layers;
-    a.wmaps = d->dp_maps;
-    a.xmaps = xm->second;
-    a.rope = v.rope;
-    a.final_norm = v.norm_w;
-    a.x_in = in;
-    a.x = d->dp_x;
-    a.x1 = d->dp_x1;
-    a.out = out;
-    a.xs = d->dp_xs;
-    a.xs_i = d->dp_xsi;
-    a.part = d->dp_part;
-    a.rope_tab = d->dp_rope;
-    a.segtab = d->dp_segtab;
-    a.tab_len = d->dp_tab_len;
-    for (int k = 0; k < DP_KINDS; ++k) {
-      a.tab_off[k] = d->dp_tab_off[k];
-      a.ncta[k] = d->dp_ncta[k];
-    }
-    a.bar = d->dp_bar;
-    a.err = ctx->dev_err;
-    a.trace = d->dp_trace;
-    VX_CUDA(ctx, launch_dit_persist(a, d->dp_grid, st));
+  if (d->dp.grid > 0 && d->dp.seq_ok && dp_wanted(d, N, S) && d->dp.xmaps.count((R + 31) / 32 * 32)) {
+    const DitPersistArgs a = persist_stack_args(d->dp, N, S, in, out, ctx->dev_err);
+    VX_CUDA(ctx, launch_dit_persist(a, d->dp.grid, st));
     return VX_OK;
   }
   return vx_lm_forward(d->dec, in, N, S, 0, 0, out);
@@ -519,10 +376,7 @@ void vx_dit_destroy(vx_dit* d) {
   cudaSetDevice(d->ctx->device);
   cudaStreamSynchronize(d->ctx->stream);
   if (d->solve_exec) cudaGraphExecDestroy(d->solve_exec);
-  dp_free(d);
-  if (d->dp_layers) cudaFree(d->dp_layers);
-  if (d->dp_bar) cudaFree(d->dp_bar);
-  if (d->dp_trace) cudaFree(d->dp_trace);
+  persist_stack_free(d->dp);
   if (d->dec) vx_lm_destroy(d->dec);
   void* ptrs[] = {d->in_w, d->cond_w, d->out_w, d->t1_w, d->t2_w, d->dt1_w, d->dt2_w, d->in_b, d->cond_b,
                   d->out_b, d->t1_b, d->t2_b, d->dt1_b, d->dt2_b, d->freqs, d->seq, d->hid, d->temb,
@@ -672,12 +526,12 @@ int cfm_solve_enqueue(vx_dit* d, const float* mu, const float* cond, const float
 vx_ctx* dit_ctx(vx_dit* d) { return d->ctx; }
 int dit_in_channels(const vx_dit* d) { return d->C; }
 int dit_trace_copy(vx_dit* d, unsigned long long* out, int n, int* grid, int* phases) {
-  if (!d || !out || !grid || !phases || !d->dp_trace) return VX_ERR_ARG;
-  *grid = d->dp_grid;
-  *phases = 8 * d->dp_view.L + 1;
+  if (!d || !out || !grid || !phases || !d->dp.trace) return VX_ERR_ARG;
+  *grid = d->dp.grid;
+  *phases = 8 * d->dp.view.L + 1;
   const size_t need = (size_t)*grid * *phases * 4;
   if ((size_t)n < need) return VX_ERR_ARG;
-  VX_CUDA(d->ctx, cudaMemcpy(out, d->dp_trace, need * 8, cudaMemcpyDeviceToHost));
+  VX_CUDA(d->ctx, cudaMemcpy(out, d->dp.trace, need * 8, cudaMemcpyDeviceToHost));
   return VX_OK;
 }
 int dit_hidden_size(const vx_dit* d) { return d->H; }

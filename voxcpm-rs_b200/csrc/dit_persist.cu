@@ -17,13 +17,15 @@
 // attention.rs:55-88, mod.rs:54-68).  Phases are separated by a grid barrier (release /
 // acquire counters; all CTAs are resident).
 //
-// GEMM phases: the weights are the A operand (128-row tiles x 64-element K chunks, TMA,
-// SWIZZLE_128B, no multicast); the activations are the B operand: the row phase before wrote
-// them as two bf16 planes x = hi + lo ([2][Rpad][K], token-major), so each K chunk is two MMAs
-// (hi, lo) into one f32 TMEM accumulator of Rpad columns.  A phase's (tile, K chunk) pairs are
-// dealt to its CTAs in contiguous runs, so a tile's K range may be split over CTAs: each run
-// inside one tile (a segment) stores its f32 partial tile into its own slot of the partial
-// buffer with plain stores, and the phase that consumes the GEMM sums a tile's slots in slot
+// GEMM phases: the weights are the A operand (units of 256 rows = two 128-row MMA tiles, one
+// 256 x 64 TMA box per K chunk, SWIZZLE_128B, no multicast); the activations are the B
+// operand: the row phase before wrote them as two bf16 planes x = hi + lo ([2][Rpad][K],
+// token-major), both fetched by one 3-D box, so each K chunk is four MMAs (two tiles x hi, lo)
+// into two f32 TMEM accumulators of Rpad columns.  Two copies per 32 KB of weights: the TMA
+// engine's per-SM copy rate, not the bytes, bounds these phases at few activation rows.  A
+// phase's (unit, K chunk) pairs are dealt to its CTAs in contiguous runs, so a unit's K range
+// may be split over CTAs: each run inside one unit (a segment) stores its f32 partial tile
+// into its own slot of the partial buffer with plain stores, and the phase that consumes the GEMM sums a tile's slots in slot
 // order.  No atomics: the sum, and so the forward, does not depend on the order in which CTAs
 // finish (deterministic).  Warp 4 issues the TMA loads, warp 5 the MMAs, warps 0-3 read TMEM;
 // the row phases run on warps 0-7 (RES) or all twelve warps (attention, SiLU*up): their partial
@@ -48,12 +50,19 @@ constexpr int DP_WARPS = 12;
 constexpr int DP_THREADS = DP_WARPS * 32;
 constexpr int DP_EPI_THREADS = 128;  // warps 0-3: GEMM epilogue (TMEM lanes 0-127)
 constexpr int DP_RES_THREADS = 256;  // warps 0-7: RES rows, one float4 group of a row each (H <= 1024)
-constexpr int DP_A_BYTES = TC_BM * TC_BK * 2;
+constexpr int DP_UM_MAX = 2 * TC_BM;  // weight rows per unit: one or two 128-row MMA tiles (a.um)
 constexpr int DP_SMAX = 16;          // tokens per sequence
 constexpr int DP_QS = 68;            // shared-memory row stride of q, k, v (floats; float4 aligned)
 constexpr int DP_SEGTAB_MAX = 2048;  // ints of segment tables held in shared memory
 constexpr int DP_HPU = 2;            // most query heads per attention unit
 constexpr int DP_ATT_FLOATS = (DP_HPU + 2) * DP_SMAX * DP_QS + DP_HPU * (DP_SMAX * DP_SMAX + DP_SMAX);
+// decode attention scratch: q [nq][d], k, v [d], cos / sin [d/2] (nq <= 12 warps, d = 128);
+// then two buffers of a 32-position K tile and V tile
+constexpr int DP_DEC_NQ = 12, DP_DEC_D = 128, DP_DEC_TILE = 32;
+constexpr int DP_DEC_TILE_OFF = 2048;  // floats; >= the scratch above, a multiple of 4
+constexpr int DP_DEC_FLOATS = DP_DEC_TILE_OFF + 2 * 2 * DP_DEC_TILE * DP_DEC_D;
+static_assert(DP_DEC_NQ * DP_DEC_D + 3 * DP_DEC_D <= DP_DEC_TILE_OFF, "decode scratch");
+__host__ __device__ constexpr int dp_att_floats(int mode) { return mode == DP_ATT_DECODE ? DP_DEC_FLOATS : DP_ATT_FLOATS; }
 enum { PH_RES_A, PH_QKV, PH_ATT, PH_O, PH_RES_B, PH_GU, PH_ACT, PH_DOWN, PH_N };
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -71,6 +80,7 @@ struct Sm {
   uint64_t* seg_done;
   uint64_t* acc_free;
   uint64_t* fin;          // the MMA thread's last commit before TMEM is freed
+  uint64_t* att_bar;      // [2] decode attention: K / V tile copies
   uint32_t* tmem_slot;
   volatile int* flags;    // [0] abort
   int* segtab;            // copy of the segment tables
@@ -101,6 +111,20 @@ __device__ __forceinline__ void res_sync() {
 __device__ __forceinline__ void cta_sync() {
   __syncwarp();
   named_sync(2, DP_THREADS);
+}
+// Barrier 2 that ORs a per-thread flag (a uniform decision over the whole CTA).
+__device__ __forceinline__ bool cta_or(bool v) {
+  int r;
+  __syncwarp();
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 2, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((int)v), "r"(DP_THREADS)
+      : "memory");
+  return r != 0;
 }
 
 // Grid barrier: thread 0 waits (bounded) for `target` arrivals on cnt, then the CTA syncs.
@@ -152,10 +176,11 @@ struct PRange {
 struct Parts {
   const float* p;        // [segments][Rpad][128]
   const int* seg_off;    // [tiles + 1], in shared memory (plain loads: not the global-only __ldg)
-  size_t stride;         // Rpad * 128
+  size_t stride;         // Rpad * um
+  int ush;               // log2 of the weight rows per unit (7 or 8)
   __device__ PRange at(int r, int c) const {
-    const int t = c >> 7, s0 = seg_off[t];
-    return {p + (size_t)s0 * stride + (size_t)r * 128 + (c & 127), seg_off[t + 1] - s0};
+    const int t = c >> ush, s0 = seg_off[t];
+    return {p + (size_t)s0 * stride + ((size_t)r << ush) + (c & ((1 << ush) - 1)), seg_off[t + 1] - s0};
   }
 };
 
@@ -184,7 +209,7 @@ __device__ __forceinline__ void psum(const PRange* x, size_t stride, float4* o) 
 }
 
 __device__ __forceinline__ Parts parts_of(const DitPersistArgs& a, const Sm& sm, int kind) {
-  return Parts{a.part, sm.segtab + a.tab_off[kind], (size_t)a.Rpad * 128};
+  return Parts{a.part, sm.segtab + a.tab_off[kind], (size_t)a.Rpad * a.um, a.um == DP_UM_MAX ? 8 : 7};
 }
 
 // Optional timeline: %globaltimer into trace [phase][CTA][4] (0: phase start, 1: first segment's
@@ -247,58 +272,83 @@ __device__ __forceinline__ void store_split4(uint16_t* xs, size_t plane, size_t 
 
 // RES rows: v = base[r] + s * (the GEMM output, summed from its partials; none for the input
 // rows), optionally stored to `store`; then RMSNorm(v) * w into the split operand (K = H), or
-// into final_out.  Run by the DP_RES_THREADS threads: thread t holds channels 4t..4t+3 of two
-// rows at a time (rows r and r + grid), so both rows' partial loads are in flight together.
+// into final_out.  Run by the DP_RES_THREADS threads.  NG = 1 (H <= 1024): thread t holds
+// channels 4t.. of two rows at a time (rows r and r + grid); NG = 2 (H <= 2048): channels
+// 4t.. and 1024 + 4t.. of one row.  Either way two partial ranges are summed together.
+template <int NG>
 __device__ void res_norm_rows(const DitPersistArgs& a, const float* base, const Parts* q, float* store,
                               const float* w, uint16_t* xs, float* final_out, const Sm& sm) {
+  constexpr int NR = NG == 1 ? 2 : 1;  // rows per pass
   const int H = a.H, G = gridDim.x;
   const size_t plane = (size_t)a.Rpad * H;
-  const int c = threadIdx.x * 4;
-  const bool on = c < H;
-  for (int r0 = blockIdx.x; r0 < a.R; r0 += 2 * G) {
-    const int rr[2] = {r0, r0 + G};
-    const bool live[2] = {on, on && r0 + G < a.R};
-    float4 v[2];
+  int cc[2];
+  float4 g[2];
 #pragma unroll
-    for (int k = 0; k < 2; ++k)
-      v[k] = live[k] ? ldcg4(base + (size_t)rr[k] * H + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < 2; ++k) {
+    cc[k] = (int)threadIdx.x * 4 + (NG == 2 ? k * 4 * DP_RES_THREADS : 0);
+    g[k] = cc[k] < H ? __ldg(reinterpret_cast<const float4*>(w + cc[k])) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int r0 = blockIdx.x; r0 < a.R; r0 += NR * G) {
+    int rr[2];
+    bool live[2];
+    float4 v[2];  // range i: row rr[i], channels cc[i]
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      rr[i] = NG == 1 ? r0 + i * G : r0;
+      live[i] = rr[i] < a.R && cc[i] < H;
+      v[i] = live[i] ? ldcg4(base + (size_t)rr[i] * H + cc[i]) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     if (q) {
-      PRange x[2] = {live[0] ? q->at(rr[0], c) : PRange{nullptr, 0}, live[1] ? q->at(rr[1], c) : PRange{nullptr, 0}};
+      PRange x[2] = {live[0] ? q->at(rr[0], cc[0]) : PRange{nullptr, 0}, live[1] ? q->at(rr[1], cc[1]) : PRange{nullptr, 0}};
       float4 o[2];
       psum<2, 4>(x, q->stride, o);
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        v[k].x += o[k].x * a.res_scale;
-        v[k].y += o[k].y * a.res_scale;
-        v[k].z += o[k].z * a.res_scale;
-        v[k].w += o[k].w * a.res_scale;
+      for (int i = 0; i < 2; ++i) {
+        v[i].x += o[i].x * a.res_scale;
+        v[i].y += o[i].y * a.res_scale;
+        v[i].z += o[i].z * a.res_scale;
+        v[i].w += o[i].w * a.res_scale;
       }
     }
-    float ss[2];
+    float ss[2] = {0.f, 0.f};  // per row (NG = 1) or both halves of one row (NG = 2, summed below)
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      ss[k] = 0.f;
-      if (!live[k]) continue;
-      if (store) *reinterpret_cast<float4*>(store + (size_t)rr[k] * H + c) = v[k];
-      ss[k] = fmaf(v[k].x, v[k].x, ss[k]);
-      ss[k] = fmaf(v[k].y, v[k].y, ss[k]);
-      ss[k] = fmaf(v[k].z, v[k].z, ss[k]);
-      ss[k] = fmaf(v[k].w, v[k].w, ss[k]);
+    for (int i = 0; i < 2; ++i) {
+      if (!live[i]) continue;
+      if (store) *reinterpret_cast<float4*>(store + (size_t)rr[i] * H + cc[i]) = v[i];
+      float t = ss[i];
+      t = fmaf(v[i].x, v[i].x, t);
+      t = fmaf(v[i].y, v[i].y, t);
+      t = fmaf(v[i].z, v[i].z, t);
+      t = fmaf(v[i].w, v[i].w, t);
+      ss[i] = t;
+    }
+    if (NG == 2) {
+      ss[0] += ss[1];
+      ss[1] = 0.f;
     }
     res_sum2(ss[0], ss[1], sm.red);
-    const float4 g = on ? __ldg(reinterpret_cast<const float4*>(w + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      if (!live[k]) continue;
-      const float inv = 1.0f / sqrtf(ss[k] / (float)H + a.eps);
-      const float4 y = make_float4((v[k].x * inv) * g.x, (v[k].y * inv) * g.y, (v[k].z * inv) * g.z,
-                                   (v[k].w * inv) * g.w);
+    for (int i = 0; i < 2; ++i) {
+      if (!live[i]) continue;
+      const float inv = 1.0f / sqrtf((NG == 1 ? ss[i] : ss[0]) / (float)H + a.eps);
+      const float4 gw = g[i];
+      const float4 y = make_float4((v[i].x * inv) * gw.x, (v[i].y * inv) * gw.y, (v[i].z * inv) * gw.z,
+                                   (v[i].w * inv) * gw.w);
+      const size_t at = (size_t)rr[i] * H + cc[i];
       if (final_out)
-        *reinterpret_cast<float4*>(final_out + (size_t)rr[k] * H + c) = y;
+        *reinterpret_cast<float4*>(final_out + at) = y;
       else
-        store_split4(xs, plane, (size_t)rr[k] * H + c, y);
+        store_split4(xs, plane, at, y);
     }
   }
+}
+
+__device__ void res_rows(const DitPersistArgs& a, const float* base, const Parts* q, float* store, const float* w,
+                         uint16_t* xs, float* final_out, const Sm& sm) {
+  if (a.H <= 4 * DP_RES_THREADS)
+    res_norm_rows<1>(a, base, q, store, w, xs, final_out, sm);
+  else
+    res_norm_rows<2>(a, base, q, store, w, xs, final_out, sm);
 }
 
 // LongRoPE cos / sin (x scaling factor) at positions 0..S-1 (rope.rs:76-95), f64 as the
@@ -411,6 +461,173 @@ __device__ void att_unit(const DitPersistArgs& a, const Parts& q, int n, int h0,
   cta_sync();  // the scratch is free for the next unit
 }
 
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Decode attention for sequence n's new row at position pos and KV head g with its
+// nq = nh / nkv query heads (attention.rs:91-154): q, k, v summed from the QKV partials;
+// LongRoPE at pos (f64 angles, rope.rs:76-95); k, v written into the static cache at pos
+// (cache.rs:47-58); then cache positions 0..pos in 32-position K / V tiles that bulk copies
+// bring into shared memory (two buffers: the next tile lands while this one is used).  Warp h
+// owns query head h, each lane 4 of its 128 dims: a tile's 32 scores are the lanes' partial
+// dot products summed by a butterfly reduce-scatter (31 shuffles; lane j ends with position
+// j), then an online softmax in registers (running max and sum: the max-subtracted softmax of
+// attention.rs:186-191, accumulated tile by tile) and P V with the probabilities broadcast by
+// shuffles.  Output into the split operand (K = nh * d).  Run by all DP_THREADS threads
+// (warps >= nq only help with the loads); `uses` counts each tile buffer's completed copies
+// (uniform over the CTA).  Returns false if a copy wait gave up (error recorded).
+__device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, int g, int l, int pos, const Sm& sm,
+                                unsigned* uses, int ph) {
+  constexpr int d = DP_DEC_D, half = d / 2, d4 = d / 4;
+  const int nq = a.nh / a.nkv, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* qs = sm.att;  // [nq][d], then k [d], v [d]
+  float* kn = qs + nq * d;
+  float* vn = kn + d;
+  float* cs = vn + d;  // [half] cos, [half] sin
+  float* sn = cs + half;
+  float* tiles = sm.att + DP_DEC_TILE_OFF;
+  const int cells = (nq + 2) * d4;
+  for (int i0 = tid; i0 < cells; i0 += 2 * DP_THREADS) {
+    PRange x[2];
+    int dst[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = i0 + k * DP_THREADS;
+      x[k] = PRange{nullptr, 0};
+      dst[k] = -1;
+      if (i < cells) {
+        const int which = i / d4, e = (i % d4) * 4;
+        const int c = which < nq ? (g * nq + which) * d : which == nq ? (a.nh + g) * d : (a.nh + a.nkv + g) * d;
+        x[k] = q.at(n, c + e);
+        dst[k] = which * d + e;
+      }
+    }
+    float4 o[2];
+    psum<2, 8>(x, q.stride, o);
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+      if (dst[k] >= 0) *reinterpret_cast<float4*>(qs + dst[k]) = o[k];
+  }
+  if (a.rope && tid < half) {
+    const double f = ((double)pos * a.rope->inv_freq[tid]) / a.rope->ext[tid];
+    double sd, cd;
+    sincos(f, &sd, &cd);
+    cs[tid] = (float)(cd * a.rope->scaling_factor);
+    sn[tid] = (float)(sd * a.rope->scaling_factor);
+  }
+  cta_sync();
+  if (a.rope) {  // rows 0..nq-1 are the queries, row nq the key (one rotation pair per thread)
+    for (int i = tid; i < (nq + 1) * half; i += DP_THREADS) {
+      float* v = qs + (i / half) * d;
+      const int j = i % half;
+      const float c = cs[j], si = sn[j];
+      const float x1 = v[j], x2 = v[j + half];
+      v[j] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(-x2, si));
+      v[j + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, si));
+    }
+    cta_sync();
+  }
+  const size_t seq = ((size_t)n * a.nkv + g) * a.max_len * d;
+  float* kc = a.kcache + (size_t)l * a.kv_layer_stride + seq;
+  float* vc = a.vcache + (size_t)l * a.kv_layer_stride + seq;
+  for (int e = tid; e < d; e += DP_THREADS) {
+    kc[(size_t)pos * d + e] = kn[e];
+    vc[(size_t)pos * d + e] = vn[e];
+  }
+  // the bulk copies below read the row just written through the generic proxy
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  cta_sync();
+  if (tid == 0) trace_at(a, ph, 1);
+  const int nt = pos / DP_DEC_TILE + 1;
+  unsigned issued[2] = {uses[0], uses[1]};
+  auto issue = [&](int t) {  // thread 0
+    const int rows = min(DP_DEC_TILE, pos + 1 - t * DP_DEC_TILE), b = t & 1;
+    const uint32_t bytes = (uint32_t)rows * d * 4;
+    float* kt = tiles + b * 2 * DP_DEC_TILE * d;
+    mbar_arrive_expect_tx(&sm.att_bar[b], 2 * bytes);
+    bulk_g2s(kt, kc + (size_t)t * DP_DEC_TILE * d, bytes, &sm.att_bar[b]);
+    bulk_g2s(kt + DP_DEC_TILE * d, vc + (size_t)t * DP_DEC_TILE * d, bytes, &sm.att_bar[b]);
+    ++issued[b];
+  };
+  if (tid == 0) issue(0);
+  // warp h < nq: query head h, lane: dims 4 lane .. 4 lane + 3
+  const bool head = warp < nq;
+  const float4 qv = head ? *reinterpret_cast<const float4*>(qs + warp * d + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  float m_run = -FLT_MAX, l_run = 0.f;
+  bool good = true;
+  for (int t = 0; t < nt; ++t) {
+    if (tid == 0 && t + 1 < nt) issue(t + 1);  // its buffer was released by the sync ending t - 1
+    const int b = t & 1, rows = min(DP_DEC_TILE, pos + 1 - t * DP_DEC_TILE);
+    const bool w = mbar_wait(&sm.att_bar[b], uses[b] & 1, a.err);
+    ++uses[b];
+    if (tid == 0 && t == 0) trace_at(a, ph, 3);
+    if (cta_or(!w)) {
+      good = false;
+      break;
+    }
+    if (head) {
+      const float* kt = tiles + b * 2 * DP_DEC_TILE * d;
+      const float* vt = kt + DP_DEC_TILE * d;
+      float v[DP_DEC_TILE];  // this lane's partial dot product with every position of the tile
+#pragma unroll
+      for (int j = 0; j < DP_DEC_TILE; ++j) {
+        const float4 k4 = j < rows ? *reinterpret_cast<const float4*>(kt + j * d + lane * 4)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[j] = fmaf(qv.x, k4.x, fmaf(qv.y, k4.y, fmaf(qv.z, k4.z, qv.w * k4.w)));
+      }
+      // reduce-scatter: after the step with offset `off`, lane keeps the half of the remaining
+      // positions selected by its bit `off`; lane j ends with position j's full sum in v[0]
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < off; ++i) {
+          const float send = upper ? v[i] : v[i + off];
+          const float keep = upper ? v[i + off] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      const float sv = lane < rows ? v[0] * a.attn_scale : -FLT_MAX;
+      const float m_new = fmaxf(m_run, warp_max(sv));
+      const float p = lane < rows ? expf(sv - m_new) : 0.f;
+      const float al = expf(m_run - m_new);
+      l_run = l_run * al + warp_sum(p);
+      m_run = m_new;
+      o.x *= al;
+      o.y *= al;
+      o.z *= al;
+      o.w *= al;
+      for (int j = 0; j < rows; ++j) {
+        const float pj = __shfl_sync(0xffffffffu, p, j);
+        const float4 v4 = *reinterpret_cast<const float4*>(vt + j * d + lane * 4);
+        o.x = fmaf(pj, v4.x, o.x);
+        o.y = fmaf(pj, v4.y, o.y);
+        o.z = fmaf(pj, v4.z, o.z);
+        o.w = fmaf(pj, v4.w, o.w);
+      }
+    }
+    cta_sync();  // every reader of this buffer is done before the copy issued at t + 1 reuses it
+  }
+  if (!good) {  // copies still in flight land before the CTA leaves
+    if (tid == 0)
+      for (int b = 0; b < 2; ++b)
+        for (; uses[b] < issued[b]; ++uses[b]) mbar_wait(&sm.att_bar[b], uses[b] & 1, a.err);
+    cta_sync();
+    return false;
+  }
+  if (head) {
+    const float iv = 1.0f / l_run;
+    store_split4(a.xs, (size_t)a.Rpad * a.nh * d, (size_t)n * a.nh * d + (g * nq + warp) * d + lane * 4,
+                 make_float4(o.x * iv, o.y * iv, o.z * iv, o.w * iv));
+  }
+  cta_sync();  // the scratch is free for the next unit
+  return true;
+}
+
 // ACT: silu(gate) * up, both summed from the GU partials, into the split operand (K = I);
 // two groups of four elements per thread in flight; run by all DP_THREADS threads.
 __device__ void act_rows(const DitPersistArgs& a, const Parts& q) {
@@ -463,34 +680,43 @@ __device__ GemmPh gemm_phase(const DitPersistArgs& a, int kind, int l) {
   else { g.n_out = a.H; K = a.I; wi = 3; g.gk = DP_KIND_DOWN; g.xmap = &a.xmaps[1]; }
   g.wmap = &a.wmaps[l * 4 + wi];
   g.kch = K / TC_BK;
-  const int total = (g.n_out / TC_BM) * g.kch, nc = a.ncta[g.gk], b = blockIdx.x;
+  const int total = (g.n_out / a.um) * g.kch, nc = a.ncta[g.gk], b = blockIdx.x;  // a.um == the kernel's UM
   g.c0 = b < nc ? (int)((long long)b * total / nc) : 0;
   g.c1 = b < nc ? (int)((long long)(b + 1) * total / nc) : 0;
   return g;
 }
 
+__device__ __forceinline__ void tmap_prefetch(const CUtensorMap* m) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
+}
+
+// MODE: the ATT phase's attention (DP_ATT_SEQ or DP_ATT_DECODE); one instantiation each, so
+// neither pays the other's registers.
+template <int MODE, int UM>
 __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPersistArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int plane_bytes = a.Rpad * TC_BK * 2;
-  const int stage_bytes = DP_A_BYTES + 2 * plane_bytes;
+  const int a_bytes = UM * TC_BK * 2;                  // one um x 64 weight box
+  const int stage_bytes = a_bytes + 2 * plane_bytes;     // weights, then the hi and lo planes
   Sm sm;
   sm.stages = base;
   sm.att = reinterpret_cast<float*>(base + (size_t)a.nst * stage_bytes);
-  sm.red = sm.att + DP_ATT_FLOATS;
+  sm.red = sm.att + dp_att_floats(MODE);
   sm.full = reinterpret_cast<uint64_t*>(sm.red + 32);
   sm.empty = sm.full + a.nst;
   sm.seg_done = sm.empty + a.nst;
   sm.acc_free = sm.seg_done + 1;
   sm.fin = sm.acc_free + 1;
-  sm.tmem_slot = reinterpret_cast<uint32_t*>(sm.fin + 1);
+  sm.att_bar = sm.fin + 1;
+  sm.tmem_slot = reinterpret_cast<uint32_t*>(sm.att_bar + 2);
   sm.flags = reinterpret_cast<volatile int*>(sm.tmem_slot + 2);
   sm.segtab = const_cast<int*>(reinterpret_cast<volatile int*>(sm.flags + 2));
   for (int i = threadIdx.x; i < a.tab_len; i += DP_THREADS) sm.segtab[i] = __ldg(a.segtab + i);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint32_t ncols = 32;
-  while ((int)ncols < a.Rpad) ncols <<= 1;
+  uint32_t ncols = 32;  // um / 128 accumulators of Rpad columns (at most 512 columns)
+  while ((int)ncols < (UM / TC_BM) * a.Rpad) ncols <<= 1;
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.nst; ++s) {
       mbar_init(&sm.full[s], 1);
@@ -499,6 +725,8 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
     mbar_init(sm.seg_done, 1);
     mbar_init(sm.acc_free, DP_EPI_THREADS);
     mbar_init(sm.fin, 1);
+    mbar_init(&sm.att_bar[0], 1);
+    mbar_init(&sm.att_bar[1], 1);
     sm.flags[0] = 0;
     fence_barrier_init();
   }
@@ -517,6 +745,13 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
   // per-role persistent state: ring position (producer, MMA), segments done
   int prod_i = 0, mma_i = 0, seg_g = 0;
   int pre_n = 0, pre_kind = 0, pre_l = 0;  // producer: weight tiles of the next GEMM phase already armed
+  unsigned att_uses[2] = {0u, 0u};         // decode attention: completed copies per tile buffer
+  const int dec_pos = MODE == DP_ATT_DECODE ? *a.pos : 0;
+  if (warp == 4 && lane == 0) {  // descriptors of layer 0's weight maps and the activation maps
+    for (int i = 0; i < 4; ++i) tmap_prefetch(&a.wmaps[i]);
+    tmap_prefetch(&a.xmaps[0]);
+    tmap_prefetch(&a.xmaps[1]);
+  }
   bool ok = true;
   const int G = gridDim.x;
   const int nph = a.L * PH_N + 1;
@@ -528,12 +763,15 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
     }
     if (threadIdx.x == 0) trace_at(a, ph, 0);
     const int l = ph / PH_N, kind = ph == nph - 1 ? -1 : ph % PH_N;
+    if (warp == 4 && lane == 0 && kind == PH_RES_A && l + 1 < a.L)  // the next layer's weight maps
+      for (int i = 0; i < 4; ++i) tmap_prefetch(&a.wmaps[(l + 1) * 4 + i]);
     const DitPersistLayer* w = a.layers + (l < a.L ? l : 0);
     const bool gemm = kind == PH_QKV || kind == PH_O || kind == PH_GU || kind == PH_DOWN;
     if (!gemm) {
       if (warp == 4 && lane == 0 && kind >= 0) {
         // the next phase is a GEMM: its first weight tiles do not depend on this phase, so they
         // stream into the (free) ring during it; the activation planes follow after the barrier
+        if (kind != PH_ATT) trace_at(a, ph, 3);
         const GemmPh g = gemm_phase(a, kind + 1, l);
         pre_kind = kind + 1;
         pre_l = l;
@@ -545,32 +783,41 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
             break;
           }
           mbar_arrive_expect_tx(&sm.full[s], stage_bytes);
-          tma_load_2d(sm.stages + (size_t)s * stage_bytes, g.wmap, (c % g.kch) * TC_BK, (c / g.kch) * TC_BM,
+          tma_load_2d(sm.stages + (size_t)s * stage_bytes, g.wmap, (c % g.kch) * TC_BK, (c / g.kch) * UM,
                       &sm.full[s]);
           pre_n = j + 1;
         }
+        if (kind != PH_ATT) trace_at(a, ph, 1);
       }
-      if (kind == PH_ATT) {  // all warps; two heads per unit when one per unit would not fit the grid
+      if (kind == PH_ATT) {  // all warps
         const Parts q = parts_of(a, sm, DP_KIND_QKV);
-        const int hpu = a.N * a.nh > G && (a.nh / a.nkv) % DP_HPU == 0 ? DP_HPU : 1, per = a.nh / hpu;
-        for (int u = blockIdx.x; u < a.N * per; u += G) att_unit(a, q, u / per, (u % per) * hpu, hpu, ph, sm);
+        if constexpr (MODE == DP_ATT_DECODE) {  // unit = (sequence, KV head)
+          for (int u = blockIdx.x; u < a.N * a.nkv; u += G)
+            if (!att_decode_unit(a, q, u / a.nkv, u % a.nkv, l, dec_pos, sm, att_uses, ph)) {
+              if (threadIdx.x == 0) sm.flags[0] = 1;
+              break;
+            }
+        } else {  // two heads per unit when one per unit would not fit the grid
+          const int hpu = a.N * a.nh > G && (a.nh / a.nkv) % DP_HPU == 0 ? DP_HPU : 1, per = a.nh / hpu;
+          for (int u = blockIdx.x; u < a.N * per; u += G) att_unit(a, q, u / per, (u % per) * hpu, hpu, ph, sm);
+        }
       } else if (kind == PH_ACT) {  // all warps
         act_rows(a, parts_of(a, sm, DP_KIND_GU));
       } else if (threadIdx.x < DP_RES_THREADS) {
         if (kind == -1) {  // final: RMSNorm(x1 + s * down) with the final norm weight
           const Parts q = parts_of(a, sm, DP_KIND_DOWN);
-          res_norm_rows(a, a.x1, &q, nullptr, a.final_norm, nullptr, a.out, sm);
+          res_rows(a, a.x1, &q, nullptr, a.final_norm, nullptr, a.out, sm);
         } else if (kind == PH_RES_A) {
           if (l == 0) {
-            if (a.rope) rope_table(a);
-            res_norm_rows(a, a.x_in, nullptr, a.x, w->ln_in, a.xs, nullptr, sm);
+            if (MODE == DP_ATT_SEQ && a.rope) rope_table(a);
+            res_rows(a, a.x_in, nullptr, a.x, w->ln_in, a.xs, nullptr, sm);
           } else {
             const Parts q = parts_of(a, sm, DP_KIND_DOWN);
-            res_norm_rows(a, a.x1, &q, a.x, w->ln_in, a.xs, nullptr, sm);
+            res_rows(a, a.x1, &q, a.x, w->ln_in, a.xs, nullptr, sm);
           }
         } else {  // PH_RES_B
           const Parts q = parts_of(a, sm, DP_KIND_O);
-          res_norm_rows(a, a.x, &q, a.x1, w->ln_post, a.xs, nullptr, sm);
+          res_rows(a, a.x, &q, a.x1, w->ln_post, a.xs, nullptr, sm);
         }
       }
       if (threadIdx.x == 0) trace_at(a, ph, 2);
@@ -598,10 +845,10 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
               break;
             }
             mbar_arrive_expect_tx(&sm.full[s], stage_bytes);
-            tma_load_2d(st, wmap, kx, tile * TC_BM, &sm.full[s]);
+            tma_load_2d(st, wmap, kx, tile * UM, &sm.full[s]);
           }
-          tma_load_3d(st + DP_A_BYTES, xmap, kx, 0, 0, &sm.full[s]);
-          tma_load_3d(st + DP_A_BYTES + plane_bytes, xmap, kx, 0, 1, &sm.full[s]);
+          tma_load_3d(st + a_bytes, xmap, kx, 0, 0, &sm.full[s]);  // both planes in one box, or the hi plane
+          if (a.split_b) tma_load_3d(st + a_bytes + plane_bytes, xmap, kx, 0, 1, &sm.full[s]);
         }
         pre_n = 0;
       }
@@ -622,11 +869,14 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
           }
           tc_fence_after();
           const uint32_t sa = smem_u32(sm.stages + (size_t)s * stage_bytes);
-          const uint32_t sh = sa + DP_A_BYTES, sl = sh + plane_bytes;
+          const uint32_t sh = sa + a_bytes, sl = sh + plane_bytes;
+          for (int m = 0; m < UM / TC_BM; ++m) {  // accumulator m: weight rows 128 m .. 128 m + 127 of the unit
+            const uint32_t am = sa + m * (TC_BM * TC_BK * 2), dm = tmem + m * a.Rpad;
 #pragma unroll
-          for (int kk = 0; kk < TC_BK / 16; ++kk) {
-            tc_mma(tmem, sw128_desc(sa + kk * 32), sw128_desc(sh + kk * 32), idesc, (!first || kk > 0) ? 1 : 0);
-            tc_mma(tmem, sw128_desc(sa + kk * 32), sw128_desc(sl + kk * 32), idesc, 1);
+            for (int kk = 0; kk < TC_BK / 16; ++kk) {
+              tc_mma(dm, sw128_desc(am + kk * 32), sw128_desc(sh + kk * 32), idesc, (!first || kk > 0) ? 1 : 0);
+              tc_mma(dm, sw128_desc(am + kk * 32), sw128_desc(sl + kk * 32), idesc, 1);
+            }
           }
           tc_commit(&sm.empty[s]);
           if (c == c1 - 1 || (c + 1) % kch == 0) {
@@ -638,8 +888,7 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
     } else if (warp < 4) {
       // ---- epilogue (warps 0-3): each segment's partial tile into its slot, rows < R
       const Parts q = parts_of(a, sm, gk);
-      int seg = b < nc ? sm.segtab[a.tab_off[gk] + n_out / TC_BM + 1 + b] : 0;
-      const int ch = warp * 32 + lane;
+      int seg = b < nc ? sm.segtab[a.tab_off[gk] + n_out / UM + 1 + b] : 0;
       for (int c = c0; c < c1; ++seg) {
         const int tile = c / kch, cend = std::min(c1, (tile + 1) * kch);
         const bool good = mbar_wait(sm.seg_done, seg_g & 1, a.err);
@@ -647,19 +896,22 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
         if (!good) sm.flags[0] = 1;
         if (epi_or(!good || sm.flags[0] != 0)) break;  // uniform over the four warps
         if (threadIdx.x == 0 && c == c0) trace_at(a, ph, 1);
-        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-        float* dst = a.part + (size_t)seg * q.stride + ch;
-        for (int sl = 0; sl < a.Rpad / 32; ++sl) {
-          float v[32];
-          tmem_ld16(trow + sl * 32, v);
-          tmem_ld16(trow + sl * 32 + 16, v + 16);
-          if (sl == a.Rpad / 32 - 1) {  // last TMEM read of the segment: the MMA warp may reuse it
-            tc_fence_before();
-            mbar_arrive(sm.acc_free);
-          }
+        const int nm = UM / TC_BM;
+        for (int m = 0; m < nm; ++m) {
+          const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16) + m * a.Rpad;
+          float* dst = a.part + (size_t)seg * q.stride + m * TC_BM + warp * 32 + lane;
+          for (int sl = 0; sl < a.Rpad / 32; ++sl) {
+            float v[32];
+            tmem_ld16(trow + sl * 32, v);
+            tmem_ld16(trow + sl * 32 + 16, v + 16);
+            if (m == nm - 1 && sl == a.Rpad / 32 - 1) {  // last TMEM read of the segment: the MMA warp may reuse it
+              tc_fence_before();
+              mbar_arrive(sm.acc_free);
+            }
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (sl * 32 + j < a.R) __stcg(dst + (size_t)(sl * 32 + j) * 128, v[j]);
+            for (int j = 0; j < 32; ++j)
+              if (sl * 32 + j < a.R) __stcg(dst + (size_t)(sl * 32 + j) * UM, v[j]);
+          }
         }
         ++seg_g;
         c = cend;
@@ -687,8 +939,8 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
     for (int j = 0; j < pre_n; ++j, ++prod_i) {
       unsigned char* st = sm.stages + (size_t)(prod_i % a.nst) * stage_bytes;
       const int kx = ((g.c0 + j) % g.kch) * TC_BK;
-      tma_load_3d(st + DP_A_BYTES, g.xmap, kx, 0, 0, &sm.full[prod_i % a.nst]);
-      tma_load_3d(st + DP_A_BYTES + plane_bytes, g.xmap, kx, 0, 1, &sm.full[prod_i % a.nst]);
+      tma_load_3d(st + UM * TC_BK * 2, g.xmap, kx, 0, 0, &sm.full[prod_i % a.nst]);
+      if (a.split_b) tma_load_3d(st + UM * TC_BK * 2 + plane_bytes, g.xmap, kx, 0, 1, &sm.full[prod_i % a.nst]);
     }
     pre_n = 0;
   }
@@ -741,24 +993,34 @@ int dit_persist_segments(int tiles, int kch, int ncta, int* tab) {
   return seg;
 }
 
-size_t dit_persist_smem(int rpad, int* nst) {
-  const int stage = TC_BM * TC_BK * 2 + 2 * rpad * TC_BK * 2;
-  const size_t fixed = 1024 + (DP_ATT_FLOATS + 32) * 4 + 8 * 32 + 128 + DP_SEGTAB_MAX * 4;
+size_t dit_persist_smem(int rpad, int um, int att_mode, int* nst) {
+  const int stage = um * TC_BK * 2 + 2 * rpad * TC_BK * 2;
+  const size_t fixed = 1024 + (size_t)(dp_att_floats(att_mode) + 32) * 4 + 8 * 32 + 128 + DP_SEGTAB_MAX * 4;
   const int n = (int)std::min<size_t>(6, (227 * 1024 - fixed) / stage);
   *nst = n;
   return fixed + (size_t)n * stage;
 }
 
 cudaError_t dit_persist_configure() {
-  return cudaFuncSetAttribute(dit_persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  const void* fns[4] = {(const void*)dit_persist_kernel<DP_ATT_SEQ, TC_BM>,
+                        (const void*)dit_persist_kernel<DP_ATT_SEQ, DP_UM_MAX>,
+                        (const void*)dit_persist_kernel<DP_ATT_DECODE, TC_BM>,
+                        (const void*)dit_persist_kernel<DP_ATT_DECODE, DP_UM_MAX>};
+  for (const void* f : fns) {
+    const cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 int dit_persist_grid() {
   int dev = 0, sms = 0, per = 0;
   int nst = 0;
-  const size_t smem = dit_persist_smem(256, &nst);
+  const size_t smem = std::max(dit_persist_smem(256, TC_BM, DP_ATT_SEQ, &nst),
+                               dit_persist_smem(64, DP_UM_MAX, DP_ATT_DECODE, &nst));
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, dit_persist_kernel, DP_THREADS, smem) != cudaSuccess) {
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, dit_persist_kernel<DP_ATT_SEQ, TC_BM>, DP_THREADS, smem) !=
+          cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
@@ -767,10 +1029,12 @@ int dit_persist_grid() {
 
 cudaError_t launch_dit_persist(const DitPersistArgs& a, int grid, cudaStream_t st) {
   int nst = 0;
-  const size_t smem = dit_persist_smem(a.Rpad, &nst);
+  const size_t smem = dit_persist_smem(a.Rpad, a.um, a.att_mode, &nst);
   DitPersistArgs b = a;
   b.nst = nst;
-  if (nst < 2 || grid <= 0) return cudaErrorInvalidValue;
+  if (nst < 2 || grid <= 0 || !a.xmaps || (a.um != TC_BM && a.um != DP_UM_MAX) || a.um * a.Rpad > 512 * TC_BM)
+    return cudaErrorInvalidValue;
+  if (a.att_mode == DP_ATT_DECODE && (a.S != 1 || !a.kcache || !a.vcache || !a.pos)) return cudaErrorInvalidValue;
   for (int k = 0; k < DP_KINDS; ++k)
     if (a.ncta[k] < 1 || a.ncta[k] > grid) return cudaErrorInvalidValue;
   if (a.tab_len < 1 || a.tab_len > DP_SEGTAB_MAX) return cudaErrorInvalidValue;
@@ -785,7 +1049,178 @@ cudaError_t launch_dit_persist(const DitPersistArgs& a, int grid, cudaStream_t s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   count_launch();
-  return cudaLaunchKernelEx(&cfg, dit_persist_kernel, b);
+  if (a.att_mode == DP_ATT_DECODE)
+    return a.um == DP_UM_MAX ? cudaLaunchKernelEx(&cfg, dit_persist_kernel<DP_ATT_DECODE, DP_UM_MAX>, b)
+                             : cudaLaunchKernelEx(&cfg, dit_persist_kernel<DP_ATT_DECODE, TC_BM>, b);
+  return a.um == DP_UM_MAX ? cudaLaunchKernelEx(&cfg, dit_persist_kernel<DP_ATT_SEQ, DP_UM_MAX>, b)
+                           : cudaLaunchKernelEx(&cfg, dit_persist_kernel<DP_ATT_SEQ, TC_BM>, b);
+}
+
+
+bool persist_stack_prepare(PersistStack& ps, const LmStackView& v, int max_rows, bool trace, bool* oom) {
+  *oom = false;
+  if (ps.grid >= 0) return ps.grid > 0;
+  ps.grid = 0;
+  ps.view = v;
+  const int nq = v.nkv > 0 ? v.nh / v.nkv : 0;
+  // few rows (<= 64): 256-row units (one 32 KB weight copy per K chunk: the copy count bounds
+  // those phases); more rows: 128-row units (twice the units to spread over the CTAs)
+  const int rmax = std::min(256, (std::max(max_rows, 1) + 31) / 32 * 32);
+  int um = rmax <= 64 ? DP_UM_MAX : TC_BM;
+  if (const char* e = getenv("VX_DIT_UM")) um = atoi(e) == DP_UM_MAX ? DP_UM_MAX : TC_BM;
+  ps.split_b = false;
+  if (const char* e = getenv("VX_DIT_SPLIT_B")) ps.split_b = atoi(e) != 0;
+  const bool shape_ok = v.L > 0 && v.L <= 64 && v.H <= 2048 && v.H % um == 0 && v.nh * v.d == v.H &&
+                        v.d % 4 == 0 && v.nkv > 0 && v.nh % v.nkv == 0 && ((v.nh + 2 * v.nkv) * v.d) % um == 0 &&
+                        (2 * v.I) % um == 0 && v.I % 64 == 0 && max_rows > 0;
+  if (!shape_ok) return false;
+  ps.seq_ok = v.d <= 64;
+  ps.decode_ok = v.d == DP_DEC_D && nq <= DP_DEC_NQ;
+  if (dit_persist_configure() != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  const int grid = dit_persist_grid();
+  cudaGetLastError();
+  if (grid <= 0) return false;
+  const size_t H = v.H, I = v.I, qkv = (size_t)(v.nh + 2 * v.nkv) * v.d;
+  // segment tables: each GEMM kind deals its (tile, K chunk) pairs to ncta CTAs, at least
+  // `min_pairs` pairs each (env VX_DIT_PAIRS="qkv,o,gu,down" overrides the minimums)
+  const int tiles[DP_KINDS] = {(int)(qkv / um), v.H / um, (int)(2 * I / um), v.H / um};
+  const int kchs[DP_KINDS] = {v.H / 64, v.nh * v.d / 64, v.H / 64, (int)(I / 64)};
+  int min_pairs[DP_KINDS] = {2, 2, 1, 4};
+  if (const char* e = getenv("VX_DIT_PAIRS"))
+    sscanf(e, "%d,%d,%d,%d", &min_pairs[0], &min_pairs[1], &min_pairs[2], &min_pairs[3]);
+  std::vector<int> tab;
+  int max_segs = 0;
+  for (int k = 0; k < DP_KINDS; ++k) {
+    const int total = tiles[k] * kchs[k];
+    ps.ncta[k] = std::max(1, std::min(grid, total / std::max(1, min_pairs[k])));
+    ps.tab_off[k] = (int)tab.size();
+    tab.resize(tab.size() + tiles[k] + 1 + ps.ncta[k]);
+    max_segs = std::max(max_segs, dit_persist_segments(tiles[k], kchs[k], ps.ncta[k], tab.data() + ps.tab_off[k]));
+  }
+  ps.tab_len = (int)tab.size();
+  if (ps.tab_len > DP_SEGTAB_MAX) return false;
+  std::vector<CUtensorMap> maps(4 * v.L);
+  const size_t nph = 8 * (size_t)v.L + 1;
+  bool ok = cudaMalloc(&ps.layers, sizeof(DitPersistLayer) * v.L) == cudaSuccess &&
+            cudaMemcpy(ps.layers, v.layers.data(), sizeof(DitPersistLayer) * v.L, cudaMemcpyHostToDevice) ==
+                cudaSuccess &&
+            cudaMalloc(&ps.bar, (nph + 1) * sizeof(unsigned)) == cudaSuccess &&
+            cudaMemset(ps.bar, 0, (nph + 1) * sizeof(unsigned)) == cudaSuccess &&
+            cudaMalloc(&ps.x, (size_t)rmax * H * 4) == cudaSuccess &&
+            cudaMalloc(&ps.x1, (size_t)rmax * H * 4) == cudaSuccess &&
+            cudaMalloc(&ps.xs, 2 * (size_t)rmax * H * 2) == cudaSuccess &&
+            cudaMalloc(&ps.xsi, 2 * (size_t)rmax * I * 2) == cudaSuccess &&
+            cudaMemset(ps.xs, 0, 2 * (size_t)rmax * H * 2) == cudaSuccess &&
+            cudaMemset(ps.xsi, 0, 2 * (size_t)rmax * I * 2) == cudaSuccess &&
+            cudaMalloc(&ps.part, (size_t)max_segs * rmax * um * 4) == cudaSuccess &&
+            cudaMalloc(&ps.rope_tab, 2 * 16 * 64 * 4) == cudaSuccess &&
+            cudaMalloc(&ps.segtab, tab.size() * 4) == cudaSuccess &&
+            cudaMemcpy(ps.segtab, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+            cudaMalloc(&ps.maps, sizeof(CUtensorMap) * 4 * v.L) == cudaSuccess;
+  for (int l = 0; ok && l < v.L; ++l) {
+    const DitPersistLayer& w = v.layers[l];
+    ok = tc_map_2d(&maps[4 * l + 0], w.wqkv, (int)qkv, (int)H, um) == cudaSuccess &&
+         tc_map_2d(&maps[4 * l + 1], w.wo, (int)H, v.nh * v.d, um) == cudaSuccess &&
+         tc_map_2d(&maps[4 * l + 2], w.wgu, (int)(2 * I), (int)H, um) == cudaSuccess &&
+         tc_map_2d(&maps[4 * l + 3], w.wd, (int)H, (int)I, um) == cudaSuccess;
+  }
+  ok = ok && cudaMemcpy(ps.maps, maps.data(), sizeof(CUtensorMap) * maps.size(), cudaMemcpyHostToDevice) == cudaSuccess;
+  if (ok && trace)
+    ok = cudaMalloc(&ps.trace, nph * grid * 4 * 8) == cudaSuccess &&
+         cudaMemset(ps.trace, 0, nph * grid * 4 * 8) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    persist_stack_free(ps);
+    ps.grid = 0;
+    *oom = true;
+    return false;
+  }
+  ps.rmax = rmax;
+  ps.um = um;
+  ps.grid = grid;
+  return true;
+}
+
+bool persist_stack_rows(PersistStack& ps, int rpad) {
+  if (ps.grid <= 0 || rpad > ps.rmax || rpad % 32 != 0) return false;
+  if (ps.xmaps.count(rpad)) return true;
+  CUtensorMap xm[2];
+  CUtensorMap* dev = nullptr;
+  const int bp = ps.split_b ? 1 : 2;
+  const bool ok = tc_map_3d(&xm[0], ps.xs, 2, rpad, ps.view.H, rpad, bp) == cudaSuccess &&
+                  tc_map_3d(&xm[1], ps.xsi, 2, rpad, ps.view.I, rpad, bp) == cudaSuccess &&
+                  cudaMalloc(&dev, sizeof(xm)) == cudaSuccess &&
+                  cudaMemcpy(dev, xm, sizeof(xm), cudaMemcpyHostToDevice) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    if (dev) cudaFree(dev);
+    return false;
+  }
+  ps.xmaps[rpad] = dev;
+  return true;
+}
+
+void persist_stack_free(PersistStack& ps) {
+  for (void* p : {(void*)ps.layers, (void*)ps.maps, (void*)ps.x, (void*)ps.x1, (void*)ps.part, (void*)ps.rope_tab,
+                  (void*)ps.xs, (void*)ps.xsi, (void*)ps.segtab, (void*)ps.bar, (void*)ps.trace})
+    if (p) cudaFree(p);
+  for (auto& kv : ps.xmaps) cudaFree(kv.second);
+  ps.xmaps.clear();
+  ps.layers = nullptr;
+  ps.maps = nullptr;
+  ps.x = ps.x1 = ps.part = ps.rope_tab = nullptr;
+  ps.xs = ps.xsi = nullptr;
+  ps.segtab = nullptr;
+  ps.bar = nullptr;
+  ps.trace = nullptr;
+}
+
+DitPersistArgs persist_stack_args(const PersistStack& ps, int N, int S, const float* x_in, float* out, int* err) {
+  const LmStackView& v = ps.view;
+  DitPersistArgs a = {};
+  a.L = v.L;
+  a.H = v.H;
+  a.I = v.I;
+  a.nh = v.nh;
+  a.nkv = v.nkv;
+  a.d = v.d;
+  a.S = S;
+  a.N = N;
+  a.R = N * S;
+  a.Rpad = (a.R + 31) / 32 * 32;
+  a.att_mode = DP_ATT_SEQ;
+  a.um = ps.um;
+  a.split_b = ps.split_b ? 1 : 0;
+  a.eps = v.eps;
+  a.res_scale = v.res_scale;
+  a.attn_scale = v.attn_scale;
+  a.layers = ps.layers;
+  a.wmaps = ps.maps;
+  const auto it = ps.xmaps.find(a.Rpad);
+  a.xmaps = it == ps.xmaps.end() ? nullptr : it->second;
+  a.rope = v.rope;
+  a.final_norm = v.norm_w;
+  a.x_in = x_in;
+  a.x = ps.x;
+  a.x1 = ps.x1;
+  a.out = out;
+  a.xs = ps.xs;
+  a.xs_i = ps.xsi;
+  a.part = ps.part;
+  a.rope_tab = ps.rope_tab;
+  a.segtab = ps.segtab;
+  a.tab_len = ps.tab_len;
+  for (int k = 0; k < DP_KINDS; ++k) {
+    a.tab_off[k] = ps.tab_off[k];
+    a.ncta[k] = ps.ncta[k];
+  }
+  a.bar = ps.bar;
+  a.err = err;
+  a.trace = ps.trace;
+  return a;
 }
 
 }  // namespace vx

@@ -79,6 +79,11 @@ struct vx_lm {
   float *bx = nullptr, *bxn = nullptr, *bqkv = nullptr, *bq = nullptr, *battn = nullptr, *bgu = nullptr,
         *bact = nullptr, *blogits = nullptr, *bhid = nullptr;
   int* btokens = nullptr;  // [max_length + 8][max_batch]
+  // the batched step's decoder layers as one persistent launch (dit_persist.cu, decode
+  // attention); env VX_LM_BATCH_PERSIST=0: the per-kernel layers
+  PersistStack bp;
+  bool bp_on = true;
+  bool bt_persist = false;  // the captured batch step uses it
   cudaGraphExec_t step_exec = nullptr;
   unsigned long long step_kernels = 0;
   // persistent decode step (one launch per token), when the shape allows it
@@ -374,11 +379,12 @@ int ensure_batch(vx_lm* lm) {
 
 // Greedy head for B rows: final norm (kept as the hidden the DiT consumes), logits over the
 // tied embedding, per-row argmax -> token and next input embedding, then step (and position).
-int enqueue_batch_head(vx_lm* lm, int B, cudaStream_t st, bool advance_pos) {
+int enqueue_batch_head(vx_lm* lm, int B, cudaStream_t st, bool advance_pos, bool normed = false) {
   vx_ctx* ctx = lm->ctx;
   const int H = lm->H;
-  VX_CUDA(ctx, launch_rmsnorm_residual(lm->bx, nullptr, lm->norm_w, 1.f, lm->cfg.rms_norm_eps, B, H, nullptr, lm->bhid,
-                                       st));
+  if (!normed)  // else bhid already holds the final-norm rows
+    VX_CUDA(ctx, launch_rmsnorm_residual(lm->bx, nullptr, lm->norm_w, 1.f, lm->cfg.rms_norm_eps, B, H, nullptr,
+                                         lm->bhid, st));
   int rc = linear(ctx, &lm->ws, lm->bhid, H, B, lm->V, H, lm->embed, nullptr, nullptr, 1.f, lm->blogits, lm->V, st);
   if (rc) return rc;
   VX_CUDA(ctx, launch_argmax_rows(lm->blogits, B, lm->V, lm->d_step, lm->btokens, lm->max_batch, lm->embed, H,
@@ -395,6 +401,17 @@ int enqueue_batch_step(vx_lm* lm, int B, cudaStream_t st) {
   const int H = lm->H, I = lm->I, qkvw = lm->qs + 2 * lm->ks;
   const float eps = lm->cfg.rms_norm_eps;
   int rc = VX_OK;
+  if (lm->bt_persist) {  // every layer and the final norm in one launch: bx -> bhid
+    DitPersistArgs a = persist_stack_args(lm->bp, B, 1, lm->bx, lm->bhid, ctx->dev_err);
+    a.att_mode = DP_ATT_DECODE;
+    a.kcache = lm->kcache;
+    a.vcache = lm->vcache;
+    a.kv_layer_stride = lm->kv_layer_stride();
+    a.max_len = lm->max_length;
+    a.pos = lm->d_pos;
+    VX_CUDA(ctx, launch_dit_persist(a, lm->bp.grid, st));
+    return enqueue_batch_head(lm, B, st, true, true);
+  }
   // the RMSNorm and SiLU*up kernels write the few-row GEMMs' split operand themselves
   uint16_t* xs = lm->ws.scratch ? tc_gemm_presplit_buffer(lm->ws.scratch) : nullptr;
   const bool ps_qkv = presplit_ok(ctx, &lm->ws, B, qkvw, H), ps_gu = presplit_ok(ctx, &lm->ws, B, 2 * I, H),
@@ -433,6 +450,17 @@ int build_batch_graph(vx_lm* lm, int B) {
     cudaGraphExecDestroy(lm->bstep_exec);
     lm->bstep_exec = nullptr;
   }
+  // the persistent layers: buffers and maps before the capture
+  lm->bt_persist = false;
+  if (lm->bp_on && lm->bp.grid < 0) {
+    LmStackView v;
+    lm_stack_view(lm, &v);
+    bool oom = false;
+    persist_stack_prepare(lm->bp, v, lm->max_batch, getenv("VX_LM_BATCH_TRACE") != nullptr, &oom);
+    if (oom) return fail(ctx, VX_ERR_OOM, "persistent batch step: allocation or tensor maps failed");
+  }
+  if (lm->bp_on && lm->bp.grid > 0 && lm->bp.decode_ok && B <= lm->bp.rmax)
+    lm->bt_persist = persist_stack_rows(lm->bp, (B + 31) / 32 * 32);
   cudaGraph_t graph = nullptr;
   const unsigned long long before = g_launches;
   VX_CUDA(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
@@ -472,6 +500,7 @@ int vx_lm_create(vx_ctx* ctx, const vx_minicpm4_config* cfg, int max_batch, int 
   cudaSetDevice(ctx->device);
   vx_lm* lm = new vx_lm();
   lm->ctx = ctx;
+  if (const char* e = getenv("VX_LM_BATCH_PERSIST")) lm->bp_on = atoi(e) != 0;
   lm->cfg = *cfg;
   lm->cfg.rope_short_factor = nullptr;
   lm->cfg.rope_long_factor = nullptr;
@@ -586,6 +615,7 @@ void vx_lm_destroy(vx_lm* lm) {
   free_prefill(lm);
   workspace_free(&lm->ws);
   if (lm->bstep_exec) cudaGraphExecDestroy(lm->bstep_exec);
+  persist_stack_free(lm->bp);
   for (void* p : {(void*)lm->bx, (void*)lm->bxn, (void*)lm->bqkv, (void*)lm->bq, (void*)lm->battn, (void*)lm->bgu,
                   (void*)lm->bact, (void*)lm->blogits, (void*)lm->bhid, (void*)lm->btokens})
     if (p) cudaFree(p);
@@ -954,6 +984,18 @@ int lm_greedy_step(vx_lm* lm) {
 }  // namespace vx
 
 extern "C" {
+
+int vx_lm_batch_trace(vx_lm* lm, unsigned long long* out, int n, int* grid, int* phases) {
+  if (!lm || !out || !grid || !phases || !lm->bp.trace) return VX_ERR_ARG;
+  *grid = lm->bp.grid;
+  *phases = 8 * lm->L + 1;
+  const size_t need = (size_t)*grid * *phases * 4;
+  if ((size_t)n < need) return VX_ERR_ARG;
+  cudaSetDevice(lm->ctx->device);
+  VX_CUDA(lm->ctx, cudaStreamSynchronize(lm->ctx->stream));
+  VX_CUDA(lm->ctx, cudaMemcpy(out, lm->bp.trace, need * 8, cudaMemcpyDeviceToHost));
+  return VX_OK;
+}
 
 int vx_lm_greedy(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_steps, int32_t* tokens_out) {
   if (!lm || !prompt_ids || !tokens_out || n_prompt <= 0 || n_steps < 0) return VX_ERR_ARG;

@@ -185,13 +185,6 @@ const int* lm_batch_tokens(const vx_lm* lm);
 int lm_max_batch(const vx_lm* lm);
 int lm_vocab_size(const vx_lm* lm);
 // A model's stack as the persistent DiT-forward kernel sees it (dit_persist.cuh).
-struct LmStackView {
-  int L, H, I, nh, nkv, d;
-  float eps, res_scale, attn_scale;
-  const RopeParams* rope;
-  const float* norm_w;
-  std::vector<DitPersistLayer> layers;
-};
 void lm_stack_view(const vx_lm* lm, LmStackView* v);
 void lm_dims(const vx_lm* lm, int* L, int* H, int* I, int* qs, int* ks, int* V);
 int lm_max_length(const vx_lm* lm);

@@ -80,6 +80,7 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* tm, in
 // Host: encode tensor maps of bf16 K-major operands (SWIZZLE_128B, 64-element boxes).
 // 2-D: [rows, K] with box [box_rows, 64]; 3-D: [planes, rows, K] with box [1, box_rows, 64].
 cudaError_t tc_map_2d(CUtensorMap* m, const void* ptr, int rows, int K, int box_rows);
-cudaError_t tc_map_3d(CUtensorMap* m, const void* ptr, int planes, int rows, int K, int box_rows);
+// [planes][rows][K] bf16; a box is 64 x box_rows x box_planes.
+cudaError_t tc_map_3d(CUtensorMap* m, const void* ptr, int planes, int rows, int K, int box_rows, int box_planes = 1);
 
 }  // namespace vx

@@ -329,11 +329,11 @@ cudaError_t make_map(CUtensorMap* m, const void* ptr, int rows, int K, int box_r
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-cudaError_t make_map_3d(CUtensorMap* m, const void* ptr, int planes, int rows, int K, int box_rows) {
-  if (((uintptr_t)ptr & 15) || (K * 2) % 16) return cudaErrorInvalidValue;
+cudaError_t make_map_3d(CUtensorMap* m, const void* ptr, int planes, int rows, int K, int box_rows, int box_planes) {
+  if (((uintptr_t)ptr & 15) || (K * 2) % 16 || box_planes < 1 || box_planes > planes) return cudaErrorInvalidValue;
   cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)planes};
   cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)K * 2 * rows};
-  cuuint32_t box[3] = {(cuuint32_t)TC_BK, (cuuint32_t)box_rows, 1};
+  cuuint32_t box[3] = {(cuuint32_t)TC_BK, (cuuint32_t)box_rows, (cuuint32_t)box_planes};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -382,9 +382,9 @@ cudaError_t tc_map_2d(CUtensorMap* m, const void* ptr, int rows, int K, int box_
   return e != cudaSuccess ? e : make_map(m, ptr, rows, K, box_rows);
 }
 
-cudaError_t tc_map_3d(CUtensorMap* m, const void* ptr, int planes, int rows, int K, int box_rows) {
+cudaError_t tc_map_3d(CUtensorMap* m, const void* ptr, int planes, int rows, int K, int box_rows, int box_planes) {
   cudaError_t e = get_encoder();
-  return e != cudaSuccess ? e : make_map_3d(m, ptr, planes, rows, K, box_rows);
+  return e != cudaSuccess ? e : make_map_3d(m, ptr, planes, rows, K, box_rows, box_planes);
 }
 
 bool tc_gemm_supported(int M, int N, int K) { return M >= 1 && M <= 128 && N % TC_BM == 0 && K % TC_BK == 0 && K > 0; }
