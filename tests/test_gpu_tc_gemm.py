@@ -1,6 +1,8 @@
 """tcgen05 few-row GEMM (bf16 weights x hi/lo-split activations, f32 accumulation in TMEM)
 through vx_linear_bf16 against the oracle's f32 Linear, over the row counts the prefill and
-the DiT use, with and without bias, single K split and split-K with the last-CTA reduction.
+the DiT use, with and without bias, single K split and split-K with the last-CTA reduction,
+and output widths that are not a multiple of 128 (the batched greedy head's 73,448-row
+tied embedding).
 Tolerance 2e-2 (bf16-weight path); the split keeps the error near f32 (< 1e-4 checked)."""
 import numpy as np
 import pytest
@@ -15,7 +17,8 @@ pytestmark = pytest.mark.gpu
                                         (22, 1280, 1024, False), (22, 8192, 1024, False), (22, 1024, 4096, True),
                                         (64, 2560, 2048, False), (100, 2048, 6144, False), (128, 12288, 2048, True),
                                         (129, 1024, 1024, False), (176, 1280, 1024, True), (176, 1024, 4096, False),
-                                        (256, 2048, 2048, True), (300, 1024, 1024, False)])
+                                        (256, 2048, 2048, True), (300, 1024, 1024, False),
+                                        (8, 1000, 2048, True), (8, 73448, 2048, False), (3, 200, 128, False)])
 def test_tc_linear(ctx, m, n, k, bias):
     import torch
     from voxcpm_rs_b200 import synth

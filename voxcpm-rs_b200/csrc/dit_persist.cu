@@ -59,6 +59,7 @@ constexpr int DP_ATT_FLOATS = (DP_HPU + 2) * DP_SMAX * DP_QS + DP_HPU * (DP_SMAX
 // decode attention scratch: q [nq][d], k, v [d], cos / sin [d/2] (nq <= 12 warps, d = 128);
 // then two buffers of a 32-position K tile and V tile
 constexpr int DP_DEC_NQ = 12, DP_DEC_D = 128, DP_DEC_TILE = 32;
+constexpr int DP_DEC_SPLITS = 16;      // most CTAs sharing one (sequence, KV head)'s cache walk
 constexpr int DP_DEC_TILE_OFF = 2048;  // floats; >= the scratch above, a multiple of 4
 constexpr int DP_DEC_FLOATS = DP_DEC_TILE_OFF + 2 * 2 * DP_DEC_TILE * DP_DEC_D;
 static_assert(DP_DEC_NQ * DP_DEC_D + 3 * DP_DEC_D <= DP_DEC_TILE_OFF, "decode scratch");
@@ -479,8 +480,8 @@ __device__ __forceinline__ float warp_max(float v) {
 // shuffles.  Output into the split operand (K = nh * d).  Run by all DP_THREADS threads
 // (warps >= nq only help with the loads); `uses` counts each tile buffer's completed copies
 // (uniform over the CTA).  Returns false if a copy wait gave up (error recorded).
-__device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, int g, int l, int pos, const Sm& sm,
-                                unsigned* uses, int ph) {
+__device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, int g, int split, int nsplit, int l,
+                                int pos, const Sm& sm, unsigned* uses, int ph) {
   constexpr int d = DP_DEC_D, half = d / 2, d4 = d / 4;
   const int nq = a.nh / a.nkv, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float* qs = sm.att;  // [nq][d], then k [d], v [d]
@@ -489,6 +490,27 @@ __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, 
   float* cs = vn + d;  // [half] cos, [half] sin
   float* sn = cs + half;
   float* tiles = sm.att + DP_DEC_TILE_OFF;
+  const size_t seq = ((size_t)n * a.nkv + g) * a.max_len * d;
+  float* kc = a.kcache + (size_t)l * a.kv_layer_stride + seq;
+  float* vc = a.vcache + (size_t)l * a.kv_layer_stride + seq;
+  const int ntt = pos / DP_DEC_TILE + 1;  // tiles of positions 0..pos; this split walks [t0, nt)
+  const int t0 = (int)((long long)split * ntt / nsplit), nt = (int)((long long)(split + 1) * ntt / nsplit);
+  const bool last_split = nt == ntt;      // its range holds position pos (this step's k, v)
+  unsigned issued[2] = {uses[0], uses[1]};
+  int next = t0;  // thread 0: the next tile to copy
+  auto issue = [&](int t) {  // thread 0
+    const int rows = min(DP_DEC_TILE, pos + 1 - t * DP_DEC_TILE), b = t & 1;
+    const uint32_t bytes = (uint32_t)rows * d * 4;
+    float* kt = tiles + b * 2 * DP_DEC_TILE * d;
+    mbar_arrive_expect_tx(&sm.att_bar[b], 2 * bytes);
+    bulk_g2s(kt, kc + (size_t)t * DP_DEC_TILE * d, bytes, &sm.att_bar[b]);
+    bulk_g2s(kt + DP_DEC_TILE * d, vc + (size_t)t * DP_DEC_TILE * d, bytes, &sm.att_bar[b]);
+    ++issued[b];
+    next = t + 1;
+  };
+  // tiles of earlier positions only do not depend on this step: they land during the setup
+  if (tid == 0)
+    while (next < t0 + 2 && next < ntt - 1 && next < nt) issue(next);
   const int cells = (nq + 2) * d4;
   for (int i0 = tid; i0 < cells; i0 += 2 * DP_THREADS) {
     PRange x[2];
@@ -511,14 +533,12 @@ __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, 
     for (int k = 0; k < 2; ++k)
       if (dst[k] >= 0) *reinterpret_cast<float4*>(qs + dst[k]) = o[k];
   }
-  if (a.rope && tid < half) {
-    const double f = ((double)pos * a.rope->inv_freq[tid]) / a.rope->ext[tid];
-    double sd, cd;
-    sincos(f, &sd, &cd);
-    cs[tid] = (float)(cd * a.rope->scaling_factor);
-    sn[tid] = (float)(sd * a.rope->scaling_factor);
+  if (a.rope && tid < half) {  // the table built at load time from the same f64 angles (rope.rs:76-95)
+    cs[tid] = __ldg(a.rope_pos + ((size_t)pos * 2) * half + tid);
+    sn[tid] = __ldg(a.rope_pos + ((size_t)pos * 2 + 1) * half + tid);
   }
   cta_sync();
+  if (tid == 0) trace_at(a, ph, 3);
   if (a.rope) {  // rows 0..nq-1 are the queries, row nq the key (one rotation pair per thread)
     for (int i = tid; i < (nq + 1) * half; i += DP_THREADS) {
       float* v = qs + (i / half) * d;
@@ -530,41 +550,30 @@ __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, 
     }
     cta_sync();
   }
-  const size_t seq = ((size_t)n * a.nkv + g) * a.max_len * d;
-  float* kc = a.kcache + (size_t)l * a.kv_layer_stride + seq;
-  float* vc = a.vcache + (size_t)l * a.kv_layer_stride + seq;
-  for (int e = tid; e < d; e += DP_THREADS) {
-    kc[(size_t)pos * d + e] = kn[e];
-    vc[(size_t)pos * d + e] = vn[e];
+  if (last_split) {
+    for (int e = tid; e < d; e += DP_THREADS) {
+      kc[(size_t)pos * d + e] = kn[e];
+      vc[(size_t)pos * d + e] = vn[e];
+    }
+    // the bulk copies below read the row just written through the generic proxy
+    asm volatile("fence.proxy.async.global;" ::: "memory");
   }
-  // the bulk copies below read the row just written through the generic proxy
-  asm volatile("fence.proxy.async.global;" ::: "memory");
   cta_sync();
-  if (tid == 0) trace_at(a, ph, 1);
-  const int nt = pos / DP_DEC_TILE + 1;
-  unsigned issued[2] = {uses[0], uses[1]};
-  auto issue = [&](int t) {  // thread 0
-    const int rows = min(DP_DEC_TILE, pos + 1 - t * DP_DEC_TILE), b = t & 1;
-    const uint32_t bytes = (uint32_t)rows * d * 4;
-    float* kt = tiles + b * 2 * DP_DEC_TILE * d;
-    mbar_arrive_expect_tx(&sm.att_bar[b], 2 * bytes);
-    bulk_g2s(kt, kc + (size_t)t * DP_DEC_TILE * d, bytes, &sm.att_bar[b]);
-    bulk_g2s(kt + DP_DEC_TILE * d, vc + (size_t)t * DP_DEC_TILE * d, bytes, &sm.att_bar[b]);
-    ++issued[b];
-  };
-  if (tid == 0) issue(0);
+  if (tid == 0) {
+    trace_at(a, ph, 1);
+    if (next == t0) issue(t0);
+  }
   // warp h < nq: query head h, lane: dims 4 lane .. 4 lane + 3
   const bool head = warp < nq;
   const float4 qv = head ? *reinterpret_cast<const float4*>(qs + warp * d + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
   float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
   float m_run = -FLT_MAX, l_run = 0.f;
   bool good = true;
-  for (int t = 0; t < nt; ++t) {
-    if (tid == 0 && t + 1 < nt) issue(t + 1);  // its buffer was released by the sync ending t - 1
+  for (int t = t0; t < nt; ++t) {
+    if (tid == 0 && next == t + 1 && next < nt) issue(next);  // its buffer was released by the sync ending t - 1
     const int b = t & 1, rows = min(DP_DEC_TILE, pos + 1 - t * DP_DEC_TILE);
     const bool w = mbar_wait(&sm.att_bar[b], uses[b] & 1, a.err);
     ++uses[b];
-    if (tid == 0 && t == 0) trace_at(a, ph, 3);
     if (cta_or(!w)) {
       good = false;
       break;
@@ -601,13 +610,16 @@ __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, 
       o.y *= al;
       o.z *= al;
       o.w *= al;
-      for (int j = 0; j < rows; ++j) {
-        const float pj = __shfl_sync(0xffffffffu, p, j);
-        const float4 v4 = *reinterpret_cast<const float4*>(vt + j * d + lane * 4);
-        o.x = fmaf(pj, v4.x, o.x);
-        o.y = fmaf(pj, v4.y, o.y);
-        o.z = fmaf(pj, v4.z, o.z);
-        o.w = fmaf(pj, v4.w, o.w);
+#pragma unroll
+      for (int j = 0; j < DP_DEC_TILE; ++j) {
+        const float pj = __shfl_sync(0xffffffffu, p, j);  // 0 past the tile's rows
+        if (j < rows) {
+          const float4 v4 = *reinterpret_cast<const float4*>(vt + j * d + lane * 4);
+          o.x = fmaf(pj, v4.x, o.x);
+          o.y = fmaf(pj, v4.y, o.y);
+          o.z = fmaf(pj, v4.z, o.z);
+          o.w = fmaf(pj, v4.w, o.w);
+        }
       }
     }
     cta_sync();  // every reader of this buffer is done before the copy issued at t + 1 reuses it
@@ -619,12 +631,59 @@ __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, 
     cta_sync();
     return false;
   }
-  if (head) {
-    const float iv = 1.0f / l_run;
-    store_split4(a.xs, (size_t)a.Rpad * a.nh * d, (size_t)n * a.nh * d + (g * nq + warp) * d + lane * 4,
-                 make_float4(o.x * iv, o.y * iv, o.z * iv, o.w * iv));
+  const size_t out_at = (size_t)n * a.nh * d + (g * nq + warp) * d + lane * 4;
+  const size_t plane = (size_t)a.Rpad * a.nh * d;
+  if (nsplit == 1) {
+    if (head) {
+      const float iv = 1.0f / l_run;
+      store_split4(a.xs, plane, out_at, make_float4(o.x * iv, o.y * iv, o.z * iv, o.w * iv));
+    }
+    cta_sync();  // the scratch is free for the next unit
+    return true;
   }
-  cta_sync();  // the scratch is free for the next unit
+  // split partials: [unit][split][head][d + 4] = o (unnormalised), running max, running sum, 2
+  // pad floats (16-byte aligned rows);
+  // the last split to arrive merges them in split order (the same sum whichever CTA it is)
+  const int unit = n * a.nkv + g;
+  float* part = a.att_part + ((size_t)unit * DP_DEC_SPLITS + split) * nq * (d + 4);
+  if (head) {
+    *reinterpret_cast<float4*>(part + warp * (d + 4) + lane * 4) = o;
+    if (lane == 0) {
+      part[warp * (d + 4) + d] = m_run;
+      part[warp * (d + 4) + d + 1] = l_run;
+    }
+  }
+  cta_sync();
+  if (tid == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(a.att_cnt + unit, 1u);
+    sm.flags[1] = prev == (unsigned)nsplit - 1;
+    if (sm.flags[1]) {
+      __threadfence();
+      a.att_cnt[unit] = 0u;  // ready for the next layer
+    }
+  }
+  cta_sync();
+  if (sm.flags[1] && head) {
+    const float* pu = a.att_part + (size_t)unit * DP_DEC_SPLITS * nq * (d + 4) + warp * (d + 4);
+    float mx = -FLT_MAX;
+    for (int sp = 0; sp < nsplit; ++sp) mx = fmaxf(mx, __ldcg(pu + (size_t)sp * nq * (d + 4) + d));
+    float den = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float* ps = pu + (size_t)sp * nq * (d + 4);
+      const float w = expf(__ldcg(ps + d) - mx);
+      den = fmaf(__ldcg(ps + d + 1), w, den);
+      const float4 os = ldcg4(ps + lane * 4);
+      acc.x = fmaf(os.x, w, acc.x);
+      acc.y = fmaf(os.y, w, acc.y);
+      acc.z = fmaf(os.z, w, acc.z);
+      acc.w = fmaf(os.w, w, acc.w);
+    }
+    const float iv = 1.0f / den;
+    store_split4(a.xs, plane, out_at, make_float4(acc.x * iv, acc.y * iv, acc.z * iv, acc.w * iv));
+  }
+  cta_sync();  // the scratch and the flag are free for the next unit
   return true;
 }
 
@@ -667,6 +726,7 @@ __device__ void act_rows(const DitPersistArgs& a, const Parts& q) {
 // the contiguous run [c0, c1) of its (tile, K chunk) pairs this CTA takes.
 struct GemmPh {
   int n_out, kch, gk, c0, c1;
+  int b;  // this CTA's rank among the phase's CTAs (the grid rotated by the kind's offset)
   const CUtensorMap* wmap;
   const CUtensorMap* xmap;
 };
@@ -680,7 +740,9 @@ __device__ GemmPh gemm_phase(const DitPersistArgs& a, int kind, int l) {
   else { g.n_out = a.H; K = a.I; wi = 3; g.gk = DP_KIND_DOWN; g.xmap = &a.xmaps[1]; }
   g.wmap = &a.wmaps[l * 4 + wi];
   g.kch = K / TC_BK;
-  const int total = (g.n_out / a.um) * g.kch, nc = a.ncta[g.gk], b = blockIdx.x;  // a.um == the kernel's UM
+  const int G = gridDim.x;
+  const int total = (g.n_out / a.um) * g.kch, nc = a.ncta[g.gk], b = ((int)blockIdx.x + G - a.cta_off[g.gk]) % G;
+  g.b = b;
   g.c0 = b < nc ? (int)((long long)b * total / nc) : 0;
   g.c1 = b < nc ? (int)((long long)(b + 1) * total / nc) : 0;
   return g;
@@ -791,9 +853,12 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
       }
       if (kind == PH_ATT) {  // all warps
         const Parts q = parts_of(a, sm, DP_KIND_QKV);
-        if constexpr (MODE == DP_ATT_DECODE) {  // unit = (sequence, KV head)
-          for (int u = blockIdx.x; u < a.N * a.nkv; u += G)
-            if (!att_decode_unit(a, q, u / a.nkv, u % a.nkv, l, dec_pos, sm, att_uses, ph)) {
+        if constexpr (MODE == DP_ATT_DECODE) {  // unit = (sequence, KV head, run of cache tiles)
+          const int nbg = a.N * a.nkv;
+          const int nsplit = max(1, min(min(DP_DEC_SPLITS, G / nbg), dec_pos / DP_DEC_TILE + 1));
+          for (int u = blockIdx.x; u < nbg * nsplit; u += G)
+            if (!att_decode_unit(a, q, (u % nbg) / a.nkv, (u % nbg) % a.nkv, u / nbg, nsplit, l, dec_pos, sm,
+                                 att_uses, ph)) {
               if (threadIdx.x == 0) sm.flags[0] = 1;
               break;
             }
@@ -828,7 +893,7 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
     }
     // ---- GEMM phase
     const GemmPh g = gemm_phase(a, kind, l);
-    const int n_out = g.n_out, kch = g.kch, gk = g.gk, c0 = g.c0, c1 = g.c1, b = blockIdx.x, nc = a.ncta[gk];
+    const int n_out = g.n_out, kch = g.kch, gk = g.gk, c0 = g.c0, c1 = g.c1, b = g.b, nc = a.ncta[gk];
     const CUtensorMap* wmap = g.wmap;
     const CUtensorMap* xmap = g.xmap;
     if (warp == 4) {
@@ -966,6 +1031,8 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
     const unsigned prev = atomicAdd(a.bar + nph, 1u);
     if (prev == (unsigned)G - 1) {
       for (int i = 0; i <= nph; ++i) a.bar[i] = 0u;
+      if (MODE == DP_ATT_DECODE)  // zero already unless a split gave up (error path)
+        for (int i = 0; i < a.N * a.nkv; ++i) a.att_cnt[i] = 0u;
       __threadfence();
     }
   }
@@ -1034,9 +1101,11 @@ cudaError_t launch_dit_persist(const DitPersistArgs& a, int grid, cudaStream_t s
   b.nst = nst;
   if (nst < 2 || grid <= 0 || !a.xmaps || (a.um != TC_BM && a.um != DP_UM_MAX) || a.um * a.Rpad > 512 * TC_BM)
     return cudaErrorInvalidValue;
-  if (a.att_mode == DP_ATT_DECODE && (a.S != 1 || !a.kcache || !a.vcache || !a.pos)) return cudaErrorInvalidValue;
+  if (a.att_mode == DP_ATT_DECODE &&
+      (a.S != 1 || !a.kcache || !a.vcache || !a.pos || (a.rope && !a.rope_pos) || !a.att_part || !a.att_cnt))
+    return cudaErrorInvalidValue;
   for (int k = 0; k < DP_KINDS; ++k)
-    if (a.ncta[k] < 1 || a.ncta[k] > grid) return cudaErrorInvalidValue;
+    if (a.ncta[k] < 1 || a.ncta[k] > grid || a.cta_off[k] < 0 || a.cta_off[k] >= grid) return cudaErrorInvalidValue;
   if (a.tab_len < 1 || a.tab_len > DP_SEGTAB_MAX) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -1057,7 +1126,23 @@ cudaError_t launch_dit_persist(const DitPersistArgs& a, int grid, cudaStream_t s
 }
 
 
-bool persist_stack_prepare(PersistStack& ps, const LmStackView& v, int max_rows, bool trace, bool* oom) {
+namespace {
+// LongRoPE cos / sin (x scaling factor) at positions 0..n_pos-1 from the f64 angles
+// (rope.rs:76-95): out [n_pos][2][half].
+__global__ void rope_pos_kernel(const RopeParams* rp, int n_pos, int half, float* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_pos * half) return;
+  const int p = i / half, j = i % half;
+  const double f = ((double)p * rp->inv_freq[j]) / rp->ext[j];
+  double sd, cd;
+  sincos(f, &sd, &cd);
+  out[(size_t)p * 2 * half + j] = (float)(cd * rp->scaling_factor);
+  out[(size_t)p * 2 * half + half + j] = (float)(sd * rp->scaling_factor);
+}
+}  // namespace
+
+bool persist_stack_prepare(PersistStack& ps, const LmStackView& v, int max_rows, bool trace, bool* oom,
+                           int rope_positions) {
   *oom = false;
   if (ps.grid >= 0) return ps.grid > 0;
   ps.grid = 0;
@@ -1088,7 +1173,14 @@ bool persist_stack_prepare(PersistStack& ps, const LmStackView& v, int max_rows,
   // `min_pairs` pairs each (env VX_DIT_PAIRS="qkv,o,gu,down" overrides the minimums)
   const int tiles[DP_KINDS] = {(int)(qkv / um), v.H / um, (int)(2 * I / um), v.H / um};
   const int kchs[DP_KINDS] = {v.H / 64, v.nh * v.d / 64, v.H / 64, (int)(I / 64)};
+  // (fewer CTAs per unit: fewer partial slots for the next row phase to sum; measured best for
+  // the 8-row LM step at 256-row units, and for the 176-row DiT forward at 128-row units)
   int min_pairs[DP_KINDS] = {2, 2, 1, 4};
+  if (um == DP_UM_MAX) {
+    min_pairs[DP_KIND_QKV] = 4;
+    min_pairs[DP_KIND_O] = 4;
+    min_pairs[DP_KIND_DOWN] = 8;
+  }
   if (const char* e = getenv("VX_DIT_PAIRS"))
     sscanf(e, "%d,%d,%d,%d", &min_pairs[0], &min_pairs[1], &min_pairs[2], &min_pairs[3]);
   std::vector<int> tab;
@@ -1131,6 +1223,20 @@ bool persist_stack_prepare(PersistStack& ps, const LmStackView& v, int max_rows,
   if (ok && trace)
     ok = cudaMalloc(&ps.trace, nph * grid * 4 * 8) == cudaSuccess &&
          cudaMemset(ps.trace, 0, nph * grid * 4 * 8) == cudaSuccess;
+  if (ok && ps.decode_ok) {  // split partials of the decode attention and their arrival counters
+    const size_t units = (size_t)rmax * v.nkv;
+    ok = cudaMalloc(&ps.att_part, units * DP_DEC_SPLITS * nq * (v.d + 4) * 4) == cudaSuccess &&
+         cudaMalloc(&ps.att_cnt, units * 4) == cudaSuccess && cudaMemset(ps.att_cnt, 0, units * 4) == cudaSuccess;
+  }
+  if (ok && v.rope && rope_positions > 0) {
+    const int half = v.d / 2, n = rope_positions * half;
+    ok = cudaMalloc(&ps.rope_pos, (size_t)rope_positions * 2 * half * 4) == cudaSuccess;
+    if (ok) {
+      count_launch();
+      rope_pos_kernel<<<(n + 255) / 256, 256>>>(v.rope, rope_positions, half, ps.rope_pos);
+      ok = cudaGetLastError() == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+    }
+  }
   if (!ok) {
     cudaGetLastError();
     persist_stack_free(ps);
@@ -1165,13 +1271,15 @@ bool persist_stack_rows(PersistStack& ps, int rpad) {
 
 void persist_stack_free(PersistStack& ps) {
   for (void* p : {(void*)ps.layers, (void*)ps.maps, (void*)ps.x, (void*)ps.x1, (void*)ps.part, (void*)ps.rope_tab,
+                  (void*)ps.rope_pos, (void*)ps.att_part, (void*)ps.att_cnt,
                   (void*)ps.xs, (void*)ps.xsi, (void*)ps.segtab, (void*)ps.bar, (void*)ps.trace})
     if (p) cudaFree(p);
   for (auto& kv : ps.xmaps) cudaFree(kv.second);
   ps.xmaps.clear();
   ps.layers = nullptr;
   ps.maps = nullptr;
-  ps.x = ps.x1 = ps.part = ps.rope_tab = nullptr;
+  ps.x = ps.x1 = ps.part = ps.rope_tab = ps.rope_pos = ps.att_part = nullptr;
+  ps.att_cnt = nullptr;
   ps.xs = ps.xsi = nullptr;
   ps.segtab = nullptr;
   ps.bar = nullptr;
@@ -1211,6 +1319,9 @@ DitPersistArgs persist_stack_args(const PersistStack& ps, int N, int S, const fl
   a.xs_i = ps.xsi;
   a.part = ps.part;
   a.rope_tab = ps.rope_tab;
+  a.rope_pos = ps.rope_pos;
+  a.att_part = ps.att_part;
+  a.att_cnt = ps.att_cnt;
   a.segtab = ps.segtab;
   a.tab_len = ps.tab_len;
   for (int k = 0; k < DP_KINDS; ++k) {

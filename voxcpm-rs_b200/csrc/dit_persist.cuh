@@ -31,8 +31,9 @@ struct LmStackView {
   std::vector<DitPersistLayer> layers;
 };
 
-// GEMM phases deal their (um-row weight unit, 64-element K chunk) pairs to the first ncta
-// CTAs in contiguous runs: CTA b < ncta takes pairs [b T / ncta, (b + 1) T / ncta) of T.  Every
+// GEMM phases deal their (um-row weight unit, 64-element K chunk) pairs to ncta CTAs in
+// contiguous runs: the CTA of rank b < ncta (rank = (blockIdx - cta_off) mod grid) takes pairs
+// [b T / ncta, (b + 1) T / ncta) of T.  Every
 // maximal run inside one tile is a segment; segments are numbered CTA-major (which is also
 // tile-major), each writes its f32 partial tile to its own slot and the consumer sums a tile's
 // slots in ascending order (deterministic).
@@ -55,6 +56,9 @@ struct DitPersistArgs {
   size_t kv_layer_stride;
   int max_len;
   const int* pos;               // device position of the new rows
+  const float* rope_pos;        // DP_ATT_DECODE: [max_len][2][d/2] LongRoPE cos, sin per position
+  float* att_part;              // DP_ATT_DECODE: per (sequence, KV head) split partials of the cache walk
+  unsigned* att_cnt;            //   and their arrival counters (zero between layers)
   float eps, res_scale, attn_scale;
   const DitPersistLayer* layers;  // device [L]
   const CUtensorMap* wmaps;       // device [L][4]: qkv, o, gate|up, down (um-row x 64 boxes)
@@ -73,6 +77,7 @@ struct DitPersistArgs {
   int tab_off[DP_KINDS];          // offset of each kind's table in segtab
   int tab_len;                    // ints in segtab (at most 2048)
   int ncta[DP_KINDS];             // CTAs each GEMM kind deals its pairs to
+  int cta_off[DP_KINDS];          // ... starting at this CTA (ranks rotate through the grid)
   unsigned* bar;                  // [8 L + 2] zeroed; the last CTA out resets them
   int* err;
   int nst;                        // ring stages (set by the launcher)
@@ -106,6 +111,9 @@ struct PersistStack {
   CUtensorMap* maps = nullptr;                 // device [4 L]
   std::map<int, CUtensorMap*> xmaps;           // device [2] per padded row count
   float *x = nullptr, *x1 = nullptr, *part = nullptr, *rope_tab = nullptr;
+  float* rope_pos = nullptr;                   // [positions][2][d/2] (decode attention)
+  float* att_part = nullptr;                   // decode attention split partials
+  unsigned* att_cnt = nullptr;                 // and their counters
   uint16_t *xs = nullptr, *xsi = nullptr;
   int* segtab = nullptr;
   unsigned* bar = nullptr;
@@ -115,7 +123,10 @@ struct PersistStack {
 // Once, outside any capture: check the shape (hidden <= 2048, a multiple of 128), allocate
 // for up to max_rows rows, build the weight maps and segment tables.  False (ps.grid = 0)
 // when the persistent forward cannot run; *oom is set when an allocation failed.
-bool persist_stack_prepare(PersistStack& ps, const LmStackView& v, int max_rows, bool trace, bool* oom);
+// rope_positions > 0: also tabulate LongRoPE cos / sin for positions 0..rope_positions-1 (the
+// decode attention reads the table instead of evaluating f64 sincos).
+bool persist_stack_prepare(PersistStack& ps, const LmStackView& v, int max_rows, bool trace, bool* oom,
+                           int rope_positions = 0);
 // Activation maps for rpad rows (kept per count); false on failure.
 bool persist_stack_rows(PersistStack& ps, int rpad);
 void persist_stack_free(PersistStack& ps);

@@ -409,6 +409,9 @@ int enqueue_batch_step(vx_lm* lm, int B, cudaStream_t st) {
     a.kv_layer_stride = lm->kv_layer_stride();
     a.max_len = lm->max_length;
     a.pos = lm->d_pos;
+    // the o_proj units go to the CTAs without an attention unit (B nkv of them have one): their
+    // weight tiles stream in while those walk the cache
+    a.cta_off[DP_KIND_O] = std::min(B * lm->nkv, std::max(0, lm->bp.grid - a.ncta[DP_KIND_O]));
     VX_CUDA(ctx, launch_dit_persist(a, lm->bp.grid, st));
     return enqueue_batch_head(lm, B, st, true, true);
   }
@@ -456,7 +459,7 @@ int build_batch_graph(vx_lm* lm, int B) {
     LmStackView v;
     lm_stack_view(lm, &v);
     bool oom = false;
-    persist_stack_prepare(lm->bp, v, lm->max_batch, getenv("VX_LM_BATCH_TRACE") != nullptr, &oom);
+    persist_stack_prepare(lm->bp, v, lm->max_batch, getenv("VX_LM_BATCH_TRACE") != nullptr, &oom, lm->max_length);
     if (oom) return fail(ctx, VX_ERR_OOM, "persistent batch step: allocation or tensor maps failed");
   }
   if (lm->bp_on && lm->bp.grid > 0 && lm->bp.decode_ok && B <= lm->bp.rmax)

@@ -387,13 +387,17 @@ cudaError_t tc_map_3d(CUtensorMap* m, const void* ptr, int planes, int rows, int
   return e != cudaSuccess ? e : make_map_3d(m, ptr, planes, rows, K, box_rows, box_planes);
 }
 
-bool tc_gemm_supported(int M, int N, int K) { return M >= 1 && M <= 128 && N % TC_BM == 0 && K % TC_BK == 0 && K > 0; }
+// N need not be a multiple of 128: the last weight tile's rows past N read as zeros (TMA) and
+// its outputs past N are not stored; at most 1024 tiles (the split-K counters).
+bool tc_gemm_supported(int M, int N, int K) {
+  return M >= 1 && M <= 128 && N >= 1 && N <= 1024 * TC_BM && K % TC_BK == 0 && K > 0;
+}
 
 // Scratch needed by launch_tc_gemm for these shapes (bf16 split X, split-K partials): the
 // grid is at most max(target_ctas, N/128) CTAs, each with one [M, 128] partial.
 size_t tc_gemm_scratch_bytes(int M, int N, int K, int target_ctas) {
   const int NB = ((2 * M + 15) / 16) * 16;
-  const int tiles = N / TC_BM;
+  const int tiles = (N + TC_BM - 1) / TC_BM;
   const size_t xs = ((size_t)NB * K * 2 + 255) & ~(size_t)255;
   const size_t part = (size_t)std::max(tiles, target_ctas) * M * TC_BM * 4;
   return xs + part + 4096;
@@ -410,7 +414,7 @@ cudaError_t tc_gemm_core(int M, int N, int K, int x_rows, const uint16_t* W, con
                          cudaStream_t st, int target_ctas) {
   cudaError_t e;
   const int NB = ((2 * M + 15) / 16) * 16;
-  const int tiles = N / TC_BM, kblocks = K / TC_BK;
+  const int tiles = (N + TC_BM - 1) / TC_BM, kblocks = K / TC_BK;
   // K splits: the largest divisor of the K blocks (at most TC_MAX_SPLITS) keeping the grid
   // within about one CTA per SM; a tile's CTAs each stream >= 1 K block of 16 KB
   int splits = 1;
