@@ -629,6 +629,64 @@ def run_dit_trace(batch=8):
     return 0
 
 
+def run_gen_batch(steps=12, trace=False):
+    """--gen-batch N: small profiling case of the batched synthesis (8 utterances, 64-id
+    prompts, N patches): the LM of the decode workload with 8 rows per greedy step (its decoder
+    layers one persistent launch per step), an 8-patch CFM solve per step, the AudioVAE.
+    --lm-batch-trace: the same, then the persistent LM step's phase timeline (last step)."""
+    import ctypes
+    import numpy as np
+    import torch
+    if trace:
+        os.environ["VX_LM_BATCH_TRACE"] = "1"
+    from __graft_entry__ import load_package
+    load_package()
+    from voxcpm_rs_b200 import config, synth
+    from voxcpm_rs_b200._lib import lib
+    from voxcpm_rs_b200.audiovae import AudioVae
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    from voxcpm_rs_b200.minicpm4 import Context, MiniCpmModel
+    from voxcpm_rs_b200.voxcpm import GenerateOptions, VoxCPM
+    ctx = Context(0)
+    cfg = lm_config()
+    lm = MiniCpmModel(ctx, cfg, synth.minicpm_weights(cfg, seed=0), max_batch=SYN_B, max_length=512)
+    dcfg = config.locdit_config(cfg)
+    dit = VoxCpmLocDiTV2(ctx, dcfg, synth.locdit_weights(dcfg, in_channels=64, seed=0), max_rows=2 * SYN_B)
+    vcfg = config.vae_config()
+    vae = AudioVae(ctx, vcfg, synth.vae_weights(vcfg, seed=0))
+    vox = VoxCPM(ctx, lm, dit, vae)
+    prompts = np.stack([synth.prompt_ids(PROMPT, VOCAB, seed=b) for b in range(SYN_B)])
+    noise = np.random.default_rng(0).standard_normal((SYN_B, steps, 64, 4), dtype=np.float32)
+    t0 = time.perf_counter()
+    vox.generate_batch(prompts, GenerateOptions(max_len=steps), noise)
+    torch.cuda.synchronize()
+    out = {"gen_batch_ms": (time.perf_counter() - t0) * 1e3, "utterances": SYN_B, "patches": steps}
+    if trace:
+        n = (8 * cfg.num_hidden_layers + 1) * 1024 * 4
+        buf = (ctypes.c_ulonglong * n)()
+        grid, phases = ctypes.c_int(), ctypes.c_int()
+        if lib().vx_lm_batch_trace(lm.h, buf, n, ctypes.byref(grid), ctypes.byref(phases)) == 0:
+            P, G = phases.value, grid.value
+            t = np.frombuffer(buf, dtype=np.uint64)[:P * G * 4].reshape(P, G, 4).astype(np.int64)
+            tz = t[:, :, 0][t[:, :, 0] > 0].min()
+            t = np.where(t > 0, t - tz, -1) / 1000.0
+            start = t[:, :, 0].max(axis=1)
+            names = ["RES_A", "QKV", "ATT", "O", "RES_B", "GU", "ACT", "DOWN"]
+            res = {}
+            for p in range(P - 1):
+                d = res.setdefault(names[p % 8], {"phase_us": [], "work_us": []})
+                work = t[p, :, 2]
+                wmax = work[work >= 0].max() if (work >= 0).any() else start[p]
+                d["phase_us"].append(start[p + 1] - start[p])
+                d["work_us"].append(wmax - start[p])
+            out["lm_batch_trace"] = {"position": PROMPT + steps - 1, "grid": G, "step_us": round(float(start[-1]), 1),
+                                     "phases": {k: {kk: round(float(np.median(vv)), 2) for kk, vv in v.items()}
+                                                for k, v in res.items()}}
+    print(json.dumps(out))
+    ctx.close()
+    return 0
+
+
 def run_cfm_only(batch=1):
     """Small profiling case: the LocDiT CFM solve (8 layers, hidden 1024, CFG 2.0, 10 uniform
     Euler steps, `batch` patches) run twice (the first call captures the solve graph)."""
@@ -670,6 +728,10 @@ def main():
     ap.add_argument("--cfm-only", action="store_true",
                     help="profiling case: two CFM solves of the LocDiT workload (10 Euler steps)")
     ap.add_argument("--cfm-batch", type=int, default=1, help="patches per solve of --cfm-only")
+    ap.add_argument("--gen-batch", type=int, default=None, metavar="N",
+                    help="profiling case: batched synthesis of 8 utterances, N patches")
+    ap.add_argument("--lm-batch-trace", type=int, default=None, metavar="N",
+                    help="phase timeline of the persistent 8-row LM step after N batched patches")
     ap.add_argument("--dit-trace", type=int, default=None, metavar="B",
                     help="phase timeline of the persistent LocDiT forward in a CFM solve of B patches")
     ap.add_argument("--vae-only", action="store_true",
@@ -693,6 +755,10 @@ def main():
         return run_cfm_only(args.cfm_batch)
     if args.dit_trace is not None:
         return run_dit_trace(args.dit_trace)
+    if args.gen_batch is not None:
+        return run_gen_batch(args.gen_batch)
+    if args.lm_batch_trace is not None:
+        return run_gen_batch(args.lm_batch_trace, trace=True)
     if args.vae_only:
         return run_vae_only()
     args.warmup = max(3, args.warmup)
