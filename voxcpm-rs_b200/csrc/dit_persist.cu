@@ -49,13 +49,15 @@ namespace {
 constexpr int DP_WARPS = 12;
 constexpr int DP_THREADS = DP_WARPS * 32;
 constexpr int DP_EPI_THREADS = 128;  // warps 0-3: GEMM epilogue (TMEM lanes 0-127)
-constexpr int DP_RES_THREADS = 256;  // warps 0-7: RES rows, one float4 group of a row each (H <= 1024)
+constexpr int DP_ROW_THREADS = DP_THREADS - 32;  // row phases: every warp but the producer's (warp 4)
+constexpr int DP_RES_THREADS = 256;  // RES rows: the first 8 row warps
 constexpr int DP_UM_MAX = 2 * TC_BM;  // weight rows per unit: one or two 128-row MMA tiles (a.um)
 constexpr int DP_SMAX = 16;          // tokens per sequence
 constexpr int DP_QS = 68;            // shared-memory row stride of q, k, v (floats; float4 aligned)
 constexpr int DP_SEGTAB_MAX = 2048;  // ints of segment tables held in shared memory
 constexpr int DP_HPU = 2;            // most query heads per attention unit
-constexpr int DP_ATT_FLOATS = (DP_HPU + 2) * DP_SMAX * DP_QS + DP_HPU * (DP_SMAX * DP_SMAX + DP_SMAX);
+constexpr int DP_ATT_FLOATS =
+    (DP_HPU + 2) * DP_SMAX * DP_QS + DP_HPU * (DP_SMAX * DP_SMAX + DP_SMAX) + 2 * DP_SMAX * 32;  // + cos / sin
 // decode attention scratch: q [nq][d], k, v [d], cos / sin [d/2] (nq <= 12 warps, d = 128);
 // then two buffers of a 32-position K tile and V tile
 constexpr int DP_DEC_NQ = 12, DP_DEC_D = 128, DP_DEC_TILE = 32;
@@ -90,6 +92,32 @@ struct Sm {
 // Named barriers: 1 = warps 0-3 (epilogue), 2 = the whole CTA, 3 = warps 0-7 (RES rows); every
 // lane of a warp reaches them together (__syncwarp first: a lane may come from a longer run of
 // a per-thread loop).
+
+// A thread's rank among the row-phase threads: warps 0-3 and 5-11.  Warp 4 (the TMA producer)
+// sits the row phases out, so its prefetch of the next GEMM phase's weight tiles (about half a
+// microsecond per copy) never holds up their barriers; -1 there.
+__device__ __forceinline__ int row_rank() {
+  const int w = threadIdx.x >> 5;
+  return w == 4 ? -1 : (w < 4 ? (int)threadIdx.x : (int)threadIdx.x - 32);
+}
+__device__ __forceinline__ void row_sync() {
+  __syncwarp();
+  named_sync(4, DP_ROW_THREADS);
+}
+// Barrier 4 that ORs a per-thread flag (a uniform decision over the row threads).
+__device__ __forceinline__ bool row_or(bool v) {
+  int r;
+  __syncwarp();
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 4, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((int)v), "r"(DP_ROW_THREADS)
+      : "memory");
+  return r != 0;
+}
 
 // Barrier 1 that ORs a per-thread flag, so every epilogue thread takes the same decision.
 __device__ __forceinline__ bool epi_or(bool v) {
@@ -229,7 +257,7 @@ __device__ __forceinline__ void trace_at(const DitPersistArgs& a, int ph, int sl
 __device__ void res_sum2(float& v0, float& v1, float* red) {
   v0 = warp_sum(v0);
   v1 = warp_sum(v1);
-  const int w = threadIdx.x >> 5;
+  const int w = row_rank() >> 5;
   if ((threadIdx.x & 31) == 0) {
     red[w] = v0;
     red[8 + w] = v1;
@@ -286,7 +314,7 @@ __device__ void res_norm_rows(const DitPersistArgs& a, const float* base, const 
   float4 g[2];
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
-    cc[k] = (int)threadIdx.x * 4 + (NG == 2 ? k * 4 * DP_RES_THREADS : 0);
+    cc[k] = row_rank() * 4 + (NG == 2 ? k * 4 * DP_RES_THREADS : 0);
     g[k] = cc[k] < H ? __ldg(reinterpret_cast<const float4*>(w + cc[k])) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   for (int r0 = blockIdx.x; r0 < a.R; r0 += NR * G) {
@@ -356,7 +384,7 @@ __device__ void res_rows(const DitPersistArgs& a, const float* base, const Parts
 // reference computes them, into rope_tab [2][16][64] (grid-stride over the RES threads).
 __device__ void rope_table(const DitPersistArgs& a) {
   const int half = a.d / 2;
-  for (int i = blockIdx.x * DP_RES_THREADS + threadIdx.x; i < a.S * half; i += gridDim.x * DP_RES_THREADS) {
+  for (int i = blockIdx.x * DP_RES_THREADS + row_rank(); i < a.S * half; i += gridDim.x * DP_RES_THREADS) {
     const int p = i / half, j = i % half;
     const double f = ((double)p * a.rope->inv_freq[j]) / a.rope->ext[j];
     double sd, cd;
@@ -377,14 +405,26 @@ __device__ void att_unit(const DitPersistArgs& a, const Parts& q, int n, int h0,
   float* vs = ks + DP_SMAX * DP_QS;                 // [16][DP_QS]
   float* sc = sm.att + (DP_HPU + 2) * DP_SMAX * DP_QS;  // [hpu][16][16]
   float* inv = sc + DP_HPU * DP_SMAX * DP_SMAX;     // [hpu][16]
-  const int tid = threadIdx.x, rows = (hpu + 2) * S, cells = rows * d4;
+  float* rt = inv + DP_HPU * DP_SMAX;               // [2][16][32] cos, sin of positions 0..S-1
+  const int tid = row_rank(), rows = (hpu + 2) * S, cells = rows * d4;
+  // the rope values are loaded while the partial sums below are in flight
+  static_assert(2 * DP_ROW_THREADS >= DP_SMAX * 32, "rope values per thread");
+  float rc[2] = {0.f, 0.f}, rs[2] = {0.f, 0.f};
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int i = tid + k * DP_ROW_THREADS;
+    if (a.rope && i < S * half) {
+      rc[k] = __ldcg(a.rope_tab + (i / half) * 64 + i % half);
+      rs[k] = __ldcg(a.rope_tab + DP_SMAX * 64 + (i / half) * 64 + i % half);
+    }
+  }
   // q, k, v rows: two float4 cells per thread, eight slots each in flight
-  for (int i0 = tid; i0 < cells; i0 += 2 * DP_THREADS) {
+  for (int i0 = tid; i0 < cells; i0 += 2 * DP_ROW_THREADS) {
     PRange x[2];
     int dst[2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-      const int i = i0 + k * DP_THREADS;
+      const int i = i0 + k * DP_ROW_THREADS;
       x[k] = PRange{nullptr, 0};
       dst[k] = -1;
       if (i < cells) {
@@ -400,21 +440,29 @@ __device__ void att_unit(const DitPersistArgs& a, const Parts& q, int n, int h0,
     for (int k = 0; k < 2; ++k)
       if (dst[k] >= 0) *reinterpret_cast<float4*>(qs + dst[k]) = o[k];
   }
-  cta_sync();
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int i = tid + k * DP_ROW_THREADS;
+    if (a.rope && i < S * half) {
+      rt[(i / half) * 32 + i % half] = rc[k];
+      rt[DP_SMAX * 32 + (i / half) * 32 + i % half] = rs[k];
+    }
+  }
+  row_sync();
   if (threadIdx.x == 0 && n * (a.nh / hpu) + h0 / hpu == (int)blockIdx.x) trace_at(a, ph, 1);
   if (a.rope) {  // rows 0..hpu S-1 are q, rows hpu S.. are k (one rotation pair per thread)
-    for (int i = tid; i < (hpu + 1) * S * half; i += DP_THREADS) {
+    for (int i = tid; i < (hpu + 1) * S * half; i += DP_ROW_THREADS) {
       const int row = i / half, j = i % half, s = row % S;
       float* v = qs + ((row / S) * DP_SMAX + s) * DP_QS;
-      const float c = __ldcg(a.rope_tab + s * 64 + j), si = __ldcg(a.rope_tab + DP_SMAX * 64 + s * 64 + j);
+      const float c = rt[s * 32 + j], si = rt[DP_SMAX * 32 + s * 32 + j];
       const float x1 = v[j], x2 = v[j + half];
       v[j] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(-x2, si));
       v[j + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, si));
     }
-    cta_sync();
+    row_sync();
   }
   if (threadIdx.x == 0 && n * (a.nh / hpu) + h0 / hpu == (int)blockIdx.x) trace_at(a, ph, 3);
-  for (int i = tid; i < hpu * S * S; i += DP_THREADS) {
+  for (int i = tid; i < hpu * S * S; i += DP_ROW_THREADS) {
     const int hh = i / (S * S), s = (i / S) % S, t = i % S;
     const float4* qr = reinterpret_cast<const float4*>(qs + (hh * DP_SMAX + s) * DP_QS);
     const float4* kr = reinterpret_cast<const float4*>(ks + t * DP_QS);
@@ -428,7 +476,7 @@ __device__ void att_unit(const DitPersistArgs& a, const Parts& q, int n, int h0,
     }
     sc[(hh * DP_SMAX + s) * DP_SMAX + t] = ((a0 + a1) + (a2 + a3)) * a.attn_scale;
   }
-  cta_sync();
+  row_sync();
   if (tid < hpu * S) {
     float* row = sc + ((tid / S) * DP_SMAX + tid % S) * DP_SMAX;
     float mx = -FLT_MAX;
@@ -441,9 +489,9 @@ __device__ void att_unit(const DitPersistArgs& a, const Parts& q, int n, int h0,
     }
     inv[(tid / S) * DP_SMAX + tid % S] = 1.0f / den;
   }
-  cta_sync();
+  row_sync();
   const size_t plane = (size_t)a.Rpad * a.nh * d;
-  for (int i = tid; i < hpu * S * d4; i += DP_THREADS) {
+  for (int i = tid; i < hpu * S * d4; i += DP_ROW_THREADS) {
     const int hh = i / (S * d4), s = (i / d4) % S, e = (i % d4) * 4;
     const float* p = sc + (hh * DP_SMAX + s) * DP_SMAX;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -459,7 +507,7 @@ __device__ void att_unit(const DitPersistArgs& a, const Parts& q, int n, int h0,
     store_split4(a.xs, plane, (size_t)(n * S + s) * a.nh * d + (h0 + hh) * d + e,
                  make_float4(o.x * iv, o.y * iv, o.z * iv, o.w * iv));
   }
-  cta_sync();  // the scratch is free for the next unit
+  row_sync();  // the scratch is free for the next unit
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -477,13 +525,13 @@ __device__ __forceinline__ float warp_max(float v) {
 // dot products summed by a butterfly reduce-scatter (31 shuffles; lane j ends with position
 // j), then an online softmax in registers (running max and sum: the max-subtracted softmax of
 // attention.rs:186-191, accumulated tile by tile) and P V with the probabilities broadcast by
-// shuffles.  Output into the split operand (K = nh * d).  Run by all DP_THREADS threads
-// (warps >= nq only help with the loads); `uses` counts each tile buffer's completed copies
+// shuffles.  Output into the split operand (K = nh * d).  Run by the DP_ROW_THREADS row threads
+// (row warps >= nq only help with the loads); `uses` counts each tile buffer's completed copies
 // (uniform over the CTA).  Returns false if a copy wait gave up (error recorded).
 __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, int g, int split, int nsplit, int l,
                                 int pos, const Sm& sm, unsigned* uses, int ph) {
   constexpr int d = DP_DEC_D, half = d / 2, d4 = d / 4;
-  const int nq = a.nh / a.nkv, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nq = a.nh / a.nkv, tid = row_rank(), warp = tid >> 5, lane = tid & 31;
   float* qs = sm.att;  // [nq][d], then k [d], v [d]
   float* kn = qs + nq * d;
   float* vn = kn + d;
@@ -512,12 +560,12 @@ __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, 
   if (tid == 0)
     while (next < t0 + 2 && next < ntt - 1 && next < nt) issue(next);
   const int cells = (nq + 2) * d4;
-  for (int i0 = tid; i0 < cells; i0 += 2 * DP_THREADS) {
+  for (int i0 = tid; i0 < cells; i0 += 2 * DP_ROW_THREADS) {
     PRange x[2];
     int dst[2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-      const int i = i0 + k * DP_THREADS;
+      const int i = i0 + k * DP_ROW_THREADS;
       x[k] = PRange{nullptr, 0};
       dst[k] = -1;
       if (i < cells) {
@@ -537,10 +585,10 @@ __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, 
     cs[tid] = __ldg(a.rope_pos + ((size_t)pos * 2) * half + tid);
     sn[tid] = __ldg(a.rope_pos + ((size_t)pos * 2 + 1) * half + tid);
   }
-  cta_sync();
+  row_sync();
   if (tid == 0) trace_at(a, ph, 3);
   if (a.rope) {  // rows 0..nq-1 are the queries, row nq the key (one rotation pair per thread)
-    for (int i = tid; i < (nq + 1) * half; i += DP_THREADS) {
+    for (int i = tid; i < (nq + 1) * half; i += DP_ROW_THREADS) {
       float* v = qs + (i / half) * d;
       const int j = i % half;
       const float c = cs[j], si = sn[j];
@@ -548,17 +596,17 @@ __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, 
       v[j] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(-x2, si));
       v[j + half] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, si));
     }
-    cta_sync();
+    row_sync();
   }
   if (last_split) {
-    for (int e = tid; e < d; e += DP_THREADS) {
+    for (int e = tid; e < d; e += DP_ROW_THREADS) {
       kc[(size_t)pos * d + e] = kn[e];
       vc[(size_t)pos * d + e] = vn[e];
     }
     // the bulk copies below read the row just written through the generic proxy
     asm volatile("fence.proxy.async.global;" ::: "memory");
   }
-  cta_sync();
+  row_sync();
   if (tid == 0) {
     trace_at(a, ph, 1);
     if (next == t0) issue(t0);
@@ -574,7 +622,7 @@ __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, 
     const int b = t & 1, rows = min(DP_DEC_TILE, pos + 1 - t * DP_DEC_TILE);
     const bool w = mbar_wait(&sm.att_bar[b], uses[b] & 1, a.err);
     ++uses[b];
-    if (cta_or(!w)) {
+    if (row_or(!w)) {
       good = false;
       break;
     }
@@ -622,13 +670,13 @@ __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, 
         }
       }
     }
-    cta_sync();  // every reader of this buffer is done before the copy issued at t + 1 reuses it
+    row_sync();  // every reader of this buffer is done before the copy issued at t + 1 reuses it
   }
   if (!good) {  // copies still in flight land before the CTA leaves
     if (tid == 0)
       for (int b = 0; b < 2; ++b)
         for (; uses[b] < issued[b]; ++uses[b]) mbar_wait(&sm.att_bar[b], uses[b] & 1, a.err);
-    cta_sync();
+    row_sync();
     return false;
   }
   const size_t out_at = (size_t)n * a.nh * d + (g * nq + warp) * d + lane * 4;
@@ -638,7 +686,7 @@ __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, 
       const float iv = 1.0f / l_run;
       store_split4(a.xs, plane, out_at, make_float4(o.x * iv, o.y * iv, o.z * iv, o.w * iv));
     }
-    cta_sync();  // the scratch is free for the next unit
+    row_sync();  // the scratch is free for the next unit
     return true;
   }
   // split partials: [unit][split][head][d + 4] = o (unnormalised), running max, running sum, 2
@@ -653,7 +701,7 @@ __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, 
       part[warp * (d + 4) + d + 1] = l_run;
     }
   }
-  cta_sync();
+  row_sync();
   if (tid == 0) {
     __threadfence();
     const unsigned prev = atomicAdd(a.att_cnt + unit, 1u);
@@ -663,7 +711,7 @@ __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, 
       a.att_cnt[unit] = 0u;  // ready for the next layer
     }
   }
-  cta_sync();
+  row_sync();
   if (sm.flags[1] && head) {
     const float* pu = a.att_part + (size_t)unit * DP_DEC_SPLITS * nq * (d + 4) + warp * (d + 4);
     float mx = -FLT_MAX;
@@ -683,17 +731,17 @@ __device__ bool att_decode_unit(const DitPersistArgs& a, const Parts& q, int n, 
     const float iv = 1.0f / den;
     store_split4(a.xs, plane, out_at, make_float4(acc.x * iv, acc.y * iv, acc.z * iv, acc.w * iv));
   }
-  cta_sync();  // the scratch and the flag are free for the next unit
+  row_sync();  // the scratch and the flag are free for the next unit
   return true;
 }
 
 // ACT: silu(gate) * up, both summed from the GU partials, into the split operand (K = I);
-// two groups of four elements per thread in flight; run by all DP_THREADS threads.
+// two groups of four elements per thread in flight; run by the DP_ROW_THREADS row threads.
 __device__ void act_rows(const DitPersistArgs& a, const Parts& q) {
   const int I = a.I, i4 = I / 4;
   const size_t plane = (size_t)a.Rpad * I, n = (size_t)a.R * i4;
-  const size_t step = (size_t)gridDim.x * DP_THREADS;
-  for (size_t i0 = (size_t)blockIdx.x * DP_THREADS + threadIdx.x; i0 < n; i0 += 2 * step) {
+  const size_t step = (size_t)gridDim.x * DP_ROW_THREADS;
+  for (size_t i0 = (size_t)blockIdx.x * DP_ROW_THREADS + row_rank(); i0 < n; i0 += 2 * step) {
     PRange x[4];
     int rr[2], jj[2];
 #pragma unroll
@@ -851,7 +899,9 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
         }
         if (kind != PH_ATT) trace_at(a, ph, 1);
       }
-      if (kind == PH_ATT) {  // all warps
+      if (warp == 4) {
+        // the producer sits the row phases out (its weight prefetch is in flight)
+      } else if (kind == PH_ATT) {  // the row warps
         const Parts q = parts_of(a, sm, DP_KIND_QKV);
         if constexpr (MODE == DP_ATT_DECODE) {  // unit = (sequence, KV head, run of cache tiles)
           const int nbg = a.N * a.nkv;
@@ -866,9 +916,9 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
           const int hpu = a.N * a.nh > G && (a.nh / a.nkv) % DP_HPU == 0 ? DP_HPU : 1, per = a.nh / hpu;
           for (int u = blockIdx.x; u < a.N * per; u += G) att_unit(a, q, u / per, (u % per) * hpu, hpu, ph, sm);
         }
-      } else if (kind == PH_ACT) {  // all warps
+      } else if (kind == PH_ACT) {  // the row warps
         act_rows(a, parts_of(a, sm, DP_KIND_GU));
-      } else if (threadIdx.x < DP_RES_THREADS) {
+      } else if (row_rank() < DP_RES_THREADS) {
         if (kind == -1) {  // final: RMSNorm(x1 + s * down) with the final norm weight
           const Parts q = parts_of(a, sm, DP_KIND_DOWN);
           res_rows(a, a.x1, &q, nullptr, a.final_norm, nullptr, a.out, sm);
@@ -1160,7 +1210,7 @@ bool persist_stack_prepare(PersistStack& ps, const LmStackView& v, int max_rows,
                         (2 * v.I) % um == 0 && v.I % 64 == 0 && max_rows > 0;
   if (!shape_ok) return false;
   ps.seq_ok = v.d <= 64;
-  ps.decode_ok = v.d == DP_DEC_D && nq <= DP_DEC_NQ;
+  ps.decode_ok = v.d == DP_DEC_D && nq <= DP_DEC_NQ && nq <= DP_ROW_THREADS / 32;
   if (dit_persist_configure() != cudaSuccess) {
     cudaGetLastError();
     return false;
@@ -1175,10 +1225,11 @@ bool persist_stack_prepare(PersistStack& ps, const LmStackView& v, int max_rows,
   const int kchs[DP_KINDS] = {v.H / 64, v.nh * v.d / 64, v.H / 64, (int)(I / 64)};
   // (fewer CTAs per unit: fewer partial slots for the next row phase to sum; measured best for
   // the 8-row LM step at 256-row units, and for the 176-row DiT forward at 128-row units)
-  int min_pairs[DP_KINDS] = {2, 2, 1, 4};
-  if (um == DP_UM_MAX) {
+  int min_pairs[DP_KINDS] = {2, 2, 8, 4};  // 176-row DiT forward: 563.5 -> 542.5 us against {2, 2, 1, 4}
+  if (um == DP_UM_MAX) {                    // 8-row LM step: 2.14 -> 2.05 ms against {2, 2, 1, 4}
     min_pairs[DP_KIND_QKV] = 4;
     min_pairs[DP_KIND_O] = 4;
+    min_pairs[DP_KIND_GU] = 1;
     min_pairs[DP_KIND_DOWN] = 8;
   }
   if (const char* e = getenv("VX_DIT_PAIRS"))
