@@ -56,8 +56,9 @@ extern "C" int vx_generate(vx_lm* lm, vx_dit* dit, vx_vae* vae, const int32_t* p
       rc = lm_greedy_step(lm);
       if (rc) break;
       // UnifiedCfm::forward(mu = hidden, cond = previous patch, z = noise_i) (model.rs:229-238)
-      rc = vx_cfm_solve(dit, lm_hid_norm(lm), cond, d_noise + patch * i, 1, H, P, P, opts->inference_timesteps,
-                        opts->cfg_value, opts->sway_sampling_coef, opts->use_cfg_zero_star, pred);
+      // queued without a host wait: the host runs ahead, the device never idles between steps
+      rc = cfm_solve_enqueue(dit, lm_hid_norm(lm), cond, d_noise + patch * i, 1, H, P, P, opts->inference_timesteps,
+                             opts->cfg_value, opts->sway_sampling_coef, opts->use_cfg_zero_star, pred);
       if (rc) break;
       // latent[:, i*P + p] = pred[:, p]
       if (cudaMemcpy2DAsync(d_latent + (size_t)i * P, frames * 4, pred, (size_t)P * 4, (size_t)P * 4, C,
@@ -138,8 +139,8 @@ extern "C" int vx_generate_batch(vx_lm* lm, vx_dit* dit, vx_vae* vae, const int3
         rc = fail(ctx, VX_ERR_CUDA, "generate: noise gather failed");
         break;
       }
-      rc = vx_cfm_solve(dit, lm_batch_hidden(lm), cond, d_z, B, H, P, P, opts->inference_timesteps, opts->cfg_value,
-                        opts->sway_sampling_coef, opts->use_cfg_zero_star, pred);
+      rc = cfm_solve_enqueue(dit, lm_batch_hidden(lm), cond, d_z, B, H, P, P, opts->inference_timesteps,
+                             opts->cfg_value, opts->sway_sampling_coef, opts->use_cfg_zero_star, pred);
       if (rc) break;
       // latent[b][c][i*P + p] = pred[b][c][p]: B*C rows of P frames
       if (cudaMemcpy2DAsync(d_latent + (size_t)i * P, frames * 4, pred, (size_t)P * 4, (size_t)P * 4, (size_t)B * C,
