@@ -595,8 +595,8 @@ int vx_lm_create(vx_ctx* ctx, const vx_minicpm4_config* cfg, int max_batch, int 
            cudaMalloc(&lm->pk_layers, sizeof(PersistLayer) * lm->L) == cudaSuccess &&
            cudaMemcpy(lm->pk_layers, pl.data(), sizeof(PersistLayer) * lm->L, cudaMemcpyHostToDevice) == cudaSuccess &&
            cudaMalloc(&lm->pk_cnt, nc * 4) == cudaSuccess && cudaMemset(lm->pk_cnt, 0, nc * 4) == cudaSuccess &&
-           cudaMalloc(&lm->pk_att_part, persist_att_part_floats(lm->nkv, lm->nh, d) * 4) ==
-               cudaSuccess;
+           cudaMalloc(&lm->pk_att_part, persist_att_global_floats(lm->nkv, lm->nh, d) * 4) == cudaSuccess &&
+           cudaMemset(lm->pk_att_part, 0, persist_att_global_floats(lm->nkv, lm->nh, d) * 4) == cudaSuccess;
       if (!ok) {
         cudaGetLastError();
         return fail_free(VX_ERR_OOM, "persistent decode buffers allocation failed");
@@ -868,7 +868,12 @@ int lm_greedy_begin(vx_lm* lm, const int32_t* prompt_ids, int n_prompt, int n_st
   rc = build_step_graph(lm);
   if (rc) return rc;
   VX_CUDA(ctx, cudaEventRecord(lm->ev[0], st));
-  if (lm->pk_cnt) VX_CUDA(ctx, cudaMemsetAsync(lm->pk_cnt, 0, persist_counter_count(lm->L) * 4, st));
+  if (lm->pk_cnt) {
+    VX_CUDA(ctx, cudaMemsetAsync(lm->pk_cnt, 0, persist_counter_count(lm->L) * 4, st));
+    // the attention arrival counters behind the split partials and the merged output
+    const size_t off = persist_att_partials_floats(lm->nkv, lm->nh, lm->d) + (size_t)lm->nh * lm->d;
+    VX_CUDA(ctx, cudaMemsetAsync(lm->pk_att_part + off, 0, (size_t)lm->nkv * 4, st));
+  }
   VX_CUDA(ctx, cudaMemsetAsync(lm->attn_counters, 0, (size_t)lm->max_batch * lm->nkv * 4, st));
   VX_CUDA(ctx, cudaMemsetAsync(lm->argmax_counter, 0, 4, st));
   // prefill: embed * scale_emb -> causal forward -> StaticKvCache::fill (voxcpm2/model.rs:144-191)
@@ -1077,6 +1082,9 @@ int vx_lm_trace_decode_step(vx_lm* lm, int pos, unsigned long long* trace_out, i
   cudaError_t e = cudaMemsetAsync(dtrace, 0, ne * 8, st);
   if (e == cudaSuccess) e = cudaMemcpyAsync(lm->d_pos, &lm->pos_host, 4, cudaMemcpyHostToDevice, st);
   if (e == cudaSuccess) e = cudaMemsetAsync(lm->pk_cnt, 0, persist_counter_count(lm->L) * 4, st);
+  if (e == cudaSuccess)
+    e = cudaMemsetAsync(lm->pk_att_part + persist_att_partials_floats(lm->nkv, lm->nh, lm->d) + (size_t)lm->nh * lm->d,
+                        0, (size_t)lm->nkv * 4, st);
   if (e == cudaSuccess) e = enqueue_persist_step(lm, st, true, dtrace);
   if (e == cudaSuccess) e = cudaMemcpyAsync(trace_out, dtrace, ne * 8, cudaMemcpyDeviceToHost, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);

@@ -19,8 +19,11 @@
 //   ATT  flash-decode over the cached prefix (attention.rs:129-150, 156-204); unit = one KV
 //        head's 8 query heads against a run of 32-position tiles whose K/V rows arrive
 //        through the ring (the current position's row, written by Q, is read after the
-//        wait); each unit leaves its online-softmax partial (o, max, sum) in global memory
-//   O    merge of the attention partials -> o_proj + residual into x1 (attention.rs:153,
+//        wait); each unit leaves its online-softmax partial (o, max, sum) in global memory.
+//        Caches of more than 16 tiles get a unit per tile (up to 64 per KV head) and the
+//        last unit of a KV head to finish merges its partials into the attention output.
+//   O    the attention output (short caches: every CTA merges the <= 8 partials per KV head
+//        itself from one bulk copy) -> o_proj + residual into x1 (attention.rs:153,
 //        layer.rs:67); unit = 8 rows.  Also seeds the next layer's residual accumulator
 //        with x1 (fixed point, below).
 //   M    post-attention RMSNorm -> gate|up rows -> silu(gate)*up -> down_proj (mlp.rs:28-34,
@@ -522,7 +525,16 @@ __device__ void load_x(const XIn& x, const float* norm_w, int K, float eps, cons
   csync();
 }
 
-// The attention output [nh*D] -> xs: per query head, the merge of its KV head's split
+// The merged attention output and the arrival counters behind the split partials in att_part.
+__device__ __forceinline__ float* att_out(const PersistArgs& a, int D) {
+  return a.att_part + persist_att_partials_floats(a.nkv, a.nh, D);
+}
+__device__ __forceinline__ unsigned* att_counters(const PersistArgs& a, int D) {
+  return reinterpret_cast<unsigned*>(att_out(a, D) + (size_t)a.nh * D);
+}
+
+// Short caches (at most PERSIST_ATT_SPLITS splits per KV head): the attention output [nh*D]
+// -> xs in every CTA of the o_proj phase: per query head, the merge of its KV head's split
 // partials (o unnormalised, max m, sum l): out = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s
 // with M the largest m_s (attention.rs:186-191 over the whole prefix).  One bulk copy per KV
 // head brings the partials into shared memory (one L2 round trip; they were written by other
@@ -532,12 +544,13 @@ __device__ void load_x(const XIn& x, const float* norm_w, int K, float eps, cons
 template <int D>
 __device__ bool att_merge(const PersistArgs& a, const AttGeo& at, const Smem& sm, int use) {
   const int nhd = a.nh * D, ns = at.nsplit;
-  const size_t gstride = (size_t)PERSIST_ATT_SPLITS * NREP * (D + 4);  // floats per KV head
+  const size_t gstride = (size_t)PERSIST_ATT_SPLITS * NREP * (D + 4);      // shared floats per KV head
+  const size_t gsrc = (size_t)PERSIST_ATT_SPLITS_MAX * NREP * (D + 4);    // global floats per KV head
   if (threadIdx.x == 0) {
     asm volatile("fence.proxy.async.global;" ::: "memory");
     const uint32_t bytes = (uint32_t)(ns * NREP * (D + 4) * 4);
     mbar_arrive_expect_tx(sm.pbar, bytes * a.nkv);
-    for (int g = 0; g < a.nkv; ++g) bulk_g2s(sm.parts + g * gstride, a.att_part + g * gstride, bytes, sm.pbar);
+    for (int g = 0; g < a.nkv; ++g) bulk_g2s(sm.parts + g * gstride, a.att_part + g * gsrc, bytes, sm.pbar);
   }
   const bool ok = wait_full(sm.pbar, use & 1, a.err, sm.flags);
   if (ok) {
@@ -570,6 +583,102 @@ __device__ bool att_merge(const PersistArgs& a, const AttGeo& at, const Smem& sm
   return !sync_or(!ok);
 }
 
+// After attention unit u (its partial stored by every warp, then a consumer barrier): count
+// it in for its KV head; the last split to arrive merges the head group's split partials
+// (o unnormalised, max m, sum l): out = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s with M
+// the largest m_s (attention.rs:186-191 over the whole prefix), in split order, into the
+// attention output (warp = query head, lane = DPL dims).  The counter is left at zero.
+template <int D>
+__device__ void att_finish(const PersistArgs& a, const AttGeo& at, int u, const Smem& sm) {
+  constexpr int DPL = D / 32;
+  const int g = u / at.nsplit, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    unsigned* cnt = att_counters(a, D) + g;
+    __threadfence();
+    const unsigned prev = atomicAdd(cnt, 1u);
+    sm.flags[1] = prev == (unsigned)at.nsplit - 1 ? 1 : 0;
+    if (sm.flags[1]) {
+      __threadfence();
+      *cnt = 0u;
+    }
+  }
+  csync();
+  if (sm.flags[1]) {
+    // warp = query head: lane s holds split s's (m, l) (and s + 32), the max and the weighted
+    // sum are warp reductions, then every split's o slice is loaded with the weights broadcast
+    const float* p0 = a.att_part + ((size_t)g * PERSIST_ATT_SPLITS_MAX * NREP + warp) * (D + 4);
+    const size_t ss = (size_t)NREP * (D + 4);
+    static_assert(PERSIST_ATT_SPLITS_MAX <= 64, "two splits per lane");
+    const int ns = at.nsplit;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    // the first 16 splits' o slices are requested together with the (m, l) pairs
+    constexpr int MB = 16;
+    float ov[MB][DPL];
+    auto load_o = [&](int s0) {
+#pragma unroll
+      for (int i = 0; i < MB; ++i) {
+        if (DPL == 4) {
+          const float4 v = s0 + i < ns ? ldcg4(p0 + (s0 + i) * ss + lane * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+          ov[i][0] = v.x;
+          ov[i][1 % DPL] = v.y;
+          ov[i][2 % DPL] = v.z;
+          ov[i][3 % DPL] = v.w;
+        } else {
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) ov[i][e] = s0 + i < ns ? __ldcg(p0 + (s0 + i) * ss + lane * DPL + e) : 0.f;
+        }
+      }
+    };
+    if (lane < ns) {
+      m0 = __ldcg(p0 + lane * ss + D);
+      l0 = __ldcg(p0 + lane * ss + D + 1);
+    }
+    if (lane + 32 < ns) {
+      m1 = __ldcg(p0 + (lane + 32) * ss + D);
+      l1 = __ldcg(p0 + (lane + 32) * ss + D + 1);
+    }
+    load_o(0);
+    const float M = warp_max(fmaxf(m0, m1));
+    const float f0 = lane < ns ? expf(m0 - M) : 0.f, f1 = lane + 32 < ns ? expf(m1 - M) : 0.f;
+    const float Ls = warp_sum(f0 * l0 + f1 * l1);
+    float acc[DPL];
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) acc[e] = 0.f;
+    for (int s0 = 0; s0 < ns; s0 += MB) {
+      if (s0 > 0) load_o(s0);
+#pragma unroll
+      for (int i = 0; i < MB; ++i) {
+        const int sp = s0 + i;
+        const float f = __shfl_sync(0xffffffffu, sp < 32 ? f0 : f1, sp & 31);
+        if (sp < ns)
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) acc[e] = fmaf(f, ov[i][e], acc[e]);
+      }
+    }
+    float* out = att_out(a, D) + (size_t)(g * NREP + warp) * D + lane * DPL;
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) out[e] = acc[e] / Ls;
+  }
+  csync();  // flags[1] is free again
+}
+
+// The attention output [nh*D] -> xs for the o_proj phase: one bulk copy (one L2 round trip;
+// written by other CTAs' generic stores, hence the proxy fence).  `use` counts this CTA's
+// earlier copies (the parity of sm.pbar).  Returns false on a failed wait.
+template <int D>
+__device__ bool att_load(const PersistArgs& a, const Smem& sm, int use) {
+  const uint32_t bytes = (uint32_t)a.nh * D * 4;
+  csync();  // nobody still reads xs
+  if (threadIdx.x == 0) {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_arrive_expect_tx(sm.pbar, bytes);
+    bulk_g2s(sm.xs, att_out(a, D), bytes, sm.pbar);
+  }
+  const bool ok = wait_full(sm.pbar, use & 1, a.err, sm.flags);
+  return !sync_or(!ok);
+}
+
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
@@ -578,7 +687,7 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
 struct CState {
   int s;      // ring stages consumed
   int bad;    // the step must stop
-  int merges; // attention merges done (parity of sm.pbar)
+  int merges; // attention output copies done (parity of sm.pbar)
 };
 
 // One attention unit: query heads g*8..g*8+7 against the positions of its tiles
@@ -667,7 +776,7 @@ __device__ bool att_unit(const PersistArgs& a, const AttGeo& at, int l, int u, c
     if (lane == 0) mbar_arrive(&sm.empty[slot]);
     ++st.s;
   }
-  float* pp = a.att_part + (((size_t)g * PERSIST_ATT_SPLITS + sp) * NREP + warp) * (D + 4);
+  float* pp = a.att_part + (((size_t)g * PERSIST_ATT_SPLITS_MAX + sp) * NREP + warp) * (D + 4);
 #pragma unroll
   for (int e = 0; e < DPL; ++e) pp[lane * DPL + e] = o[e];
   if (lane == 0) {
@@ -683,11 +792,12 @@ __device__ __forceinline__ CState att_units(const PersistArgs& a, const Smem& sm
                                             int l, int first) {
   for (int u = first; u < at.items; u += gridDim.x) {
     const bool ok = att_unit<KC, D>(a, at, l, u, sm, st, nst);
-    csync();  // xs (queries) reused by the next unit
+    csync();  // xs (queries) reused by the next unit; every warp's partial is stored
     if (!ok) {
       st.bad = 1;
       break;
     }
+    if (at.nsplit > PERSIST_ATT_SPLITS) att_finish<D>(a, at, u, sm);
   }
   return st;
 }
@@ -774,7 +884,7 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
     resv[k] = (kind == PH_O && lane == 0 && u < U) ? ldx1(resid, u * PK_ROWS + warp) : 0.f;
   }
   if (kind == PH_O) {
-    if (!att_merge<D>(a, at, sm, st.merges++)) {
+    if (!(at.nsplit > PERSIST_ATT_SPLITS ? att_load<D>(a, sm, st.merges++) : att_merge<D>(a, at, sm, st.merges++))) {
       st.bad = 1;
       return st;
     }
@@ -1027,7 +1137,10 @@ __global__ void __launch_bounds__(PK_THREADS, 1) persist_decode_kernel(const Per
   at.len = at.pos + 1;
   at.span = att_span;
   at.ntiles = (at.len + att_span - 1) / att_span;
-  at.nsplit = min(at.ntiles, PERSIST_ATT_SPLITS);
+  // up to 16 tiles: at most PERSIST_ATT_SPLITS splits, merged from shared memory in every o_proj
+  // CTA; longer caches: a split per tile (up to the grid), merged once per KV head
+  at.nsplit = at.ntiles <= 2 * PERSIST_ATT_SPLITS ? min(at.ntiles, PERSIST_ATT_SPLITS)
+                                                  : min(at.ntiles, min(PERSIST_ATT_SPLITS_MAX, max(1, G / a.nkv)));
   at.tps = (at.ntiles + at.nsplit - 1) / at.nsplit;
   at.nsplit = (at.ntiles + at.tps - 1) / at.tps;
   at.items = a.nkv * at.nsplit;
@@ -1192,6 +1305,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) persist_decode_kernel(const Per
     const unsigned prev = atomicAdd(a.phase_cnt + nc - 1, 1u);
     if (prev == (unsigned)G - 1) {
       for (int i = 0; i < nc; ++i) a.phase_cnt[i] = 0u;
+      for (int g = 0; g < a.nkv; ++g) att_counters(a, D)[g] = 0u;  // zero already unless a unit gave up
       __threadfence();
     }
   }

@@ -21,9 +21,13 @@ struct PersistLayer {
 
 // Phases per decoder layer: qkv+rope, attention, o_proj, MLP (gate|up + down); then the head.
 constexpr int PERSIST_PHASES_PER_LAYER = 4;
-// Attention splits per KV head (each split covers whole 32-position tiles); the O phase
-// stages all partials of a layer in shared memory.
+// Attention splits per KV head: the cache walk of a KV head is split over up to
+// PERSIST_ATT_SPLITS_MAX units (whole 32-position tiles each); each leaves its online-softmax
+// partial (o, m, l) in att_part and the last to finish merges them (split order) into the
+// attention output that the o_proj phase copies in.  PERSIST_ATT_SPLITS sizes the kernel's
+// shared scratch (the head phase keeps its row partials there).
 constexpr int PERSIST_ATT_SPLITS = 8;
+constexpr int PERSIST_ATT_SPLITS_MAX = 64;
 
 struct PersistArgs {
   int L, H, I, nh, nkv, d, V, s_max;
@@ -47,7 +51,8 @@ struct PersistArgs {
   float* q;                    // post-RoPE queries [nh*d]
   float* logits;               // optional [V]
   float* hid_norm;             // final-norm hidden [H]
-  float* att_part;             // [nkv][PERSIST_ATT_SPLITS][nh/nkv][d+4] split partials (o, m, l)
+  float* att_part;             // [nkv][PERSIST_ATT_SPLITS_MAX][nh/nkv][d+4] split partials (o, m, l),
+                               // then the merged output [nh][d], then [nkv] arrival counters (zeroed)
   float2* am_part;             // [grid] per-CTA argmax partials
   unsigned* phase_cnt;         // [4L + 2] phase arrival counters, zero between launches
   int* err;                    // device error word
@@ -77,6 +82,14 @@ inline size_t persist_trace_entries(int L, int grid) { return persist_phase_coun
 inline size_t persist_counter_count(int L) { return (size_t)PERSIST_PHASES_PER_LAYER * L + 2; }
 __host__ __device__ inline size_t persist_att_part_floats(int nkv, int nh, int d) {
   return (size_t)nkv * PERSIST_ATT_SPLITS * (nh / (nkv > 0 ? nkv : 1)) * (d + 4);
+}
+// att_part as allocated: the partials of PERSIST_ATT_SPLITS_MAX splits, the merged output and
+// the counters (one 4-byte word per KV head).
+__host__ __device__ inline size_t persist_att_partials_floats(int nkv, int nh, int d) {
+  return (size_t)nkv * PERSIST_ATT_SPLITS_MAX * (nh / (nkv > 0 ? nkv : 1)) * (d + 4);
+}
+__host__ __device__ inline size_t persist_att_global_floats(int nkv, int nh, int d) {
+  return persist_att_partials_floats(nkv, nh, d) + (size_t)nh * d + (size_t)((nkv + 3) / 4) * 4;
 }
 
 // Whether the persistent step supports this model shape (else the per-kernel step is used).
