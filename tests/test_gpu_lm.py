@@ -116,6 +116,30 @@ def test_greedy_tokens_exact(ctx):
     m.close()
 
 
+def test_greedy_long_cache(ctx):
+    """Greedy decode past position 512 (600-id prompt + 24 steps: 19-20 cache tiles), where the
+    persistent step splits the cache walk into one attention unit per tile and the last unit
+    of each KV head merges the partials: ids bit-exact with the oracle, last logits identical
+    over two runs."""
+    from voxcpm_rs_b200 import config, synth
+    from voxcpm_rs_b200.minicpm4 import MiniCpmModel
+    cfg = config.lm_decode_config(layers=2, vocab=4096)
+    w = synth.minicpm_weights(cfg, seed=7, std=0.2)
+    prompt = synth.prompt_ids(600, cfg.vocab_size, seed=7)
+    n_steps = 24
+    want, margins = om.greedy_generate(cfg, synth.minicpm_f32_view(w), prompt, n_steps, 4096, return_margins=True)
+    assert len(set(want)) > 10 and min(margins) > 1e-3, "degenerate or tie-ambiguous seed"
+    m = MiniCpmModel(ctx, cfg, w, max_length=4096)
+    got = m.greedy(prompt, n_steps)
+    lg = m.last_logits().view(np.uint32).copy()
+    m.reset()
+    got2 = m.greedy(prompt, n_steps)
+    lg2 = m.last_logits().view(np.uint32).copy()
+    m.close()
+    assert got.tolist() == want, f"tokens differ: {got.tolist()} vs {want}"
+    assert got2.tolist() == want and np.array_equal(lg, lg2)
+
+
 def test_kv_full_and_cancel(ctx, small_lm):
     """`KV cache is full` (cache.rs:61) and Error::Cancelled surface as status codes."""
     from voxcpm_rs_b200._lib import Cancelled, VxError
