@@ -187,6 +187,8 @@ int vx_ctx_synchronize(vx_ctx* ctx) {
   VX_CUDA(ctx, cudaMemcpy(&derr, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost));
   if (derr) {
     cudaMemset(ctx->dev_err, 0, sizeof(int));
+    if (derr == VX_DEVICE_ERR_BOUNDS)  // a kernel's own bounds check refused an index (nothing written)
+      return fail(ctx, VX_ERR_ARG, "device-side bounds check failed (code %d)", derr);
     return fail(ctx, VX_ERR_TIMEOUT, "device-side wait gave up (code %d)", derr);
   }
   return VX_OK;

@@ -863,6 +863,10 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
     tmap_prefetch(&a.xmaps[1]);
   }
   bool ok = true;
+  if (MODE == DP_ATT_DECODE && (dec_pos < 0 || dec_pos >= a.max_len)) {  // no cache row for it: stop
+    if (threadIdx.x == 0) record_error(a.err, VX_DEVICE_ERR_BOUNDS);
+    ok = false;
+  }
   const int G = gridDim.x;
   const int nph = a.L * PH_N + 1;
 
