@@ -1,12 +1,17 @@
-// Persistent forward of a non-causal MiniCPM-4 stack over a few token rows on the tensor cores
-// (sm_100a): the LocDiT decoder of every CFM Euler step (reference MiniCpmModel::forward with
-// is_causal = false, src/minicpm4/model.rs:43-62, as VoxCpmLocDiTV2::forward_cached runs it,
-// src/locdit/local_dit.rs:138-159).  One cooperative launch runs all layers; per layer
+// Persistent forward of a MiniCPM-4 stack over a few token rows on the tensor cores (sm_100a),
+// one cooperative launch for all layers, in two attention modes:
+//   DP_ATT_SEQ     the LocDiT decoder of every CFM Euler step: non-causal attention within
+//                  each sequence of S <= 16 rows (reference MiniCpmModel::forward with
+//                  is_causal = false, src/minicpm4/model.rs:43-62, as VoxCpmLocDiTV2::
+//                  forward_cached runs it, src/locdit/local_dit.rs:138-159);
+//   DP_ATT_DECODE  a batched greedy step: one new row per sequence at the device position,
+//                  attending to the static KV cache after writing its k, v there (forward_step,
+//                  model.rs:64-84, attention.rs:91-154, cache.rs:47-58).
+// Per layer
 //
 //   RES_A   x = x1 + s * down (layer 0: the input rows); x_n = RMSNorm(x)   -> split operand
 //   QKV     qkv = W_qkv x_n                                                  (tcgen05 GEMM)
-//   ATT     LongRoPE on q, k; softmax(q k^T / sqrt(d)) v per sequence and
-//           KV head (GQA, no mask)                                           -> split operand
+//   ATT     LongRoPE on q, k; softmax(q k^T / sqrt(d)) v (GQA)               -> split operand
 //   O       o = W_o attn                                                     (tcgen05 GEMM)
 //   RES_B   x1 = x + s * o; x1_n = RMSNorm(x1)                               -> split operand
 //   GU      [g | u] = W_gu x1_n                                              (tcgen05 GEMM)
@@ -17,21 +22,24 @@
 // attention.rs:55-88, mod.rs:54-68).  Phases are separated by a grid barrier (release /
 // acquire counters; all CTAs are resident).
 //
-// GEMM phases: the weights are the A operand (units of 256 rows = two 128-row MMA tiles, one
-// 256 x 64 TMA box per K chunk, SWIZZLE_128B, no multicast); the activations are the B
-// operand: the row phase before wrote them as two bf16 planes x = hi + lo ([2][Rpad][K],
-// token-major), both fetched by one 3-D box, so each K chunk is four MMAs (two tiles x hi, lo)
-// into two f32 TMEM accumulators of Rpad columns.  Two copies per 32 KB of weights: the TMA
-// engine's per-SM copy rate, not the bytes, bounds these phases at few activation rows.  A
-// phase's (unit, K chunk) pairs are dealt to its CTAs in contiguous runs, so a unit's K range
-// may be split over CTAs: each run inside one unit (a segment) stores its f32 partial tile
-// into its own slot of the partial buffer with plain stores, and the phase that consumes the GEMM sums a tile's slots in slot
-// order.  No atomics: the sum, and so the forward, does not depend on the order in which CTAs
-// finish (deterministic).  Warp 4 issues the TMA loads, warp 5 the MMAs, warps 0-3 read TMEM;
-// the row phases run on warps 0-7 (RES) or all twelve warps (attention, SiLU*up): their partial
-// sums are L2 reads, whose rate grows with the loads in flight per SM.  Weight tiles of the next
-// GEMM phase stream into the ring during the row phase before it.  Every wait is bounded; a
-// timeout records an error and the CTA stops cleanly.
+// GEMM phases: the weights are the A operand (units of UM = 128 or 256 rows, one UM x 64 TMA
+// box per K chunk, SWIZZLE_128B, no multicast); the activations are the B operand: the row
+// phase before wrote them as two bf16 planes x = hi + lo ([2][Rpad][K], token-major), both
+// fetched by one 3-D box, so each K chunk is 2 UM / 128 MMAs (per 128-row tile: hi, lo) into
+// UM / 128 f32 TMEM accumulators of Rpad columns.  256-row units (stacks of <= 64 rows) halve
+// the copies per byte of weights: the TMA engine's per-SM copy rate, not the bytes, bounds
+// these phases at few activation rows.  A phase's (unit, K chunk) pairs are dealt to its CTAs
+// in contiguous runs, so a unit's K range may be split over CTAs: each run inside one unit (a
+// segment) stores its f32 partial tile into its own slot of the partial buffer with plain
+// stores, and the phase that consumes the GEMM sums a unit's slots in slot order.  No atomics:
+// the sum, and so the forward, does not depend on the order in which CTAs finish
+// (deterministic; the decode attention's split merge is in split order too).
+//
+// Warps: 4 issues the TMA loads, 5 the MMAs, 0-3 read TMEM; the row phases run on the other
+// eleven warps (RES on eight of them): their partial sums are L2 reads, whose rate grows with
+// the loads in flight per SM, and the producer warp meanwhile streams the next GEMM phase's
+// first weight tiles into the ring.  Every wait is bounded; a timeout records an error and the
+// CTA stops cleanly (in-flight copies landed, TMEM freed).
 #include <cuda_bf16.h>
 
 #include <algorithm>
