@@ -129,6 +129,8 @@ struct vx_dit {
   size_t xw_cap = 0;
   float* tsched = nullptr;
   int tsched_cap = 0;
+  float* temb_all = nullptr;  // [steps][H]: every Euler step's time embedding, computed once per solve
+  float* temb_tmp = nullptr;  // [steps][H]: its scratch
   cudaGraphExec_t solve_exec = nullptr;
   CfmKey solve_key{};
   unsigned long long solve_kernels = 0;
@@ -176,24 +178,26 @@ int dit_buffers(vx_dit* d, int rows, int S, int C, int T, int Tc, int Cmu) {
   return VX_OK;
 }
 
+// tmp: scratch of rows x H floats (default d->tmp, which holds the forward's rows).
 int launch_time_mlp(vx_dit* d, const uint16_t* w1, const float* b1, const uint16_t* w2, const float* b2,
-                    const float* tvals, int rows, float* out, cudaStream_t st) {
+                    const float* tvals, int rows, float* out, cudaStream_t st, float* tmp = nullptr) {
   // TimestepEmbedding::forward(SinusoidalPosEmb(t, 1000)) (local_dit.rs:50-54, 147-148)
   vx_ctx* ctx = d->ctx;
   const int H = d->H, half = H / 2;
+  if (!tmp) tmp = d->tmp;
   count_launch();
   sinusoidal_kernel<<<std::max(1, (rows * half + 255) / 256), 256, 0, st>>>(tvals, rows, 1000.0f, d->freqs, half,
-                                                                              d->tmp);
+                                                                              tmp);
   VX_CUDA(ctx, cudaGetLastError());
   const LinearWorkspace* ws = lm_workspace(d->dec);
-  int rc = linear(ctx, ws, d->tmp, H, rows, H, H, w1, b1, nullptr, 1.f, out, H, st);
+  int rc = linear(ctx, ws, tmp, H, rows, H, H, w1, b1, nullptr, 1.f, out, H, st);
   if (rc) return rc;
   count_launch();
   silu_inplace_kernel<<<std::max(1, (rows * H + 255) / 256), 256, 0, st>>>(out, (size_t)rows * H);
   VX_CUDA(ctx, cudaGetLastError());
-  rc = linear(ctx, ws, out, H, rows, H, H, w2, b2, nullptr, 1.f, d->tmp, H, st);
+  rc = linear(ctx, ws, out, H, rows, H, H, w2, b2, nullptr, 1.f, tmp, H, st);
   if (rc) return rc;
-  VX_CUDA(ctx, cudaMemcpyAsync(out, d->tmp, (size_t)rows * H * 4, cudaMemcpyDeviceToDevice, st));
+  VX_CUDA(ctx, cudaMemcpyAsync(out, tmp, (size_t)rows * H * 4, cudaMemcpyDeviceToDevice, st));
   return VX_OK;
 }
 
@@ -292,12 +296,15 @@ int build_solve_graph(vx_dit* d, const CfmKey& k) {
       break;
     }
     rc = launch_time_mlp(d, d->dt1_w, d->dt1_b, d->dt2_w, d->dt2_b, d->tsched, 1, d->dtemb, st);
+    // the time embeddings of all steps at once (the t schedule is known up front): one
+    // multi-row GEMM per layer of the time MLP instead of a GEMV pair per step
+    if (!rc)
+      rc = launch_time_mlp(d, d->t1_w, d->t1_b, d->t2_w, d->t2_b, d->tsched + 1, n - 1, d->temb_all, st, d->temb_tmp);
     for (int step = 1; step < n && !rc; ++step) {
       if (!run[step]) continue;
-      rc = launch_time_mlp(d, d->t1_w, d->t1_b, d->t2_w, d->t2_b, d->tsched + step, 1, d->temb, st);
-      if (rc) break;
       count_launch();
-      seq_head_kernel<<<N, 256, 0, st>>>(d->mu_in, mu_tokens, d->temb, 1, d->dtemb, 1, N, S, H, d->seq);
+      seq_head_kernel<<<N, 256, 0, st>>>(d->mu_in, mu_tokens, d->temb_all + (size_t)(step - 1) * H, 1, d->dtemb, 1,
+                                         N, S, H, d->seq);
       if (cudaGetLastError() != cudaSuccess) {
         rc = fail(ctx, VX_ERR_CUDA, "cfm graph: sequence assembly launch failed");
         break;
@@ -380,7 +387,7 @@ void vx_dit_destroy(vx_dit* d) {
   if (d->dec) vx_lm_destroy(d->dec);
   void* ptrs[] = {d->in_w, d->cond_w, d->out_w, d->t1_w, d->t2_w, d->dt1_w, d->dt2_w, d->in_b, d->cond_b,
                   d->out_b, d->t1_b, d->t2_b, d->dt1_b, d->dt2_b, d->freqs, d->seq, d->hid, d->temb,
-                  d->dtemb, d->tmp, d->tvals, d->out2b, d->mu_in, d->cond_in, d->xw, d->tsched};
+                  d->dtemb, d->tmp, d->tvals, d->out2b, d->mu_in, d->cond_in, d->xw, d->tsched, d->temb_all, d->temb_tmp};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   delete d;
@@ -503,6 +510,11 @@ int cfm_solve_enqueue(vx_dit* d, const float* mu, const float* cond, const float
     d->tsched = nullptr;
     VX_CUDA(ctx, cudaMalloc(&d->tsched, (size_t)(n_timesteps + 2) * 4));
     d->tsched_cap = n_timesteps + 2;
+    for (float** p : {&d->temb_all, &d->temb_tmp}) {
+      if (*p) cudaFree(*p);
+      *p = nullptr;
+      VX_CUDA(ctx, cudaMalloc(p, (size_t)(n_timesteps + 2) * d->H * 4));
+    }
   }
   // inputs staged into fixed buffers so one captured graph serves every call with this shape:
   // mu_in = [mu; 0], cond_in = [cond; cond] (unified_cfm.rs:96-98), x = z
