@@ -88,10 +88,13 @@ def test_cfm_solve_full(ctx, full_dit, sway, zero_star):
     dit.close()
 
 
-def test_dit_forward_producer_split_is_exact(full_dit):
-    """The RMSNorm, attention and SiLU*up kernels write the few-row GEMMs' split operand
-    themselves (default); VX_PRESPLIT=0 runs the separate split kernel instead.  The two
-    paths do the same arithmetic, so the LocDiT forward must match bit for bit."""
+@pytest.mark.parametrize("knob", ["VX_PRESPLIT", "VX_ATT_ROPE_FUSED"])
+def test_dit_forward_fusions_are_exact(full_dit, knob):
+    """Fusions that must not change a bit of the per-kernel LocDiT forward:
+    VX_PRESPLIT — the RMSNorm, attention and SiLU*up kernels write the few-row GEMMs' split
+    operand themselves (default) instead of a separate split kernel;
+    VX_ATT_ROPE_FUSED — the attention rotates q / k as it loads them from the fused
+    projection (default) instead of after a separate RoPE + scatter pass."""
     from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
     from voxcpm_rs_b200.minicpm4 import Context
     dcfg, w, _ = full_dit
@@ -101,15 +104,15 @@ def test_dit_forward_producer_split_is_exact(full_dit):
     cond = rng.standard_normal((2, 64, 4), dtype=np.float32)
     outs = []
     for flag in ("0", "1"):
-        old_env = os.environ.get("VX_PRESPLIT")
-        os.environ["VX_PRESPLIT"] = flag
+        old_env = os.environ.get(knob)
+        os.environ[knob] = flag
         try:
             c = Context(0)
         finally:
             if old_env is None:
-                del os.environ["VX_PRESPLIT"]
+                del os.environ[knob]
             else:
-                os.environ["VX_PRESPLIT"] = old_env
+                os.environ[knob] = old_env
         dit = VoxCpmLocDiTV2(c, dcfg, w)
         outs.append(dit.forward(_t(x), _t(mu), [0.4, 0.4], _t(cond), [0.0, 0.0]).cpu().numpy())
         dit.close()

@@ -1,6 +1,8 @@
 """MiniCPM-4 model parity on the GPU through the C ABI: decoder layer step (the one-layer
 decode workload), causal prefill + cache fill, forward_step, and greedy decoding with
 bit-exact token ids.  Tolerance 2e-2 max-abs/rel (bf16-weight path); token ids exact."""
+import os
+
 import numpy as np
 import pytest
 
@@ -79,6 +81,34 @@ def test_prefill_and_steps(ctx, small_lm):
         assert_close(got[None], want, **BF16_TOL, what=f"forward_step {step}")
     assert m.current_length == S + 3
     m.close()
+
+
+def test_uncached_causal_forward_rope_fused_exact(small_lm):
+    """A causal forward without the cache (its keys never stored): the attention rotates q / k
+    from the fused projection (default) or reads them after the separate RoPE pass
+    (VX_ATT_ROPE_FUSED=0); same bits either way, and close to the oracle."""
+    from voxcpm_rs_b200.minicpm4 import Context, MiniCpmModel
+    cfg, w, fw = small_lm
+    rng = np.random.default_rng(14)
+    x = rng.standard_normal((2, 9, cfg.hidden_size), dtype=np.float32)
+    outs = []
+    for flag in ("0", "1"):
+        old_env = os.environ.get("VX_ATT_ROPE_FUSED")
+        os.environ["VX_ATT_ROPE_FUSED"] = flag
+        try:
+            c = Context(0)
+        finally:
+            if old_env is None:
+                del os.environ["VX_ATT_ROPE_FUSED"]
+            else:
+                os.environ["VX_ATT_ROPE_FUSED"] = old_env
+        m = MiniCpmModel(c, cfg, w, max_batch=2, max_length=64)
+        outs.append(m.forward(_t(x), True).cpu().numpy())
+        m.close()
+        c.close()
+    assert np.array_equal(outs[0], outs[1]), np.abs(outs[0] - outs[1]).max()
+    want, _ = om.model_forward(cfg, fw, x, True)
+    assert_close(outs[1], want, **BF16_TOL, what="uncached causal forward")
 
 
 def test_noncausal_forward(ctx, small_lm):

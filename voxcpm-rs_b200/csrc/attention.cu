@@ -178,7 +178,9 @@ template <int D>
 __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnPrefillArgs a) {
   // The 8 query rows of a CTA share one (batch, head) and so one KV head: 32-position K/V
   // tiles are staged in shared memory once per CTA (coalesced) and every warp reads them there.
-  constexpr int DPL = D / 32;
+  // With a.qkv the rows come straight from the fused projection and q / k are rotated here
+  // (apply_rotary_pos_emb, rope.rs:76-95): k in shared memory once per staged tile, q per lane.
+  constexpr int DPL = D / 32, HALF = D / 2;
   __shared__ __align__(16) float ks[ATT_TILE][D];
   __shared__ __align__(16) float vs[ATT_TILE][D];
   pdl_wait();
@@ -188,15 +190,33 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnPrefillArgs
   const int h = blockIdx.y, b = blockIdx.z;
   const bool active = i < a.S;
   const int g = h / (a.nh / a.nkv);  // repeat_kv head map (attention.rs:196-204)
+  const bool fused = a.qkv != nullptr;
+  const size_t W = (size_t)(a.nh + 2 * a.nkv) * D;  // fused projection row width
   float qr[DPL], o[DPL];
 #pragma unroll
   for (int e = 0; e < DPL; ++e) {
-    qr[e] = active ? a.q[((size_t)b * a.S + i) * a.nh * D + h * D + lane * DPL + e] : 0.f;
+    const int c = lane * DPL + e;
+    float x = 0.f;
+    if (active && !fused) {
+      x = a.q[((size_t)b * a.S + i) * a.nh * D + h * D + c];
+    } else if (active) {
+      const float* qrow = a.qkv + ((size_t)b * a.S + i) * W + (size_t)h * D;
+      x = qrow[c];
+      if (a.rope_tab) {  // q'[c] = q[c] cos - q[c+half] sin (c < half); q[c] cos + q[c-half] sin
+        const float xp = qrow[c < HALF ? c + HALF : c - HALF];
+        const float cs = a.rope_tab[(size_t)i * D + c % HALF], sn = a.rope_tab[(size_t)i * D + HALF + c % HALF];
+        x = c < HALF ? __fadd_rn(__fmul_rn(x, cs), __fmul_rn(-xp, sn)) : __fadd_rn(__fmul_rn(x, cs), __fmul_rn(xp, sn));
+      }
+    }
+    qr[e] = x;
     o[e] = 0.f;
   }
   float m = -INFINITY, l = 0.f;
-  const float* kb = a.k + ((size_t)(b * a.nkv + g) * a.s_max) * D;
-  const float* vb = a.v + ((size_t)(b * a.nkv + g) * a.s_max) * D;
+  const float* kb = fused ? a.qkv + (size_t)b * a.S * W + (size_t)(a.nh + g) * D
+                          : a.k + ((size_t)(b * a.nkv + g) * a.s_max) * D;
+  const float* vb = fused ? a.qkv + (size_t)b * a.S * W + (size_t)(a.nh + a.nkv + g) * D
+                          : a.v + ((size_t)(b * a.nkv + g) * a.s_max) * D;
+  const size_t kv_stride = fused ? W : (size_t)D;  // floats between consecutive positions
   // keys this CTA needs: all S (non-causal) or up to its last query row (causal mask j > i)
   const int last_row = min(a.S, (int)blockIdx.x * 8 + 8);
   const int jmax = a.causal ? last_row : a.S;
@@ -206,10 +226,22 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnPrefillArgs
     __syncthreads();
     for (int c = threadIdx.x; c < nt * (D / 4); c += 256) {
       const int row = c / (D / 4), ch = c % (D / 4);
-      *reinterpret_cast<float4*>(&ks[row][ch * 4]) = __ldg(reinterpret_cast<const float4*>(kb + (size_t)(t0 + row) * D) + ch);
-      *reinterpret_cast<float4*>(&vs[row][ch * 4]) = __ldg(reinterpret_cast<const float4*>(vb + (size_t)(t0 + row) * D) + ch);
+      *reinterpret_cast<float4*>(&ks[row][ch * 4]) =
+          __ldg(reinterpret_cast<const float4*>(kb + (size_t)(t0 + row) * kv_stride) + ch);
+      *reinterpret_cast<float4*>(&vs[row][ch * 4]) =
+          __ldg(reinterpret_cast<const float4*>(vb + (size_t)(t0 + row) * kv_stride) + ch);
     }
     __syncthreads();
+    if (fused && a.rope_tab) {  // rotate the staged k rows in place, one (position, pair) per thread
+      for (int c = threadIdx.x; c < nt * HALF; c += 256) {
+        const int row = c / HALF, j = c % HALF;
+        const float cs = a.rope_tab[(size_t)(t0 + row) * D + j], sn = a.rope_tab[(size_t)(t0 + row) * D + HALF + j];
+        const float xa = ks[row][j], xb = ks[row][j + HALF];
+        ks[row][j] = __fadd_rn(__fmul_rn(xa, cs), __fmul_rn(-xb, sn));
+        ks[row][j + HALF] = __fadd_rn(__fmul_rn(xb, cs), __fmul_rn(xa, sn));
+      }
+      __syncthreads();
+    }
     if (!active) continue;
     const int jend = min(nt, jn - t0);
     for (int jj = 0; jj < jend; ++jj) {
@@ -246,6 +278,7 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const AttnPrefillArgs
 
 cudaError_t launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t st, bool pdl) {
   if (a.nh % a.nkv != 0 || (a.d != 128 && a.d != 64)) return cudaErrorInvalidValue;
+  if (a.qkv && a.S > ATT_FUSED_ROPE_MAX_S) return cudaErrorInvalidValue;  // every CTA rotates all S keys
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.S + 7) / 8, a.nh, a.B);
   cfg.blockDim = dim3(256);

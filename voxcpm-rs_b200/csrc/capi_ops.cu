@@ -145,6 +145,7 @@ int vx_ctx_create(int device, vx_ctx** out) {
   if (const char* s = getenv("VX_PERSIST_PF")) ctx->persist_pf = std::max(0, std::min(256, atoi(s)));
   if (const char* s = getenv("VX_PERSIST_EF")) ctx->persist_ef = atoi(s) != 0;
   if (const char* s = getenv("VX_PRESPLIT")) ctx->presplit = atoi(s) != 0;
+  if (const char* s = getenv("VX_ATT_ROPE_FUSED")) ctx->att_rope_fused = atoi(s) != 0;
   if (cudaSetDevice(device) != cudaSuccess ||
       cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&ctx->counters, 4096 * sizeof(unsigned)) != cudaSuccess ||

@@ -29,6 +29,8 @@ __global__ void chan_proj_kernel(const float* __restrict__ src, int Ns, int C, i
   // grid (Ns*T, ceil(H/256)): one output channel h per thread; the W row is read in 16-byte
   // chunks (C % 8 == 0), the input column (n, :, t) is staged in shared memory
   extern __shared__ float xs[];  // [C] column of one (n, t)
+  pdl_wait();
+  pdl_launch_dependents();
   const int n = blockIdx.x / T, t = blockIdx.x % T;
   for (int c = threadIdx.x; c < C; c += blockDim.x) xs[c] = src[((size_t)n * C + c) * T + t];
   __syncthreads();
@@ -44,14 +46,16 @@ __global__ void chan_proj_kernel(const float* __restrict__ src, int Ns, int C, i
 void launch_chan_proj(const float* src, int Ns, int C, int T, const uint16_t* W, const float* b, int H, float* dst,
                       int S, int row_off, int copies, cudaStream_t st) {
   count_launch();
-  chan_proj_kernel<<<dim3(Ns * T, (H + 255) / 256), 256, C * sizeof(float), st>>>(src, Ns, C, T, W, b, H, dst, S,
-                                                                                  row_off, copies);
+  PdlLaunch l(dim3(Ns * T, (H + 255) / 256), dim3(256), C * sizeof(float), st);
+  cudaLaunchKernelEx(&l.cfg, chan_proj_kernel, src, Ns, C, T, W, b, H, dst, S, row_off, copies);
 }
 
 // out[n, c, t] = b[c] + sum_h W[c, h] * hid[n, skip + t, h]   (out_proj + swap_dims, local_dit.rs:155-158)
 __global__ void out_proj_kernel(const float* __restrict__ hid, int N, int S, int skip, int T, int H,
                                 const uint16_t* __restrict__ W, const float* __restrict__ b, int C,
                                 float* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= N * C * T) return;
   const int t = warp % T, c = (warp / T) % C, n = warp / (T * C);
@@ -84,6 +88,8 @@ __global__ void silu_inplace_kernel(float* x, size_t n) {
 // token temb[n % nt] + dtemb[n % nd] (local_dit.rs:147-152).
 __global__ void seq_head_kernel(const float* __restrict__ mu, int mu_tokens, const float* __restrict__ temb, int nt,
                                 const float* __restrict__ dtemb, int nd, int N, int S, int H, float* __restrict__ seq) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int n = blockIdx.x;
   for (int i = threadIdx.x; i < (mu_tokens + 1) * H; i += blockDim.x) {
     const int r = i / H, h = i % H;
@@ -249,8 +255,9 @@ int dit_forward_prepared(vx_dit* d, const float* x, int Nx, int copies, int N, i
   if (rc) return rc;
   const int warps = N * C * T;
   count_launch();
-  out_proj_kernel<<<(warps * 32 + 255) / 256, 256, 0, st>>>(d->hid, N, S, skip, T, H, d->out_w, d->out_b, C, out);
-  VX_CUDA(ctx, cudaGetLastError());
+  PdlLaunch lo(dim3((warps * 32 + 255) / 256), dim3(256), 0, st);
+  VX_CUDA(ctx, cudaLaunchKernelEx(&lo.cfg, out_proj_kernel, (const float*)d->hid, N, S, skip, T, H,
+                                  (const uint16_t*)d->out_w, (const float*)d->out_b, C, out));
   return VX_OK;
 }
 
@@ -303,9 +310,10 @@ int build_solve_graph(vx_dit* d, const CfmKey& k) {
     for (int step = 1; step < n && !rc; ++step) {
       if (!run[step]) continue;
       count_launch();
-      seq_head_kernel<<<N, 256, 0, st>>>(d->mu_in, mu_tokens, d->temb_all + (size_t)(step - 1) * H, 1, d->dtemb, 1,
-                                         N, S, H, d->seq);
-      if (cudaGetLastError() != cudaSuccess) {
+      PdlLaunch lh(dim3(N), dim3(256), 0, st);
+      if (cudaLaunchKernelEx(&lh.cfg, seq_head_kernel, (const float*)d->mu_in, mu_tokens,
+                             (const float*)(d->temb_all + (size_t)(step - 1) * H), 1, (const float*)d->dtemb, 1, N, S,
+                             H, d->seq) != cudaSuccess) {
         rc = fail(ctx, VX_ERR_CUDA, "cfm graph: sequence assembly launch failed");
         break;
       }

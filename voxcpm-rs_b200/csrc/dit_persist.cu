@@ -1188,20 +1188,6 @@ cudaError_t launch_dit_persist(const DitPersistArgs& a, int grid, cudaStream_t s
 }
 
 
-namespace {
-// LongRoPE cos / sin (x scaling factor) at positions 0..n_pos-1 from the f64 angles
-// (rope.rs:76-95): out [n_pos][2][half].
-__global__ void rope_pos_kernel(const RopeParams* rp, int n_pos, int half, float* out) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n_pos * half) return;
-  const int p = i / half, j = i % half;
-  const double f = ((double)p * rp->inv_freq[j]) / rp->ext[j];
-  double sd, cd;
-  sincos(f, &sd, &cd);
-  out[(size_t)p * 2 * half + j] = (float)(cd * rp->scaling_factor);
-  out[(size_t)p * 2 * half + half + j] = (float)(sd * rp->scaling_factor);
-}
-}  // namespace
 
 bool persist_stack_prepare(PersistStack& ps, const LmStackView& v, int max_rows, bool trace, bool* oom,
                            int rope_positions) {
@@ -1292,13 +1278,11 @@ bool persist_stack_prepare(PersistStack& ps, const LmStackView& v, int max_rows,
          cudaMalloc(&ps.att_cnt, units * 4) == cudaSuccess && cudaMemset(ps.att_cnt, 0, units * 4) == cudaSuccess;
   }
   if (ok && v.rope && rope_positions > 0) {
-    const int half = v.d / 2, n = rope_positions * half;
+    const int half = v.d / 2;
     ok = cudaMalloc(&ps.rope_pos, (size_t)rope_positions * 2 * half * 4) == cudaSuccess;
-    if (ok) {
-      count_launch();
-      rope_pos_kernel<<<(n + 255) / 256, 256>>>(v.rope, rope_positions, half, ps.rope_pos);
-      ok = cudaGetLastError() == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
-    }
+    if (ok)
+      ok = launch_rope_table(v.rope, rope_positions, half, ps.rope_pos, 0) == cudaSuccess &&
+           cudaDeviceSynchronize() == cudaSuccess;
   }
   if (!ok) {
     cudaGetLastError();

@@ -162,6 +162,29 @@ cudaError_t launch_rope_scatter(const float* qkv, int B, int S, int nh, int nkv,
                             vcache, s_max);
 }
 
+// ------------------------------------------------------------ LongRoPE table
+// cos / sin (x scaling factor) at positions 0..n_pos-1 from the f64 angles (rope.rs:38-46,
+// the same expression as rope_scatter_kernel, so a table entry has the bits that kernel
+// computes in place): out [n_pos][2][half] (cos row, then sin row).
+__global__ void rope_table_kernel(const RopeParams* rp, int n_pos, int half, float* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_pos * half) return;
+  const int p = i / half, j = i % half;
+  const double f = ((double)p * rp->inv_freq[j]) / rp->ext[j];
+  double sd, cd;
+  sincos(f, &sd, &cd);
+  out[(size_t)p * 2 * half + j] = (float)(cd * rp->scaling_factor);
+  out[(size_t)p * 2 * half + half + j] = (float)(sd * rp->scaling_factor);
+}
+
+cudaError_t launch_rope_table(const RopeParams* rp, int n_pos, int half, float* out, cudaStream_t st) {
+  const int n = n_pos * half;
+  if (n <= 0) return cudaErrorInvalidValue;
+  count_launch();
+  rope_table_kernel<<<(n + 255) / 256, 256, 0, st>>>(rp, n_pos, half, out);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------ RoPE apply on [B,H,S,D]
 // apply_rotary_pos_emb with explicit cos/sin rows [S, D] (rope.rs:76-95), in place.
 __global__ void rope_apply_kernel(float* x, int B, int H, int S, int d, const float* cos, const float* sin) {
@@ -318,6 +341,8 @@ __global__ void __launch_bounds__(256) cfg_euler_kernel(const float* __restrict_
                                                         int B, int n, float cfg, float one_minus_cfg, float dt,
                                                         int zero_star) {
   __shared__ float red[2][8];
+  pdl_wait();
+  pdl_launch_dependents();
   const int b = blockIdx.x;
   const float* pos = out2b + (size_t)b * n;
   const float* neg = out2b + (size_t)(B + b) * n;
@@ -375,8 +400,9 @@ cudaError_t launch_fsq_quant(float* h, size_t n, float scale, cudaStream_t st) {
 cudaError_t launch_cfg_euler(const float* out2b, float* x, int B, int n, double cfg, double dt, int zero_star,
                              cudaStream_t st) {
   count_launch();
-  cfg_euler_kernel<<<B, 256, 0, st>>>(out2b, x, B, n, (float)cfg, (float)(1.0 - cfg), (float)dt, zero_star);
-  return cudaGetLastError();
+  PdlLaunch l(dim3(B), dim3(256), 0, st);
+  return cudaLaunchKernelEx(&l.cfg, cfg_euler_kernel, out2b, x, B, n, (float)cfg, (float)(1.0 - cfg), (float)dt,
+                            zero_star);
 }
 
 }  // namespace vx

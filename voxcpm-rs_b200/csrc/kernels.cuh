@@ -28,7 +28,14 @@ struct AttnPrefillArgs {
   int causal;
   float* out;    // [B, S, nh*d]
   uint16_t* xs;  // optional: out written instead as the tcgen05 GEMM's split operand [2 B S, nh*d]
+  // optional (no KV cache, S <= ATT_FUSED_ROPE_MAX_S): q, k, v read from the fused projection
+  // rows [B*S, (nh+2nkv)*d] instead of q/k/v, with LongRoPE applied to q and k as they are
+  // loaded (rope_tab: cos / sin rows [S][2][d/2] of positions 0..S-1; null: no rotation);
+  // k, v and s_max are then unused
+  const float* qkv;
+  const float* rope_tab;
 };
+constexpr int ATT_FUSED_ROPE_MAX_S = 64;
 
 struct GemmArgs {
   const float* X;  // [M, K] (row stride ldx)

@@ -46,6 +46,7 @@ struct vx_lm {
   float* norm_w = nullptr;
   uint16_t* embed = nullptr;
   RopeParams* rope = nullptr;  // device, nullptr when no_rope
+  float* rope_tab = nullptr;   // cos / sin of positions 0..ATT_FUSED_ROPE_MAX_S-1 [pos][2][d/2]
   float* kcache = nullptr;
   float* vcache = nullptr;
 
@@ -536,7 +537,10 @@ int vx_lm_create(vx_ctx* ctx, const vx_minicpm4_config* cfg, int max_batch, int 
       return fail(ctx, rc, "%s", err.c_str());
     }
     if (cudaMalloc(&lm->rope, sizeof(RopeParams)) != cudaSuccess ||
-        cudaMemcpy(lm->rope, &rp, sizeof(RopeParams), cudaMemcpyHostToDevice) != cudaSuccess)
+        cudaMemcpy(lm->rope, &rp, sizeof(RopeParams), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMalloc(&lm->rope_tab, (size_t)ATT_FUSED_ROPE_MAX_S * lm->d * 4) != cudaSuccess ||
+        launch_rope_table(lm->rope, ATT_FUSED_ROPE_MAX_S, lm->d / 2, lm->rope_tab, 0) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess)
       return fail_free(VX_ERR_OOM, "rope params allocation failed");
   }
   const size_t H = lm->H, I = lm->I;
@@ -622,7 +626,7 @@ void vx_lm_destroy(vx_lm* lm) {
   for (void* p : {(void*)lm->bx, (void*)lm->bxn, (void*)lm->bqkv, (void*)lm->bq, (void*)lm->battn, (void*)lm->bgu,
                   (void*)lm->bact, (void*)lm->blogits, (void*)lm->bhid, (void*)lm->btokens})
     if (p) cudaFree(p);
-  void* ptrs[] = {lm->weight_slab, lm->norm_w, lm->embed, lm->rope, lm->kcache, lm->vcache, lm->d_pos,
+  void* ptrs[] = {lm->weight_slab, lm->norm_w, lm->embed, lm->rope, lm->rope_tab, lm->kcache, lm->vcache, lm->d_pos,
                   lm->d_step, lm->d_tokens, lm->x, lm->hid_norm, lm->q, lm->attn, lm->act, lm->logits,
                   lm->attn_partials,
                   lm->attn_counters, lm->argmax_partials, lm->argmax_counter, lm->pf_ids,
@@ -748,6 +752,7 @@ int vx_lm_forward(vx_lm* lm, const float* embeds, int B, int S, int causal, int 
   const bool ps_qkv = presplit_ok(ctx, &lm->ws, Mi, qkvw, H), ps_gu = presplit_ok(ctx, &lm->ws, Mi, 2 * I, H),
              ps_d = presplit_ok(ctx, &lm->ws, Mi, H, I),
              ps_o = presplit_ok(ctx, &lm->ws, Mi, H, lm->qs) && (!fill_cache || B == 1);
+  const bool rope_in_att = !fill_cache && ctx->att_rope_fused && S <= ATT_FUSED_ROPE_MAX_S;
   for (int l = 0; l < lm->L; ++l) {
     const LmLayer& w = lm->layers[l];
     // K/V for this layer: the cache itself (prefill) or a [B, nkv, S, d] temporary
@@ -764,19 +769,22 @@ int vx_lm_forward(vx_lm* lm, const float* embeds, int B, int S, int causal, int 
         VX_CUDA(ctx, launch_rope_scatter(lm->pf_qkv + (size_t)b * S * qkvw, 1, S, lm->nh, lm->nkv, lm->d, lm->rope, 0,
                                          lm->pf_q + (size_t)b * S * lm->qs, lm->kc(l, b), lm->vc(l, b), lm->max_length,
                                          st));
-    } else {
+    } else if (!rope_in_att) {
       VX_CUDA(ctx, launch_rope_scatter(lm->pf_qkv, B, S, lm->nh, lm->nkv, lm->d, lm->rope, 0, lm->pf_q, kd, vd, S, st));
     }
     if (fill_cache) {
       for (int b = 0; b < B; ++b) {
         AttnPrefillArgs ap = {lm->pf_q + (size_t)b * S * lm->qs, lm->kc(l, b), lm->vc(l, b), 1, S, lm->nh, lm->nkv,
                               lm->d, s_max, lm->attn_scale, causal, lm->pf_attn + (size_t)b * S * lm->qs,
-                              ps_o ? xs : nullptr};
+                              ps_o ? xs : nullptr, nullptr, nullptr};
         VX_CUDA(ctx, launch_attn_prefill(ap, st, true));
       }
     } else {
-      AttnPrefillArgs ap = {lm->pf_q,  kd,     vd,          B,           S, lm->nh, lm->nkv, lm->d, s_max, lm->attn_scale,
-                            causal, lm->pf_attn, ps_o ? xs : nullptr};
+      // few rows without a cache (the DiT and LocEnc stacks): q / k rotated as the attention
+      // loads them from the fused projection, no separate RoPE pass
+      AttnPrefillArgs ap = {lm->pf_q, kd, vd, B, S, lm->nh, lm->nkv, lm->d, s_max, lm->attn_scale, causal, lm->pf_attn,
+                            ps_o ? xs : nullptr, rope_in_att ? lm->pf_qkv : nullptr,
+                            rope_in_att ? lm->rope_tab : nullptr};
       VX_CUDA(ctx, launch_attn_prefill(ap, st, true));
     }
     rc = ps_o ? linear_presplit(ctx, &lm->ws, Mi, H, lm->qs, w.wo, nullptr, lm->pf_x, lm->res_scale, lm->pf_x, H, st)

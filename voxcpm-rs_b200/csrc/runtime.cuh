@@ -47,6 +47,7 @@ cudaError_t launch_tc_gemm_presplit(int M, int N, int K, const uint16_t* W, cons
 cudaError_t launch_rmsnorm_residual(const float* x, const float* r, const float* w, float resid_scale, float eps,
                                     int rows, int hidden, float* h_out, float* y_out, cudaStream_t st,
                                     uint16_t* xs = nullptr);
+cudaError_t launch_rope_table(const RopeParams* rp, int n_pos, int half, float* out, cudaStream_t st);
 cudaError_t launch_rope_scatter(const float* qkv, int B, int S, int nh, int nkv, int d, const RopeParams* rope,
                                 int pos0, float* q_out, float* kcache, float* vcache, int s_max, cudaStream_t st,
                                 const int* pos_ptr = nullptr);
@@ -86,6 +87,7 @@ struct vx_ctx {
   bool tc_gemm = true;               // tcgen05 path for few-row GEMMs (env VX_TC_GEMM=0: CUDA cores)
   bool presplit = true;              // producers write the tcgen05 GEMM's split operand (env VX_PRESPLIT=0: a split kernel)
   bool l2_prefetch = false;          // decode kernels prefetch the next kernel's weights into L2
+                                     // (env VX_L2_PREFETCH=1; measured: no gain with separate kernels)
   bool persist = true;               // batch-1 decode step as one persistent launch (env VX_PERSIST=0: 141 launches)
   int persist_nst = 0;               // its ring depth cap in stages, 0 = shared-memory limit (env VX_PERSIST_NST)
   int persist_grid = 0;              // its CTA count cap (env VX_PERSIST_GRID), 0 = one CTA per SM
@@ -93,7 +95,7 @@ struct vx_ctx {
   int persist_mlp_pf = 0;            // its MLP stages staged in L2 per earlier phase (env VX_PERSIST_MLP_PF)
   int persist_pf = 0;                // its L2 prefetch distance beyond the ring, in stages (env VX_PERSIST_PF)
   int persist_ef = 0;                // its weight copies mark L2 lines evict-first (env VX_PERSIST_EF)
-                                     // (env VX_L2_PREFETCH=1; measured: no gain with separate kernels)
+  bool att_rope_fused = true;        // few-row uncached attention applies RoPE at load (env VX_ATT_ROPE_FUSED=0: separate pass)
 };
 
 namespace vx {
