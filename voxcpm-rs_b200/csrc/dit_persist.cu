@@ -1223,7 +1223,9 @@ bool persist_stack_prepare(PersistStack& ps, const LmStackView& v, int max_rows,
   const int kchs[DP_KINDS] = {v.H / 64, v.nh * v.d / 64, v.H / 64, (int)(I / 64)};
   // (fewer CTAs per unit: fewer partial slots for the next row phase to sum; measured best for
   // the 8-row LM step at 256-row units, and for the 176-row DiT forward at 128-row units)
-  int min_pairs[DP_KINDS] = {2, 2, 8, 4};  // 176-row DiT forward: 563.5 -> 542.5 us against {2, 2, 1, 4}
+  // 176-row DiT forward (8-patch CFM solve): {4, 4, 8, 8} 5.16 ms per solve against 5.36 for {2, 2, 8, 4},
+  // 5.30-5.32 for 8 or 6 instead of any one 4 or 8, 5.51 for gate|up at 16 (same box)
+  int min_pairs[DP_KINDS] = {4, 4, 8, 8};
   if (um == DP_UM_MAX) {                    // 8-row LM step: 2.14 -> 2.05 ms against {2, 2, 1, 4}
     min_pairs[DP_KIND_QKV] = 4;
     min_pairs[DP_KIND_O] = 4;
