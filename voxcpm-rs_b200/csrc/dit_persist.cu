@@ -898,7 +898,7 @@ __global__ void __launch_bounds__(DP_THREADS, 1) dit_persist_kernel(const DitPer
         pre_kind = kind + 1;
         pre_l = l;
         pre_n = 0;
-        for (int j = 0; j < std::min(a.nst, g.c1 - g.c0); ++j) {
+        for (int j = 0; j < std::min(a.pf_stages, g.c1 - g.c0); ++j) {
           const int pi = prod_i + j, s = pi % a.nst, c = g.c0 + j;
           if (pi >= a.nst && !mbar_wait(&sm.empty[s], ((pi / a.nst) - 1) & 1, a.err)) {
             sm.flags[0] = 1;
@@ -1161,6 +1161,7 @@ cudaError_t launch_dit_persist(const DitPersistArgs& a, int grid, cudaStream_t s
   const size_t smem = dit_persist_smem(a.Rpad, a.um, a.att_mode, &nst);
   DitPersistArgs b = a;
   b.nst = nst;
+  b.pf_stages = std::max(0, std::min(a.pf_stages, nst));
   if (nst < 2 || grid <= 0 || !a.xmaps || (a.um != TC_BM && a.um != DP_UM_MAX) || a.um * a.Rpad > 512 * TC_BM)
     return cudaErrorInvalidValue;
   if (a.att_mode == DP_ATT_DECODE &&
@@ -1203,6 +1204,7 @@ bool persist_stack_prepare(PersistStack& ps, const LmStackView& v, int max_rows,
   if (const char* e = getenv("VX_DIT_UM")) um = atoi(e) == DP_UM_MAX ? DP_UM_MAX : TC_BM;
   ps.split_b = false;
   if (const char* e = getenv("VX_DIT_SPLIT_B")) ps.split_b = atoi(e) != 0;
+  if (const char* e = getenv("VX_DIT_PF")) ps.pf_stages = std::max(0, atoi(e));
   const bool shape_ok = v.L > 0 && v.L <= 64 && v.H <= 2048 && v.H % um == 0 && v.nh * v.d == v.H &&
                         v.d % 4 == 0 && v.nkv > 0 && v.nh % v.nkv == 0 && ((v.nh + 2 * v.nkv) * v.d) % um == 0 &&
                         (2 * v.I) % um == 0 && v.I % 64 == 0 && max_rows > 0;
@@ -1371,6 +1373,7 @@ DitPersistArgs persist_stack_args(const PersistStack& ps, int N, int S, const fl
   a.rope_pos = ps.rope_pos;
   a.att_part = ps.att_part;
   a.att_cnt = ps.att_cnt;
+  a.pf_stages = ps.pf_stages;
   a.segtab = ps.segtab;
   a.tab_len = ps.tab_len;
   for (int k = 0; k < DP_KINDS; ++k) {

@@ -81,6 +81,7 @@ struct DitPersistArgs {
   unsigned* bar;                  // [8 L + 2] zeroed; the last CTA out resets them
   int* err;
   int nst;                        // ring stages (set by the launcher)
+  int pf_stages;                  // weight stages of the next GEMM phase copied during a row phase (clamped to nst)
   unsigned long long* trace;      // optional [phases][grid][4] timeline (%globaltimer)
 };
 
@@ -119,6 +120,10 @@ struct PersistStack {
   unsigned* bar = nullptr;
   unsigned long long* trace = nullptr;         // optional phase timeline
   int tab_off[DP_KINDS] = {}, ncta[DP_KINDS] = {}, tab_len = 0;
+  // weight stages of the next GEMM phase each CTA copies during a row phase (env VX_DIT_PF):
+  // one keeps the row phase's L2 reads clear of the weight stream (8-row step 2.06 -> 2.03 ms,
+  // 8-patch CFM 5.15 -> 5.12 ms against a full ring; none: 2.14 ms / 5.22 ms)
+  int pf_stages = 1;
 };
 // Once, outside any capture: check the shape (hidden <= 2048, a multiple of 128), allocate
 // for up to max_rows rows, build the weight maps and segment tables.  False (ps.grid = 0)
