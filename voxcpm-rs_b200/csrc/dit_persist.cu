@@ -23,7 +23,7 @@
 // acquire counters; all CTAs are resident).
 //
 // GEMM phases: the weights are the A operand (units of UM = 128 or 256 rows, one UM x 64 TMA
-// box per K chunk, SWIZZLE_128B, no multicast); the activations are the B operand: the row
+// box per K chunk, SWIZZLE_128B, into this CTA only); the activations are the B operand: the row
 // phase before wrote them as two bf16 planes x = hi + lo ([2][Rpad][K], token-major), both
 // fetched by one 3-D box, so each K chunk is 2 UM / 128 MMAs (per 128-row tile: hi, lo) into
 // UM / 128 f32 TMEM accumulators of Rpad columns.  256-row units (stacks of <= 64 rows) halve

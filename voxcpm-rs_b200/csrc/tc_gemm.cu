@@ -12,7 +12,7 @@
 // the hi and lo columns.
 //
 // Pipeline per CTA (one 128-row weight tile x one K split): warp 0 lane 0 issues TMA tile
-// loads (SWIZZLE_128B, 64-element K blocks, no multicast) into a ring of shared-memory
+// loads (SWIZZLE_128B, 64-element K blocks, each into this CTA only) into a ring of shared-memory
 // stages; warp 1 lane 0 issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32 in TMEM) and
 // releases each stage with tcgen05.commit; after the last block all four warps read the
 // accumulator with tcgen05.ld (warp w owns TMEM lanes 32w..32w+31 = weight rows).  With

@@ -19,7 +19,7 @@
 // earlier (a TMA load may start at row -1: that row reads as zero, the causal left edge).
 //
 // Pipeline per CTA (one 128-row A tile x 128 time columns): warp 0 lane 0 issues the TMA
-// tile loads (SWIZZLE_128B, no multicast) into a ring of shared-memory stages; warp 1 lane 0
+// tile loads (SWIZZLE_128B, each into this CTA only) into a ring of shared-memory stages; warp 1 lane 0
 // issues tcgen05.mma (kind::f16) and releases each stage with tcgen05.commit; all four warps
 // then read the accumulator (tcgen05.ld; warp w owns TMEM lanes 32w..32w+31) and store
 // bias (+ residual) + acc.  Every mbarrier wait is bounded; on a timeout the CTA records an
