@@ -171,3 +171,22 @@ def test_cfm_solve_batch8(ctx, full_dit):
     assert np.abs(got - want).max() < 2e-3
     assert np.array_equal(got, again)
     dit.close()
+
+
+@pytest.mark.parametrize("B", [3, 11])
+def test_cfm_solve_ragged_batches(ctx, full_dit, B):
+    """Patch counts whose decoder rows are not a multiple of 32 (3 patches: 66 rows, padded to
+    96; 11 patches: 242 rows, padded to 256, the largest stack) through the persistent decoder,
+    against the oracle."""
+    dcfg, w, fw = full_dit
+    rng = np.random.default_rng(25 + B)
+    mu = rng.standard_normal((B, 2048), dtype=np.float32)
+    cond = (0.5 * rng.standard_normal((B, 64, 4))).astype(np.float32)
+    z = rng.standard_normal((B, 64, 4), dtype=np.float32)
+    want = old.cfm_forward(dcfg, fw, mu, 10, cond, z, 2.0, 1.0, True)
+    from voxcpm_rs_b200.locdit import VoxCpmLocDiTV2
+    dit = VoxCpmLocDiTV2(ctx, dcfg, w, max_rows=2 * B)
+    got = dit.cfm_forward(_t(mu), 10, _t(cond), _t(z), 2.0, 1.0, True).cpu().numpy()
+    assert_close(got, want, **TOL, what=f"cfm solve B={B}")
+    assert np.abs(got - want).max() < 2e-3
+    dit.close()
