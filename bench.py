@@ -731,6 +731,19 @@ def run_cfm_only(batch=1):
     return 0
 
 
+def run_rmsnorm_only():
+    """Small profiling case: the RMSNorm + residual op at [512, 2048] (16 rotating buffer sets,
+    1,024 timed calls in a replayed CUDA graph, as in extras.rmsnorm)."""
+    import torch
+    from __graft_entry__ import load_package
+    load_package()
+    from voxcpm_rs_b200.minicpm4 import Context
+    ctx = Context(0)
+    print(json.dumps(measure_rmsnorm(ctx, torch.device("cuda", 0))))
+    ctx.close()
+    return 0
+
+
 # ------------------------------------------------------------------ our arm
 def main():
     ap = argparse.ArgumentParser()
@@ -754,6 +767,8 @@ def main():
                     help="phase timeline of the persistent LocDiT forward in a CFM solve of B patches")
     ap.add_argument("--vae-only", action="store_true",
                     help="profiling case: two AudioVAE decodes of 1024 latent frames")
+    ap.add_argument("--rmsnorm-only", action="store_true",
+                    help="profiling case: the RMSNorm + residual op at [512, 2048] (extras.rmsnorm)")
     ap.add_argument("--lm-only", action="store_true",
                     help="profiling case: the LM-decode model, two greedy runs of 32 decode steps each")
     ap.add_argument("--lm-layers", type=int, default=LAYERS,
@@ -779,6 +794,8 @@ def main():
         return run_gen_batch(args.lm_batch_trace, trace=True)
     if args.vae_only:
         return run_vae_only()
+    if args.rmsnorm_only:
+        return run_rmsnorm_only()
     args.warmup = max(3, args.warmup)
 
     import numpy as np
