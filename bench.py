@@ -511,7 +511,8 @@ def run_lm_only(layers=LAYERS):
 def phase_trace(model, ctx, pos, layers):
     """Phase trace of one persistent decode step of `model` at position `pos`
     (vx_lm_trace_decode_step): per phase kind, medians over layers 2..L-2 of the time after
-    the previous phase was published at which the median CTA had its inputs, finished its
+    the previous phase was published at which the median CTA saw the dependency met, had its
+    input's bytes (before the RMSNorm / attention merge), had its inputs ready, finished its
     last unit and published, and the phase duration (microseconds).  Advances the model's
     position like a decode step."""
     import numpy as np
@@ -536,9 +537,12 @@ def phase_trace(model, ctx, pos, layers):
             prev = pub[p - 1]
             rows.append([pub[p] - prev, np.median(a[has, 1] - prev), np.median(a[has, 5] - prev),
                          np.max(a[has, 5] - prev), np.median(a[has, 2] - prev) if name != "head" else np.nan,
-                         int(has.sum())])
+                         int(has.sum()), np.median(a[has, 6] - prev),
+                         np.nanmedian(a[has, 7] - prev) if name != "attention" else np.nan])
         r = np.median(np.array(rows, dtype=np.float64), axis=0)
-        out[name] = {"duration_us": round(r[0], 2), "inputs_ready_us": round(r[1], 2),
+        out[name] = {"duration_us": round(r[0], 2), "dependency_met_us": round(r[6], 2),
+                     "input_bytes_in_us": None if name == "attention" else round(r[7], 2),
+                     "inputs_ready_us": round(r[1], 2),
                      "last_unit_median_us": round(r[2], 2), "last_unit_max_us": round(r[3], 2),
                      "published_us": None if name == "head" else round(r[4], 2), "ctas": int(r[5])}
     layer_us = [pub[p + 3] - pub[p - 1] for p in range(4, nph - 1, 4) if 2 <= p // 4 < layers - 1]

@@ -71,7 +71,6 @@ constexpr int PK_MAX_SMEM = 232448 - PK_MAX_LAYERS * (int)sizeof(PersistLayer); 
 constexpr int PK_KP_FLOATS = 2 * 2 * PK_ROWS * PK_CWARPS;  // per-warp row partials: 2 units x 2 row groups
 constexpr int PK_MISC_FLOATS = 64 + 64 + 64 + PK_KP_FLOATS;  // rope tables, reduction scratch, row partials
 constexpr int PK_RES_UNITS = 4;                    // residual rows preloaded per warp and phase
-constexpr int PK_XREG = 4;                         // float4 per thread held by a normalising load_x (K <= 4096)
 constexpr int NREP = 8;                            // query heads per KV head
 
 enum { PH_Q = 0, PH_ATT = 1, PH_O = 2, PH_M = 3, PH_PER_LAYER = PERSIST_PHASES_PER_LAYER, PH_HEAD = 4 };
@@ -480,8 +479,11 @@ __device__ void produce(const PersistArgs& a, const Smem& sm, int nst, const Att
 
 // x (f32 [K], produced in this launch or the previous one) -> xs, optionally RMS-normalised
 // exactly as MiniCpmRmsNorm::forward (src/minicpm4/mod.rs:62-67).  With a norm, x and the
-// norm weight are fetched in one round trip and held in registers (K <= 4096).
-__device__ void load_x(const XIn& x, const float* norm_w, int K, float eps, const Smem& sm) {
+// norm weight are fetched in one round trip and held in registers (K <= KC).
+template <int KC>
+__device__ void load_x(const PersistArgs& a, int tph, const XIn& x, const float* norm_w, int K, float eps,
+                       const Smem& sm) {
+  constexpr int PK_XREG = (KC + PK_CTHREADS * 4 - 1) / (PK_CTHREADS * 4);  // float4 per thread
   const int tid = threadIdx.x;
   if (norm_w == nullptr) {
 #pragma unroll 4
@@ -489,15 +491,35 @@ __device__ void load_x(const XIn& x, const float* norm_w, int K, float eps, cons
     csync();
     return;
   }
+  // the input's two encodings are told apart outside the load loops, and a fixed-point input
+  // is converted only after all its loads are in flight, so no conversion waits on one load
+  // while the next is still to be issued
   float4 v[PK_XREG], w[PK_XREG];
   float ss = 0.f;
+  if (x.i == nullptr) {
 #pragma unroll
-  for (int i = 0; i < PK_XREG; ++i) {
-    const int k = (tid + i * PK_CTHREADS) * 4;
-    if (k < K) {
-      v[i] = ldx4(x, k);
-      w[i] = __ldg(reinterpret_cast<const float4*>(norm_w + k));
+    for (int i = 0; i < PK_XREG; ++i) {
+      const int k = (tid + i * PK_CTHREADS) * 4;
+      if (k < K) {
+        v[i] = __ldcg(reinterpret_cast<const float4*>(x.f + k));
+        w[i] = __ldg(reinterpret_cast<const float4*>(norm_w + k));
+      }
     }
+  } else {
+    longlong2 p[PK_XREG], q[PK_XREG];
+#pragma unroll
+    for (int i = 0; i < PK_XREG; ++i) {
+      const int k = (tid + i * PK_CTHREADS) * 4;
+      if (k < K) {
+        p[i] = __ldcg(reinterpret_cast<const longlong2*>(x.i + k));
+        q[i] = __ldcg(reinterpret_cast<const longlong2*>(x.i + k + 2));
+        w[i] = __ldg(reinterpret_cast<const float4*>(norm_w + k));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PK_XREG; ++i)
+      if ((tid + i * PK_CTHREADS) * 4 < K)
+        v[i] = make_float4(from_fix(p[i].x), from_fix(p[i].y), from_fix(q[i].x), from_fix(q[i].y));
   }
 #pragma unroll
   for (int i = 0; i < PK_XREG; ++i) {
@@ -508,6 +530,7 @@ __device__ void load_x(const XIn& x, const float* norm_w, int K, float eps, cons
       ss = fmaf(v[i].w, v[i].w, ss);
     }
   }
+  if (threadIdx.x == 0) trace_mark(a, tph, 7);
   ss = group_sum(ss, sm.red, PK_CWARPS, 1);
   const float inv = 1.0f / sqrtf(ss / (float)K + eps);
 #pragma unroll
@@ -542,7 +565,7 @@ __device__ __forceinline__ unsigned* att_counters(const PersistArgs& a, int D) {
 // `use` counts this CTA's earlier merges (the parity of sm.pbar).  Returns false on a failed
 // wait.
 template <int D>
-__device__ bool att_merge(const PersistArgs& a, const AttGeo& at, const Smem& sm, int use) {
+__device__ bool att_merge(const PersistArgs& a, const AttGeo& at, const Smem& sm, int use, int tph) {
   const int nhd = a.nh * D, ns = at.nsplit;
   const size_t gstride = (size_t)PERSIST_ATT_SPLITS * NREP * (D + 4);      // shared floats per KV head
   const size_t gsrc = (size_t)PERSIST_ATT_SPLITS_MAX * NREP * (D + 4);    // global floats per KV head
@@ -553,6 +576,7 @@ __device__ bool att_merge(const PersistArgs& a, const AttGeo& at, const Smem& sm
     for (int g = 0; g < a.nkv; ++g) bulk_g2s(sm.parts + g * gstride, a.att_part + g * gsrc, bytes, sm.pbar);
   }
   const bool ok = wait_full(sm.pbar, use & 1, a.err, sm.flags);
+  if (threadIdx.x == 0) trace_mark(a, tph, 7);
   if (ok) {
     for (int e = threadIdx.x * 4; e < nhd; e += PK_CTHREADS * 4) {
       const int h = e / D, dd = e % D;
@@ -884,12 +908,13 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
     resv[k] = (kind == PH_O && lane == 0 && u < U) ? ldx1(resid, u * PK_ROWS + warp) : 0.f;
   }
   if (kind == PH_O) {
-    if (!(at.nsplit > PERSIST_ATT_SPLITS ? att_load<D>(a, sm, st.merges++) : att_merge<D>(a, at, sm, st.merges++))) {
+    if (!(at.nsplit > PERSIST_ATT_SPLITS ? att_load<D>(a, sm, st.merges++)
+                                         : att_merge<D>(a, at, sm, st.merges++, l * PH_PER_LAYER + kind))) {
       st.bad = 1;
       return st;
     }
   } else {
-    load_x(xsrc, norm_w, K, a.eps, sm);
+    load_x<KC>(a, kind == PH_HEAD ? a.L * PH_PER_LAYER : l * PH_PER_LAYER + kind, xsrc, norm_w, K, a.eps, sm);
   }
   if (tid == 0) trace_mark(a, kind == PH_HEAD ? a.L * PH_PER_LAYER : l * PH_PER_LAYER + kind, 1);
   // Each warp owns a K slice of every row (columns warp*SL + lane*CPL ..), so a lane needs
@@ -1202,6 +1227,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) persist_decode_kernel(const Per
         st.bad = 1;
         break;
       }
+      if (tid == 0) trace_mark(a, ph, 6);
       if (kind == PH_ATT) {
         if (tid == 0) trace_mark(a, ph, 1);
         st = att_units<KC, D>(a, sm, st, nst, at, l, first);

@@ -68,9 +68,9 @@ struct PersistArgs {
   // Optional phase trace (nullptr: off): per phase p (4 per layer, then the head) and CTA c,
   // trace[(p * grid + c) * PERSIST_TRACE_FIELDS + k] = %globaltimer ns at k = 0 consumer
   // phase start, 1 inputs ready (dependency met, x loaded), 2 phase published, 3 producer's
-  // first copy of the phase issued, 4 its last copy issued, 5 last unit computed, 6 first
-  // stage available, 7 first unit's dot products done (GEMV phases).  Zero where the CTA had
-  // no units.
+  // first copy of the phase issued, 4 its last copy issued, 5 last unit computed, 6 dependency
+  // met (the previous phase's counter seen), 7 the phase input's bytes arrived (before the
+  // RMSNorm or attention-merge arithmetic; GEMV phases).  Zero where the CTA had no units.
   unsigned long long* trace;
 };
 
