@@ -142,6 +142,7 @@ int vx_ctx_create(int device, vx_ctx** out) {
   if (const char* s = getenv("VX_PERSIST_GRID")) ctx->persist_grid = std::max(0, atoi(s));
   if (const char* s = getenv("VX_PERSIST_INFLIGHT")) ctx->persist_inflight = std::max(0, atoi(s));
   if (const char* s = getenv("VX_PERSIST_MLP_PF")) ctx->persist_mlp_pf = std::max(0, std::min(64, atoi(s)));
+  if (const char* s = getenv("VX_PERSIST_MERGE_TILES")) ctx->persist_merge_tiles = std::max(0, atoi(s));
   if (const char* s = getenv("VX_PERSIST_PF")) ctx->persist_pf = std::max(0, std::min(256, atoi(s)));
   if (const char* s = getenv("VX_PERSIST_EF")) ctx->persist_ef = atoi(s) != 0;
   if (const char* s = getenv("VX_PRESPLIT")) ctx->presplit = atoi(s) != 0;

@@ -312,6 +312,7 @@ cudaError_t enqueue_persist_step(vx_lm* lm, cudaStream_t st, bool cooperative,
   a.evict_first = lm->ctx->persist_ef;
   a.inflight = lm->ctx->persist_inflight;
   a.mlp_pf = lm->ctx->persist_mlp_pf;
+  a.merge_tiles = lm->ctx->persist_merge_tiles;
   return launch_persist(a, lm->pk_grid, lm->ctx->persist_nst, st, cooperative);
 }
 

@@ -160,6 +160,7 @@ struct Smem {
 // positions cover [0, len); split sp of a KV head covers tiles [sp*tps, (sp+1)*tps).
 struct AttGeo {
   int pos, len, span, ntiles, nsplit, tps, items;
+  bool merge_once;  // the last split of a KV head merges its splits (else every o_proj CTA does)
 };
 
 __device__ __forceinline__ int att_tiles(const AttGeo& at, int u) {
@@ -821,7 +822,7 @@ __device__ __forceinline__ CState att_units(const PersistArgs& a, const Smem& sm
       st.bad = 1;
       break;
     }
-    if (at.nsplit > PERSIST_ATT_SPLITS) att_finish<D>(a, at, u, sm);
+    if (at.merge_once) att_finish<D>(a, at, u, sm);
   }
   return st;
 }
@@ -908,7 +909,7 @@ __device__ __forceinline__ CState gemv_units(const PersistArgs& a, const Smem& s
     resv[k] = (kind == PH_O && lane == 0 && u < U) ? ldx1(resid, u * PK_ROWS + warp) : 0.f;
   }
   if (kind == PH_O) {
-    if (!(at.nsplit > PERSIST_ATT_SPLITS ? att_load<D>(a, sm, st.merges++)
+    if (!(at.merge_once ? att_load<D>(a, sm, st.merges++)
                                          : att_merge<D>(a, at, sm, st.merges++, l * PH_PER_LAYER + kind))) {
       st.bad = 1;
       return st;
@@ -1162,10 +1163,11 @@ __global__ void __launch_bounds__(PK_THREADS, 1) persist_decode_kernel(const Per
   at.len = at.pos + 1;
   at.span = att_span;
   at.ntiles = (at.len + att_span - 1) / att_span;
-  // up to 16 tiles: at most PERSIST_ATT_SPLITS splits, merged from shared memory in every o_proj
-  // CTA; longer caches: a split per tile (up to the grid), merged once per KV head
-  at.nsplit = at.ntiles <= 2 * PERSIST_ATT_SPLITS ? min(at.ntiles, PERSIST_ATT_SPLITS)
-                                                  : min(at.ntiles, min(PERSIST_ATT_SPLITS_MAX, max(1, G / a.nkv)));
+  // up to merge_tiles tiles: at most PERSIST_ATT_SPLITS splits, merged from shared memory in
+  // every o_proj CTA; longer caches: a split per tile (up to the grid), merged once per KV head
+  at.merge_once = at.ntiles > a.merge_tiles;
+  at.nsplit = !at.merge_once ? min(at.ntiles, PERSIST_ATT_SPLITS)
+                             : min(at.ntiles, min(PERSIST_ATT_SPLITS_MAX, max(1, G / a.nkv)));
   at.tps = (at.ntiles + at.nsplit - 1) / at.nsplit;
   at.nsplit = (at.ntiles + at.tps - 1) / at.tps;
   at.items = a.nkv * at.nsplit;

@@ -65,6 +65,10 @@ struct PersistArgs {
   int inflight;
   // MLP stages each of the Q, ATT and O phases prefetches into L2 for the layer's MLP phase.
   int mlp_pf;
+  // Caches of more than merge_tiles 32-position tiles: one attention split per tile, the last
+  // split of a KV head to finish merges them once; shorter caches: at most
+  // PERSIST_ATT_SPLITS splits, merged by every o_proj CTA.
+  int merge_tiles;
   // Optional phase trace (nullptr: off): per phase p (4 per layer, then the head) and CTA c,
   // trace[(p * grid + c) * PERSIST_TRACE_FIELDS + k] = %globaltimer ns at k = 0 consumer
   // phase start, 1 inputs ready (dependency met, x loaded), 2 phase published, 3 producer's

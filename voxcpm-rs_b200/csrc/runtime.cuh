@@ -93,6 +93,8 @@ struct vx_ctx {
   int persist_grid = 0;              // its CTA count cap (env VX_PERSIST_GRID), 0 = one CTA per SM
   int persist_inflight = 0;          // its ring copies in flight cap (env VX_PERSIST_INFLIGHT), 0 = none
   int persist_mlp_pf = 0;            // its MLP stages staged in L2 per earlier phase (env VX_PERSIST_MLP_PF)
+  int persist_merge_tiles = 16;      // caches of more tiles merge the attention splits once per KV head
+                                     // (env VX_PERSIST_MERGE_TILES; fewer: every o_proj CTA merges)
   int persist_pf = 0;                // its L2 prefetch distance beyond the ring, in stages (env VX_PERSIST_PF)
   int persist_ef = 0;                // its weight copies mark L2 lines evict-first (env VX_PERSIST_EF)
   bool att_rope_fused = true;        // few-row uncached attention applies RoPE at load (env VX_ATT_ROPE_FUSED=0: separate pass)
