@@ -125,3 +125,21 @@ def test_greedy_ids_vs_transformers(which):
     got = out[0, len(prompt):].tolist()
     print(f"{which}: ids {want}, top-2 margin min {min(margins):.4f} max {max(margins):.4f}")
     assert got == list(want)
+
+
+def test_noncausal_forward_vs_transformers():
+    """The non-causal ``MiniCpmModel::forward`` that LocDiT and LocEnc run (model.rs:64-84
+    with ``is_causal`` false) against LlamaModel given an all-zero additive attention mask
+    (every row attends to every position)."""
+    cfg = _configs()["short"]
+    fw = _weights(cfg, 5, 0.2)
+    ids = np.random.default_rng(11).integers(0, cfg.vocab_size, 16)
+    x = om.embed(cfg, fw, ids[None])
+    want, _ = om.model_forward(cfg, fw, x, False, om.RopeRows(cfg, 16))
+    causal, _ = om.model_forward(cfg, fw, x, True, om.RopeRows(cfg, 16))
+    m = _llama(cfg, fw)
+    with torch.no_grad():
+        got = m.model(input_ids=torch.from_numpy(ids)[None],
+                      attention_mask=torch.zeros(1, 1, 16, 16)).last_hidden_state[0].numpy()
+    assert np.abs(got - want[0]).max() < 2e-4 * max(1.0, float(np.abs(want).max()))
+    assert np.abs(got - causal[0]).max() > 0.1  # the mask really lifted causality
