@@ -1,6 +1,7 @@
 """The persistent decode step (one launch per token) against the per-kernel step and the
 oracle: greedy ids bit-exact, last logits within the bf16-weight tolerance, one kernel per
-replayed step, long-context attention (32 splits), and a second run after reset."""
+replayed step, long-context attention (32 splits), the once-per-KV-head split merge at short
+caches, and a second run after reset."""
 import os
 
 import numpy as np
@@ -14,17 +15,21 @@ pytestmark = pytest.mark.gpu
 BF16_TOL = dict(atol=2e-2, rtol=2e-2)
 
 
-def _context(persist):
+def _context(persist, **env):
+    """A context created with VX_PERSIST (and any other VX_* settings in ``env``) set; the
+    library reads them at context creation."""
     from voxcpm_rs_b200.minicpm4 import Context
-    old = os.environ.get("VX_PERSIST")
-    os.environ["VX_PERSIST"] = "1" if persist else "0"
+    env = {"VX_PERSIST": "1" if persist else "0", **env}
+    old = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
     try:
         return Context(0)
     finally:
-        if old is None:
-            del os.environ["VX_PERSIST"]
-        else:
-            os.environ["VX_PERSIST"] = old
+        for k, v in old.items():
+            if v is None:
+                del os.environ[k]
+            else:
+                os.environ[k] = v
 
 
 @pytest.fixture(scope="module")
@@ -67,6 +72,28 @@ def test_persist_matches_per_kernel_and_oracle(two_layer):
     assert got[True] == want, f"persistent: {got[True]} vs {want}"
     assert got[False] == want
     assert_close(logits[True], logits[False], atol=1e-4, rtol=1e-4, what="persistent vs per-kernel logits")
+
+
+def test_persist_merge_once_short_cache(two_layer):
+    """VX_PERSIST_MERGE_TILES=0: at positions 64-88 (3 tiles) the attention splits are merged
+    once per KV head by the last split (the long-cache path) instead of by every o_proj CTA;
+    ids bit-exact with the oracle, logits within 1e-4 of the default merge."""
+    from voxcpm_rs_b200 import synth
+    from voxcpm_rs_b200.minicpm4 import MiniCpmModel
+    cfg, w, fw = two_layer
+    prompt = synth.prompt_ids(64, cfg.vocab_size, seed=0)
+    n_steps = 24
+    want = om.greedy_generate(cfg, fw, prompt, n_steps, 4096)
+    got, logits = {}, {}
+    for tiles in ("16", "0"):
+        ctx = _context(True, VX_PERSIST_MERGE_TILES=tiles)
+        m = MiniCpmModel(ctx, cfg, w, max_length=4096)
+        got[tiles] = m.greedy(prompt, n_steps).tolist()
+        logits[tiles] = m.last_logits().copy()
+        m.close()
+        ctx.close()
+    assert got["0"] == want and got["16"] == want
+    assert_close(logits["0"], logits["16"], atol=1e-4, rtol=1e-4, what="merge once vs every-CTA merge logits")
 
 
 def test_persist_long_context(two_layer):
