@@ -619,13 +619,12 @@ __device__ void att_finish(const PersistArgs& a, const AttGeo& at, int u, const 
   const int g = u / at.nsplit, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     unsigned* cnt = att_counters(a, D) + g;
-    __threadfence();
-    const unsigned prev = atomicAdd(cnt, 1u);
+    // release: this CTA's partial (stored before the consumer barrier) is visible to the split
+    // that arrives last; acquire: the last split then sees every other split's partial
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(cnt) : "memory");
     sm.flags[1] = prev == (unsigned)at.nsplit - 1 ? 1 : 0;
-    if (sm.flags[1]) {
-      __threadfence();
-      *cnt = 0u;
-    }
+    if (sm.flags[1]) *cnt = 0u;
   }
   csync();
   if (sm.flags[1]) {
@@ -716,10 +715,10 @@ struct CState {
 };
 
 // One attention unit: query heads g*8..g*8+7 against the positions of its tiles
-// (attention.rs:129-150 for one split).  Warp r is query head r, lane j scores position
-// j0 + j of a tile (dims visited in a lane-rotated order so the row-per-lane reads hit
-// distinct banks); the softmax runs online across the unit's tiles.  Leaves the partial
-// (o, m, l) in att_part.  Returns false if the CTA must stop.
+// (attention.rs:129-150 for one split).  Warp r is query head r; its lanes split the head's
+// dims for the dot products and the reduce-scatter hands lane j the score of position j0 + j
+// of a tile; the softmax runs online across the unit's tiles.  Leaves the partial (o, m, l)
+// in att_part.  Returns false if the CTA must stop.
 template <int KC, int D>
 __device__ bool att_unit(const PersistArgs& a, const AttGeo& at, int l, int u, const Smem& sm, CState& st, int nst) {
   constexpr int NC = D / 4, DPL = D / 32;
@@ -760,24 +759,43 @@ __device__ bool att_unit(const PersistArgs& a, const AttGeo& at, int l, int u, c
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     if (sync_or(lbad)) return false;
-    // scores q.k^T * scale (attention.rs:166)
-    float sc0 = 0.f, sc1 = 0.f, sc2 = 0.f, sc3 = 0.f;  // four independent FMA chains
-    if (lane < nt) {
-      const float* kr = Ks + (size_t)lane * D;
-      const float* qr = qs + warp * D;
-#pragma unroll 8
-      for (int ch = 0; ch < NC; ++ch) {
-        const int c = (ch + lane) & (NC - 1);
-        const float4 kk = *reinterpret_cast<const float4*>(kr + c * 4);
-        const float4 qq = *reinterpret_cast<const float4*>(qr + c * 4);
-        sc0 = fmaf(qq.x, kk.x, sc0);
-        sc1 = fmaf(qq.y, kk.y, sc1);
-        sc2 = fmaf(qq.z, kk.z, sc2);
-        sc3 = fmaf(qq.w, kk.w, sc3);
+    // scores q.k^T * scale (attention.rs:166): lane l holds dims [l DPL, (l + 1) DPL) of its
+    // warp's query head and forms its partial dot product with every position of the tile
+    // (a K row is one contiguous 32-lane read); a butterfly reduce-scatter over the lanes then
+    // leaves position l's full score in lane l (fixed order: deterministic)
+    float qv[DPL];
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) qv[e] = qs[warp * D + lane * DPL + e];
+    float sc[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float t = 0.f;
+      if (j < nt) {
+        const float* kr = Ks + (size_t)j * D + lane * DPL;
+        if constexpr (DPL == 4) {
+          const float4 kk = *reinterpret_cast<const float4*>(kr);
+          t = fmaf(qv[0], kk.x, t);
+          t = fmaf(qv[1], kk.y, t);
+          t = fmaf(qv[2], kk.z, t);
+          t = fmaf(qv[3], kk.w, t);
+        } else {
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) t = fmaf(qv[e], kr[e], t);
+        }
+      }
+      sc[j] = t;
+    }
+#pragma unroll
+    for (int bit = 16; bit >= 1; bit >>= 1) {  // keep the half of the positions whose bit matches
+      const bool up = (lane & bit) != 0;
+#pragma unroll
+      for (int i = 0; i < bit; ++i) {
+        const float send = up ? sc[i] : sc[i + bit];
+        sc[i] = (up ? sc[i + bit] : sc[i]) + __shfl_xor_sync(0xffffffffu, send, bit);
       }
     }
     const bool valid = lane < nt;
-    const float sv = valid ? ((sc0 + sc1) + (sc2 + sc3)) * a.attn_scale : -INFINITY;
+    const float sv = valid ? sc[0] * a.attn_scale : -INFINITY;
     const float mn = fmaxf(m, warp_max(sv));
     const float corr = expf(m - mn);  // 0 on the first tile (m = -inf)
     const float p = valid ? expf(sv - mn) : 0.f;
@@ -792,8 +810,16 @@ __device__ bool att_unit(const PersistArgs& a, const AttGeo& at, int l, int u, c
     for (int j = 0; j < nt; ++j) {
       const float pj = ps[j];
       const float* vr = Vs + (size_t)j * D + lane * DPL;
+      if constexpr (DPL == 4) {
+        const float4 vv = *reinterpret_cast<const float4*>(vr);
+        o[0] = fmaf(pj, vv.x, o[0]);
+        o[1] = fmaf(pj, vv.y, o[1]);
+        o[2] = fmaf(pj, vv.z, o[2]);
+        o[3] = fmaf(pj, vv.w, o[3]);
+      } else {
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) o[e] = fmaf(pj, vr[e], o[e]);
+        for (int e = 0; e < DPL; ++e) o[e] = fmaf(pj, vr[e], o[e]);
+      }
     }
     __syncwarp();  // ps is rewritten by the next tile
     m = mn;
