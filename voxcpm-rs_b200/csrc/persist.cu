@@ -19,9 +19,11 @@
 //   ATT  flash-decode over the cached prefix (attention.rs:129-150, 156-204); unit = one KV
 //        head's 8 query heads against a run of 32-position tiles whose K/V rows arrive
 //        through the ring (the current position's row, written by Q, is read after the
-//        wait); each unit leaves its online-softmax partial (o, max, sum) in global memory.
-//        Caches of more than 16 tiles get a unit per tile (up to 64 per KV head) and the
-//        last unit of a KV head to finish merges its partials into the attention output.
+//        wait); warp = query head, its lanes split the head's dims and a butterfly
+//        reduce-scatter gives lane j position j's score; each unit leaves its online-softmax
+//        partial (o, max, sum) in global memory.  Caches of more than merge_tiles tiles (16
+//        by default) get a unit per tile (up to 64 per KV head) and the last unit of a KV
+//        head to finish merges its partials into the attention output.
 //   O    the attention output (short caches: every CTA merges the <= 8 partials per KV head
 //        itself from one bulk copy) -> o_proj + residual into x1 (attention.rs:153,
 //        layer.rs:67); unit = 8 rows.  Also seeds the next layer's residual accumulator
